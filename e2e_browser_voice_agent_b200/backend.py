@@ -1,0 +1,170 @@
+"""The "cuda" backend object: the shape of the reference's CPU / WebGPU backends over libh2cuda.
+
+createCPU (h2-own-inference-engine/engine/cpu.js:17-69) returns
+  {name, ctx, threads, build, memoryBytes, info, forward, readLogits, rawForward, profile, readTest, barrierTest,
+   destroy};
+create_cuda returns an object with the same members (snake_case) whose work runs in libh2cuda on a B200:
+  forward(ids, pos, temperature=0, seed=1, want_logits=False) -> next token id
+      writes ids at pos; raises RuntimeError("context full") when pos + len(ids) >= ctx (cpu-worker.js:173);
+      prompts run in chunks of prefill_chunk tokens; logits exist for the last id only.
+  read_logits() -> float32 array of the last forward's logits, or None (cpu.js:60-62: the CPU backend keeps them
+      only when asked with want_logits / keep_logits)
+  raw_forward(ids, pos) -> {"next", "ms", "logits"} (cpu.js:63)
+  profile(ids, pos) -> {op name: ms} (cpu-worker.js:31-37 names)
+  destroy()
+Added for the multi-session configuration: every call takes an optional `seq` (an independent KV cache).
+
+Weight upload follows the CPU host's init (cpu-worker.js:57-128): per layer the [q;k;v] and [gate;up] Q4_0
+matrices are concatenated row-wise, norms and [bq;bk;bv] biases are F32, token_embd is Q4_0 and output.weight is
+Q8_0 (the reference's requirement) or Q4_0; a model without output.weight uses tied embeddings.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import time
+from typing import Dict, Optional, Sequence
+
+import numpy as np
+
+from . import _lib
+from . import gguf as G
+
+
+class CudaBackend:
+    name = "cuda"
+
+    def __init__(self, parsed, data, cfg: Dict, ctx: int = 2048, prefill_chunk: int = 16, max_seqs: int = 1,
+                 device: int = 0, keep_logits: bool = False, on_progress=None):
+        L = _lib.load()
+        self._L = L
+        D, NL, F, H, KVH, V = cfg["dim"], cfg["layers"], cfg["ffn"], cfg["heads"], cfg["kv_heads"], cfg["vocab"]
+        self.cfg = cfg
+        self.ctx = int(ctx)
+        self.prefill_chunk = int(prefill_chunk)
+        self.max_seqs = int(max_seqs)
+        self.keep_logits = keep_logits
+        c = _lib.Config(dim=D, layers=NL, ffn=F, heads=H, kv_heads=KVH, vocab=V, ctx=self.ctx,
+                        max_chunk=self.prefill_chunk, max_seqs=self.max_seqs, eps=float(cfg["eps"]),
+                        rope_theta=float(cfg["rope_theta"]))
+        h = C.c_void_p()
+        _lib.check(L.h2c_create(int(device), C.byref(c), C.byref(h)), None)
+        self._h = h
+        self._next = C.c_int32()
+        self._last_logits: Dict[int, Optional[np.ndarray]] = {}
+        T = parsed["tensors"]
+
+        def raw(name: str, want: int) -> np.ndarray:
+            t = T.get(name)
+            if t is None:
+                raise ValueError(f"{name}: missing")
+            if t["type"] != want:
+                kind = {G.TYPE["Q4_0"]: "Q4_0", G.TYPE["F32"]: "F32"}.get(want, str(want))
+                raise ValueError(f"{name}: expected {kind}")  # cpu-worker.js:105, 112
+            return G.tensor_view(data, t)
+
+        def put(kind: int, layer: int, ggml_type: int, blob: np.ndarray) -> None:
+            blob = np.ascontiguousarray(blob)
+            _lib.check(L.h2c_set_tensor(self._h, kind, layer, ggml_type, blob.ctypes.data, blob.nbytes), self._h)
+
+        q4, f32 = G.TYPE["Q4_0"], G.TYPE["F32"]
+        for l in range(NL):
+            p = f"blk.{l}."
+            put(_lib.KIND_QKV, l, q4, np.concatenate([raw(p + n, q4) for n in ("attn_q.weight", "attn_k.weight", "attn_v.weight")]))
+            put(_lib.KIND_O, l, q4, raw(p + "attn_output.weight", q4))
+            put(_lib.KIND_GATE_UP, l, q4, np.concatenate([raw(p + n, q4) for n in ("ffn_gate.weight", "ffn_up.weight")]))
+            put(_lib.KIND_DOWN, l, q4, raw(p + "ffn_down.weight", q4))
+            put(_lib.KIND_ATTN_NORM, l, f32, raw(p + "attn_norm.weight", f32))
+            put(_lib.KIND_FFN_NORM, l, f32, raw(p + "ffn_norm.weight", f32))
+            put(_lib.KIND_QKV_BIAS, l, f32, np.concatenate([raw(p + n, f32) for n in ("attn_q.bias", "attn_k.bias", "attn_v.bias")]))
+            if on_progress:
+                on_progress(l + 1, NL)
+        put(_lib.KIND_EMBED, 0, q4, raw("token_embd.weight", q4))
+        out = T.get("output.weight")
+        if out is not None:
+            if out["type"] not in (G.TYPE["Q8_0"], G.TYPE["Q4_0"]):
+                raise ValueError("output.weight: expected Q8_0")  # cpu-worker.js:126
+            put(_lib.KIND_OUTPUT, 0, out["type"], G.tensor_view(data, out))
+        put(_lib.KIND_OUTPUT_NORM, 0, f32, raw("output_norm.weight", f32))
+        self.memory_bytes = int(L.h2c_device_bytes(self._h))
+        self.build = _lib.LIB_PATH
+        self.threads = 1
+        self.info = (f"B200 sm_100a, {self.max_seqs} sequence(s) x {self.ctx} positions, prefill chunk "
+                     f"{self.prefill_chunk}, {self.memory_bytes / 2**20:.0f} MiB on device")
+
+    # ---------------------------------------------------------------- backend API (cpu.js:52-68)
+    def forward(self, ids: Sequence[int], pos: int, temperature: float = 0.0, seed: int = 1,
+                want_logits: bool = False, seq: int = 0) -> int:
+        if self._h is None:
+            raise RuntimeError("backend destroyed")
+        arr = np.ascontiguousarray(np.asarray(ids, dtype=np.int32).reshape(-1))
+        if pos + arr.size >= self.ctx:
+            raise RuntimeError("context full")
+        rc = self._L.h2c_forward(self._h, int(seq), arr.ctypes.data, int(arr.size), int(pos), float(temperature),
+                                 int(seed) & 0xFFFFFFFF, C.byref(self._next))
+        if rc == _lib.ERR_CONTEXT_FULL:
+            raise RuntimeError("context full")
+        _lib.check(rc, self._h)
+        self._last_logits = {}
+        if want_logits or self.keep_logits:
+            self._last_logits[seq] = self._read(seq)
+        return int(self._next.value)
+
+    def _read(self, seq: int) -> np.ndarray:
+        out = np.empty(self.cfg["vocab"], dtype=np.float32)
+        _lib.check(self._L.h2c_read_logits(self._h, int(seq), out.ctypes.data, out.size), self._h)
+        return out
+
+    def read_logits(self, seq: int = 0) -> Optional[np.ndarray]:
+        return self._last_logits.get(seq)
+
+    def raw_forward(self, ids: Sequence[int], pos: int, seq: int = 0) -> Dict:
+        t0 = time.perf_counter()
+        nxt = self.forward(ids, pos, want_logits=True, seq=seq)
+        return {"next": nxt, "ms": (time.perf_counter() - t0) * 1e3, "logits": self._last_logits.get(seq)}
+
+    def profile(self, ids: Sequence[int], pos: int, seq: int = 0) -> Dict[str, float]:
+        arr = np.ascontiguousarray(np.asarray(ids, dtype=np.int32).reshape(-1))
+        ms = (C.c_double * _lib.NPROF)()
+        _lib.check(self._L.h2c_profile(self._h, int(seq), arr.ctypes.data, int(arr.size), int(pos), ms), self._h)
+        return {n: float(ms[i]) for i, n in enumerate(_lib.PROFILE_NAMES)}
+
+    def generate(self, first_id: int, pos: int, steps: int, seq: int = 0):
+        """Greedy decode of `steps` tokens on the device (h2c_generate). Returns (ids, device milliseconds)."""
+        out = np.empty(steps, dtype=np.int32)
+        ms = C.c_float()
+        rc = self._L.h2c_generate(self._h, int(seq), int(first_id), int(pos), int(steps), out.ctypes.data, C.byref(ms))
+        if rc == _lib.ERR_CONTEXT_FULL:
+            raise RuntimeError("context full")
+        _lib.check(rc, self._h)
+        self._last_logits = {}
+        return out, float(ms.value)
+
+    def decode_kernels(self) -> int:
+        n = self._L.h2c_decode_kernels(self._h)
+        if n < 0:
+            _lib.check(n, self._h)
+        return n
+
+    def destroy(self) -> None:
+        if self._h is not None:
+            self._L.h2c_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.destroy()
+        except Exception:
+            pass
+
+
+def create_cuda(parsed, data, cfg: Dict, **opts) -> CudaBackend:
+    """The counterpart of createCPU(gguf, bytes, cfg, opts) (cpu.js:17)."""
+    return CudaBackend(parsed, data, cfg, **opts)
+
+
+def open_model(path: str, **opts) -> CudaBackend:
+    parsed, data = G.load_file(path)
+    cfg = G.qwen2_config(parsed["meta"])
+    if cfg["arch"] != "qwen2":
+        raise ValueError(f"unsupported architecture {cfg['arch']}")  # llm.js:19
+    return CudaBackend(parsed, data, cfg, **opts)

@@ -1,0 +1,700 @@
+// h2cuda: C-ABI implementation (include/h2cuda.h). The engine owns device weights, KV cache, scratch and the
+// CUDA graph of one decode step; callers pass host pointers only.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/h2cuda.h"
+#include "kernels.cuh"
+
+using namespace h2;
+
+namespace {
+
+thread_local std::string g_create_error;
+
+struct Q4Mat {
+  uint8_t* qs = nullptr;
+  __half* d = nullptr;
+  int N = 0, K = 0;
+};
+struct Q8Mat {
+  int8_t* qs = nullptr;
+  __half* d = nullptr;
+  int N = 0, K = 0;
+};
+struct LayerW {
+  Q4Mat qkv, o, gu, down;
+  float *attn_norm = nullptr, *ffn_norm = nullptr, *bqkv = nullptr;
+};
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+}  // namespace
+
+struct h2c_engine {
+  h2c_config cfg{};
+  int dev = 0, HD = 0, QKV = 0;
+  std::vector<LayerW> L;
+  Q4Mat embd;
+  Q4Mat out4;
+  Q8Mat out8;
+  int out_type = -1;  // -1 tied to embd, 2 Q4_0, 8 Q8_0
+  float* out_norm = nullptr;
+  float* rope = nullptr;
+  float *kc = nullptr, *vc = nullptr;
+  float *x = nullptr, *qkv = nullptr, *att = nullptr, *gu = nullptr, *logits = nullptr;
+  int8_t* xq = nullptr;
+  float* xd = nullptr;
+  int* xs = nullptr;
+  float* attn_part = nullptr;
+  int nsplit_max = 0;
+  float* am_v = nullptr;
+  int* am_i = nullptr;
+  int am_np = 0;
+  int32_t* prm = nullptr;      // device params [P_IDS + max_chunk]
+  int32_t* next_d = nullptr;   // device next token
+  int32_t* toklog = nullptr;   // device token log [max_seqs][ctx + 1]
+  int graph_kernels = 0;       // kernel nodes in the decode-step graph
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  int32_t* prm_h = nullptr;    // pinned host params, one slot per chunk of a forward
+  int prm_slots = 0;
+  int32_t* next_h = nullptr;   // pinned
+  cudaStream_t st = nullptr;
+  cudaGraphExec_t gexec = nullptr;
+  cudaGraph_t graph = nullptr;
+  std::string err;
+  int64_t dev_bytes = 0;
+  std::vector<void*> dallocs;
+  std::vector<int> layer_set;  // bit mask of kinds 0..6 set per layer
+  bool embd_set = false, out_norm_set = false;
+  std::vector<int> last_logits_valid;
+
+  int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    err = buf;
+    return code;
+  }
+};
+
+#define CUDA_TRY(e, call)                                                                          \
+  do {                                                                                             \
+    cudaError_t _c = (call);                                                                       \
+    if (_c != cudaSuccess) return (e)->fail(H2C_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(_c)); \
+  } while (0)
+
+namespace {
+
+int dalloc(h2c_engine* e, void** p, size_t bytes) {
+  cudaError_t c = cudaMalloc(p, bytes);
+  if (c != cudaSuccess) {
+    *p = nullptr;
+    return e->fail(c == cudaErrorMemoryAllocation ? H2C_ERR_NO_MEMORY : H2C_ERR_CUDA, "cudaMalloc(%zu): %s", bytes,
+                   cudaGetErrorString(c));
+  }
+  e->dallocs.push_back(*p);
+  e->dev_bytes += (int64_t)bytes;
+  c = cudaMemset(*p, 0, bytes);
+  if (c != cudaSuccess) return e->fail(H2C_ERR_CUDA, "cudaMemset: %s", cudaGetErrorString(c));
+  return H2C_OK;
+}
+
+template <typename T>
+int dalloc_t(h2c_engine* e, T** p, size_t count) {
+  return dalloc(e, reinterpret_cast<void**>(p), count * sizeof(T));
+}
+
+// GGUF Q4_0 blocks (18 B: fp16 d, 16 nibble bytes) -> device layout: values [N][nb][16], then fp16 scales [N][nb].
+void pack_q4_host(const uint8_t* src, int64_t nblocks, uint8_t* dst_qs, uint16_t* dst_d) {
+  for (int64_t b = 0; b < nblocks; b++) {
+    const uint8_t* s = src + b * 18;
+    dst_d[b] = (uint16_t)(s[0] | (s[1] << 8));
+    memcpy(dst_qs + b * 16, s + 2, 16);
+  }
+}
+void pack_q8_host(const uint8_t* src, int64_t nblocks, uint8_t* dst_qs, uint16_t* dst_d) {
+  for (int64_t b = 0; b < nblocks; b++) {
+    const uint8_t* s = src + b * 34;
+    dst_d[b] = (uint16_t)(s[0] | (s[1] << 8));
+    memcpy(dst_qs + b * 32, s + 2, 32);
+  }
+}
+
+int upload_q4(h2c_engine* e, Q4Mat* m, int N, int K, const void* data, uint64_t nbytes) {
+  const int64_t nb = (int64_t)N * (K / 32);
+  if ((uint64_t)nb * 18 != nbytes) return e->fail(H2C_ERR_INVALID, "Q4_0 tensor %dx%d: %llu bytes, expected %lld", N, K,
+                                                  (unsigned long long)nbytes, (long long)(nb * 18));
+  if (!m->qs) {
+    int r = dalloc_t(e, &m->qs, (size_t)nb * 16);
+    if (r) return r;
+    r = dalloc_t(e, &m->d, (size_t)nb);
+    if (r) return r;
+  }
+  std::vector<uint8_t> qs((size_t)nb * 16);
+  std::vector<uint16_t> d((size_t)nb);
+  pack_q4_host((const uint8_t*)data, nb, qs.data(), d.data());
+  CUDA_TRY(e, cudaMemcpy(m->qs, qs.data(), qs.size(), cudaMemcpyHostToDevice));
+  CUDA_TRY(e, cudaMemcpy(m->d, d.data(), d.size() * 2, cudaMemcpyHostToDevice));
+  m->N = N;
+  m->K = K;
+  return H2C_OK;
+}
+
+int upload_q8(h2c_engine* e, Q8Mat* m, int N, int K, const void* data, uint64_t nbytes) {
+  const int64_t nb = (int64_t)N * (K / 32);
+  if ((uint64_t)nb * 34 != nbytes) return e->fail(H2C_ERR_INVALID, "Q8_0 tensor %dx%d: %llu bytes, expected %lld", N, K,
+                                                  (unsigned long long)nbytes, (long long)(nb * 34));
+  if (!m->qs) {
+    int r = dalloc_t(e, &m->qs, (size_t)nb * 32);
+    if (r) return r;
+    r = dalloc_t(e, &m->d, (size_t)nb);
+    if (r) return r;
+  }
+  std::vector<uint8_t> qs((size_t)nb * 32);
+  std::vector<uint16_t> d((size_t)nb);
+  pack_q8_host((const uint8_t*)data, nb, qs.data(), d.data());
+  CUDA_TRY(e, cudaMemcpy(m->qs, qs.data(), qs.size(), cudaMemcpyHostToDevice));
+  CUDA_TRY(e, cudaMemcpy(m->d, d.data(), d.size() * 2, cudaMemcpyHostToDevice));
+  m->N = N;
+  m->K = K;
+  return H2C_OK;
+}
+
+int upload_f32(h2c_engine* e, float** p, int64_t count, const void* data, uint64_t nbytes) {
+  if ((uint64_t)count * 4 != nbytes)
+    return e->fail(H2C_ERR_INVALID, "F32 tensor: %llu bytes, expected %lld", (unsigned long long)nbytes, (long long)count * 4);
+  if (!*p) {
+    int r = dalloc_t(e, p, (size_t)count);
+    if (r) return r;
+  }
+  CUDA_TRY(e, cudaMemcpy(*p, data, nbytes, cudaMemcpyHostToDevice));
+  return H2C_OK;
+}
+
+// ---------------------------------------------------------------- launch helpers
+
+template <int MAXM>
+void launch_mv(int op, const Q4Mat& W, const int8_t* xq, const float* xd, const int* xs, int M, float* y, int ldy,
+               const float* bias, cudaStream_t st) {
+  constexpr int R = MAXM == 1 ? 2 : 1;
+  const int warps = (W.N + R - 1) / R;
+  const int blocks = (warps + 3) / 4;
+  if (op == OP_STORE) k_matvec_q4<R, MAXM, OP_STORE><<<blocks, 128, 0, st>>>(W.qs, W.d, W.N, W.K, xq, xd, xs, M, y, ldy, bias);
+  else if (op == OP_BIAS) k_matvec_q4<R, MAXM, OP_BIAS><<<blocks, 128, 0, st>>>(W.qs, W.d, W.N, W.K, xq, xd, xs, M, y, ldy, bias);
+  else k_matvec_q4<R, MAXM, OP_ADD><<<blocks, 128, 0, st>>>(W.qs, W.d, W.N, W.K, xq, xd, xs, M, y, ldy, bias);
+}
+
+// y[m] (op)= W . xq[m] for M tokens, in sub-batches of at most 8 tokens per launch
+void matvec(int op, const Q4Mat& W, const int8_t* xq, const float* xd, const int* xs, int M, float* y, int ldy,
+            const float* bias, cudaStream_t st) {
+  const int nb = W.K / 32;
+  for (int m0 = 0; m0 < M; m0 += 8) {
+    const int mm = M - m0 < 8 ? M - m0 : 8;
+    const int8_t* q = xq + (size_t)m0 * W.K;
+    const float* d = xd + (size_t)m0 * nb;
+    const int* s = xs + (size_t)m0 * nb;
+    float* yy = y + (size_t)m0 * ldy;
+    if (mm == 1) launch_mv<1>(op, W, q, d, s, mm, yy, ldy, bias, st);
+    else if (mm <= 2) launch_mv<2>(op, W, q, d, s, mm, yy, ldy, bias, st);
+    else if (mm <= 4) launch_mv<4>(op, W, q, d, s, mm, yy, ldy, bias, st);
+    else launch_mv<8>(op, W, q, d, s, mm, yy, ldy, bias, st);
+  }
+}
+
+struct Prof {
+  cudaEvent_t ev[64];
+  int op[64];
+  int n = 0;
+  bool on = false;
+};
+
+inline void mark(Prof* p, int op, cudaStream_t st) {
+  if (p && p->on && p->n < 64) {
+    p->op[p->n] = op;
+    cudaEventRecord(p->ev[p->n++], st);
+  }
+}
+
+// Enqueue one pass of M tokens (positions and ids are read from e->prm on the device). logits: compute the
+// last token's logits and the greedy next token into e->next_d.
+void enqueue_pass(h2c_engine* e, int M, bool logits, Prof* pf) {
+  const h2c_config& c = e->cfg;
+  const int D = c.dim, F = c.ffn, H = c.heads, KVH = c.kv_heads, HD = e->HD, QKV = e->QKV, NL = c.layers;
+  cudaStream_t st = e->st;
+  mark(pf, -1, st);
+  k_embed<<<M, 128, 0, st>>>(e->prm, e->embd.qs, e->embd.d, D, e->x);
+  mark(pf, 0, st);
+  for (int l = 0; l < NL; l++) {
+    const LayerW& W = e->L[l];
+    k_norm_quant<<<M, 256, 0, st>>>(e->x, 0, W.attn_norm, D, c.eps, e->xq, e->xd, e->xs);
+    mark(pf, 1, st);
+    matvec(OP_BIAS, W.qkv, e->xq, e->xd, e->xs, M, e->qkv, QKV, W.bqkv, st);
+    mark(pf, 2, st);
+    k_rope_kv<<<M, 256, 0, st>>>(e->prm, e->qkv, QKV, e->rope, e->kc, e->vc, H, KVH, HD, c.ctx, NL, l);
+    mark(pf, 3, st);
+    dim3 ag(e->nsplit_max, KVH, M);
+    if (HD == 64)
+      k_attn_split<64><<<ag, 128, 0, st>>>(e->prm, e->qkv, QKV, e->kc, e->vc, H, KVH, c.ctx, NL, l, e->attn_part, e->nsplit_max);
+    else
+      k_attn_split<128><<<ag, 128, 0, st>>>(e->prm, e->qkv, QKV, e->kc, e->vc, H, KVH, c.ctx, NL, l, e->attn_part, e->nsplit_max);
+    k_attn_combine<<<dim3(H, M), HD, 0, st>>>(e->prm, e->attn_part, H, HD, e->nsplit_max, e->att, D);
+    mark(pf, 4, st);
+    {
+      const int warps = M * (D / 32);
+      k_quant<<<(warps + 7) / 8, 256, 0, st>>>(e->att, D, M, e->xq, e->xd, e->xs);
+    }
+    mark(pf, 5, st);
+    matvec(OP_ADD, W.o, e->xq, e->xd, e->xs, M, e->x, D, nullptr, st);
+    mark(pf, 6, st);
+    k_norm_quant<<<M, 256, 0, st>>>(e->x, 0, W.ffn_norm, D, c.eps, e->xq, e->xd, e->xs);
+    mark(pf, 1, st);
+    matvec(OP_STORE, W.gu, e->xq, e->xd, e->xs, M, e->gu, 2 * F, nullptr, st);
+    mark(pf, 7, st);
+    {
+      const int warps = M * (F / 32);
+      k_swiglu_quant<<<(warps + 7) / 8, 256, 0, st>>>(e->gu, F, M, e->xq, e->xd, e->xs);
+    }
+    mark(pf, 8, st);
+    matvec(OP_ADD, W.down, e->xq, e->xd, e->xs, M, e->x, D, nullptr, st);
+    mark(pf, 9, st);
+  }
+  if (logits) {
+    k_norm_quant<<<1, 256, 0, st>>>(e->x, M - 1, e->out_norm, D, c.eps, e->xq, e->xd, e->xs);
+    if (e->out_type == 8) {
+      const int warps = (c.vocab + 1) / 2;
+      k_matvec_q8<2><<<(warps + 3) / 4, 128, 0, st>>>(e->out8.qs, e->out8.d, c.vocab, D, e->xq, e->xd, e->logits);
+    } else {
+      matvec(OP_STORE, e->out_type == 2 ? e->out4 : e->embd, e->xq, e->xd, e->xs, 1, e->logits, c.vocab, nullptr, st);
+    }
+    k_argmax1<<<e->am_np, 256, 0, st>>>(e->logits, c.vocab, e->am_v, e->am_i);
+    k_argmax2<<<1, 32, 0, st>>>(e->am_v, e->am_i, e->am_np, e->prm, e->toklog, e->cfg.ctx, e->next_d);
+    mark(pf, 10, st);
+  }
+}
+
+int check_ready(h2c_engine* e) {
+  for (int l = 0; l < e->cfg.layers; l++)
+    if (e->layer_set[l] != 0x7f) return e->fail(H2C_ERR_NOT_READY, "layer %d: tensor kinds missing (mask 0x%x)", l, e->layer_set[l]);
+  if (!e->embd_set) return e->fail(H2C_ERR_NOT_READY, "token embedding not set");
+  if (!e->out_norm_set) return e->fail(H2C_ERR_NOT_READY, "output norm not set");
+  return H2C_OK;
+}
+
+int build_graph(h2c_engine* e) {
+  if (e->gexec) return H2C_OK;
+  CUDA_TRY(e, cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal));
+  enqueue_pass(e, 1, true, nullptr);
+  cudaError_t c = cudaStreamEndCapture(e->st, &e->graph);
+  if (c != cudaSuccess) return e->fail(H2C_ERR_CUDA, "graph capture: %s", cudaGetErrorString(c));
+  CUDA_TRY(e, cudaGraphInstantiate(&e->gexec, e->graph, 0));
+  size_t nn = 0;
+  CUDA_TRY(e, cudaGraphGetNodes(e->graph, nullptr, &nn));
+  std::vector<cudaGraphNode_t> nodes(nn);
+  CUDA_TRY(e, cudaGraphGetNodes(e->graph, nodes.data(), &nn));
+  int k = 0;
+  for (auto n : nodes) {
+    cudaGraphNodeType t;
+    CUDA_TRY(e, cudaGraphNodeGetType(n, &t));
+    if (t == cudaGraphNodeTypeKernel) k++;
+  }
+  e->graph_kernels = k;
+  return H2C_OK;
+}
+
+// mulberry32 + softmax sampling in double precision, cpu-worker.js:154-167
+double mulberry32(uint32_t* s) {
+  *s = *s + 0x6d2b79f5u;
+  uint32_t t = *s;
+  t = (t ^ (t >> 15)) * (t | 1u);
+  t ^= t + (t ^ (t >> 7)) * (t | 61u);
+  return (double)(t ^ (t >> 14)) / 4294967296.0;
+}
+
+int sample_host(const float* lg, int n, double temperature, uint32_t seed) {
+  int best = 0;
+  for (int i = 1; i < n; i++)
+    if (lg[i] > lg[best]) best = i;
+  if (!(temperature > 0)) return best;
+  uint32_t s = seed;
+  const double mx = (double)lg[best] / temperature;
+  double sum = 0;
+  for (int i = 0; i < n; i++) sum += std::exp((double)lg[i] / temperature - mx);
+  double r = mulberry32(&s) * sum;
+  for (int i = 0; i < n; i++) {
+    r -= std::exp((double)lg[i] / temperature - mx);
+    if (r <= 0) return i;
+  }
+  return best;
+}
+
+int run_forward(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t pos, Prof* pf) {
+  const h2c_config& c = e->cfg;
+  if (!ids || n < 1) return e->fail(H2C_ERR_INVALID, "forward needs at least one token");
+  if (seq < 0 || seq >= c.max_seqs) return e->fail(H2C_ERR_INVALID, "sequence %d out of range [0, %d)", seq, c.max_seqs);
+  if (pos < 0) return e->fail(H2C_ERR_INVALID, "negative position");
+  if ((int64_t)pos + n >= c.ctx) return e->fail(H2C_ERR_CONTEXT_FULL, "context full");
+  for (int i = 0; i < n; i++)
+    if (ids[i] < 0 || ids[i] >= c.vocab) return e->fail(H2C_ERR_INVALID, "token id %d out of range", ids[i]);
+  int r = check_ready(e);
+  if (r) return r;
+  const int MT = c.max_chunk;
+  const int nchunks = (n + MT - 1) / MT;
+  if (nchunks > e->prm_slots) return e->fail(H2C_ERR_INVALID, "too many chunks");
+  const int stride = P_IDS + MT;
+  for (int ci = 0; ci < nchunks; ci++) {
+    const int c0 = ci * MT, mlen = n - c0 < MT ? n - c0 : MT;
+    const bool last = ci == nchunks - 1;
+    int32_t* h = e->prm_h + (size_t)ci * stride;
+    h[P_POS0] = pos + c0;
+    h[P_M] = mlen;
+    h[P_SEQ] = seq;
+    h[3] = 0;
+    memcpy(h + P_IDS, ids + c0, sizeof(int32_t) * mlen);
+    CUDA_TRY(e, cudaMemcpyAsync(e->prm, h, sizeof(int32_t) * (P_IDS + mlen), cudaMemcpyHostToDevice, e->st));
+    if (mlen == 1 && !pf) {
+      if (!e->gexec) {
+        r = build_graph(e);
+        if (r) return r;
+      }
+      CUDA_TRY(e, cudaGraphLaunch(e->gexec, e->st));
+    } else {
+      enqueue_pass(e, mlen, last, pf);
+      CUDA_TRY(e, cudaGetLastError());
+    }
+  }
+  return H2C_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int h2c_create(int device, const h2c_config* cfg, h2c_engine** out) {
+  if (!out || !cfg) {
+    g_create_error = "null argument";
+    return H2C_ERR_INVALID;
+  }
+  *out = nullptr;
+  const h2c_config& c = *cfg;
+  if (c.dim <= 0 || c.dim % 32 || c.ffn <= 0 || c.ffn % 32 || c.heads <= 0 || c.kv_heads <= 0 || c.heads % c.kv_heads ||
+      c.dim % c.heads || c.layers <= 0 || c.vocab <= 0 || c.ctx < 2 || c.max_chunk < 1 || c.max_chunk > 256 ||
+      c.max_seqs < 1) {
+    g_create_error = "invalid configuration";
+    return H2C_ERR_INVALID;
+  }
+  const int HD = c.dim / c.heads;
+  if (HD != 64 && HD != 128) {
+    g_create_error = "head_dim must be 64 or 128";
+    return H2C_ERR_INVALID;
+  }
+  if (c.heads / c.kv_heads > MAXG) {
+    g_create_error = "more than 8 query heads per KV head";
+    return H2C_ERR_INVALID;
+  }
+  h2c_engine* e = new h2c_engine();
+  e->cfg = c;
+  e->dev = device;
+  e->HD = HD;
+  e->QKV = c.dim + 2 * c.kv_heads * HD;
+  e->L.resize(c.layers);
+  e->layer_set.assign(c.layers, 0);
+  e->last_logits_valid.assign(c.max_seqs, 0);
+  auto bail = [&](int code) {
+    g_create_error = e->err;
+    h2c_destroy(e);
+    return code;
+  };
+  cudaError_t ce = cudaSetDevice(device);
+  if (ce != cudaSuccess) {
+    e->err = std::string("cudaSetDevice: ") + cudaGetErrorString(ce);
+    return bail(H2C_ERR_CUDA);
+  }
+  ce = cudaStreamCreateWithFlags(&e->st, cudaStreamNonBlocking);
+  if (ce != cudaSuccess) {
+    e->err = std::string("cudaStreamCreate: ") + cudaGetErrorString(ce);
+    return bail(H2C_ERR_CUDA);
+  }
+  const int MT = c.max_chunk, D = c.dim, F = c.ffn;
+  const size_t kv = (size_t)c.max_seqs * c.layers * c.kv_heads * c.ctx * HD;
+  e->nsplit_max = (c.ctx + ATT_CH - 1) / ATT_CH;
+  e->am_np = 296;
+  int r = 0;
+  const int KQ = F > D ? F : D;
+  if ((r = dalloc_t(e, &e->kc, kv)) || (r = dalloc_t(e, &e->vc, kv)) || (r = dalloc_t(e, &e->x, (size_t)MT * D)) ||
+      (r = dalloc_t(e, &e->qkv, (size_t)MT * e->QKV)) || (r = dalloc_t(e, &e->att, (size_t)MT * D)) ||
+      (r = dalloc_t(e, &e->gu, (size_t)MT * 2 * F)) || (r = dalloc_t(e, &e->logits, (size_t)c.vocab)) ||
+      (r = dalloc_t(e, &e->xq, (size_t)MT * KQ)) || (r = dalloc_t(e, &e->xd, (size_t)MT * KQ / 32)) ||
+      (r = dalloc_t(e, &e->xs, (size_t)MT * KQ / 32)) ||
+      (r = dalloc_t(e, &e->attn_part, (size_t)MT * c.heads * e->nsplit_max * (HD + 2))) ||
+      (r = dalloc_t(e, &e->am_v, (size_t)e->am_np)) || (r = dalloc_t(e, &e->am_i, (size_t)e->am_np)) ||
+      (r = dalloc_t(e, &e->prm, (size_t)(P_IDS + MT))) || (r = dalloc_t(e, &e->next_d, 1)) ||
+      (r = dalloc_t(e, &e->toklog, (size_t)c.max_seqs * (c.ctx + 1))) ||
+      (r = dalloc_t(e, &e->rope, (size_t)c.ctx * HD)))
+    return bail(r);
+  // RoPE table in double precision, cpu-worker.js:131-135
+  {
+    std::vector<float> t((size_t)c.ctx * HD);
+    for (int i = 0; i < HD / 2; i++) {
+      const double inv = std::pow(c.rope_theta, (2.0 * i) / HD);
+      for (int p = 0; p < c.ctx; p++) {
+        const double a = p / inv;
+        t[(size_t)p * HD + 2 * i] = (float)std::cos(a);
+        t[(size_t)p * HD + 2 * i + 1] = (float)std::sin(a);
+      }
+    }
+    ce = cudaMemcpy(e->rope, t.data(), t.size() * 4, cudaMemcpyHostToDevice);
+    if (ce != cudaSuccess) {
+      e->err = std::string("rope upload: ") + cudaGetErrorString(ce);
+      return bail(H2C_ERR_CUDA);
+    }
+  }
+  e->prm_slots = (c.ctx + MT - 1) / MT + 1;
+  ce = cudaMallocHost(&e->prm_h, sizeof(int32_t) * (size_t)(P_IDS + MT) * e->prm_slots);
+  if (ce == cudaSuccess) ce = cudaMallocHost(&e->next_h, sizeof(int32_t));
+  if (ce != cudaSuccess) {
+    e->err = std::string("pinned allocation: ") + cudaGetErrorString(ce);
+    return bail(H2C_ERR_NO_MEMORY);
+  }
+  ce = cudaEventCreate(&e->ev0);
+  if (ce == cudaSuccess) ce = cudaEventCreate(&e->ev1);
+  if (ce != cudaSuccess) {
+    e->err = std::string("cudaEventCreate: ") + cudaGetErrorString(ce);
+    return bail(H2C_ERR_CUDA);
+  }
+  *out = e;
+  return H2C_OK;
+}
+
+int h2c_set_tensor(h2c_engine* e, int kind, int layer, int ggml_type, const void* data, uint64_t nbytes) {
+  if (!e || !data) return H2C_ERR_INVALID;
+  const h2c_config& c = e->cfg;
+  CUDA_TRY(e, cudaSetDevice(e->dev));
+  if (kind < 0 || kind > 9) return e->fail(H2C_ERR_INVALID, "unknown tensor kind %d", kind);
+  if (kind <= 6 && (layer < 0 || layer >= c.layers)) return e->fail(H2C_ERR_INVALID, "layer %d out of range", layer);
+  const int D = c.dim, F = c.ffn;
+  int r = H2C_OK;
+  auto need = [&](int t) { return ggml_type == t; };
+  switch (kind) {
+    case H2C_KIND_QKV:
+    case H2C_KIND_O:
+    case H2C_KIND_GATE_UP:
+    case H2C_KIND_DOWN: {
+      if (!need(H2C_GGML_Q4_0)) return e->fail(H2C_ERR_BAD_TYPE, "layer %d kind %d: expected Q4_0", layer, kind);
+      LayerW& W = e->L[layer];
+      if (kind == 0) r = upload_q4(e, &W.qkv, e->QKV, D, data, nbytes);
+      if (kind == 1) r = upload_q4(e, &W.o, D, D, data, nbytes);
+      if (kind == 2) r = upload_q4(e, &W.gu, 2 * F, D, data, nbytes);
+      if (kind == 3) r = upload_q4(e, &W.down, D, F, data, nbytes);
+      break;
+    }
+    case H2C_KIND_ATTN_NORM:
+    case H2C_KIND_FFN_NORM:
+    case H2C_KIND_QKV_BIAS: {
+      if (!need(H2C_GGML_F32)) return e->fail(H2C_ERR_BAD_TYPE, "layer %d kind %d: expected F32", layer, kind);
+      LayerW& W = e->L[layer];
+      if (kind == 4) r = upload_f32(e, &W.attn_norm, D, data, nbytes);
+      if (kind == 5) r = upload_f32(e, &W.ffn_norm, D, data, nbytes);
+      if (kind == 6) r = upload_f32(e, &W.bqkv, e->QKV, data, nbytes);
+      break;
+    }
+    case H2C_KIND_EMBED:
+      if (!need(H2C_GGML_Q4_0)) return e->fail(H2C_ERR_BAD_TYPE, "token_embd: expected Q4_0");
+      r = upload_q4(e, &e->embd, c.vocab, D, data, nbytes);
+      if (!r) e->embd_set = true;
+      return r;
+    case H2C_KIND_OUTPUT:
+      if (need(H2C_GGML_Q8_0)) {
+        r = upload_q8(e, &e->out8, c.vocab, D, data, nbytes);
+        if (!r) e->out_type = 8;
+      } else if (need(H2C_GGML_Q4_0)) {
+        r = upload_q4(e, &e->out4, c.vocab, D, data, nbytes);
+        if (!r) e->out_type = 2;
+      } else {
+        return e->fail(H2C_ERR_BAD_TYPE, "output.weight: expected Q8_0 or Q4_0");
+      }
+      return r;
+    case H2C_KIND_OUTPUT_NORM:
+      if (!need(H2C_GGML_F32)) return e->fail(H2C_ERR_BAD_TYPE, "output_norm: expected F32");
+      r = upload_f32(e, &e->out_norm, D, data, nbytes);
+      if (!r) e->out_norm_set = true;
+      return r;
+  }
+  if (!r) e->layer_set[layer] |= 1 << kind;
+  return r;
+}
+
+int h2c_forward(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t pos, float temperature, uint32_t seed,
+                int32_t* next) {
+  if (!e || !next) return H2C_ERR_INVALID;
+  CUDA_TRY(e, cudaSetDevice(e->dev));
+  int r = run_forward(e, seq, ids, n, pos, nullptr);
+  if (r) return r;
+  const uint32_t sseed = seed + (uint32_t)pos;
+  if (temperature > 0) {
+    std::vector<float> lg(e->cfg.vocab);
+    CUDA_TRY(e, cudaMemcpyAsync(lg.data(), e->logits, lg.size() * 4, cudaMemcpyDeviceToHost, e->st));
+    CUDA_TRY(e, cudaStreamSynchronize(e->st));
+    *next = sample_host(lg.data(), e->cfg.vocab, temperature, sseed);
+  } else {
+    CUDA_TRY(e, cudaMemcpyAsync(e->next_h, e->next_d, 4, cudaMemcpyDeviceToHost, e->st));
+    CUDA_TRY(e, cudaStreamSynchronize(e->st));
+    *next = *e->next_h;
+  }
+  e->last_logits_valid.assign(e->cfg.max_seqs, 0);
+  e->last_logits_valid[seq] = 1;
+  return H2C_OK;
+}
+
+int h2c_generate(h2c_engine* e, int seq, int32_t first_id, int32_t pos, int32_t steps, int32_t* out_tokens,
+                 float* device_ms) {
+  if (!e || steps < 1) return H2C_ERR_INVALID;
+  const h2c_config& c = e->cfg;
+  if (seq < 0 || seq >= c.max_seqs) return e->fail(H2C_ERR_INVALID, "sequence %d out of range", seq);
+  if (pos < 0 || (int64_t)pos + steps >= c.ctx) return e->fail(H2C_ERR_CONTEXT_FULL, "context full");
+  if (first_id < 0 || first_id >= c.vocab) return e->fail(H2C_ERR_INVALID, "token id %d out of range", first_id);
+  CUDA_TRY(e, cudaSetDevice(e->dev));
+  int r = check_ready(e);
+  if (r) return r;
+  if (!e->gexec && (r = build_graph(e))) return r;
+  int32_t* h = e->prm_h;
+  h[P_POS0] = pos;
+  h[P_M] = 1;
+  h[P_SEQ] = seq;
+  h[3] = 0;
+  h[P_IDS] = first_id;
+  CUDA_TRY(e, cudaMemcpyAsync(e->prm, h, sizeof(int32_t) * (P_IDS + 1), cudaMemcpyHostToDevice, e->st));
+  CUDA_TRY(e, cudaEventRecord(e->ev0, e->st));
+  for (int i = 0; i < steps; i++) CUDA_TRY(e, cudaGraphLaunch(e->gexec, e->st));
+  CUDA_TRY(e, cudaEventRecord(e->ev1, e->st));
+  if (out_tokens)
+    CUDA_TRY(e, cudaMemcpyAsync(out_tokens, e->toklog + (size_t)seq * (c.ctx + 1) + pos + 1, sizeof(int32_t) * steps,
+                                cudaMemcpyDeviceToHost, e->st));
+  CUDA_TRY(e, cudaStreamSynchronize(e->st));
+  if (device_ms) CUDA_TRY(e, cudaEventElapsedTime(device_ms, e->ev0, e->ev1));
+  e->last_logits_valid.assign(c.max_seqs, 0);
+  e->last_logits_valid[seq] = 1;
+  return H2C_OK;
+}
+
+int h2c_decode_kernels(h2c_engine* e) {
+  if (!e) return H2C_ERR_INVALID;
+  CUDA_TRY(e, cudaSetDevice(e->dev));
+  if (!e->gexec) {
+    int r = check_ready(e);
+    if (r) return r;
+    if ((r = build_graph(e))) return r;
+  }
+  return e->graph_kernels;
+}
+
+int h2c_read_logits(h2c_engine* e, int seq, float* out, int64_t n) {
+  if (!e || !out) return H2C_ERR_INVALID;
+  if (seq < 0 || seq >= e->cfg.max_seqs || !e->last_logits_valid[seq])
+    return e->fail(H2C_ERR_INVALID, "no logits for sequence %d (its last forward was not the latest)", seq);
+  if (n < e->cfg.vocab) return e->fail(H2C_ERR_INVALID, "output holds %lld floats, vocab is %d", (long long)n, e->cfg.vocab);
+  CUDA_TRY(e, cudaSetDevice(e->dev));
+  CUDA_TRY(e, cudaMemcpyAsync(out, e->logits, (size_t)e->cfg.vocab * 4, cudaMemcpyDeviceToHost, e->st));
+  CUDA_TRY(e, cudaStreamSynchronize(e->st));
+  return H2C_OK;
+}
+
+int h2c_profile(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t pos, double* ms) {
+  if (!e || !ms) return H2C_ERR_INVALID;
+  CUDA_TRY(e, cudaSetDevice(e->dev));
+  Prof pf;
+  for (int i = 0; i < 64; i++) CUDA_TRY(e, cudaEventCreate(&pf.ev[i]));
+  pf.on = true;
+  int r = run_forward(e, seq, ids, n, pos, &pf);
+  if (!r) {
+    cudaError_t c = cudaStreamSynchronize(e->st);
+    if (c != cudaSuccess) r = e->fail(H2C_ERR_CUDA, "profile: %s", cudaGetErrorString(c));
+  }
+  for (int i = 0; i < H2C_NPROF; i++) ms[i] = 0;
+  if (!r) {
+    // events are reused in a ring when more than 64 marks are recorded: fold only the final window
+    for (int i = 1; i < pf.n; i++) {
+      float t = 0;
+      cudaEventElapsedTime(&t, pf.ev[i - 1], pf.ev[i]);
+      if (pf.op[i] >= 0 && pf.op[i] < H2C_NPROF) ms[pf.op[i]] += t;
+    }
+  }
+  for (int i = 0; i < 64; i++) cudaEventDestroy(pf.ev[i]);
+  if (!r) {
+    e->last_logits_valid.assign(e->cfg.max_seqs, 0);
+    e->last_logits_valid[seq] = 1;
+  }
+  return r;
+}
+
+int h2c_destroy(h2c_engine* e) {
+  if (!e) return H2C_OK;
+  cudaSetDevice(e->dev);
+  if (e->st) cudaStreamSynchronize(e->st);
+  if (e->gexec) cudaGraphExecDestroy(e->gexec);
+  if (e->graph) cudaGraphDestroy(e->graph);
+  for (void* p : e->dallocs) cudaFree(p);
+  if (e->prm_h) cudaFreeHost(e->prm_h);
+  if (e->next_h) cudaFreeHost(e->next_h);
+  if (e->ev0) cudaEventDestroy(e->ev0);
+  if (e->ev1) cudaEventDestroy(e->ev1);
+  if (e->st) cudaStreamDestroy(e->st);
+  delete e;
+  return H2C_OK;
+}
+
+const char* h2c_last_error(const h2c_engine* e) { return e ? e->err.c_str() : g_create_error.c_str(); }
+
+int64_t h2c_device_bytes(const h2c_engine* e) { return e ? e->dev_bytes : 0; }
+
+uint64_t h2c_q4_matrix_bytes(int32_t n_rows, int32_t k) {
+  const uint64_t nb = (uint64_t)n_rows * (uint64_t)(k / 32);
+  return align_up(nb * 16, 256) + align_up(nb * 2, 16);
+}
+
+int h2c_q4_pack(const void* gguf_blocks, int32_t n_rows, int32_t k, void* packed_host) {
+  if (!gguf_blocks || !packed_host || n_rows <= 0 || k <= 0 || k % 32) return H2C_ERR_INVALID;
+  const int64_t nb = (int64_t)n_rows * (k / 32);
+  uint8_t* dst = (uint8_t*)packed_host;
+  pack_q4_host((const uint8_t*)gguf_blocks, nb, dst, (uint16_t*)(dst + align_up((size_t)nb * 16, 256)));
+  return H2C_OK;
+}
+
+uint64_t h2c_q4_matvec_scratch_bytes(int32_t m, int32_t k) {
+  const uint64_t nb = (uint64_t)m * (uint64_t)(k / 32);
+  return align_up((uint64_t)m * k, 256) + align_up(nb * 4, 256) + align_up(nb * 4, 256);
+}
+
+int h2c_q4_matvec(const void* w, int32_t n_rows, int32_t k, const float* x, int32_t m, float* y, int32_t op,
+                  const float* bias, void* scratch, void* stream) {
+  if (!w || !x || !y || !scratch || n_rows <= 0 || k <= 0 || k % 32 || m < 1 || op < 0 || op > 2 || (op == 1 && !bias))
+    return H2C_ERR_INVALID;
+  if (((uintptr_t)w | (uintptr_t)scratch | (uintptr_t)x) & 15) return H2C_ERR_INVALID;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t nb = (int64_t)n_rows * (k / 32);
+  Q4Mat W;
+  W.qs = (uint8_t*)w;
+  W.d = (__half*)((uint8_t*)w + align_up((size_t)nb * 16, 256));
+  W.N = n_rows;
+  W.K = k;
+  uint8_t* s = (uint8_t*)scratch;
+  int8_t* xq = (int8_t*)s;
+  const size_t mb = (size_t)m * (k / 32);
+  float* xd = (float*)(s + align_up((size_t)m * k, 256));
+  int* xs = (int*)(s + align_up((size_t)m * k, 256) + align_up(mb * 4, 256));
+  const int warps = (int)mb;
+  k_quant<<<(warps + 7) / 8, 256, 0, st>>>(x, k, m, xq, xd, xs);
+  matvec(op, W, xq, xd, xs, m, y, n_rows, bias, st);
+  cudaError_t c = cudaGetLastError();
+  return c == cudaSuccess ? H2C_OK : H2C_ERR_CUDA;
+}
+
+}  // extern "C"

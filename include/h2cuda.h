@@ -1,0 +1,138 @@
+/* h2cuda: the B200 (sm_100a) backend of the H2 engine's Qwen2 Q4_0 token loop, as a plain C ABI.
+ *
+ * This is the drop-in boundary. It replaces the reference's WebAssembly kernel exports
+ * (h2-own-inference-engine/engine/kernels.c:418-496: set_config / set_tensor / set_buffers / run /
+ * profile_* / run_read_test), which its CPU backend host binds (cpu-worker.js:85-137, 169-182), and it
+ * implements the backend object contract of cpu.js:52-68 / webgpu.js:616-620 one layer up:
+ *   forward(ids, pos, {temperature, seed, wantLogits}) -> next token id   => h2c_forward
+ *   readLogits()                                                          => h2c_read_logits
+ *   profile(ids, pos)                                                     => h2c_profile
+ *   destroy()                                                             => h2c_destroy
+ *
+ * Ownership differs from the reference on purpose: there, JavaScript owns all memory (set_buffers); here the
+ * library owns the device weights, the KV cache, the scratch buffers and the CUDA graph of a decode step, and
+ * callers pass only host pointers. No torch types cross this boundary.
+ *
+ * Every call returns a status (H2C_OK = 0, negative on error) and never aborts; h2c_last_error() gives the
+ * message of the last failing call on that engine. Calls on one engine must be serialised by the caller (the
+ * reference keeps a single outstanding request per backend, cpu.js:33-50).
+ */
+#ifndef H2CUDA_H
+#define H2CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define H2C_OK 0
+#define H2C_ERR_INVALID (-1)      /* bad argument or call order */
+#define H2C_ERR_CONTEXT_FULL (-2) /* pos + n >= ctx: "context full", cpu-worker.js:173, webgpu.js:552 */
+#define H2C_ERR_BAD_TYPE (-3)     /* unsupported tensor type: cpu-worker.js:105, 112, 126 */
+#define H2C_ERR_CUDA (-4)         /* a CUDA runtime call failed */
+#define H2C_ERR_NOT_READY (-5)    /* forward before every tensor was set */
+#define H2C_ERR_NO_MEMORY (-6)    /* device or pinned allocation failed */
+#define H2C_ERR_TIMEOUT (-7)      /* a bounded device-side wait expired (persistent decode kernel) */
+
+/* GGML tensor types accepted by h2c_set_tensor (gguf.js:6) */
+#define H2C_GGML_F32 0
+#define H2C_GGML_Q4_0 2
+#define H2C_GGML_Q8_0 8
+
+/* tensor kinds: the numbering of the reference's set_tensor (kernels.c:422-430) */
+#define H2C_KIND_QKV 0         /* [Wq; Wk; Wv] rows concatenated, Q4_0 (cpu-worker.js:60, 108-115) */
+#define H2C_KIND_O 1           /* attn_output, Q4_0 */
+#define H2C_KIND_GATE_UP 2     /* [Wgate; Wup] rows concatenated, Q4_0 */
+#define H2C_KIND_DOWN 3        /* ffn_down, Q4_0 */
+#define H2C_KIND_ATTN_NORM 4   /* F32 [dim] */
+#define H2C_KIND_FFN_NORM 5    /* F32 [dim] */
+#define H2C_KIND_QKV_BIAS 6    /* F32 [dim + 2*kv_heads*head_dim]: [bq; bk; bv] */
+#define H2C_KIND_EMBED 7       /* token_embd, Q4_0 [vocab][dim] */
+#define H2C_KIND_OUTPUT 8      /* output.weight, Q8_0 (the reference's only type) or Q4_0; unset = tied to EMBED */
+#define H2C_KIND_OUTPUT_NORM 9 /* F32 [dim] */
+
+/* Model and runtime configuration: set_config(dim, layers, ffn, heads, kvh, vocab, ctx, mt, eps)
+ * (kernels.c:418-421) plus the RoPE base the reference host uses for its table (cpu-worker.js:131-135). */
+typedef struct h2c_config {
+  int32_t dim, layers, ffn, heads, kv_heads, vocab;
+  int32_t ctx;        /* positions per sequence (KV cache length); forward needs pos + n < ctx */
+  int32_t max_chunk;  /* tokens per prefill pass (the reference's mt / prefillChunk: cpu.js:46) */
+  int32_t max_seqs;   /* independent sequences (sessions), each with its own KV cache; >= 1 */
+  float eps;          /* RMSNorm epsilon */
+  double rope_theta;  /* RoPE frequency base (gguf.js:82) */
+} h2c_config;
+
+typedef struct h2c_engine h2c_engine;
+
+/* Per-operation device time of one forward pass, in the reference's profile order (cpu-worker.js:32). */
+#define H2C_NPROF 11
+/* 0 embed, 1 norm+quantize, 2 matvec qkv, 3 rope+kv, 4 attention, 5 quantize, 6 matvec o, 7 matvec gate+up,
+ * 8 swiglu+quantize, 9 matvec down, 10 matvec output */
+
+/* Create an engine on CUDA device `device`: allocates the KV cache and scratch (replaces set_config +
+ * set_buffers, kernels.c:418-437 and the layout of cpu-worker.js:52-88). */
+int h2c_create(int device, const h2c_config* cfg, h2c_engine** out);
+
+/* Upload one tensor from host memory holding raw GGUF bytes of `ggml_type` (blocks for Q4_0 / Q8_0, floats for
+ * F32). Replaces set_tensor (kernels.c:423-431) and the repack of cpu-worker.js:97-128: the library splits
+ * GGUF blocks into its own device layout. `layer` is ignored for kinds 7..9. */
+int h2c_set_tensor(h2c_engine* e, int kind, int layer, int ggml_type, const void* data, uint64_t nbytes);
+
+/* Run ids[0..n) of sequence `seq` at positions pos..pos+n-1 (prefill when n > 1, one decode step when n == 1)
+ * and return the next token in *next: greedy argmax (ties to the lowest id) when temperature <= 0, else a
+ * sample of softmax(logits / temperature) with mulberry32 seeded by (seed + pos) (cpu-worker.js:154-180).
+ * Prompts run in chunks of max_chunk tokens; logits exist for the last token only (kernels.c:404-414).
+ * Replaces run() (kernels.c:454-465) plus the host loop of cpu-worker.js:169-182. */
+int h2c_forward(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t pos, float temperature,
+                uint32_t seed, int32_t* next);
+
+/* Greedy decode of `steps` tokens of sequence `seq` entirely on the device: first_id is processed at `pos`, each
+ * step's argmax becomes the next step's input without a host round trip (the WebGPU backend keeps its sampled
+ * token on the GPU the same way, webgpu.js:391, 553-574). out_tokens (nullable) receives the `steps` generated
+ * ids; device_ms (nullable) the CUDA-event time of the steps on the engine's stream. Needs pos + steps < ctx.
+ * Equivalent to steps calls of h2c_forward(e, seq, &id, 1, pos + i, 0, 0, &id). */
+int h2c_generate(h2c_engine* e, int seq, int32_t first_id, int32_t pos, int32_t steps, int32_t* out_tokens,
+                 float* device_ms);
+
+/* Number of kernels one decode step launches (the kernel nodes of the decode-step CUDA graph); < 0 on error. */
+int h2c_decode_kernels(h2c_engine* e);
+
+/* Copy the logits of the last forward of `seq` (vocab floats) to host memory (cpu.js:60-62, webgpu.js:605-611). */
+int h2c_read_logits(h2c_engine* e, int seq, float* out, int64_t n);
+
+/* One forward pass like h2c_forward with greedy sampling, timing each operation with CUDA events (no graph):
+ * ms[H2C_NPROF] receives milliseconds per operation class (profile_start/get/stop, kernels.c:481-483). */
+int h2c_profile(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t pos, double* ms);
+
+/* Free everything the engine owns (cpu.js:67 destroy). Safe on NULL. */
+int h2c_destroy(h2c_engine* e);
+
+/* Message of the last error on this engine (or of the last failed h2c_create when e is NULL). */
+const char* h2c_last_error(const h2c_engine* e);
+
+/* Bytes of device memory the engine holds (cpu.js:53 memoryBytes / webgpu.js uploadedBytes). */
+int64_t h2c_device_bytes(const h2c_engine* e);
+
+/* ---- Q4_0 matvec, the reference's matmul_q4 (kernels.c:200-273) with its quantize_row (kernels.c:90-114)
+ * as a stand-alone device operation: the Q4_0 matvec microbench. Pointers are DEVICE pointers. ---- */
+
+/* Bytes of the device layout of an N x K Q4_0 matrix (values, then fp16 scales). */
+uint64_t h2c_q4_matrix_bytes(int32_t n_rows, int32_t k);
+/* Convert raw GGUF Q4_0 blocks (host) to the device layout (host buffer of h2c_q4_matrix_bytes). */
+int h2c_q4_pack(const void* gguf_blocks, int32_t n_rows, int32_t k, void* packed_host);
+/* Scratch bytes h2c_q4_matvec needs for m tokens of length k (the int8 activations and their scales). */
+uint64_t h2c_q4_matvec_scratch_bytes(int32_t m, int32_t k);
+/* y[m][n] (op)= W[n] . quantize(x[m]) for m < M on `stream` (a cudaStream_t, 0 = default).
+ * op: 0 store, 1 add bias[n], 2 accumulate into y (the reference's put(): kernels.c:190-194).
+ * w: packed matrix (h2c_q4_pack layout) on the device; x: float32 [M][K]; y: float32 [M][N]; bias: float32 [N]
+ * or NULL; scratch: h2c_q4_matvec_scratch_bytes(M, K) bytes of device memory, 16-byte aligned. */
+int h2c_q4_matvec(const void* w, int32_t n_rows, int32_t k, const float* x, int32_t m, float* y, int32_t op,
+                  const float* bias, void* scratch, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

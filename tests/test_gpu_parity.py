@@ -1,0 +1,188 @@
+"""Parity of the CUDA engine with the CPU oracle (the reference's algorithm), through the C ABI.
+
+Tolerances (north star): per-step logits under teacher forcing within max-abs 2e-3 of the logit range; greedy
+tokens identical except where the oracle's top-2 gap is below that tolerance. Integer parts (Q4_0 unpacking,
+int8 activation quantization, block dot products) are exact; only float summation order differs, so the
+matvec microbench is held to a much tighter 1e-5 of the output range.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from e2e_browser_voice_agent_b200 import _lib, backend, synth
+from e2e_browser_voice_agent_b200 import gguf as G
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-3
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _gpu():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    _lib.load()
+
+
+def rel_err(a, b):
+    return float(np.abs(a - b).max() / (b.max() - b.min()))
+
+
+def top2_gap(lg):
+    s = np.sort(lg)
+    return float((s[-1] - s[-2]) / (lg.max() - lg.min()))
+
+
+def teacher_forced(model, n_prompt, steps, chunk, ctx=96, seed=0):
+    path = synth.ensure(model)
+    be = backend.open_model(path, ctx=ctx, prefill_chunk=chunk)
+    ref = O.open_model("oracle", path, ctx=ctx, mt=chunk, threads=4)
+    V = be.cfg["vocab"]
+    prompt = synth.prompt_ids(V, n_prompt, seed=100 + seed)
+    forced = synth.prompt_ids(V, steps, seed=200 + seed)
+    worst, mism = 0.0, []
+    feed, pos = list(prompt), 0
+    for s in range(steps + 1):
+        nxt = be.forward(feed, pos, want_logits=True)
+        r = ref.forward(feed, pos, want_logits=True)
+        e = rel_err(be.read_logits(), r["logits"])
+        worst = max(worst, e)
+        assert e <= TOL, f"{model} step {s}: |dlogits| = {e:.3g} of range"
+        if nxt != r["next"] and top2_gap(r["logits"]) >= TOL:
+            mism.append(s)
+        pos += len(feed)
+        if s < steps:
+            feed = [int(forced[s])]
+    be.destroy()
+    assert not mism, f"greedy token differs at steps {mism}"
+    return worst
+
+
+@pytest.mark.parametrize("model,chunk", [("tiny", 4), ("small", 16), ("gqa7", 3), ("small-q8", 8), ("hd128", 5)])
+def test_teacher_forced_logits(model, chunk):
+    teacher_forced(model, n_prompt=11, steps=8, chunk=chunk)
+
+
+def test_golden_fixtures_through_cuda():
+    """The reference's own logits (tests/golden, made by the reference kernels) against the CUDA engine."""
+    import glob, os
+    for fx in sorted(glob.glob(os.path.join(os.path.dirname(__file__), "golden", "*.npz"))):
+        g = np.load(fx)
+        path = synth.ensure(str(g["model"]))
+        assert synth.file_sha256(path) == str(g["sha256"])
+        be = backend.open_model(path, ctx=64, prefill_chunk=int(g["mt"]))
+        be.forward(g["prompt"], 0, want_logits=True)
+        lgs = [be.read_logits()]
+        pos = len(g["prompt"])
+        for t in g["forced"]:
+            be.forward([int(t)], pos, want_logits=True)
+            lgs.append(be.read_logits())
+            pos += 1
+        for s, (a, b) in enumerate(zip(lgs, g["logits"])):
+            assert rel_err(a, b) <= TOL, f"{os.path.basename(fx)} step {s}"
+        be.destroy()
+
+
+def test_chunking_invariance():
+    """Same logits (within tolerance) whether the prompt runs in one call, in two, or token by token."""
+    path = synth.ensure("small")
+    p = synth.prompt_ids(2048, 19, seed=4)
+    a = backend.open_model(path, ctx=64, prefill_chunk=16)
+    a.forward(p, 0, want_logits=True)
+    la = a.read_logits()
+    b = backend.open_model(path, ctx=64, prefill_chunk=4)
+    b.forward(p[:7], 0)
+    b.forward(p[7:], 7, want_logits=True)
+    lb = b.read_logits()
+    c = backend.open_model(path, ctx=64, prefill_chunk=1)
+    for i, t in enumerate(p):
+        c.forward([int(t)], i, want_logits=True)
+    lc = c.read_logits()
+    assert rel_err(la, lc) <= 1e-4 and rel_err(lb, lc) <= 1e-4
+
+
+def test_sequences_are_independent():
+    path = synth.ensure("tiny")
+    be = backend.open_model(path, ctx=32, prefill_chunk=8, max_seqs=3)
+    p0 = synth.prompt_ids(512, 6, seed=1)
+    p1 = synth.prompt_ids(512, 9, seed=2)
+    n0 = be.forward(p0, 0, want_logits=True, seq=0)
+    l0 = be.read_logits(0)
+    be.forward(p1, 0, seq=1)
+    be.forward([5], 9, seq=1)
+    n0b = be.forward(p0, 0, want_logits=True, seq=2)
+    assert n0 == n0b and np.array_equal(l0, be.read_logits(2))
+
+
+def test_errors():
+    path = synth.ensure("tiny")
+    be = backend.open_model(path, ctx=8, prefill_chunk=4)
+    be.forward([1, 2, 3], 0)
+    with pytest.raises(RuntimeError, match="context full"):
+        be.forward([1, 2, 3, 4, 5], 3)
+    with pytest.raises(_lib.H2CError):
+        be.forward([600], 3)  # id >= vocab
+    with pytest.raises(_lib.H2CError):
+        be.forward([1], 0, seq=1)  # one sequence only
+    parsed, data = G.load_file(path)
+    cfg = G.qwen2_config(parsed["meta"])
+    L = _lib.load()
+    h = C.c_void_p()
+    c = _lib.Config(dim=cfg["dim"], layers=cfg["layers"], ffn=cfg["ffn"], heads=cfg["heads"], kv_heads=cfg["kv_heads"],
+                    vocab=cfg["vocab"], ctx=16, max_chunk=4, max_seqs=1, eps=1e-6, rope_theta=1e6)
+    assert L.h2c_create(0, C.byref(c), C.byref(h)) == 0
+    nxt = C.c_int32()
+    ids = np.array([1], np.int32)
+    assert L.h2c_forward(h, 0, ids.ctypes.data, 1, 0, 0.0, 1, C.byref(nxt)) == _lib.ERR_NOT_READY
+    f = np.zeros(128, np.float32)
+    assert L.h2c_set_tensor(h, _lib.KIND_EMBED, 0, _lib.GGML_F32, f.ctypes.data, f.nbytes) == _lib.ERR_BAD_TYPE
+    assert L.h2c_destroy(h) == 0
+
+
+def test_temperature_sampling_matches_oracle_sampler():
+    path = synth.ensure("small")
+    be = backend.open_model(path, ctx=32, prefill_chunk=8)
+    p = synth.prompt_ids(2048, 6, seed=8)
+    for seed in range(5):
+        nxt = be.forward(p, 0, temperature=0.7, seed=seed, want_logits=True)
+        lg = be.read_logits()
+        exp = O.lib("oracle").h2o_sample(lg.ctypes.data, lg.size, 0.7, (seed + 0) & 0xFFFFFFFF)
+        assert nxt == exp
+
+
+def test_profile_names():
+    be = backend.open_model(synth.ensure("tiny"), ctx=32, prefill_chunk=8)
+    prof = be.profile([1, 2, 3], 0)
+    assert list(prof) == _lib.PROFILE_NAMES and all(v >= 0 for v in prof.values())
+    assert prof["matvec gate+up"] > 0
+
+
+@pytest.mark.parametrize("N,K", [(896, 896), (128, 896), (4864, 896), (896, 4864), (151936, 896), (70, 96)])
+@pytest.mark.parametrize("M", [1, 3])
+def test_q4_matvec_microbench(N, K, M):
+    """The Q4_0 matvec microbench shapes: y = W . quantize(x) against the oracle's quantize_row + matmul_q4."""
+    if N == 151936 and M == 3:
+        pytest.skip("one token for the lm_head shape")
+    rng = np.random.default_rng(N + K + M)
+    blocks = G.q4_0_quantize(rng.standard_normal(N * K, dtype=np.float32) * np.float32(0.02))
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    bias = rng.standard_normal(N, dtype=np.float32)
+    L = _lib.load()
+    packed = np.zeros(L.h2c_q4_matrix_bytes(N, K), np.uint8)
+    assert L.h2c_q4_pack(blocks.ctypes.data, N, K, packed.ctypes.data) == 0
+    dev = torch.device("cuda")
+    w = torch.from_numpy(packed).to(dev)
+    xt = torch.from_numpy(x).to(dev)
+    scratch = torch.zeros(L.h2c_q4_matvec_scratch_bytes(M, K), dtype=torch.uint8, device=dev)
+    y0 = rng.standard_normal((M, N), dtype=np.float32)
+    for op in (0, 1, 2):
+        y = torch.from_numpy(y0).to(dev)
+        b = torch.from_numpy(bias).to(dev)
+        rc = L.h2c_q4_matvec(w.data_ptr(), N, K, xt.data_ptr(), M, y.data_ptr(), op, b.data_ptr() if op == 1 else None,
+                             scratch.data_ptr(), None)
+        assert rc == 0
+        torch.cuda.synchronize()
+        ref = O.matvec_q4(blocks, N, K, x, op=op, bias=bias if op == 1 else None, y=y0, nth=8)
+        got = y.cpu().numpy()
+        assert rel_err(got, ref) <= 1e-5, f"op {op}"
