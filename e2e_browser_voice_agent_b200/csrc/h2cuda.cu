@@ -51,9 +51,7 @@ struct h2c_engine {
   float *x = nullptr, *qkv = nullptr, *att = nullptr, *gu = nullptr, *logits = nullptr;
   int8_t* xq = nullptr;
   float* xd = nullptr;
-  int* xs = nullptr;
-  float* attn_part = nullptr;
-  int nsplit_max = 0;
+  int4* xs = nullptr;
   float* am_v = nullptr;
   int* am_i = nullptr;
   int am_np = 0;
@@ -113,35 +111,42 @@ int dalloc_t(h2c_engine* e, T** p, size_t count) {
   return dalloc(e, reinterpret_cast<void**>(p), count * sizeof(T));
 }
 
-// GGUF Q4_0 blocks (18 B: fp16 d, 16 nibble bytes) -> device layout: values [N][nb][16], then fp16 scales [N][nb].
-void pack_q4_host(const uint8_t* src, int64_t nblocks, uint8_t* dst_qs, uint16_t* dst_d) {
-  for (int64_t b = 0; b < nblocks; b++) {
-    const uint8_t* s = src + b * 18;
-    dst_d[b] = (uint16_t)(s[0] | (s[1] << 8));
-    memcpy(dst_qs + b * 16, s + 2, 16);
+// GGUF blocks -> device layout (kernels.cuh): rows in groups of 32, [group][block][32 rows][BB bytes] with each
+// 16-byte half permuted so that 32-bit word l holds lane l's bytes, and fp16 scales [group][block][32 rows].
+// Rows past N (padding to a multiple of 32) are zero. src_block_bytes: 18 (Q4_0) or 34 (Q8_0).
+void pack_blocks_host(const uint8_t* src, int N, int K, int src_block_bytes, uint8_t* dst_qs, uint16_t* dst_d) {
+  const int nb = K / 32, BB = src_block_bytes - 2, Np = (N + 31) / 32 * 32;
+  memset(dst_qs, 0, (size_t)Np * nb * BB);
+  memset(dst_d, 0, (size_t)Np * nb * 2);
+  for (int n = 0; n < N; n++) {
+    const int g = n >> 5, r = n & 31;
+    for (int b = 0; b < nb; b++) {
+      const uint8_t* s = src + ((size_t)n * nb + b) * src_block_bytes;
+      const size_t e = ((size_t)g * nb + b) * 32 + r;
+      dst_d[e] = (uint16_t)(s[0] | (s[1] << 8));
+      uint8_t* d = dst_qs + e * BB;
+      for (int h = 0; h < BB; h += 16)
+        for (int p = 0; p < 16; p++) d[h + p] = s[2 + h + perm16(p)];
+    }
   }
 }
-void pack_q8_host(const uint8_t* src, int64_t nblocks, uint8_t* dst_qs, uint16_t* dst_d) {
-  for (int64_t b = 0; b < nblocks; b++) {
-    const uint8_t* s = src + b * 34;
-    dst_d[b] = (uint16_t)(s[0] | (s[1] << 8));
-    memcpy(dst_qs + b * 32, s + 2, 32);
-  }
-}
+
+size_t padded_rows(int N) { return (size_t)(N + 31) / 32 * 32; }
 
 int upload_q4(h2c_engine* e, Q4Mat* m, int N, int K, const void* data, uint64_t nbytes) {
   const int64_t nb = (int64_t)N * (K / 32);
   if ((uint64_t)nb * 18 != nbytes) return e->fail(H2C_ERR_INVALID, "Q4_0 tensor %dx%d: %llu bytes, expected %lld", N, K,
                                                   (unsigned long long)nbytes, (long long)(nb * 18));
+  const size_t nbp = padded_rows(N) * (K / 32);
   if (!m->qs) {
-    int r = dalloc_t(e, &m->qs, (size_t)nb * 16);
+    int r = dalloc_t(e, &m->qs, nbp * 16);
     if (r) return r;
-    r = dalloc_t(e, &m->d, (size_t)nb);
+    r = dalloc_t(e, &m->d, nbp);
     if (r) return r;
   }
-  std::vector<uint8_t> qs((size_t)nb * 16);
-  std::vector<uint16_t> d((size_t)nb);
-  pack_q4_host((const uint8_t*)data, nb, qs.data(), d.data());
+  std::vector<uint8_t> qs(nbp * 16);
+  std::vector<uint16_t> d(nbp);
+  pack_blocks_host((const uint8_t*)data, N, K, 18, qs.data(), d.data());
   CUDA_TRY(e, cudaMemcpy(m->qs, qs.data(), qs.size(), cudaMemcpyHostToDevice));
   CUDA_TRY(e, cudaMemcpy(m->d, d.data(), d.size() * 2, cudaMemcpyHostToDevice));
   m->N = N;
@@ -153,15 +158,16 @@ int upload_q8(h2c_engine* e, Q8Mat* m, int N, int K, const void* data, uint64_t 
   const int64_t nb = (int64_t)N * (K / 32);
   if ((uint64_t)nb * 34 != nbytes) return e->fail(H2C_ERR_INVALID, "Q8_0 tensor %dx%d: %llu bytes, expected %lld", N, K,
                                                   (unsigned long long)nbytes, (long long)(nb * 34));
+  const size_t nbp = padded_rows(N) * (K / 32);
   if (!m->qs) {
-    int r = dalloc_t(e, &m->qs, (size_t)nb * 32);
+    int r = dalloc_t(e, &m->qs, nbp * 32);
     if (r) return r;
-    r = dalloc_t(e, &m->d, (size_t)nb);
+    r = dalloc_t(e, &m->d, nbp);
     if (r) return r;
   }
-  std::vector<uint8_t> qs((size_t)nb * 32);
-  std::vector<uint16_t> d((size_t)nb);
-  pack_q8_host((const uint8_t*)data, nb, qs.data(), d.data());
+  std::vector<uint8_t> qs(nbp * 32);
+  std::vector<uint16_t> d(nbp);
+  pack_blocks_host((const uint8_t*)data, N, K, 34, qs.data(), d.data());
   CUDA_TRY(e, cudaMemcpy(m->qs, qs.data(), qs.size(), cudaMemcpyHostToDevice));
   CUDA_TRY(e, cudaMemcpy(m->d, d.data(), d.size() * 2, cudaMemcpyHostToDevice));
   m->N = N;
@@ -182,32 +188,66 @@ int upload_f32(h2c_engine* e, float** p, int64_t count, const void* data, uint64
 
 // ---------------------------------------------------------------- launch helpers
 
-template <int MAXM>
-void launch_mv(int op, const Q4Mat& W, const int8_t* xq, const float* xd, const int* xs, int M, float* y, int ldy,
-               const float* bias, cudaStream_t st) {
-  constexpr int R = MAXM == 1 ? 2 : 1;
-  const int warps = (W.N + R - 1) / R;
-  const int blocks = (warps + 3) / 4;
-  if (op == OP_STORE) k_matvec_q4<R, MAXM, OP_STORE><<<blocks, 128, 0, st>>>(W.qs, W.d, W.N, W.K, xq, xd, xs, M, y, ldy, bias);
-  else if (op == OP_BIAS) k_matvec_q4<R, MAXM, OP_BIAS><<<blocks, 128, 0, st>>>(W.qs, W.d, W.N, W.K, xq, xd, xs, M, y, ldy, bias);
-  else k_matvec_q4<R, MAXM, OP_ADD><<<blocks, 128, 0, st>>>(W.qs, W.d, W.N, W.K, xq, xd, xs, M, y, ldy, bias);
+// Launch shapes: decode (M == 1) uses 32-row tiles (16 for long rows, to bound shared memory); prefill runs
+// sub-batches of up to 4 tokens on 8-row tiles.
+template <int WT, int ROWS, int MB>
+void launch_mv_t(int op, const uint8_t* qs, const __half* d, int N, int K, const int8_t* xq, const float* xd,
+                 const int4* xs, int M, float* y, int ldy, const float* bias, cudaStream_t st) {
+  const int blocks = (int)(padded_rows(N) / ROWS);
+  const size_t smem = (size_t)MB * (K / 32) * ROWS * 16;
+  if (op == OP_STORE) k_matvec<WT, ROWS, MB, OP_STORE><<<blocks, 256, smem, st>>>(qs, d, N, K, xq, xd, xs, M, y, ldy, bias);
+  else if (op == OP_BIAS) k_matvec<WT, ROWS, MB, OP_BIAS><<<blocks, 256, smem, st>>>(qs, d, N, K, xq, xd, xs, M, y, ldy, bias);
+  else k_matvec<WT, ROWS, MB, OP_ADD><<<blocks, 256, smem, st>>>(qs, d, N, K, xq, xd, xs, M, y, ldy, bias);
 }
 
-// y[m] (op)= W . xq[m] for M tokens, in sub-batches of at most 8 tokens per launch
-void matvec(int op, const Q4Mat& W, const int8_t* xq, const float* xd, const int* xs, int M, float* y, int ldy,
-            const float* bias, cudaStream_t st) {
-  const int nb = W.K / 32;
-  for (int m0 = 0; m0 < M; m0 += 8) {
-    const int mm = M - m0 < 8 ? M - m0 : 8;
-    const int8_t* q = xq + (size_t)m0 * W.K;
-    const float* d = xd + (size_t)m0 * nb;
-    const int* s = xs + (size_t)m0 * nb;
-    float* yy = y + (size_t)m0 * ldy;
-    if (mm == 1) launch_mv<1>(op, W, q, d, s, mm, yy, ldy, bias, st);
-    else if (mm <= 2) launch_mv<2>(op, W, q, d, s, mm, yy, ldy, bias, st);
-    else if (mm <= 4) launch_mv<4>(op, W, q, d, s, mm, yy, ldy, bias, st);
-    else launch_mv<8>(op, W, q, d, s, mm, yy, ldy, bias, st);
+template <int WT>
+void matvec_w(int op, const uint8_t* qs, const __half* d, int N, int K, const int8_t* xq, const float* xd,
+              const int4* xs, int M, float* y, int ldy, const float* bias, cudaStream_t st) {
+  const int nb = K / 32;
+  if (M == 1) {
+    if (nb <= 64) launch_mv_t<WT, 32, 1>(op, qs, d, N, K, xq, xd, xs, 1, y, ldy, bias, st);
+    else launch_mv_t<WT, 16, 1>(op, qs, d, N, K, xq, xd, xs, 1, y, ldy, bias, st);
+    return;
   }
+  if ((size_t)8 * 4 * nb * 16 > 200 * 1024) {  // very long rows: one token per launch
+    for (int m0 = 0; m0 < M; m0++)
+      launch_mv_t<WT, 16, 1>(op, qs, d, N, K, xq + (size_t)m0 * K, xd + (size_t)m0 * nb, xs + (size_t)m0 * nb, 1,
+                             y + (size_t)m0 * ldy, ldy, bias, st);
+    return;
+  }
+  for (int m0 = 0; m0 < M; m0 += 4) {
+    const int mm = M - m0 < 4 ? M - m0 : 4;
+    launch_mv_t<WT, 8, 4>(op, qs, d, N, K, xq + (size_t)m0 * K, xd + (size_t)m0 * nb, xs + (size_t)m0 * nb, mm,
+                          y + (size_t)m0 * ldy, ldy, bias, st);
+  }
+}
+
+void matvec(int op, const Q4Mat& W, const int8_t* xq, const float* xd, const int4* xs, int M, float* y, int ldy,
+            const float* bias, cudaStream_t st) {
+  matvec_w<WQ4>(op, W.qs, W.d, W.N, W.K, xq, xd, xs, M, y, ldy, bias, st);
+}
+
+// Opt every kernel that takes more than 48 KB of dynamic shared memory into the larger carve-out.
+template <int WT, int ROWS, int MB>
+cudaError_t mv_attr(int max_smem) {
+  cudaError_t c = cudaFuncSetAttribute(k_matvec<WT, ROWS, MB, OP_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  if (c == cudaSuccess) c = cudaFuncSetAttribute(k_matvec<WT, ROWS, MB, OP_BIAS>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  if (c == cudaSuccess) c = cudaFuncSetAttribute(k_matvec<WT, ROWS, MB, OP_ADD>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  return c;
+}
+
+cudaError_t set_kernel_attrs(int ctx) {
+  const int big = 200 * 1024;
+  cudaError_t c = mv_attr<WQ4, 32, 1>(big);
+  if (c == cudaSuccess) c = mv_attr<WQ4, 16, 1>(big);
+  if (c == cudaSuccess) c = mv_attr<WQ4, 8, 4>(big);
+  if (c == cudaSuccess) c = mv_attr<WQ8, 32, 1>(big);
+  if (c == cudaSuccess) c = mv_attr<WQ8, 16, 1>(big);
+  if (c == cudaSuccess) c = mv_attr<WQ8, 8, 4>(big);
+  const int att = ctx * 4 > 48 * 1024 ? ctx * 4 : 48 * 1024;
+  if (c == cudaSuccess) c = cudaFuncSetAttribute(k_attention<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, att);
+  if (c == cudaSuccess) c = cudaFuncSetAttribute(k_attention<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, att);
+  return c;
 }
 
 struct Prof {
@@ -235,18 +275,16 @@ void enqueue_pass(h2c_engine* e, int M, bool logits, Prof* pf) {
   mark(pf, 0, st);
   for (int l = 0; l < NL; l++) {
     const LayerW& W = e->L[l];
-    k_norm_quant<<<M, 256, 0, st>>>(e->x, 0, W.attn_norm, D, c.eps, e->xq, e->xd, e->xs);
+    k_norm_quant<<<M, 256, D * 4, st>>>(e->x, 0, W.attn_norm, D, c.eps, e->xq, e->xd, e->xs);
     mark(pf, 1, st);
     matvec(OP_BIAS, W.qkv, e->xq, e->xd, e->xs, M, e->qkv, QKV, W.bqkv, st);
     mark(pf, 2, st);
     k_rope_kv<<<M, 256, 0, st>>>(e->prm, e->qkv, QKV, e->rope, e->kc, e->vc, H, KVH, HD, c.ctx, NL, l);
     mark(pf, 3, st);
-    dim3 ag(e->nsplit_max, KVH, M);
     if (HD == 64)
-      k_attn_split<64><<<ag, 128, 0, st>>>(e->prm, e->qkv, QKV, e->kc, e->vc, H, KVH, c.ctx, NL, l, e->attn_part, e->nsplit_max);
+      k_attention<64><<<dim3(H, M), 128, (size_t)c.ctx * 4, st>>>(e->prm, e->qkv, QKV, e->kc, e->vc, H, KVH, c.ctx, NL, l, e->att, D);
     else
-      k_attn_split<128><<<ag, 128, 0, st>>>(e->prm, e->qkv, QKV, e->kc, e->vc, H, KVH, c.ctx, NL, l, e->attn_part, e->nsplit_max);
-    k_attn_combine<<<dim3(H, M), HD, 0, st>>>(e->prm, e->attn_part, H, HD, e->nsplit_max, e->att, D);
+      k_attention<128><<<dim3(H, M), 128, (size_t)c.ctx * 4, st>>>(e->prm, e->qkv, QKV, e->kc, e->vc, H, KVH, c.ctx, NL, l, e->att, D);
     mark(pf, 4, st);
     {
       const int warps = M * (D / 32);
@@ -255,7 +293,7 @@ void enqueue_pass(h2c_engine* e, int M, bool logits, Prof* pf) {
     mark(pf, 5, st);
     matvec(OP_ADD, W.o, e->xq, e->xd, e->xs, M, e->x, D, nullptr, st);
     mark(pf, 6, st);
-    k_norm_quant<<<M, 256, 0, st>>>(e->x, 0, W.ffn_norm, D, c.eps, e->xq, e->xd, e->xs);
+    k_norm_quant<<<M, 256, D * 4, st>>>(e->x, 0, W.ffn_norm, D, c.eps, e->xq, e->xd, e->xs);
     mark(pf, 1, st);
     matvec(OP_STORE, W.gu, e->xq, e->xd, e->xs, M, e->gu, 2 * F, nullptr, st);
     mark(pf, 7, st);
@@ -268,10 +306,10 @@ void enqueue_pass(h2c_engine* e, int M, bool logits, Prof* pf) {
     mark(pf, 9, st);
   }
   if (logits) {
-    k_norm_quant<<<1, 256, 0, st>>>(e->x, M - 1, e->out_norm, D, c.eps, e->xq, e->xd, e->xs);
+    k_norm_quant<<<1, 256, D * 4, st>>>(e->x, M - 1, e->out_norm, D, c.eps, e->xq, e->xd, e->xs);
     if (e->out_type == 8) {
-      const int warps = (c.vocab + 1) / 2;
-      k_matvec_q8<2><<<(warps + 3) / 4, 128, 0, st>>>(e->out8.qs, e->out8.d, c.vocab, D, e->xq, e->xd, e->logits);
+      matvec_w<WQ8>(OP_STORE, (const uint8_t*)e->out8.qs, e->out8.d, c.vocab, D, e->xq, e->xd, e->xs, 1, e->logits,
+                    c.vocab, nullptr, st);
     } else {
       matvec(OP_STORE, e->out_type == 2 ? e->out4 : e->embd, e->xq, e->xd, e->xs, 1, e->logits, c.vocab, nullptr, st);
     }
@@ -396,10 +434,6 @@ int h2c_create(int device, const h2c_config* cfg, h2c_engine** out) {
     g_create_error = "head_dim must be 64 or 128";
     return H2C_ERR_INVALID;
   }
-  if (c.heads / c.kv_heads > MAXG) {
-    g_create_error = "more than 8 query heads per KV head";
-    return H2C_ERR_INVALID;
-  }
   h2c_engine* e = new h2c_engine();
   e->cfg = c;
   e->dev = device;
@@ -425,8 +459,16 @@ int h2c_create(int device, const h2c_config* cfg, h2c_engine** out) {
   }
   const int MT = c.max_chunk, D = c.dim, F = c.ffn;
   const size_t kv = (size_t)c.max_seqs * c.layers * c.kv_heads * c.ctx * HD;
-  e->nsplit_max = (c.ctx + ATT_CH - 1) / ATT_CH;
   e->am_np = 296;
+  if (c.ctx > 50000) {
+    e->err = "ctx above 50000 positions (attention keeps one score per position in shared memory)";
+    return bail(H2C_ERR_INVALID);
+  }
+  ce = set_kernel_attrs(c.ctx);
+  if (ce != cudaSuccess) {
+    e->err = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(ce);
+    return bail(H2C_ERR_CUDA);
+  }
   int r = 0;
   const int KQ = F > D ? F : D;
   if ((r = dalloc_t(e, &e->kc, kv)) || (r = dalloc_t(e, &e->vc, kv)) || (r = dalloc_t(e, &e->x, (size_t)MT * D)) ||
@@ -434,7 +476,6 @@ int h2c_create(int device, const h2c_config* cfg, h2c_engine** out) {
       (r = dalloc_t(e, &e->gu, (size_t)MT * 2 * F)) || (r = dalloc_t(e, &e->logits, (size_t)c.vocab)) ||
       (r = dalloc_t(e, &e->xq, (size_t)MT * KQ)) || (r = dalloc_t(e, &e->xd, (size_t)MT * KQ / 32)) ||
       (r = dalloc_t(e, &e->xs, (size_t)MT * KQ / 32)) ||
-      (r = dalloc_t(e, &e->attn_part, (size_t)MT * c.heads * e->nsplit_max * (HD + 2))) ||
       (r = dalloc_t(e, &e->am_v, (size_t)e->am_np)) || (r = dalloc_t(e, &e->am_i, (size_t)e->am_np)) ||
       (r = dalloc_t(e, &e->prm, (size_t)(P_IDS + MT))) || (r = dalloc_t(e, &e->next_d, 1)) ||
       (r = dalloc_t(e, &e->toklog, (size_t)c.max_seqs * (c.ctx + 1))) ||
@@ -656,21 +697,24 @@ const char* h2c_last_error(const h2c_engine* e) { return e ? e->err.c_str() : g_
 int64_t h2c_device_bytes(const h2c_engine* e) { return e ? e->dev_bytes : 0; }
 
 uint64_t h2c_q4_matrix_bytes(int32_t n_rows, int32_t k) {
-  const uint64_t nb = (uint64_t)n_rows * (uint64_t)(k / 32);
-  return align_up(nb * 16, 256) + align_up(nb * 2, 16);
+  if (n_rows <= 0 || k <= 0) return 0;
+  const uint64_t nbp = padded_rows(n_rows) * (uint64_t)(k / 32);
+  return align_up(nbp * 16, 256) + align_up(nbp * 2, 16);
 }
 
 int h2c_q4_pack(const void* gguf_blocks, int32_t n_rows, int32_t k, void* packed_host) {
   if (!gguf_blocks || !packed_host || n_rows <= 0 || k <= 0 || k % 32) return H2C_ERR_INVALID;
-  const int64_t nb = (int64_t)n_rows * (k / 32);
+  const size_t nbp = padded_rows(n_rows) * (k / 32);
   uint8_t* dst = (uint8_t*)packed_host;
-  pack_q4_host((const uint8_t*)gguf_blocks, nb, dst, (uint16_t*)(dst + align_up((size_t)nb * 16, 256)));
+  memset(dst, 0, h2c_q4_matrix_bytes(n_rows, k));
+  pack_blocks_host((const uint8_t*)gguf_blocks, n_rows, k, 18, dst, (uint16_t*)(dst + align_up(nbp * 16, 256)));
   return H2C_OK;
 }
 
 uint64_t h2c_q4_matvec_scratch_bytes(int32_t m, int32_t k) {
+  if (m <= 0 || k <= 0) return 0;
   const uint64_t nb = (uint64_t)m * (uint64_t)(k / 32);
-  return align_up((uint64_t)m * k, 256) + align_up(nb * 4, 256) + align_up(nb * 4, 256);
+  return align_up((uint64_t)m * k, 256) + align_up(nb * 4, 256) + align_up(nb * 16, 256);
 }
 
 int h2c_q4_matvec(const void* w, int32_t n_rows, int32_t k, const float* x, int32_t m, float* y, int32_t op,
@@ -678,18 +722,23 @@ int h2c_q4_matvec(const void* w, int32_t n_rows, int32_t k, const float* x, int3
   if (!w || !x || !y || !scratch || n_rows <= 0 || k <= 0 || k % 32 || m < 1 || op < 0 || op > 2 || (op == 1 && !bias))
     return H2C_ERR_INVALID;
   if (((uintptr_t)w | (uintptr_t)scratch | (uintptr_t)x) & 15) return H2C_ERR_INVALID;
+  static bool attrs_set = false;
+  if (!attrs_set) {
+    if (set_kernel_attrs(2) != cudaSuccess) return H2C_ERR_CUDA;
+    attrs_set = true;
+  }
   cudaStream_t st = (cudaStream_t)stream;
-  const int64_t nb = (int64_t)n_rows * (k / 32);
+  const size_t nbp = padded_rows(n_rows) * (k / 32);
   Q4Mat W;
   W.qs = (uint8_t*)w;
-  W.d = (__half*)((uint8_t*)w + align_up((size_t)nb * 16, 256));
+  W.d = (__half*)((uint8_t*)w + align_up(nbp * 16, 256));
   W.N = n_rows;
   W.K = k;
   uint8_t* s = (uint8_t*)scratch;
-  int8_t* xq = (int8_t*)s;
   const size_t mb = (size_t)m * (k / 32);
+  int8_t* xq = (int8_t*)s;
   float* xd = (float*)(s + align_up((size_t)m * k, 256));
-  int* xs = (int*)(s + align_up((size_t)m * k, 256) + align_up(mb * 4, 256));
+  int4* xs = (int4*)(s + align_up((size_t)m * k, 256) + align_up(mb * 4, 256));
   const int warps = (int)mb;
   k_quant<<<(warps + 7) / 8, 256, 0, st>>>(x, k, m, xq, xd, xs);
   matvec(op, W, xq, xd, xs, m, y, n_rows, bias, st);

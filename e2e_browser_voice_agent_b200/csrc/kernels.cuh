@@ -1,19 +1,29 @@
-// Device kernels of the H2 Qwen2 token loop for sm_100a.
+// Device kernels of the H2 Qwen2 token loop for sm_100a, bit-exact with the reference CPU path.
 //
-// Data layout in HBM (all per engine):
-//   Q4_0 matrix [N][K]: values [N][K/32][16] bytes (byte j: low nibble = element j, high = element j+16, as in
-//                       GGUF), then scales [N][K/32] fp16 (the GGUF bits; fp16 -> fp32 is exact).
-//   Q8_0 matrix [N][K]: values [N][K/32][32] int8, then scales [N][K/32] fp16.
-//   activations: x [M][D] f32 residual stream; qkv [M][D + 2*KVH*HD]; att [M][D]; gu [M][2F];
-//   int8 activations xq [M][K] with per-32 scales xd [M][K/32] f32 and integer sums xs [M][K/32];
+// Why bit-exact: the reference quantizes every matrix input to int8 per 32 values (kernels.c:90-114). That
+// re-quantization turns a 1-ulp difference anywhere upstream into a flipped int8 somewhere downstream, and 24
+// layers amplify it: reordering only the RMSNorm sum moves the 0.5B model's logits by ~1.4% of their range, far
+// outside the 2e-3 parity tolerance. So every floating-point result here is produced by the reference's own
+// operation order and roundings (IEEE round-to-nearest intrinsics; no fused multiply-add):
+//   - four "lanes" per vector, as the reference's 128-bit SIMD computes them: element i goes to lane i mod 4 in
+//     RMSNorm and attention dots (kernels.c:80-86, 362-366); lane l of a Q4_0/Q8_0 block dot sums elements
+//     {2l, 2l+1, 8+2l, 9+2l} of each half (the i32x4.dot_i16x8 lanes of kernels.c:121-139, 157-170);
+//   - each lane accumulates in block (or position) order; lanes are added ((l0 + l1) + l2) + l3;
+//   - softmax sums and the probability-weighted V sums run in position order (kernels.c:367-375).
+// The parallel part of every op (integer block dots, products, exponentials) runs wide; only those ordered
+// float sums run as short per-output chains.
+//
+// Data layout in HBM:
+//   Q4_0 matrix [N][K]: rows in groups of 32; group g holds values [K/32][32 rows][16 B] then (separately) scales
+//     [K/32][32 rows] fp16, so one warp-wide 16-byte load of block b reads 32 rows contiguously. Within each
+//     16-byte block the bytes are permuted so that 32-bit word l holds the bytes of lane l (PERM below): word l =
+//     GGUF bytes {2l, 2l+1, 8+2l, 9+2l}; its low nibbles are elements {2l, 2l+1, 8+2l, 9+2l} and its high nibbles
+//     elements 16 + those. N is padded to a multiple of 32 with zero blocks.
+//   Q8_0 matrix: the same grouping with 32-byte blocks, each 16-byte half permuted the same way.
+//   int8 activations xq [M][K]: per block of 32 the two halves (elements 0..15, 16..31) permuted like the
+//     weights, scale xd [M][K/32] f32, and per-lane integer sums xs [M][K/32] int4 (for the -8 nibble offset).
+//   activations: x [M][D] f32 residual stream; qkv [M][D + 2*KVH*HD]; att [M][D]; gu [M][2F].
 //   KV cache [seq][layer][kv_head][ctx][HD] f32 (the reference's dtype and order, kernels.c:347-348).
-//
-// Arithmetic follows the reference CPU path (h2-own-inference-engine/engine/kernels.c): matrix inputs are
-// quantized to int8 per 32 values with round-to-nearest-even of x * (1 / (amax / 127)) (kernels.c:90-114),
-// every block dot product is an exact integer, scaled by f32(dw * dx) and accumulated in f32 (kernels.c:121-139);
-// RoPE, SwiGLU, softmax use the reference's own fast_exp (kernels.c:69-78) and its operation order, with IEEE
-// round-to-nearest intrinsics so that nvcc does not contract them into fused multiply-adds. Only the order of
-// floating-point sums (rmsnorm, matvec rows, attention) differs from the CPU's lane order.
 #pragma once
 #include <cuda_fp16.h>
 #include <stdint.h>
@@ -23,8 +33,10 @@ namespace h2 {
 // device-resident parameters of one pass, written by the host with one copy before each pass
 enum { P_POS0 = 0, P_M = 1, P_SEQ = 2, P_IDS = 4 };
 
-constexpr int ATT_CH = 64;   // positions per attention split
-constexpr int MAXG = 8;      // query heads per KV head handled by one attention CTA
+// byte p of a permuted 16-byte block holds GGUF byte PERM[p]
+__host__ __device__ constexpr int perm16(int p) { return ((p & 3) >> 1) * 8 + (p >> 2) * 2 + (p & 1); }
+// position of GGUF byte j (0..15) in the permuted block
+__host__ __device__ constexpr int invperm16(int j) { return (((j & 7) >> 1) << 2) | ((j >> 3) << 1) | (j & 1); }
 
 __device__ __forceinline__ float fast_exp_ref(float x) {  // kernels.c:69-78
   if (x < -87.0f) return 0.0f;
@@ -40,78 +52,87 @@ __device__ __forceinline__ float fast_exp_ref(float x) {  // kernels.c:69-78
   return __int_as_float(__float_as_int(p) + ((int)n << 23));
 }
 
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-__device__ __forceinline__ int warp_sum_i(int v) {
-#pragma unroll
-  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
 }
 
-// Quantize the 32 values held one per lane (kernels.c:90-114): d = amax / 127, q = nearest-even(x * (1/d)).
-// Lane 0 stores the scale and the integer sum of the block (the int8 values the dot products use).
-__device__ __forceinline__ void quant_block_warp(float v, int lane, int8_t* q, float* d, int* s) {
-  float amax = warp_max(fabsf(v));
-  float dd = __fdiv_rn(amax, 127.0f);
-  float id = dd != 0.0f ? __fdiv_rn(1.0f, dd) : 0.0f;
-  int qi = __float2int_rn(__fmul_rn(v, id));
-  qi = max(-128, min(127, qi));
-  q[lane] = (int8_t)qi;
-  int sum = warp_sum_i(qi);
-  if (lane == 0) { *d = dd; *s = sum; }
+// ((l0 + l1) + l2) + l3 across 4 consecutive threads; valid in the thread with (tid & 3) == 0.
+__device__ __forceinline__ float hsum4_quad(float a) {
+  const float a1 = __shfl_down_sync(0xffffffffu, a, 1), a2 = __shfl_down_sync(0xffffffffu, a, 2),
+              a3 = __shfl_down_sync(0xffffffffu, a, 3);
+  return __fadd_rn(__fadd_rn(__fadd_rn(a, a1), a2), a3);
 }
 
-// x[m] = dequant(embedding row ids[m]) (kernels.c:313-322)
+// Quantize the 32 values held one per lane (kernels.c:90-114): amax over the block (a max is exact in any order),
+// d = amax / 127, q = nearest-even(x * (1 / d)) saturated to int8. Stores the permuted int8 block, the scale and
+// the four lane sums of the int8 values.
+__device__ __forceinline__ void quant_block_warp(float v, int lane, int8_t* q, float* d, int4* s) {
+  const float amax = warp_max(fabsf(v));
+  const float dd = __fdiv_rn(amax, 127.0f);
+  const float id = dd != 0.0f ? __fdiv_rn(1.0f, dd) : 0.0f;
+  int qi = __float2int_rn(__fmul_rn(v, id));
+  qi = max(-128, min(127, qi));
+  q[(lane & 16) | invperm16(lane & 15)] = (int8_t)qi;
+  const int l = (lane & 7) >> 1;
+  const int s0 = __reduce_add_sync(0xffffffffu, l == 0 ? qi : 0);
+  const int s1 = __reduce_add_sync(0xffffffffu, l == 1 ? qi : 0);
+  const int s2 = __reduce_add_sync(0xffffffffu, l == 2 ? qi : 0);
+  const int s3 = __reduce_add_sync(0xffffffffu, l == 3 ? qi : 0);
+  if (lane == 0) {
+    *d = dd;
+    *s = make_int4(s0, s1, s2, s3);
+  }
+}
+
+// x[m] = dequant(embedding row ids[m]) (kernels.c:313-322), from the grouped / permuted Q4_0 layout
 __global__ void k_embed(const int32_t* __restrict__ prm, const uint8_t* __restrict__ qs, const __half* __restrict__ dsc,
                         int D, float* __restrict__ x) {
   const int m = blockIdx.x;
   const int t = prm[P_IDS + m];
-  const int nb = D / 32;
-  const uint8_t* q = qs + (size_t)t * nb * 16;
-  const __half* d = dsc + (size_t)t * nb;
+  const int nb = D / 32, g = t >> 5, r = t & 31;
   float* xr = x + (size_t)m * D;
   for (int i = threadIdx.x; i < D / 2; i += blockDim.x) {
-    int blk = i >> 4, j = i & 15;
-    uint8_t b = q[blk * 16 + j];
-    float s = __half2float(d[blk]);
+    const int blk = i >> 4, j = i & 15;
+    const size_t e = ((size_t)g * nb + blk) * 32 + r;
+    const uint8_t b = qs[e * 16 + invperm16(j)];
+    const float s = __half2float(dsc[e]);
     xr[32 * blk + j] = __fmul_rn((float)((b & 15) - 8), s);
     xr[32 * blk + 16 + j] = __fmul_rn((float)((b >> 4) - 8), s);
   }
 }
 
-// RMSNorm (kernels.c:80-86) of row `row` of x, then int8 quantization (kernels.c:90-114) into slot blockIdx.x.
-// One CTA per token; blockDim a multiple of 32.
+// RMSNorm (kernels.c:80-86) of row (row0 + blockIdx.x) of x, then int8 quantization into slot blockIdx.x.
+// The sum of squares runs as the reference's four lane chains (threads 0..3), in element order.
+// dynamic smem: D floats
 __global__ void k_norm_quant(const float* __restrict__ x, int row0, const float* __restrict__ w, int D, float eps,
-                             int8_t* __restrict__ xq, float* __restrict__ xd, int* __restrict__ xs) {
-  __shared__ float red[32];
+                             int8_t* __restrict__ xq, float* __restrict__ xd, int4* __restrict__ xs) {
+  extern __shared__ float xsm[];
+  __shared__ float part[4];
   __shared__ float rs;
   const int slot = blockIdx.x;
   const float* xr = x + (size_t)(row0 + slot) * D;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  float ss = 0.f;
-  for (int i = threadIdx.x; i < D; i += blockDim.x) { float v = xr[i]; ss = __fadd_rn(ss, __fmul_rn(v, v)); }
-  ss = warp_sum(ss);
-  if (lane == 0) red[warp] = ss;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) xsm[i] = xr[i];
+  __syncthreads();
+  if (threadIdx.x < 4) {
+    float s = 0.f;
+    const int l = threadIdx.x;
+#pragma unroll 8
+    for (int i = l; i < D; i += 4) s = __fadd_rn(s, __fmul_rn(xsm[i], xsm[i]));
+    part[l] = s;
+  }
   __syncthreads();
   if (threadIdx.x == 0) {
-    float t = 0.f;
-    for (int i = 0; i < nw; i++) t += red[i];
-    rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)D), eps)));
+    const float ss = __fadd_rn(__fadd_rn(__fadd_rn(part[0], part[1]), part[2]), part[3]);
+    rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), eps)));
   }
   __syncthreads();
   const float r = rs;
-  const int nb = D / 32;
+  const int nb = D / 32, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   for (int b = warp; b < nb; b += nw) {
-    int i = b * 32 + lane;
-    float v = __fmul_rn(__fmul_rn(xr[i], r), w[i]);
+    const int i = b * 32 + lane;
+    const float v = __fmul_rn(__fmul_rn(xsm[i], r), w[i]);
     quant_block_warp(v, lane, xq + (size_t)slot * D + b * 32, xd + (size_t)slot * nb + b, xs + (size_t)slot * nb + b);
   }
 }
@@ -119,44 +140,30 @@ __global__ void k_norm_quant(const float* __restrict__ x, int row0, const float*
 // int8 quantization of M rows of length K (the attention output before the O projection, kernels.c:379):
 // one warp per 32-value block.
 __global__ void k_quant(const float* __restrict__ x, int K, int M, int8_t* __restrict__ xq, float* __restrict__ xd,
-                        int* __restrict__ xs) {
+                        int4* __restrict__ xs) {
   const int nb = K / 32;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (gw >= M * nb) return;
   const int m = gw / nb, b = gw % nb;
-  float v = x[(size_t)m * K + b * 32 + lane];
+  const float v = x[(size_t)m * K + b * 32 + lane];
   quant_block_warp(v, lane, xq + (size_t)m * K + b * 32, xd + (size_t)m * nb + b, xs + (size_t)m * nb + b);
 }
 
 // act = silu(gate) * up, then int8 quantization (kernels.c:393-397); one warp per 32-value block of act.
 __global__ void k_swiglu_quant(const float* __restrict__ gu, int F, int M, int8_t* __restrict__ xq,
-                               float* __restrict__ xd, int* __restrict__ xs) {
+                               float* __restrict__ xd, int4* __restrict__ xs) {
   const int nb = F / 32;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (gw >= M * nb) return;
   const int m = gw / nb, b = gw % nb;
   const float* g = gu + (size_t)m * 2 * F;
-  float gt = g[b * 32 + lane], up = g[F + b * 32 + lane];
-  float v = __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, fast_exp_ref(-gt))), up);
+  const float gt = g[b * 32 + lane], up = g[F + b * 32 + lane];
+  const float v = __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, fast_exp_ref(-gt))), up);
   quant_block_warp(v, lane, xq + (size_t)m * F + b * 32, xd + (size_t)m * nb + b, xs + (size_t)m * nb + b);
 }
 
 enum { OP_STORE = 0, OP_BIAS = 1, OP_ADD = 2 };
-
-// Exact integer dot of one Q4_0 block (16 bytes of nibbles) with 32 int8 activations: sum((q - 8) * x) computed
-// as sum(q * x) - 8 * sum(x). Nibble values 0..15 are the same as signed bytes, so signed dp4a applies.
-__device__ __forceinline__ int q4_block_dot(uint4 w, int4 x0, int4 x1, int xsum) {
-  int p = 0;
-  p = __dp4a((int)(w.x & 0x0f0f0f0fu), x0.x, p);
-  p = __dp4a((int)(w.y & 0x0f0f0f0fu), x0.y, p);
-  p = __dp4a((int)(w.z & 0x0f0f0f0fu), x0.z, p);
-  p = __dp4a((int)(w.w & 0x0f0f0f0fu), x0.w, p);
-  p = __dp4a((int)((w.x >> 4) & 0x0f0f0f0fu), x1.x, p);
-  p = __dp4a((int)((w.y >> 4) & 0x0f0f0f0fu), x1.y, p);
-  p = __dp4a((int)((w.z >> 4) & 0x0f0f0f0fu), x1.z, p);
-  p = __dp4a((int)((w.w >> 4) & 0x0f0f0f0fu), x1.w, p);
-  return p - 8 * xsum;
-}
+enum { WQ4 = 0, WQ8 = 1 };
 
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {  // weights are read once per pass: no L1 allocation
   uint4 v;
@@ -165,104 +172,79 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {  // weights are rea
   return v;
 }
 
-// y[m][n] (op)= sum_b f32(int dot_b) * (dw * dx), for R rows per warp and up to MAXM tokens (matmul_q4,
-// kernels.c:200-273). Lanes stride over the K/32 blocks of a row with 16-byte loads (512 contiguous bytes per
-// warp and row); lane partial sums are reduced with shuffles.
-template <int R, int MAXM, int OP>
-__global__ void __launch_bounds__(128) k_matvec_q4(const uint8_t* __restrict__ qs, const __half* __restrict__ dsc,
-                                                   int N, int K, const int8_t* __restrict__ xq,
-                                                   const float* __restrict__ xd, const int* __restrict__ xs, int M,
-                                                   float* __restrict__ y, int ldy, const float* __restrict__ bias) {
-  const int nb = K / 32;
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  const int row0 = warp * R;
-  if (row0 >= N) return;
-  float acc[R][MAXM];
-#pragma unroll
-  for (int r = 0; r < R; r++)
-#pragma unroll
-    for (int m = 0; m < MAXM; m++) acc[r][m] = 0.f;
-  for (int b = lane; b < nb; b += 32) {
-    uint4 w[R];
-    float dw[R];
-#pragma unroll
-    for (int r = 0; r < R; r++) {
-      int n = min(row0 + r, N - 1);
-      w[r] = ldg_stream(qs + ((size_t)n * nb + b) * 16);
-      dw[r] = __half2float(dsc[(size_t)n * nb + b]);
-    }
-#pragma unroll
-    for (int m = 0; m < MAXM; m++) {
-      if (m < M) {
-        const int4* xp = reinterpret_cast<const int4*>(xq + (size_t)m * K + b * 32);
-        int4 x0 = __ldg(xp), x1 = __ldg(xp + 1);
-        float dx = __ldg(xd + (size_t)m * nb + b);
-        int sx = __ldg(xs + (size_t)m * nb + b);
-#pragma unroll
-        for (int r = 0; r < R; r++) {
-          int p = q4_block_dot(w[r], x0, x1, sx);
-          acc[r][m] = __fadd_rn(acc[r][m], __fmul_rn((float)p, __fmul_rn(dw[r], dx)));
-        }
-      }
-    }
-  }
-#pragma unroll
-  for (int r = 0; r < R; r++)
-#pragma unroll
-    for (int m = 0; m < MAXM; m++) acc[r][m] = warp_sum(acc[r][m]);
-  if (lane == 0) {
-#pragma unroll
-    for (int r = 0; r < R; r++) {
-      const int n = row0 + r;
-      if (n >= N) break;
-#pragma unroll
-      for (int m = 0; m < MAXM; m++) {
-        if (m < M) {
-          float* o = y + (size_t)m * ldy + n;
-          if (OP == OP_ADD) *o = __fadd_rn(*o, acc[r][m]);
-          else if (OP == OP_BIAS) *o = __fadd_rn(acc[r][m], bias[n]);
-          else *o = acc[r][m];
-        }
-      }
-    }
-  }
+// Lane l of a Q4_0 block dot: sum over its 8 elements of (q - 8) * x = dp4a(low nibbles, x0 word l) +
+// dp4a(high nibbles, x1 word l) - 8 * (sum of those 8 x). Nibbles 0..15 equal their signed-byte values.
+__device__ __forceinline__ int q4_lane(uint32_t w, int x0, int x1, int xsum) {
+  return __dp4a((int)(w & 0x0f0f0f0fu), x0, __dp4a((int)((w >> 4) & 0x0f0f0f0fu), x1, 0)) - 8 * xsum;
 }
 
-// logits[n] = sum_b f32(int dot_b) * (dw * dx) for a Q8_0 output matrix (dot_q8_q8, kernels.c:157-170).
-template <int R>
-__global__ void __launch_bounds__(128) k_matvec_q8(const int8_t* __restrict__ qs, const __half* __restrict__ dsc, int N,
-                                                   int K, const int8_t* __restrict__ xq, const float* __restrict__ xd,
-                                                   float* __restrict__ y) {
+// y[m][n] (op)= sum over blocks of the reference's lane arithmetic (matmul_q4 / dot_q8_q8, kernels.c:121-273).
+// One CTA (256 threads) takes ROWS rows (within one 32-row group) for up to MB tokens:
+//   phase 1 (wide): every (block, row) item loads its 16 (Q4) or 32 (Q8) weight bytes once, computes the four
+//     exact integer lane dots per token and the products f32(p_l) * (dw * dx) into shared memory;
+//   phase 2 (ordered): thread (token, row, lane) adds its lane's products in block order; four threads then form
+//     ((l0 + l1) + l2) + l3 and apply the epilogue (put(), kernels.c:190-194).
+// dynamic smem: MB * (K/32) * ROWS * 16 bytes
+template <int WT, int ROWS, int MB, int OP>
+__global__ void __launch_bounds__(256) k_matvec(const uint8_t* __restrict__ qs, const __half* __restrict__ dsc, int N,
+                                                int K, const int8_t* __restrict__ xq, const float* __restrict__ xd,
+                                                const int4* __restrict__ xs, int M, float* __restrict__ y, int ldy,
+                                                const float* __restrict__ bias) {
+  extern __shared__ float4 prod[];  // [m][b][r]
+  constexpr int BB = WT == WQ4 ? 16 : 32;
   const int nb = K / 32;
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  const int row0 = warp * R;
-  if (row0 >= N) return;
-  float acc[R];
+  const int n0 = blockIdx.x * ROWS;
+  const int g = n0 >> 5, r0 = n0 & 31;
+  const uint8_t* wg = qs + (size_t)g * nb * 32 * BB;
+  const __half* dg = dsc + (size_t)g * nb * 32;
+  for (int it = threadIdx.x; it < nb * ROWS; it += blockDim.x) {
+    const int b = it / ROWS, r = it % ROWS;
+    const size_t e = (size_t)b * 32 + r0 + r;
+    const float dw = __half2float(dg[e]);
+    uint4 w0 = ldg_stream(wg + e * BB), w1;
+    if (WT == WQ8) w1 = ldg_stream(wg + e * BB + 16);
 #pragma unroll
-  for (int r = 0; r < R; r++) acc[r] = 0.f;
-  for (int b = lane; b < nb; b += 32) {
-    const int4* xp = reinterpret_cast<const int4*>(xq + b * 32);
-    int4 x0 = __ldg(xp), x1 = __ldg(xp + 1);
-    float dx = __ldg(xd + b);
-#pragma unroll
-    for (int r = 0; r < R; r++) {
-      int n = min(row0 + r, N - 1);
-      const int8_t* wp = qs + ((size_t)n * nb + b) * 32;
-      uint4 w0 = ldg_stream(wp), w1 = ldg_stream(wp + 16);
-      int p = 0;
-      p = __dp4a((int)w0.x, x0.x, p); p = __dp4a((int)w0.y, x0.y, p);
-      p = __dp4a((int)w0.z, x0.z, p); p = __dp4a((int)w0.w, x0.w, p);
-      p = __dp4a((int)w1.x, x1.x, p); p = __dp4a((int)w1.y, x1.y, p);
-      p = __dp4a((int)w1.z, x1.z, p); p = __dp4a((int)w1.w, x1.w, p);
-      acc[r] = __fadd_rn(acc[r], __fmul_rn((float)p, __fmul_rn(__half2float(dsc[(size_t)n * nb + b]), dx)));
+    for (int m = 0; m < MB; m++) {
+      if (m < M) {
+        const int4* xp = reinterpret_cast<const int4*>(xq + (size_t)m * K + b * 32);
+        const int4 x0 = __ldg(xp), x1 = __ldg(xp + 1);
+        const float sc = __fmul_rn(dw, __ldg(xd + (size_t)m * nb + b));
+        int p0, p1, p2, p3;
+        if (WT == WQ4) {
+          const int4 s = __ldg(xs + (size_t)m * nb + b);
+          p0 = q4_lane(w0.x, x0.x, x1.x, s.x);
+          p1 = q4_lane(w0.y, x0.y, x1.y, s.y);
+          p2 = q4_lane(w0.z, x0.z, x1.z, s.z);
+          p3 = q4_lane(w0.w, x0.w, x1.w, s.w);
+        } else {
+          p0 = __dp4a((int)w0.x, x0.x, __dp4a((int)w1.x, x1.x, 0));
+          p1 = __dp4a((int)w0.y, x0.y, __dp4a((int)w1.y, x1.y, 0));
+          p2 = __dp4a((int)w0.z, x0.z, __dp4a((int)w1.z, x1.z, 0));
+          p3 = __dp4a((int)w0.w, x0.w, __dp4a((int)w1.w, x1.w, 0));
+        }
+        prod[((size_t)m * nb + b) * ROWS + r] = make_float4(__fmul_rn((float)p0, sc), __fmul_rn((float)p1, sc),
+                                                            __fmul_rn((float)p2, sc), __fmul_rn((float)p3, sc));
+      }
     }
   }
-#pragma unroll
-  for (int r = 0; r < R; r++) acc[r] = warp_sum(acc[r]);
-  if (lane == 0) {
-#pragma unroll
-    for (int r = 0; r < R; r++)
-      if (row0 + r < N) y[row0 + r] = acc[r];
+  __syncthreads();
+  const int t = threadIdx.x;
+  const int l = t & 3, r = (t >> 2) % ROWS, m = (t >> 2) / ROWS;
+  if (m < MB) {
+    float acc = 0.f;
+    if (m < M) {
+      const float* pp = reinterpret_cast<const float*>(prod) + ((size_t)m * nb * ROWS + r) * 4 + l;
+#pragma unroll 8
+      for (int b = 0; b < nb; b++) acc = __fadd_rn(acc, pp[(size_t)b * ROWS * 4]);
+    }
+    const float v = hsum4_quad(acc);
+    const int n = n0 + r;
+    if (l == 0 && m < M && n < N) {
+      float* o = y + (size_t)m * ldy + n;
+      if (OP == OP_ADD) *o = __fadd_rn(*o, v);
+      else if (OP == OP_BIAS) *o = __fadd_rn(v, bias[n]);
+      else *o = v;
+    }
   }
 }
 
@@ -296,121 +278,67 @@ __global__ void k_rope_kv(const int32_t* __restrict__ prm, float* __restrict__ q
   }
 }
 
-// Split-K flash decode (kernels.c:355-377 computes the same softmax(q.K^T / sqrt(HD)) V per (token, head)).
-// grid (split, kv_head, token): one CTA takes ATT_CH cached positions of one KV head for all G = H/KVH query
-// heads that share it, and writes unnormalised partials (o[HD], max, sum) per head and split.
+// Attention for one (head, token), kernels.c:355-377: scores q.k_t in four lanes of HD/4 products each,
+// * 1/sqrt(HD); max; e_t = fast_exp(s_t - max); sum in position order; p_t = e_t / sum; o = sum_t p_t v_t in
+// position order. Scores and exponentials run one position per thread; the two ordered sums run as chains.
+// grid (H, M), 128 threads, dynamic smem T_max floats.
 template <int HD>
-__global__ void __launch_bounds__(128) k_attn_split(const int32_t* __restrict__ prm, const float* __restrict__ qkv, int QKV,
-                                                    const float* __restrict__ kc, const float* __restrict__ vc, int H,
-                                                    int KVH, int ctx, int layers, int layer, float* __restrict__ part,
-                                                    int nsplit_max) {
-  const int split = blockIdx.x, kh = blockIdx.y, m = blockIdx.z;
-  const int pos0 = prm[P_POS0], seq = prm[P_SEQ];
-  const int T = pos0 + m + 1;
-  const int t0 = split * ATT_CH;
-  if (t0 >= T) return;
-  const int n = min(ATT_CH, T - t0);
-  const int G = H / KVH;
-  __shared__ float q_s[MAXG][HD];
-  __shared__ float s_s[MAXG][ATT_CH];
-  __shared__ float mx_s[MAXG], l_s[MAXG];
-  __shared__ float o_s[2][MAXG][HD];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+__global__ void __launch_bounds__(128) k_attention(const int32_t* __restrict__ prm, const float* __restrict__ qkv, int QKV,
+                                                   const float* __restrict__ kc, const float* __restrict__ vc, int H,
+                                                   int KVH, int ctx, int layers, int layer, float* __restrict__ att,
+                                                   int D) {
+  extern __shared__ float sc[];
+  __shared__ float q_s[HD];
+  __shared__ float red[4];
+  __shared__ float sum_s;
+  const int h = blockIdx.x, m = blockIdx.y, tid = threadIdx.x;
+  const int T = prm[P_POS0] + m + 1, seq = prm[P_SEQ];
+  const int kh = h / (H / KVH);
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
-  const float* qrow = qkv + (size_t)m * QKV + (size_t)kh * G * HD;
-  for (int i = tid; i < G * HD; i += blockDim.x) q_s[i / HD][i % HD] = qrow[i];
+  for (int i = tid; i < HD; i += blockDim.x) q_s[i] = qkv[(size_t)m * QKV + (size_t)h * HD + i];
   __syncthreads();
   const size_t cbase = (((size_t)seq * layers + layer) * KVH + kh) * (size_t)ctx * HD;
   const float* kb = kc + cbase;
   const float* vb = vc + cbase;
-  // scores: thread = (position p, head parity)
-  {
-    const int p = tid % ATT_CH, g0 = tid / ATT_CH;
-    if (p < n) {
-      const float4* kr = reinterpret_cast<const float4*>(kb + (size_t)(t0 + p) * HD);
-      float dots[MAXG];
-#pragma unroll
-      for (int g = 0; g < MAXG; g++) dots[g] = 0.f;
-#pragma unroll 4
-      for (int i = 0; i < HD / 4; i++) {
-        float4 k4 = __ldg(kr + i);
-#pragma unroll
-        for (int g = 0; g < MAXG; g++) {
-          if (g < G && (g & 1) == g0) {
-            dots[g] = __fadd_rn(dots[g], __fmul_rn(q_s[g][4 * i], k4.x));
-            dots[g] = __fadd_rn(dots[g], __fmul_rn(q_s[g][4 * i + 1], k4.y));
-            dots[g] = __fadd_rn(dots[g], __fmul_rn(q_s[g][4 * i + 2], k4.z));
-            dots[g] = __fadd_rn(dots[g], __fmul_rn(q_s[g][4 * i + 3], k4.w));
-          }
-        }
-      }
-#pragma unroll
-      for (int g = 0; g < MAXG; g++)
-        if (g < G && (g & 1) == g0) s_s[g][p] = __fmul_rn(dots[g], scale);
-    }
-  }
-  __syncthreads();
-  // per head: max and sum of exp over this split's positions
-  for (int g = warp; g < G; g += 4) {
-    float mx = -1e30f;
-    for (int p = lane; p < n; p += 32) mx = fmaxf(mx, s_s[g][p]);
-    mx = warp_max(mx);
-    float l = 0.f;
-    for (int p = lane; p < n; p += 32) {
-      float e = fast_exp_ref(__fsub_rn(s_s[g][p], mx));
-      s_s[g][p] = e;
-      l += e;
-    }
-    l = warp_sum(l);
-    if (lane == 0) { mx_s[g] = mx; l_s[g] = l; }
-  }
-  __syncthreads();
-  // o[g][d] = sum_p e[g][p] * v[p][d]; thread = (dim d, half of the positions)
-  {
-    const int halves = 128 / HD;  // 2 for HD=64, 1 for HD=128
-    const int d = tid % HD, hf = tid / HD;
-    float o[MAXG];
-#pragma unroll
-    for (int g = 0; g < MAXG; g++) o[g] = 0.f;
-    for (int p = hf; p < n; p += halves) {
-      float v = __ldg(vb + (size_t)(t0 + p) * HD + d);
-#pragma unroll
-      for (int g = 0; g < MAXG; g++)
-        if (g < G) o[g] = __fadd_rn(o[g], __fmul_rn(s_s[g][p], v));
-    }
-#pragma unroll
-    for (int g = 0; g < MAXG; g++)
-      if (g < G) o_s[hf][g][d] = o[g];
-  }
-  __syncthreads();
-  for (int i = tid; i < G * HD; i += blockDim.x) {
-    const int g = i / HD, d = i % HD;
-    float v = o_s[0][g][d];
-    if (128 / HD > 1) v = __fadd_rn(v, o_s[1][g][d]);
-    const int h = kh * G + g;
-    float* dst = part + (((size_t)m * H + h) * nsplit_max + split) * (HD + 2);
-    dst[d] = v;
-    if (d == 0) { dst[HD] = mx_s[g]; dst[HD + 1] = l_s[g]; }
-  }
-}
-
-// Merge the splits of each (token, head): att = sum_s o_s e^(m_s - m) / sum_s l_s e^(m_s - m).
-__global__ void k_attn_combine(const int32_t* __restrict__ prm, const float* __restrict__ part, int H, int HD,
-                               int nsplit_max, float* __restrict__ att, int D) {
-  const int h = blockIdx.x, m = blockIdx.y, d = threadIdx.x;
-  const int T = prm[P_POS0] + m + 1;
-  const int ns = (T + ATT_CH - 1) / ATT_CH;
-  const float* src = part + ((size_t)m * H + h) * nsplit_max * (HD + 2);
   float mx = -1e30f;
-  for (int s = 0; s < ns; s++) mx = fmaxf(mx, src[s * (HD + 2) + HD]);
-  float l = 0.f, o = 0.f;
-  for (int s = 0; s < ns; s++) {
-    const float* e = src + s * (HD + 2);
-    float f = fast_exp_ref(__fsub_rn(e[HD], mx));
-    l = __fadd_rn(l, __fmul_rn(e[HD + 1], f));
-    if (d < HD) o = __fadd_rn(o, __fmul_rn(e[d], f));
+  for (int t = tid; t < T; t += blockDim.x) {
+    const float4* kr = reinterpret_cast<const float4*>(kb + (size_t)t * HD);
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll 8
+    for (int i = 0; i < HD / 4; i++) {
+      const float4 k4 = __ldg(kr + i);
+      s0 = __fadd_rn(s0, __fmul_rn(q_s[4 * i], k4.x));
+      s1 = __fadd_rn(s1, __fmul_rn(q_s[4 * i + 1], k4.y));
+      s2 = __fadd_rn(s2, __fmul_rn(q_s[4 * i + 2], k4.z));
+      s3 = __fadd_rn(s3, __fmul_rn(q_s[4 * i + 3], k4.w));
+    }
+    const float v = __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(s0, s1), s2), s3), scale);
+    sc[t] = v;
+    mx = fmaxf(mx, v);
   }
-  if (d < HD) att[(size_t)m * D + h * HD + d] = __fdiv_rn(o, l);
+  mx = warp_max(mx);
+  if ((tid & 31) == 0) red[tid >> 5] = mx;
+  __syncthreads();
+  mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  for (int t = tid; t < T; t += blockDim.x) sc[t] = fast_exp_ref(__fsub_rn(sc[t], mx));
+  __syncthreads();
+  if (tid == 0) {
+    float s = 0.f;
+#pragma unroll 8
+    for (int t = 0; t < T; t++) s = __fadd_rn(s, sc[t]);
+    sum_s = s;
+  }
+  __syncthreads();
+  const float sum = sum_s;
+  for (int t = tid; t < T; t += blockDim.x) sc[t] = __fdiv_rn(sc[t], sum);
+  __syncthreads();
+  for (int d = tid; d < HD; d += blockDim.x) {
+    float o = 0.f;
+    const float* vp = vb + d;
+#pragma unroll 8
+    for (int t = 0; t < T; t++) o = __fadd_rn(o, __fmul_rn(sc[t], __ldg(vp + (size_t)t * HD)));
+    att[(size_t)m * D + (size_t)h * HD + d] = o;
+  }
 }
 
 // Greedy argmax, stage 1: per-CTA (value, index) with ties to the lowest index (cpu-worker.js:156-157 scans
@@ -426,8 +354,8 @@ __global__ void k_argmax1(const float* __restrict__ logits, int V, float* __rest
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < V; i += gridDim.x * blockDim.x) amax_merge(v, idx, logits[i], i);
 #pragma unroll
   for (int o = 16; o; o >>= 1) {
-    float v2 = __shfl_xor_sync(0xffffffffu, v, o);
-    int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
+    const float v2 = __shfl_xor_sync(0xffffffffu, v, o);
+    const int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
     amax_merge(v, idx, v2, i2);
   }
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -439,6 +367,7 @@ __global__ void k_argmax1(const float* __restrict__ logits, int V, float* __rest
     pi[blockIdx.x] = idx;
   }
 }
+
 // stage 2: one warp merges the partials and stores the token. Like the WebGPU backend (webgpu.js:391), the token
 // stays on the device: it is logged at tokens[seq][pos0 + M] and the pass parameters are advanced to
 // (pos0 + M, one token, that id), so the next decode step can start without the host.
@@ -449,8 +378,8 @@ __global__ void k_argmax2(const float* __restrict__ pv, const int* __restrict__ 
   for (int i = threadIdx.x; i < np; i += 32) amax_merge(v, idx, pv[i], pi[i]);
 #pragma unroll
   for (int o = 16; o; o >>= 1) {
-    float v2 = __shfl_xor_sync(0xffffffffu, v, o);
-    int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
+    const float v2 = __shfl_xor_sync(0xffffffffu, v, o);
+    const int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
     amax_merge(v, idx, v2, i2);
   }
   if (threadIdx.x == 0) {

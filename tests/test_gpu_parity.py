@@ -1,9 +1,10 @@
 """Parity of the CUDA engine with the CPU oracle (the reference's algorithm), through the C ABI.
 
-Tolerances (north star): per-step logits under teacher forcing within max-abs 2e-3 of the logit range; greedy
-tokens identical except where the oracle's top-2 gap is below that tolerance. Integer parts (Q4_0 unpacking,
-int8 activation quantization, block dot products) are exact; only float summation order differs, so the
-matvec microbench is held to a much tighter 1e-5 of the output range.
+The north star's bound is per-step logits under teacher forcing within max-abs 2e-3 of the logit range, with
+greedy tokens identical except at near-ties. The reference re-quantizes every matrix input to int8, which makes
+any change of float summation order grow into logit differences above that bound, so the engine reproduces the
+reference's operation order exactly and these tests hold it to the stronger standard: bit-identical logits and
+identical tokens (the 2e-3 bound is also asserted, to report the distance when bits differ).
 """
 import ctypes as C
 
@@ -23,6 +24,10 @@ TOL = 2e-3
 def _gpu():
     assert torch.cuda.is_available(), "GPU tests need a CUDA device"
     _lib.load()
+
+
+def bits(a):
+    return np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
 
 
 def rel_err(a, b):
@@ -46,10 +51,12 @@ def teacher_forced(model, n_prompt, steps, chunk, ctx=96, seed=0):
     for s in range(steps + 1):
         nxt = be.forward(feed, pos, want_logits=True)
         r = ref.forward(feed, pos, want_logits=True)
-        e = rel_err(be.read_logits(), r["logits"])
+        lg = be.read_logits()
+        e = rel_err(lg, r["logits"])
         worst = max(worst, e)
         assert e <= TOL, f"{model} step {s}: |dlogits| = {e:.3g} of range"
-        if nxt != r["next"] and top2_gap(r["logits"]) >= TOL:
+        assert np.array_equal(bits(lg), bits(r["logits"])), f"{model} step {s}: logits not bit-identical ({e:.3g})"
+        if nxt != r["next"]:
             mism.append(s)
         pos += len(feed)
         if s < steps:
@@ -80,7 +87,7 @@ def test_golden_fixtures_through_cuda():
             lgs.append(be.read_logits())
             pos += 1
         for s, (a, b) in enumerate(zip(lgs, g["logits"])):
-            assert rel_err(a, b) <= TOL, f"{os.path.basename(fx)} step {s}"
+            assert np.array_equal(bits(a), bits(b)), f"{os.path.basename(fx)} step {s}: {rel_err(a, b):.3g}"
         be.destroy()
 
 
@@ -99,7 +106,7 @@ def test_chunking_invariance():
     for i, t in enumerate(p):
         c.forward([int(t)], i, want_logits=True)
     lc = c.read_logits()
-    assert rel_err(la, lc) <= 1e-4 and rel_err(lb, lc) <= 1e-4
+    assert np.array_equal(bits(la), bits(lc)) and np.array_equal(bits(lb), bits(lc))
 
 
 def test_sequences_are_independent():
@@ -185,4 +192,4 @@ def test_q4_matvec_microbench(N, K, M):
         torch.cuda.synchronize()
         ref = O.matvec_q4(blocks, N, K, x, op=op, bias=bias if op == 1 else None, y=y0, nth=8)
         got = y.cpu().numpy()
-        assert rel_err(got, ref) <= 1e-5, f"op {op}"
+        assert np.array_equal(bits(got), bits(ref)), f"op {op}: {rel_err(got, ref):.3g}"
