@@ -23,7 +23,7 @@ PROFILE_NAMES = ["embed", "norm+quantize", "matvec qkv", "rope+kv", "attention",
 # the exported symbols of include/h2cuda.h
 EXPORTS = ["h2c_create", "h2c_set_tensor", "h2c_forward", "h2c_generate", "h2c_decode_kernels", "h2c_read_logits", "h2c_profile", "h2c_destroy",
            "h2c_last_error", "h2c_device_bytes", "h2c_q4_matrix_bytes", "h2c_q4_pack", "h2c_q4_matvec_scratch_bytes",
-           "h2c_q4_matvec"]
+           "h2c_q4_matvec", "h2c_q4_matvec_noalloc"]
 
 
 class Config(C.Structure):
@@ -68,8 +68,9 @@ def load(path: str = LIB_PATH) -> C.CDLL:
     L.h2c_q4_matvec_scratch_bytes.argtypes = [i32, i32]
     L.h2c_q4_matvec_scratch_bytes.restype = u64
     L.h2c_q4_matvec.argtypes = [p, i32, i32, p, i32, p, i32, p, p, p]
+    L.h2c_q4_matvec_noalloc.argtypes = [p, i32, i32, p, i32, p, i32, p, p]
     for name in ("h2c_create", "h2c_set_tensor", "h2c_forward", "h2c_generate", "h2c_decode_kernels", "h2c_read_logits", "h2c_profile", "h2c_destroy",
-                 "h2c_q4_pack", "h2c_q4_matvec"):
+                 "h2c_q4_pack", "h2c_q4_matvec", "h2c_q4_matvec_noalloc"):
         getattr(L, name).restype = C.c_int
     _lib = L
     return L

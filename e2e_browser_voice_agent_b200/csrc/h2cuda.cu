@@ -6,6 +6,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -747,3 +748,71 @@ int h2c_q4_matvec(const void* w, int32_t n_rows, int32_t k, const float* x, int3
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- Q4_0 matvec without any allocation
+//
+// Some callers cannot call cudaMalloc: a host application that owns all device memory through its own pool and
+// forbids side allocations, or code on a latency-critical thread (a voice pipeline's audio callback, say), where
+// cudaMalloc can block and synchronize the device. For them h2c_q4_matvec_noalloc takes its scratch (the int8
+// activations, their scales and lane sums) from this fixed array instead of from the caller.
+//
+// The array is a file-scope __device__ variable: every GPU that loads this library holds its 256 KiB until the
+// process exits. On the host, its name is only a stand-in, not a device address, so the address the kernels get
+// comes from cudaGetSymbolAddress, looked up once per device with that device current (the first call of
+// h2c_q4_matvec_noalloc on a device does it; make that first call before any stream capture). Every call shares
+// the array and it keeps the last call's contents: nothing has to start at zero, because each call writes every
+// scratch byte it reads before reading it, but calls that overlap on the GPU (concurrent streams or threads) race
+// on it and must be serialised by the caller.
+
+namespace {
+constexpr uint64_t NOALLOC_SCRATCH_BYTES = 256 * 1024;
+constexpr int NOALLOC_MAX_DEVICES = 64;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[NOALLOC_SCRATCH_BYTES];
+void* g_noalloc_ptr[NOALLOC_MAX_DEVICES];
+std::mutex g_noalloc_mutex;
+
+// The device address of g_noalloc_scratch on the current device (looked up once per device); nullptr on error.
+void* noalloc_scratch(std::string* why) {
+  int dev = -1;
+  cudaError_t c = cudaGetDevice(&dev);
+  if (c != cudaSuccess || dev < 0 || dev >= NOALLOC_MAX_DEVICES) {
+    *why = std::string("cudaGetDevice: ") + (c != cudaSuccess ? cudaGetErrorString(c) : "device index out of range");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_ptr[dev]) {
+    void* ptr = nullptr;
+    c = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (c != cudaSuccess || !ptr) {
+      *why = std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(c);
+      return nullptr;
+    }
+    g_noalloc_ptr[dev] = ptr;
+  }
+  return g_noalloc_ptr[dev];
+}
+}  // namespace
+
+extern "C" int h2c_q4_matvec_noalloc(const void* w, int32_t n_rows, int32_t k, const float* x, int32_t m, float* y,
+                                     int32_t op, const float* bias, void* stream) {
+  if (!w || !x || !y || n_rows <= 0 || k <= 0 || k % 32 || m < 1 || op < 0 || op > 2 || (op == 1 && !bias)) {
+    g_create_error = "h2c_q4_matvec_noalloc: invalid argument";
+    return H2C_ERR_INVALID;
+  }
+  const uint64_t need = h2c_q4_matvec_scratch_bytes(m, k);
+  if (need > NOALLOC_SCRATCH_BYTES) {
+    char buf[200];
+    snprintf(buf, sizeof buf,
+             "h2c_q4_matvec_noalloc: %d x %d inputs need %llu bytes of scratch, above the %llu-byte static buffer",
+             m, k, (unsigned long long)need, (unsigned long long)NOALLOC_SCRATCH_BYTES);
+    g_create_error = buf;
+    return H2C_ERR_INVALID;
+  }
+  std::string why;
+  void* scratch = noalloc_scratch(&why);
+  if (!scratch) {
+    g_create_error = "h2c_q4_matvec_noalloc: " + why;
+    return H2C_ERR_CUDA;
+  }
+  return h2c_q4_matvec(w, n_rows, k, x, m, y, op, bias, scratch, stream);
+}

@@ -132,6 +132,18 @@ uint64_t h2c_q4_matvec_scratch_bytes(int32_t m, int32_t k);
 int h2c_q4_matvec(const void* w, int32_t n_rows, int32_t k, const float* x, int32_t m, float* y, int32_t op,
                   const float* bias, void* scratch, void* stream);
 
+/* h2c_q4_matvec without any allocation, for callers that cannot call cudaMalloc (a host that owns all device
+ * memory through its own pool, or a latency-critical thread such as a voice pipeline's audio callback, where
+ * cudaMalloc can block and synchronize the device). This entry point has no counterpart in the reference.
+ * Same arguments and result as h2c_q4_matvec, minus `scratch`: the scratch lives in a fixed 256 KiB
+ * __device__ array inside this library (held on every GPU that loads it until the process exits), so m and k are
+ * limited to h2c_q4_matvec_scratch_bytes(m, k) <= 262144 (for example m = 32 tokens of k = 4864); larger inputs
+ * are rejected with H2C_ERR_INVALID and a message in h2c_last_error(NULL). The first call on a device looks the
+ * array's device address up (make it before any stream capture). All calls share the array: calls that overlap
+ * on the GPU race and must be serialised by the caller. */
+int h2c_q4_matvec_noalloc(const void* w, int32_t n_rows, int32_t k, const float* x, int32_t m, float* y,
+                          int32_t op, const float* bias, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
