@@ -17,11 +17,13 @@ GGML_F32, GGML_Q4_0, GGML_Q8_0 = 0, 2, 8
 KIND_QKV, KIND_O, KIND_GATE_UP, KIND_DOWN, KIND_ATTN_NORM, KIND_FFN_NORM, KIND_QKV_BIAS, KIND_EMBED, KIND_OUTPUT, \
     KIND_OUTPUT_NORM = range(10)
 NPROF = 11
+DECODE_AUTO, DECODE_GRAPH, DECODE_PERSISTENT = 0, 1, 2
 PROFILE_NAMES = ["embed", "norm+quantize", "matvec qkv", "rope+kv", "attention", "quantize", "matvec o",
                  "matvec gate+up", "swiglu+quantize", "matvec down", "matvec output"]  # cpu-worker.js:32
 
 # the exported symbols of include/h2cuda.h
-EXPORTS = ["h2c_create", "h2c_set_tensor", "h2c_forward", "h2c_generate", "h2c_decode_kernels", "h2c_read_logits", "h2c_profile", "h2c_destroy",
+EXPORTS = ["h2c_create", "h2c_set_tensor", "h2c_forward", "h2c_generate", "h2c_decode_kernels", "h2c_set_decode_mode",
+           "h2c_decode_path", "h2c_trace_decode", "h2c_read_logits", "h2c_profile", "h2c_destroy",
            "h2c_last_error", "h2c_device_bytes", "h2c_q4_matrix_bytes", "h2c_q4_pack", "h2c_q4_matvec_scratch_bytes",
            "h2c_q4_matvec", "h2c_q4_matvec_noalloc"]
 
@@ -55,6 +57,9 @@ def load(path: str = LIB_PATH) -> C.CDLL:
     L.h2c_forward.argtypes = [p, C.c_int, p, i32, i32, C.c_float, u32, C.POINTER(i32)]
     L.h2c_generate.argtypes = [p, C.c_int, i32, i32, i32, p, C.POINTER(C.c_float)]
     L.h2c_decode_kernels.argtypes = [p]
+    L.h2c_set_decode_mode.argtypes = [p, C.c_int]
+    L.h2c_decode_path.argtypes = [p]
+    L.h2c_trace_decode.argtypes = [p, C.c_int, i32, i32, i32, p, i64]
     L.h2c_read_logits.argtypes = [p, C.c_int, p, i64]
     L.h2c_profile.argtypes = [p, C.c_int, p, i32, i32, C.POINTER(C.c_double)]
     L.h2c_destroy.argtypes = [p]
@@ -69,7 +74,8 @@ def load(path: str = LIB_PATH) -> C.CDLL:
     L.h2c_q4_matvec_scratch_bytes.restype = u64
     L.h2c_q4_matvec.argtypes = [p, i32, i32, p, i32, p, i32, p, p, p]
     L.h2c_q4_matvec_noalloc.argtypes = [p, i32, i32, p, i32, p, i32, p, p]
-    for name in ("h2c_create", "h2c_set_tensor", "h2c_forward", "h2c_generate", "h2c_decode_kernels", "h2c_read_logits", "h2c_profile", "h2c_destroy",
+    for name in ("h2c_create", "h2c_set_tensor", "h2c_forward", "h2c_generate", "h2c_decode_kernels", "h2c_set_decode_mode",
+                 "h2c_decode_path", "h2c_trace_decode", "h2c_read_logits", "h2c_profile", "h2c_destroy",
                  "h2c_q4_pack", "h2c_q4_matvec", "h2c_q4_matvec_noalloc"):
         getattr(L, name).restype = C.c_int
     _lib = L

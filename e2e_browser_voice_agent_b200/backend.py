@@ -34,7 +34,7 @@ class CudaBackend:
     name = "cuda"
 
     def __init__(self, parsed, data, cfg: Dict, ctx: int = 2048, prefill_chunk: int = 16, max_seqs: int = 1,
-                 device: int = 0, keep_logits: bool = False, on_progress=None):
+                 device: int = 0, keep_logits: bool = False, on_progress=None, decode_mode: str = "auto"):
         L = _lib.load()
         self._L = L
         D, NL, F, H, KVH, V = cfg["dim"], cfg["layers"], cfg["ffn"], cfg["heads"], cfg["kv_heads"], cfg["vocab"]
@@ -85,6 +85,8 @@ class CudaBackend:
                 raise ValueError("output.weight: expected Q8_0")  # cpu-worker.js:126
             put(_lib.KIND_OUTPUT, 0, out["type"], G.tensor_view(data, out))
         put(_lib.KIND_OUTPUT_NORM, 0, f32, raw("output_norm.weight", f32))
+        if decode_mode != "auto":
+            self.set_decode_mode(decode_mode)
         self.memory_bytes = int(L.h2c_device_bytes(self._h))
         self.build = _lib.LIB_PATH
         self.threads = 1
@@ -138,6 +140,26 @@ class CudaBackend:
         _lib.check(rc, self._h)
         self._last_logits = {}
         return out, float(ms.value)
+
+    def set_decode_mode(self, mode: str) -> None:
+        """'auto' (persistent kernel when the model fits it), 'graph' or 'persistent'."""
+        code = {"auto": _lib.DECODE_AUTO, "graph": _lib.DECODE_GRAPH, "persistent": _lib.DECODE_PERSISTENT}[mode]
+        _lib.check(self._L.h2c_set_decode_mode(self._h, code), self._h)
+
+    @property
+    def decode_path(self) -> str:
+        n = self._L.h2c_decode_path(self._h)
+        if n < 0:
+            _lib.check(n, self._h)
+        return {_lib.DECODE_GRAPH: "graph", _lib.DECODE_PERSISTENT: "persistent"}[n]
+
+    def trace_decode(self, first_id: int, pos: int, steps: int, seq: int = 0) -> np.ndarray:
+        """Stage timestamps (ns) of the persistent kernel: array [2 CTAs][steps][layers + 1][16]."""
+        L = self.cfg["layers"]
+        out = np.zeros((2, steps, L + 1, 16), dtype=np.uint64)
+        _lib.check(self._L.h2c_trace_decode(self._h, int(seq), int(first_id), int(pos), int(steps), out.ctypes.data,
+                                            out.size), self._h)
+        return out
 
     def decode_kernels(self) -> int:
         n = self._L.h2c_decode_kernels(self._h)

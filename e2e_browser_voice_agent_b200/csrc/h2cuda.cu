@@ -6,11 +6,13 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <algorithm>
 #include <mutex>
 #include <string>
 #include <vector>
 
 #include "../../include/h2cuda.h"
+#include "decode_mk.cuh"
 #include "kernels.cuh"
 
 using namespace h2;
@@ -73,6 +75,22 @@ struct h2c_engine {
   std::vector<int> layer_set;  // bit mask of kinds 0..6 set per layer
   bool embd_set = false, out_norm_set = false;
   std::vector<int> last_logits_valid;
+  // persistent decode kernel (decode_mk.cuh)
+  int decode_mode = H2C_DECODE_AUTO;
+  bool mk_built = false, mk_ok = false;
+  std::string mk_why;
+  int mk_ncta = 0, mk_tile_stride = 0, mk_prod_items = 0, mk_kv_stage = 0;
+  size_t mk_smem = 0;
+  uint8_t* mk_stream = nullptr;
+  MkTile* mk_tiles = nullptr;
+  float *mk_attn_norm = nullptr, *mk_ffn_norm = nullptr, *mk_bqkv = nullptr;
+  unsigned long long *mk_xw = nullptr, *mk_qw = nullptr, *mk_kvw = nullptr, *mk_attw = nullptr, *mk_actw = nullptr,
+                     *mk_lmw = nullptr;
+  size_t mk_tagged_words = 0;  // mk_xw .. mk_lmw are one allocation of this many words
+  int32_t* mk_io = nullptr;   // device: [0] next token, [4..7] error words
+  int* mk_tile_count = nullptr;
+  int32_t* mk_io_h = nullptr; // pinned
+  bool mk_pending = false;    // the last pass of the current forward ran on the persistent kernel
 
   int fail(int code, const char* fmt, ...) {
     char buf[512];
@@ -375,6 +393,222 @@ int sample_host(const float* lg, int n, double temperature, uint32_t seed) {
   return best;
 }
 
+// ---------------------------------------------------------------- persistent decode kernel: layout and launch
+
+struct TileSpec {
+  const uint8_t* qs;  // grouped layout on the host copy
+  const uint16_t* d;
+  int nb;
+  std::vector<int> rows;
+};
+
+size_t tile_bytes(int nb, int R) { return align_up((size_t)nb * R * 16, 16) + align_up((size_t)nb * R * 2, 16); }
+
+// gather rows of a grouped-layout matrix into one row-major tile: values [R][nb][16], then scales [R][nb]
+void gather_tile(const TileSpec& t, uint8_t* dst) {
+  const int R = (int)t.rows.size(), nb = t.nb;
+  uint16_t* dd = reinterpret_cast<uint16_t*>(dst + align_up((size_t)nb * R * 16, 16));
+  for (int j = 0; j < R; j++)
+    for (int b = 0; b < nb; b++) {
+      const int n = t.rows[j], g = n >> 5, r = n & 31;
+      const size_t e = ((size_t)g * nb + b) * 32 + r;
+      memcpy(dst + ((size_t)j * nb + b) * 16, t.qs + e * 16, 16);
+      dd[(size_t)j * nb + b] = t.d[e];
+    }
+}
+
+int mk_unsupported(h2c_engine* e, const char* why) {
+  e->mk_ok = false;
+  e->mk_why = why;
+  return H2C_OK;
+}
+
+// Decide whether the persistent kernel applies to this model and, if so, lay out the weight stream.
+int mk_build(h2c_engine* e) {
+  if (e->mk_built) return H2C_OK;
+  e->mk_built = true;
+  const h2c_config& c = e->cfg;
+  const int D = c.dim, F = c.ffn, H = c.heads, KVH = c.kv_heads, HD = e->HD, QKV = e->QKV, NL = c.layers,
+            V = c.vocab;
+  const int nbd = D / 32, nbf = F / 32;
+  int dev_sms = 0, coop = 0;
+  CUDA_TRY(e, cudaDeviceGetAttribute(&dev_sms, cudaDevAttrMultiProcessorCount, e->dev));
+  CUDA_TRY(e, cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, e->dev));
+  if (!coop) return mk_unsupported(e, "device without cooperative launch");
+  if (e->out_type == 8) return mk_unsupported(e, "Q8_0 output matrix (the persistent kernel streams Q4_0 tiles)");
+  if (HD % MK_TILE_ROWS) return mk_unsupported(e, "head_dim not a multiple of 64");
+  if (F < D) return mk_unsupported(e, "ffn narrower than the hidden size");
+  if (tile_bytes(nbd, MK_TILE_ROWS) > (size_t)MK_SLOT) return mk_unsupported(e, "rows too long for 64-row tiles");
+  const int nh = std::min(dev_sms - H, D / 4);  // CTAs owning O / down rows
+  if (nh < 1) return mk_unsupported(e, "not enough SMs");
+  const int ncta = H + nh;
+  if (V < ncta) return mk_unsupported(e, "vocabulary smaller than the grid");
+  const int o_max = (D + nh - 1) / nh;
+  if (o_max > 64 || tile_bytes(nbf, o_max) > (size_t)MK_SLOT)
+    return mk_unsupported(e, "per-CTA O/down tiles larger than a ring slot");
+  const int npair = QKV / 2, pr_max = (npair + ncta - 1) / ncta;
+  if (2 * pr_max > 64) return mk_unsupported(e, "more than 64 QKV rows per CTA");
+  if (nbf > MK_NT) return mk_unsupported(e, "rows longer than the tile kernel's thread count");
+  // product buffer: R rows of (4 nb + 4) floats, in float4 units
+  const int prod_items =
+      std::max({MK_TILE_ROWS * (nbd + 1), o_max * (nbd + 1), o_max * (nbf + 1), 2 * pr_max * (nbd + 1)});
+  const size_t base = mk_smem_base(D, F, HD, c.ctx, prod_items);
+  int max_optin = 0;
+  CUDA_TRY(e, cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, e->dev));
+  const size_t budget = (size_t)max_optin - 1024;  // static shared memory of the kernel is far below 1 KB
+  if (base > budget) return mk_unsupported(e, "context too long for the shared-memory score buffer");
+  // K rows are staged with 4 floats of padding (conflict-free dot products), V rows unpadded
+  const int kv_stage = (int)std::min<size_t>((size_t)c.ctx, (budget - base) / ((size_t)(2 * HD + 4) * 4));
+  const size_t smem = base + (size_t)kv_stage * (2 * HD + 4) * 4;
+  CUDA_TRY(e, cudaFuncSetAttribute(k_decode_persistent, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  int occ = 0;
+  CUDA_TRY(e, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_decode_persistent, MK_THREADS, smem));
+  if (occ < 1) return mk_unsupported(e, "persistent kernel does not fit on an SM");
+
+  // host copies of the packed (grouped) matrices
+  auto fetch = [&](const Q4Mat& m, std::vector<uint8_t>& qs, std::vector<uint16_t>& d) -> int {
+    const size_t nbp = padded_rows(m.N) * (m.K / 32);
+    qs.resize(nbp * 16);
+    d.resize(nbp);
+    CUDA_TRY(e, cudaMemcpy(qs.data(), m.qs, qs.size(), cudaMemcpyDeviceToHost));
+    CUDA_TRY(e, cudaMemcpy(d.data(), m.d, d.size() * 2, cudaMemcpyDeviceToHost));
+    return H2C_OK;
+  };
+  std::vector<std::vector<uint8_t>> hq(4 * NL + 1);
+  std::vector<std::vector<uint16_t>> hd(4 * NL + 1);
+  int r = 0;
+  for (int l = 0; l < NL; l++) {
+    const LayerW& W = e->L[l];
+    if ((r = fetch(W.qkv, hq[4 * l], hd[4 * l])) || (r = fetch(W.o, hq[4 * l + 1], hd[4 * l + 1])) ||
+        (r = fetch(W.gu, hq[4 * l + 2], hd[4 * l + 2])) || (r = fetch(W.down, hq[4 * l + 3], hd[4 * l + 3])))
+      return r;
+  }
+  if ((r = fetch(e->out_type == 2 ? e->out4 : e->embd, hq[4 * NL], hd[4 * NL]))) return r;
+
+  // per-CTA tile lists, in consumption order (must match k_decode_persistent)
+  std::vector<std::vector<TileSpec>> specs(ncta);
+  const int half = HD / 2;
+  auto rows_tile = [&](int mat, int nb, int first, int count) {
+    TileSpec t{hq[mat].data(), hd[mat].data(), nb, {}};
+    for (int n = first; n < first + count; n++) t.rows.push_back(n);
+    return t;
+  };
+  for (int cta = 0; cta < ncta; cta++) {
+    const bool head = cta < H;
+    const int jj = cta - H;
+    const int o_lo = head ? 0 : (int)((long long)jj * D / nh), o_hi = head ? 0 : (int)((long long)(jj + 1) * D / nh);
+    const int v_lo = (int)((long long)cta * V / ncta), v_hi = (int)((long long)(cta + 1) * V / ncta);
+    const int pr_lo = (int)((long long)cta * npair / ncta), pr_hi = (int)((long long)(cta + 1) * npair / ncta);
+    auto& Lst = specs[cta];
+    for (int l = 0; l < NL; l++) {
+      TileSpec a{hq[4 * l].data(), hd[4 * l].data(), nbd, {}};
+      for (int pi = pr_lo; pi < pr_hi; pi++) {  // QKV rows in RoPE pairs (i, i + HD/2) of a head
+        const int hh = pi / half, i = pi % half;
+        a.rows.push_back(hh * HD + i);
+        a.rows.push_back(hh * HD + i + half);
+      }
+      Lst.push_back(a);
+      if (!head) Lst.push_back(rows_tile(4 * l + 1, nbd, o_lo, o_hi - o_lo));
+      for (int ab = cta; ab < nbf; ab += ncta) {
+        TileSpec g{hq[4 * l + 2].data(), hd[4 * l + 2].data(), nbd, {}};
+        for (int q = 0; q < 32; q++) g.rows.push_back(32 * ab + q);
+        for (int q = 0; q < 32; q++) g.rows.push_back(F + 32 * ab + q);
+        Lst.push_back(g);
+      }
+      if (!head) Lst.push_back(rows_tile(4 * l + 3, nbf, o_lo, o_hi - o_lo));
+    }
+    for (int r0 = v_lo; r0 < v_hi; r0 += MK_TILE_ROWS)
+      Lst.push_back(rows_tile(4 * NL, nbd, r0, std::min(v_hi, r0 + MK_TILE_ROWS) - r0));
+  }
+  size_t maxt = 0, total = 0;
+  for (auto& Lst : specs) {
+    maxt = std::max(maxt, Lst.size());
+    for (auto& t : Lst) total += tile_bytes(t.nb, (int)t.rows.size());
+  }
+  if (maxt > (size_t)MK_MAX_TILES) return mk_unsupported(e, "more tiles per token than the shared-memory table holds");
+  std::vector<uint8_t> stream(total);
+  std::vector<MkTile> table((size_t)ncta * maxt);
+  std::vector<int> counts(ncta);
+  size_t off = 0;
+  for (int cta = 0; cta < ncta; cta++) {
+    counts[cta] = (int)specs[cta].size();
+    for (size_t i = 0; i < specs[cta].size(); i++) {
+      const TileSpec& t = specs[cta][i];
+      const size_t b = tile_bytes(t.nb, (int)t.rows.size());
+      if (b > (size_t)MK_SLOT) return mk_unsupported(e, "tile larger than a ring slot");
+      gather_tile(t, stream.data() + off);
+      table[(size_t)cta * maxt + i] = MkTile{(uint64_t)off, (uint32_t)b, (uint16_t)t.rows.size(), (uint16_t)t.nb};
+      off += b;
+    }
+  }
+  const size_t words = (size_t)D * 3 + (size_t)2 * KVH * HD + (size_t)nbf * MK_ACT_WORDS + (size_t)ncta * 2;
+  unsigned long long* tagged = nullptr;
+  if ((r = dalloc_t(e, &e->mk_stream, total)) || (r = dalloc_t(e, &e->mk_tiles, table.size())) ||
+      (r = dalloc_t(e, &e->mk_attn_norm, (size_t)NL * D)) || (r = dalloc_t(e, &e->mk_ffn_norm, (size_t)NL * D)) ||
+      (r = dalloc_t(e, &e->mk_bqkv, (size_t)NL * QKV)) || (r = dalloc_t(e, &tagged, words)) ||
+      (r = dalloc_t(e, &e->mk_io, 8)) || (r = dalloc_t(e, &e->mk_tile_count, (size_t)ncta)))
+    return r;
+  e->mk_xw = tagged;
+  e->mk_qw = tagged + D;
+  e->mk_attw = tagged + 2 * D;
+  e->mk_kvw = tagged + 3 * D;
+  e->mk_actw = e->mk_kvw + (size_t)2 * KVH * HD;
+  e->mk_lmw = e->mk_actw + (size_t)nbf * MK_ACT_WORDS;
+  e->mk_tagged_words = words;
+  CUDA_TRY(e, cudaMallocHost(&e->mk_io_h, 8 * sizeof(int32_t)));
+  CUDA_TRY(e, cudaMemcpy(e->mk_tile_count, counts.data(), counts.size() * sizeof(int), cudaMemcpyHostToDevice));
+  CUDA_TRY(e, cudaMemcpy(e->mk_stream, stream.data(), total, cudaMemcpyHostToDevice));
+  CUDA_TRY(e, cudaMemcpy(e->mk_tiles, table.data(), table.size() * sizeof(MkTile), cudaMemcpyHostToDevice));
+  for (int l = 0; l < NL; l++) {
+    CUDA_TRY(e, cudaMemcpy(e->mk_attn_norm + (size_t)l * D, e->L[l].attn_norm, D * 4, cudaMemcpyDeviceToDevice));
+    CUDA_TRY(e, cudaMemcpy(e->mk_ffn_norm + (size_t)l * D, e->L[l].ffn_norm, D * 4, cudaMemcpyDeviceToDevice));
+    CUDA_TRY(e, cudaMemcpy(e->mk_bqkv + (size_t)l * QKV, e->L[l].bqkv, (size_t)QKV * 4, cudaMemcpyDeviceToDevice));
+  }
+  e->mk_ncta = ncta;
+  e->mk_tile_stride = (int)maxt;
+  e->mk_prod_items = prod_items;
+  e->mk_kv_stage = kv_stage;
+  e->mk_smem = smem;
+  e->mk_ok = true;
+  return H2C_OK;
+}
+
+bool use_persistent(h2c_engine* e) {
+  if (e->decode_mode == H2C_DECODE_GRAPH) return false;
+  return e->mk_ok;
+}
+
+// Launch `steps` decode steps of the persistent kernel (parameters already in e->prm on the stream).
+int mk_launch(h2c_engine* e, int steps, unsigned long long* trace = nullptr) {
+  const h2c_config& c = e->cfg;
+  MkParams p{};
+  p.D = c.dim; p.F = c.ffn; p.H = c.heads; p.KVH = c.kv_heads; p.HD = e->HD; p.QKV = e->QKV; p.L = c.layers;
+  p.V = c.vocab; p.ctx = c.ctx; p.ncta = e->mk_ncta; p.eps = c.eps;
+  p.stream = e->mk_stream; p.tiles = e->mk_tiles; p.tile_count = e->mk_tile_count; p.tile_stride = e->mk_tile_stride;
+  p.prod_items = e->mk_prod_items; p.kv_stage = e->mk_kv_stage;
+  p.attn_norm = e->mk_attn_norm; p.ffn_norm = e->mk_ffn_norm; p.bqkv = e->mk_bqkv; p.out_norm = e->out_norm;
+  p.rope = e->rope; p.embd_qs = e->embd.qs; p.embd_d = e->embd.d; p.kc = e->kc; p.vc = e->vc; p.logits = e->logits;
+  p.xw = e->mk_xw; p.qw = e->mk_qw; p.kvw = e->mk_kvw; p.attw = e->mk_attw; p.actw = e->mk_actw; p.lmw = e->mk_lmw;
+  p.err = e->mk_io + 4; p.prm = e->prm; p.toklog = e->toklog; p.next = e->mk_io; p.steps = steps;
+  p.timeout_ns = 2000000000ull;
+  p.trace = trace;
+  CUDA_TRY(e, cudaMemsetAsync(e->mk_xw, 0, e->mk_tagged_words * sizeof(unsigned long long), e->st));
+  CUDA_TRY(e, cudaMemsetAsync(e->mk_io, 0, 8 * sizeof(int32_t), e->st));
+  void* args[] = {&p};
+  CUDA_TRY(e, cudaLaunchCooperativeKernel((void*)k_decode_persistent, dim3(e->mk_ncta), dim3(MK_THREADS), args,
+                                          e->mk_smem, e->st));
+  return H2C_OK;
+}
+
+// After a persistent launch has completed (stream synchronised): turn its error words into a status.
+int mk_status(h2c_engine* e) {
+  const int32_t* io = e->mk_io_h;
+  if (io[4] != 0)
+    return e->fail(H2C_ERR_TIMEOUT, "persistent decode kernel: bounded wait expired (code %d, CTA %d, stage %d)", io[4],
+                   io[5], io[6]);
+  return H2C_OK;
+}
+
 int run_forward(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t pos, Prof* pf) {
   const h2c_config& c = e->cfg;
   if (!ids || n < 1) return e->fail(H2C_ERR_INVALID, "forward needs at least one token");
@@ -389,7 +623,9 @@ int run_forward(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t p
   const int nchunks = (n + MT - 1) / MT;
   if (nchunks > e->prm_slots) return e->fail(H2C_ERR_INVALID, "too many chunks");
   const int stride = P_IDS + MT;
+  e->mk_pending = false;
   for (int ci = 0; ci < nchunks; ci++) {
+    e->mk_pending = false;
     const int c0 = ci * MT, mlen = n - c0 < MT ? n - c0 : MT;
     const bool last = ci == nchunks - 1;
     int32_t* h = e->prm_h + (size_t)ci * stride;
@@ -400,6 +636,12 @@ int run_forward(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t p
     memcpy(h + P_IDS, ids + c0, sizeof(int32_t) * mlen);
     CUDA_TRY(e, cudaMemcpyAsync(e->prm, h, sizeof(int32_t) * (P_IDS + mlen), cudaMemcpyHostToDevice, e->st));
     if (mlen == 1 && !pf) {
+      if (e->decode_mode != H2C_DECODE_GRAPH && (r = mk_build(e))) return r;
+      if (use_persistent(e)) {
+        if ((r = mk_launch(e, 1))) return r;
+        e->mk_pending = true;
+        continue;
+      }
       if (!e->gexec) {
         r = build_graph(e);
         if (r) return r;
@@ -584,8 +826,16 @@ int h2c_forward(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t p
   if (temperature > 0) {
     std::vector<float> lg(e->cfg.vocab);
     CUDA_TRY(e, cudaMemcpyAsync(lg.data(), e->logits, lg.size() * 4, cudaMemcpyDeviceToHost, e->st));
+    if (e->mk_pending)
+      CUDA_TRY(e, cudaMemcpyAsync(e->mk_io_h, e->mk_io, 8 * sizeof(int32_t), cudaMemcpyDeviceToHost, e->st));
     CUDA_TRY(e, cudaStreamSynchronize(e->st));
+    if (e->mk_pending && (r = mk_status(e))) return r;
     *next = sample_host(lg.data(), e->cfg.vocab, temperature, sseed);
+  } else if (e->mk_pending) {
+    CUDA_TRY(e, cudaMemcpyAsync(e->mk_io_h, e->mk_io, 8 * sizeof(int32_t), cudaMemcpyDeviceToHost, e->st));
+    CUDA_TRY(e, cudaStreamSynchronize(e->st));
+    if ((r = mk_status(e))) return r;
+    *next = e->mk_io_h[0];
   } else {
     CUDA_TRY(e, cudaMemcpyAsync(e->next_h, e->next_d, 4, cudaMemcpyDeviceToHost, e->st));
     CUDA_TRY(e, cudaStreamSynchronize(e->st));
@@ -606,7 +856,8 @@ int h2c_generate(h2c_engine* e, int seq, int32_t first_id, int32_t pos, int32_t 
   CUDA_TRY(e, cudaSetDevice(e->dev));
   int r = check_ready(e);
   if (r) return r;
-  if (!e->gexec && (r = build_graph(e))) return r;
+  if (e->decode_mode != H2C_DECODE_GRAPH && (r = mk_build(e))) return r;
+  if (!use_persistent(e) && !e->gexec && (r = build_graph(e))) return r;
   int32_t* h = e->prm_h;
   h[P_POS0] = pos;
   h[P_M] = 1;
@@ -614,28 +865,92 @@ int h2c_generate(h2c_engine* e, int seq, int32_t first_id, int32_t pos, int32_t 
   h[3] = 0;
   h[P_IDS] = first_id;
   CUDA_TRY(e, cudaMemcpyAsync(e->prm, h, sizeof(int32_t) * (P_IDS + 1), cudaMemcpyHostToDevice, e->st));
+  const bool mk = use_persistent(e);
   CUDA_TRY(e, cudaEventRecord(e->ev0, e->st));
-  for (int i = 0; i < steps; i++) CUDA_TRY(e, cudaGraphLaunch(e->gexec, e->st));
+  if (mk) {
+    if ((r = mk_launch(e, steps))) return r;
+  } else {
+    for (int i = 0; i < steps; i++) CUDA_TRY(e, cudaGraphLaunch(e->gexec, e->st));
+  }
   CUDA_TRY(e, cudaEventRecord(e->ev1, e->st));
+  if (mk) CUDA_TRY(e, cudaMemcpyAsync(e->mk_io_h, e->mk_io, 8 * sizeof(int32_t), cudaMemcpyDeviceToHost, e->st));
   if (out_tokens)
     CUDA_TRY(e, cudaMemcpyAsync(out_tokens, e->toklog + (size_t)seq * (c.ctx + 1) + pos + 1, sizeof(int32_t) * steps,
                                 cudaMemcpyDeviceToHost, e->st));
   CUDA_TRY(e, cudaStreamSynchronize(e->st));
+  if (mk && (r = mk_status(e))) return r;
   if (device_ms) CUDA_TRY(e, cudaEventElapsedTime(device_ms, e->ev0, e->ev1));
   e->last_logits_valid.assign(c.max_seqs, 0);
   e->last_logits_valid[seq] = 1;
   return H2C_OK;
 }
 
+int h2c_trace_decode(h2c_engine* e, int seq, int32_t first_id, int32_t pos, int32_t steps, uint64_t* out, int64_t n) {
+  if (!e || !out || steps < 1) return H2C_ERR_INVALID;
+  const h2c_config& c = e->cfg;
+  const int64_t need = 2 * (int64_t)steps * (c.layers + 1) * MK_TRACE_PTS;
+  if (n < need) return e->fail(H2C_ERR_INVALID, "trace needs %lld entries", (long long)need);
+  if (seq < 0 || seq >= c.max_seqs || pos < 0 || (int64_t)pos + steps >= c.ctx || first_id < 0 || first_id >= c.vocab)
+    return e->fail(H2C_ERR_INVALID, "bad trace arguments");
+  CUDA_TRY(e, cudaSetDevice(e->dev));
+  int r = check_ready(e);
+  if (r) return r;
+  if ((r = mk_build(e))) return r;
+  if (!e->mk_ok) return e->fail(H2C_ERR_INVALID, "persistent decode kernel unavailable: %s", e->mk_why.c_str());
+  unsigned long long* d = nullptr;
+  CUDA_TRY(e, cudaMalloc(&d, need * 8));
+  CUDA_TRY(e, cudaMemsetAsync(d, 0, need * 8, e->st));
+  int32_t* h = e->prm_h;
+  h[P_POS0] = pos; h[P_M] = 1; h[P_SEQ] = seq; h[3] = 0; h[P_IDS] = first_id;
+  CUDA_TRY(e, cudaMemcpyAsync(e->prm, h, sizeof(int32_t) * (P_IDS + 1), cudaMemcpyHostToDevice, e->st));
+  r = mk_launch(e, steps, d);
+  if (!r) {
+    CUDA_TRY(e, cudaMemcpyAsync(e->mk_io_h, e->mk_io, 8 * sizeof(int32_t), cudaMemcpyDeviceToHost, e->st));
+    CUDA_TRY(e, cudaMemcpyAsync(out, d, need * 8, cudaMemcpyDeviceToHost, e->st));
+    CUDA_TRY(e, cudaStreamSynchronize(e->st));
+    r = mk_status(e);
+  }
+  cudaFree(d);
+  return r;
+}
+
 int h2c_decode_kernels(h2c_engine* e) {
   if (!e) return H2C_ERR_INVALID;
   CUDA_TRY(e, cudaSetDevice(e->dev));
+  {
+    int r = check_ready(e);
+    if (r) return r;
+    if (e->decode_mode != H2C_DECODE_GRAPH && (r = mk_build(e))) return r;
+    if (use_persistent(e)) return 1;
+  }
   if (!e->gexec) {
     int r = check_ready(e);
     if (r) return r;
     if ((r = build_graph(e))) return r;
   }
   return e->graph_kernels;
+}
+
+int h2c_set_decode_mode(h2c_engine* e, int mode) {
+  if (!e || mode < H2C_DECODE_AUTO || mode > H2C_DECODE_PERSISTENT) return H2C_ERR_INVALID;
+  if (mode == H2C_DECODE_PERSISTENT) {
+    CUDA_TRY(e, cudaSetDevice(e->dev));
+    int r = check_ready(e);
+    if (r) return r;
+    if ((r = mk_build(e))) return r;
+    if (!e->mk_ok) return e->fail(H2C_ERR_INVALID, "persistent decode kernel unavailable: %s", e->mk_why.c_str());
+  }
+  e->decode_mode = mode;
+  return H2C_OK;
+}
+
+int h2c_decode_path(h2c_engine* e) {
+  if (!e) return H2C_ERR_INVALID;
+  CUDA_TRY(e, cudaSetDevice(e->dev));
+  int r = check_ready(e);
+  if (r) return r;
+  if (e->decode_mode != H2C_DECODE_GRAPH && (r = mk_build(e))) return r;
+  return use_persistent(e) ? H2C_DECODE_PERSISTENT : H2C_DECODE_GRAPH;
 }
 
 int h2c_read_logits(h2c_engine* e, int seq, float* out, int64_t n) {
@@ -685,6 +1000,7 @@ int h2c_destroy(h2c_engine* e) {
   if (e->graph) cudaGraphDestroy(e->graph);
   for (void* p : e->dallocs) cudaFree(p);
   if (e->prm_h) cudaFreeHost(e->prm_h);
+  if (e->mk_io_h) cudaFreeHost(e->mk_io_h);
   if (e->next_h) cudaFreeHost(e->next_h);
   if (e->ev0) cudaEventDestroy(e->ev0);
   if (e->ev1) cudaEventDestroy(e->ev1);

@@ -21,7 +21,8 @@
 //     elements 16 + those. N is padded to a multiple of 32 with zero blocks.
 //   Q8_0 matrix: the same grouping with 32-byte blocks, each 16-byte half permuted the same way.
 //   int8 activations xq [M][K]: per block of 32 the two halves (elements 0..15, 16..31) permuted like the
-//     weights, scale xd [M][K/32] f32, and per-lane integer sums xs [M][K/32] int4 (for the -8 nibble offset).
+//     weights, scale xd [M][K/32] f32, and per lane the accumulator start of its Q4_0 block dot xs [M][K/32] int4
+//     (-8 x the sum of its int8 values, for the nibble offset, plus the float-conversion constant MK_MAGIC).
 //   activations: x [M][D] f32 residual stream; qkv [M][D + 2*KVH*HD]; att [M][D]; gu [M][2F].
 //   KV cache [seq][layer][kv_head][ctx][HD] f32 (the reference's dtype and order, kernels.c:347-348).
 #pragma once
@@ -65,9 +66,16 @@ __device__ __forceinline__ float hsum4_quad(float a) {
   return __fadd_rn(__fadd_rn(__fadd_rn(a, a1), a2), a3);
 }
 
+// Integers |p| < 2^22 converted to float without the (quarter-rate) int->float instruction: the bit pattern
+// MK_MAGIC + p is the float 12582912 + p exactly, and subtracting 12582912 is exact. Block dots carry MK_MAGIC in
+// their accumulator, so f32(p) = __int_as_float(acc) - 12582912.0f.
+constexpr int MK_MAGIC = 0x4B400000;
+__device__ __forceinline__ float magic_to_float(int acc) { return __fsub_rn(__int_as_float(acc), 12582912.0f); }
+
 // Quantize the 32 values held one per lane (kernels.c:90-114): amax over the block (a max is exact in any order),
-// d = amax / 127, q = nearest-even(x * (1 / d)) saturated to int8. Stores the permuted int8 block, the scale and
-// the four lane sums of the int8 values.
+// d = amax / 127, q = nearest-even(x * (1 / d)) saturated to int8. Stores the permuted int8 block, the scale and,
+// per lane, MK_MAGIC - 8 x (sum of the lane's int8 values): the accumulator start of the lane's Q4_0 block dot
+// (the -8 nibble offset and the float-conversion constant folded in).
 __device__ __forceinline__ void quant_block_warp(float v, int lane, int8_t* q, float* d, int4* s) {
   const float amax = warp_max(fabsf(v));
   const float dd = __fdiv_rn(amax, 127.0f);
@@ -75,14 +83,52 @@ __device__ __forceinline__ void quant_block_warp(float v, int lane, int8_t* q, f
   int qi = __float2int_rn(__fmul_rn(v, id));
   qi = max(-128, min(127, qi));
   q[(lane & 16) | invperm16(lane & 15)] = (int8_t)qi;
-  const int l = (lane & 7) >> 1;
-  const int s0 = __reduce_add_sync(0xffffffffu, l == 0 ? qi : 0);
-  const int s1 = __reduce_add_sync(0xffffffffu, l == 1 ? qi : 0);
-  const int s2 = __reduce_add_sync(0xffffffffu, l == 2 ? qi : 0);
-  const int s3 = __reduce_add_sync(0xffffffffu, l == 3 ? qi : 0);
+  // lane l of the dot owns elements {2l, 2l+1, 8+2l, 9+2l} of each half: after the three butterflies below, lane
+  // 2l holds the sum over those eight elements
+  int t = qi + __shfl_xor_sync(0xffffffffu, qi, 1);
+  t += __shfl_xor_sync(0xffffffffu, t, 8);
+  t += __shfl_xor_sync(0xffffffffu, t, 16);
+  const int s1 = __shfl_sync(0xffffffffu, t, 2), s2 = __shfl_sync(0xffffffffu, t, 4),
+            s3 = __shfl_sync(0xffffffffu, t, 6);
   if (lane == 0) {
     *d = dd;
-    *s = make_int4(s0, s1, s2, s3);
+    *s = make_int4(MK_MAGIC - 8 * t, MK_MAGIC - 8 * s1, MK_MAGIC - 8 * s2, MK_MAGIC - 8 * s3);
+  }
+}
+
+// Two blocks at once (v0 -> q0/d0/s0, v1 -> q1/d1/s1): the same arithmetic as quant_block_warp, written
+// interleaved so the shuffle and division latencies of the two blocks overlap.
+__device__ __forceinline__ void quant_block_warp2(float v0, float v1, int lane, int8_t* q0, float* d0, int4* s0,
+                                                  int8_t* q1, float* d1, int4* s1) {
+  float a0 = fabsf(v0), a1 = fabsf(v1);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const float b0 = __shfl_xor_sync(0xffffffffu, a0, o), b1 = __shfl_xor_sync(0xffffffffu, a1, o);
+    a0 = fmaxf(a0, b0);
+    a1 = fmaxf(a1, b1);
+  }
+  const float dd0 = __fdiv_rn(a0, 127.0f), dd1 = __fdiv_rn(a1, 127.0f);
+  const float id0 = dd0 != 0.0f ? __fdiv_rn(1.0f, dd0) : 0.0f, id1 = dd1 != 0.0f ? __fdiv_rn(1.0f, dd1) : 0.0f;
+  const int i0 = max(-128, min(127, __float2int_rn(__fmul_rn(v0, id0))));
+  const int i1 = max(-128, min(127, __float2int_rn(__fmul_rn(v1, id1))));
+  const int pos = (lane & 16) | invperm16(lane & 15);
+  q0[pos] = (int8_t)i0;
+  q1[pos] = (int8_t)i1;
+  int t0 = i0 + __shfl_xor_sync(0xffffffffu, i0, 1), t1 = i1 + __shfl_xor_sync(0xffffffffu, i1, 1);
+  t0 += __shfl_xor_sync(0xffffffffu, t0, 8);
+  t1 += __shfl_xor_sync(0xffffffffu, t1, 8);
+  t0 += __shfl_xor_sync(0xffffffffu, t0, 16);
+  t1 += __shfl_xor_sync(0xffffffffu, t1, 16);
+  // lane 0 gathers the lane sums held by lanes 0, 2, 4, 6 (see quant_block_warp)
+  const int u1 = __shfl_sync(0xffffffffu, t0, 2), u2 = __shfl_sync(0xffffffffu, t0, 4),
+            u3 = __shfl_sync(0xffffffffu, t0, 6);
+  const int w1 = __shfl_sync(0xffffffffu, t1, 2), w2 = __shfl_sync(0xffffffffu, t1, 4),
+            w3 = __shfl_sync(0xffffffffu, t1, 6);
+  if (lane == 0) {
+    *d0 = dd0;
+    *d1 = dd1;
+    *s0 = make_int4(MK_MAGIC - 8 * t0, MK_MAGIC - 8 * u1, MK_MAGIC - 8 * u2, MK_MAGIC - 8 * u3);
+    *s1 = make_int4(MK_MAGIC - 8 * t1, MK_MAGIC - 8 * w1, MK_MAGIC - 8 * w2, MK_MAGIC - 8 * w3);
   }
 }
 
@@ -172,10 +218,11 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {  // weights are rea
   return v;
 }
 
-// Lane l of a Q4_0 block dot: sum over its 8 elements of (q - 8) * x = dp4a(low nibbles, x0 word l) +
-// dp4a(high nibbles, x1 word l) - 8 * (sum of those 8 x). Nibbles 0..15 equal their signed-byte values.
-__device__ __forceinline__ int q4_lane(uint32_t w, int x0, int x1, int xsum) {
-  return __dp4a((int)(w & 0x0f0f0f0fu), x0, __dp4a((int)((w >> 4) & 0x0f0f0f0fu), x1, 0)) - 8 * xsum;
+// Lane l of a Q4_0 block dot as a float: sum over its 8 elements of (q - 8) * x = dp4a(low nibbles, x0 word l)
+// + dp4a(high nibbles, x1 word l) - 8 * (sum of those 8 x); xsn (from the quantizer) starts the accumulator with
+// that last term plus MK_MAGIC. Nibbles 0..15 equal their signed-byte values, so signed dp4a applies.
+__device__ __forceinline__ float q4_lane(uint32_t w, int x0, int x1, int xsn) {
+  return magic_to_float(__dp4a((int)(w & 0x0f0f0f0fu), x0, __dp4a((int)((w >> 4) & 0x0f0f0f0fu), x1, xsn)));
 }
 
 // y[m][n] (op)= sum over blocks of the reference's lane arithmetic (matmul_q4 / dot_q8_q8, kernels.c:121-273).
@@ -209,7 +256,7 @@ __global__ void __launch_bounds__(256) k_matvec(const uint8_t* __restrict__ qs, 
         const int4* xp = reinterpret_cast<const int4*>(xq + (size_t)m * K + b * 32);
         const int4 x0 = __ldg(xp), x1 = __ldg(xp + 1);
         const float sc = __fmul_rn(dw, __ldg(xd + (size_t)m * nb + b));
-        int p0, p1, p2, p3;
+        float p0, p1, p2, p3;
         if (WT == WQ4) {
           const int4 s = __ldg(xs + (size_t)m * nb + b);
           p0 = q4_lane(w0.x, x0.x, x1.x, s.x);
@@ -217,13 +264,13 @@ __global__ void __launch_bounds__(256) k_matvec(const uint8_t* __restrict__ qs, 
           p2 = q4_lane(w0.z, x0.z, x1.z, s.z);
           p3 = q4_lane(w0.w, x0.w, x1.w, s.w);
         } else {
-          p0 = __dp4a((int)w0.x, x0.x, __dp4a((int)w1.x, x1.x, 0));
-          p1 = __dp4a((int)w0.y, x0.y, __dp4a((int)w1.y, x1.y, 0));
-          p2 = __dp4a((int)w0.z, x0.z, __dp4a((int)w1.z, x1.z, 0));
-          p3 = __dp4a((int)w0.w, x0.w, __dp4a((int)w1.w, x1.w, 0));
+          p0 = magic_to_float(__dp4a((int)w0.x, x0.x, __dp4a((int)w1.x, x1.x, MK_MAGIC)));
+          p1 = magic_to_float(__dp4a((int)w0.y, x0.y, __dp4a((int)w1.y, x1.y, MK_MAGIC)));
+          p2 = magic_to_float(__dp4a((int)w0.z, x0.z, __dp4a((int)w1.z, x1.z, MK_MAGIC)));
+          p3 = magic_to_float(__dp4a((int)w0.w, x0.w, __dp4a((int)w1.w, x1.w, MK_MAGIC)));
         }
-        prod[((size_t)m * nb + b) * ROWS + r] = make_float4(__fmul_rn((float)p0, sc), __fmul_rn((float)p1, sc),
-                                                            __fmul_rn((float)p2, sc), __fmul_rn((float)p3, sc));
+        prod[((size_t)m * nb + b) * ROWS + r] = make_float4(__fmul_rn(p0, sc), __fmul_rn(p1, sc),
+                                                            __fmul_rn(p2, sc), __fmul_rn(p3, sc));
       }
     }
   }

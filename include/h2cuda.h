@@ -97,6 +97,24 @@ int h2c_forward(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t p
 int h2c_generate(h2c_engine* e, int seq, int32_t first_id, int32_t pos, int32_t steps, int32_t* out_tokens,
                  float* device_ms);
 
+/* Decode-step implementations. AUTO (default) uses the persistent kernel when the model fits it (one cooperative
+ * launch runs every layer of one or more tokens; weights stream into shared memory ahead of use) and otherwise
+ * the CUDA graph of per-operation kernels. Both give bit-identical results. */
+#define H2C_DECODE_AUTO 0
+#define H2C_DECODE_GRAPH 1
+#define H2C_DECODE_PERSISTENT 2
+/* Select the decode path; H2C_DECODE_PERSISTENT fails with H2C_ERR_INVALID if the model does not fit it. */
+int h2c_set_decode_mode(h2c_engine* e, int mode);
+/* The path single-token steps will take: H2C_DECODE_GRAPH or H2C_DECODE_PERSISTENT (< 0 on error). */
+int h2c_decode_path(h2c_engine* e);
+
+/* Profiling aid for the persistent decode kernel: runs h2c_generate's device-side greedy decode once with
+ * %globaltimer stamps (nanoseconds) taken at the stage boundaries of CTA 0 (a head CTA) and of the last CTA.
+ * out receives 2 * steps * (layers + 1) * 16 entries: [cta 0 | last cta][step][layer or lm_head][point], 0 where a
+ * point does not apply. The per-operation profile of the reference (profile_start/get, kernels.c:481-483) for
+ * this path. Allocates a temporary device buffer. */
+int h2c_trace_decode(h2c_engine* e, int seq, int32_t first_id, int32_t pos, int32_t steps, uint64_t* out, int64_t n);
+
 /* Number of kernels one decode step launches (the kernel nodes of the decode-step CUDA graph); < 0 on error. */
 int h2c_decode_kernels(h2c_engine* e);
 

@@ -39,9 +39,19 @@ def top2_gap(lg):
     return float((s[-1] - s[-2]) / (lg.max() - lg.min()))
 
 
-def teacher_forced(model, n_prompt, steps, chunk, ctx=96, seed=0):
+def open_mode(path, mode, **kw):
+    be = backend.open_model(path, **kw)
+    try:
+        be.set_decode_mode(mode)
+    except _lib.H2CError as ex:
+        be.destroy()
+        pytest.skip(f"{mode} decode unavailable for this model: {ex}")
+    return be
+
+
+def teacher_forced(model, n_prompt, steps, chunk, ctx=96, seed=0, mode="auto"):
     path = synth.ensure(model)
-    be = backend.open_model(path, ctx=ctx, prefill_chunk=chunk)
+    be = open_mode(path, mode, ctx=ctx, prefill_chunk=chunk)
     ref = O.open_model("oracle", path, ctx=ctx, mt=chunk, threads=4)
     V = be.cfg["vocab"]
     prompt = synth.prompt_ids(V, n_prompt, seed=100 + seed)
@@ -66,9 +76,75 @@ def teacher_forced(model, n_prompt, steps, chunk, ctx=96, seed=0):
     return worst
 
 
+@pytest.mark.parametrize("mode", ["graph", "persistent"])
 @pytest.mark.parametrize("model,chunk", [("tiny", 4), ("small", 16), ("gqa7", 3), ("small-q8", 8), ("hd128", 5)])
-def test_teacher_forced_logits(model, chunk):
-    teacher_forced(model, n_prompt=11, steps=8, chunk=chunk)
+def test_teacher_forced_logits(model, chunk, mode):
+    teacher_forced(model, n_prompt=11, steps=8, chunk=chunk, mode=mode)
+
+
+@pytest.mark.parametrize("mode", ["graph", "persistent"])
+@pytest.mark.parametrize("model", ["tiny", "gqa7", "hd128"])
+def test_device_generate_matches_stepwise_and_oracle(model, mode):
+    """h2c_generate (next token never leaves the GPU) = per-step forward = the oracle's greedy tokens."""
+    path = synth.ensure(model)
+    be = open_mode(path, mode, ctx=64, prefill_chunk=8)
+    V = be.cfg["vocab"]
+    prompt = synth.prompt_ids(V, 9, seed=77)
+    first = be.forward(prompt, 0)
+    dev, ms = be.generate(first, len(prompt), 20)
+    assert ms > 0
+    lg_dev = None
+    step = []
+    nxt = first
+    for i in range(20):
+        nxt = be.forward([nxt], len(prompt) + i, want_logits=(i == 19))
+        step.append(nxt)
+    ref = O.open_model("oracle", path, ctx=64, mt=8, threads=4)
+    r = ref.forward(prompt, 0)
+    want, nxt = [], r["next"]
+    assert nxt == first
+    for i in range(20):
+        r = ref.forward([nxt], len(prompt) + i, want_logits=(i == 19))
+        nxt = r["next"]
+        want.append(nxt)
+    assert list(dev) == step == want
+    assert np.array_equal(bits(be.read_logits()), bits(r["logits"]))
+    be.destroy()
+
+
+def test_full_size_qwen2_0_5b_bit_exact():
+    """The benchmark model (24 layers, hidden 896, vocab 151936, tied Q4_0 lm_head): 32-token prompt, then
+    teacher-forced steps and device-side greedy decode, bit-identical to the oracle in both decode paths."""
+    path = synth.ensure("qwen2-0.5b")
+    ref = O.open_model("oracle", path, ctx=128, mt=16, threads=8)
+    prompt = synth.prompt_ids(151936, 32, seed=1)
+    forced = synth.prompt_ids(151936, 6, seed=2)
+    r = ref.forward(prompt, 0, want_logits=True)
+    want = [(r["next"], r["logits"])]
+    pos = 32
+    for t in forced:
+        r = ref.forward([int(t)], pos, want_logits=True)
+        want.append((r["next"], r["logits"]))
+        pos += 1
+    greedy = []
+    nxt = want[-1][0]
+    for i in range(8):
+        nxt = ref.forward([nxt], pos + i)["next"]
+        greedy.append(nxt)
+    for mode in ("graph", "persistent"):
+        be = open_mode(path, mode, ctx=128, prefill_chunk=16)
+        got = [be.forward(prompt, 0, want_logits=True)]
+        lgs = [be.read_logits()]
+        p2 = 32
+        for t in forced:
+            got.append(be.forward([int(t)], p2, want_logits=True))
+            lgs.append(be.read_logits())
+            p2 += 1
+        for s_, ((n_ref, l_ref), n_got, l_got) in enumerate(zip(want, got, lgs)):
+            assert n_got == n_ref and np.array_equal(bits(l_got), bits(l_ref)), f"{mode} step {s_}"
+        dev, _ = be.generate(got[-1], p2, 8)
+        assert list(dev) == greedy, mode
+        be.destroy()
 
 
 def test_golden_fixtures_through_cuda():
