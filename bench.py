@@ -43,6 +43,11 @@ WEIGHT_BYTES = 201_277_440 + 286_208 + 76_575_744
 KV_BYTES_PER_POS = 24 * 2 * 64 * 4 * 2
 
 
+# DRAM bytes (read + write) of one decode step of k_decode_persistent, from the ncu capture of a 4-step launch at
+# positions 32..35 (profiles/k_decode_persistent_qwen2-0.5b_full.md): 1,129,449,584 B / 4
+NCU_TRAFFIC_PER_STEP = 282_362_396
+
+
 def step_bytes(pos: int) -> int:
     """Bytes one decode step at position pos must move (T = pos + 1 cached positions read, one written)."""
     return WEIGHT_BYTES + KV_BYTES_PER_POS * (pos + 1) + KV_BYTES_PER_POS + 504
@@ -223,20 +228,22 @@ def main():
     first = be.forward(prompt, 0)
 
     def device_rounds(n):
-        ms, k = 0.0, 0
+        """n decode steps as rounds of the 64-token decode; returns (device ms, generate calls)."""
+        ms, k, calls = 0.0, 0, 0
         while k < n:
             s = min(ROUND, n - k)
             _, t = be.generate(first, PROMPT, s)
             ms += t
             k += s
-        return ms
+            calls += 1
+        return ms, calls
 
     # ---- value: device-chained decode, device time
     device_rounds(warm)
     clocks = Clocks(local)
     barrier()
     clocks.start()
-    ms = device_rounds(steps)
+    ms, calls = device_rounds(steps)
     barrier()
     ck = clocks.stop()
     ms = max_over_ranks(ms)
@@ -267,6 +274,15 @@ def main():
     peak, peak_kind = measured_peaks()
     achieved = bytes_step / (ms / steps / 1e3) / 1e9
     kernels = be.decode_kernels()
+    persistent = be.decode_path == "persistent"
+    if persistent:  # one cooperative launch runs a whole generate call (up to 64 device-chained steps)
+        kdesc = "k_decode_persistent (one cooperative launch per 64-step round, 1 CTA per SM)"
+        launches = calls
+        d2h = 8 * 4  # next id + status words
+    else:
+        kdesc = f"decode step ({kernels} kernels in one CUDA graph)"
+        launches = kernels * steps
+        d2h = 4
 
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
@@ -285,12 +301,14 @@ def main():
                                    "rounds of 64 (positions 32..95)",
                        "global_batch": world, "seq_len": PROMPT + ROUND, "parallelism": f"sessions x{world}",
                        "l2": "no flush: 278 MB of weights per step > 126 MB L2"},
-            "roofline": {"bound": "hbm", "kernel": f"decode step ({kernels} kernels in one CUDA graph)",
+            "roofline": {"bound": "hbm", "kernel": kdesc,
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                         "bytes_per_step": bytes_step, "traffic": None},
-            "e2e": {"value": round(e2e, 2), "unit": UNIT, "h2d_bytes_per_step": 4 * 5, "d2h_bytes_per_step": 4},
-            "gpu_launches": kernels * steps,
+                         "bytes_per_step": bytes_step,
+                         "traffic": NCU_TRAFFIC_PER_STEP if persistent else None,
+                         "traffic_note": "DRAM read+write bytes per decode step, ncu capture of k_decode_persistent"},
+            "e2e": {"value": round(e2e, 2), "unit": UNIT, "h2d_bytes_per_step": 4 * 5, "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches,
             "clocks": ck,
             "cpu_baseline": cpu,
         }
