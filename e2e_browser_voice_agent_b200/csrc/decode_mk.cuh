@@ -83,6 +83,7 @@ struct MkParams {
   unsigned long long* attw;       // [D] tagged att
   unsigned long long* actw;       // [F/32][MK_ACT_WORDS] tagged act blocks
   unsigned long long* lmw;        // [ncta][2] tagged lm_head partials (value, index)
+  unsigned long long* kvdone;     // [ncta] epoch of the last layer whose KV-cache rows this CTA has released
   int* err;                       // [4]: code, cta, stage, abort flag
   int32_t* prm;                   // pass parameters (P_POS0, P_M, P_SEQ, P_IDS)
   int32_t* toklog;                // [seqs][ctx + 1]
@@ -210,18 +211,31 @@ __device__ __forceinline__ uint32_t wait_word(const unsigned long long* w, uint3
 
 // ---------------------------------------------------------------- shared building blocks
 
-// s = ((s + p[0]) + p[stride]) + ... over n terms in order, with the shared-memory loads issued 16 at a time ahead of
-// the dependent adds (a chain step then costs one add latency, not a load latency).
+// s = ((s + p[0]) + p[stride]) + ... over n terms in order. The shared-memory loads of the next 16 terms issue
+// before the adds of the current 16, so a step costs one add latency, not a load latency.
 __device__ __forceinline__ float chain_sum(float s, const float* p, int stride, int n) {
-  int k = 0;
-  for (; k + 16 <= n; k += 16) {
-    float v[16];
+  float a[16], nx[16];
+  const int n16 = n & ~15;
+  if (n16) {
 #pragma unroll
-    for (int u = 0; u < 16; u++) v[u] = p[(size_t)(k + u) * stride];
+    for (int u = 0; u < 16; u++) a[u] = p[u * stride];
+    for (int k = 16; k < n16; k += 16) {
 #pragma unroll
-    for (int u = 0; u < 16; u++) s = __fadd_rn(s, v[u]);
+      for (int u = 0; u < 16; u++) nx[u] = p[(k + u) * stride];
+#pragma unroll
+      for (int u = 0; u < 16; u++) s = __fadd_rn(s, a[u]);
+#pragma unroll
+      for (int u = 0; u < 16; u++) a[u] = nx[u];
+    }
+#pragma unroll
+    for (int u = 0; u < 16; u++) s = __fadd_rn(s, a[u]);
   }
-  for (; k < n; k++) s = __fadd_rn(s, p[(size_t)k * stride]);
+  const int rem = n - n16;
+#pragma unroll
+  for (int u = 0; u < 16; u++) a[u] = u < rem ? p[(n16 + u) * stride] : 0.f;
+#pragma unroll
+  for (int u = 0; u < 16; u++)
+    if (u < rem) s = __fadd_rn(s, a[u]);
   return s;
 }
 
@@ -243,35 +257,23 @@ __device__ __forceinline__ void mk_quant_blocks(int nblk, Fn f, int8_t* xq, floa
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (int b = warp; b < nblk; b += 2 * MK_WARPS) {
     const int b2 = b + MK_WARPS;
-    if (b2 < nblk)
-      quant_block_warp2(f(b * 32 + lane), f(b2 * 32 + lane), lane, xq + b * 32, xd + b, xs + b, xq + b2 * 32, xd + b2,
-                        xs + b2);
-    else
-      quant_block_warp(f(b * 32 + lane), lane, xq + b * 32, xd + b, xs + b);
+    const float v0 = f(b * 32 + lane);
+    const float v1 = b2 < nblk ? f(b2 * 32 + lane) : 0.f;
+    quant_block_redux(v0, lane, xq + b * 32, xd + b, xs + b);
+    if (b2 < nblk) quant_block_redux(v1, lane, xq + b2 * 32, xd + b2, xs + b2);
   }
   compute_bar();
 }
 
 // RMSNorm of xf[0..D) (shared) into int8 blocks xq/xd/xs (shared), the reference's lane order (kernels.c:80-114):
-// thread l < 4 sums x[4k+l]^2 over k in order; the products are independent of the chain and issue ahead of it.
+// the squares are formed by all threads into sq (shared, D floats), then thread l < 4 adds sq[4k + l] over k in
+// order and ((l0 + l1) + l2) + l3 combines the four chains.
 __device__ void mk_norm_quant(const float* xf, const float* w, int D, float eps, int8_t* xq, float* xd, int4* xs,
-                              float* red) {
+                              float* red, float* sq) {
   const int tid = threadIdx.x;
-  if (tid < 4) {  // loads and squares issue 16 steps ahead of the dependent adds
-    float s = 0.f;
-    int i = tid;
-    for (; i + 64 <= D; i += 64) {
-      float v[16];
-#pragma unroll
-      for (int u = 0; u < 16; u++) v[u] = xf[i + 4 * u];
-#pragma unroll
-      for (int u = 0; u < 16; u++) v[u] = __fmul_rn(v[u], v[u]);
-#pragma unroll
-      for (int u = 0; u < 16; u++) s = __fadd_rn(s, v[u]);
-    }
-    for (; i < D; i += 4) s = __fadd_rn(s, __fmul_rn(xf[i], xf[i]));
-    red[tid] = s;
-  }
+  for (int i = tid; i < D; i += MK_NT) sq[i] = __fmul_rn(xf[i], xf[i]);
+  compute_bar();
+  if (tid < 4) red[tid] = chain_sum(0.f, sq + tid, 4, D / 4);
   compute_bar();
   const float ss = __fadd_rn(__fadd_rn(__fadd_rn(red[0], red[1]), red[2]), red[3]);
   const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), eps)));
@@ -437,6 +439,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
   };
 
   const TileMap map_d = tile_map(nbd), map_f = tile_map(nbf);
+  float* sqs = reinterpret_cast<float*>(prod);  // norm squares (prod is free between tiles)
   const bool head = cta < H;
   const int nh = ncta - H;                  // CTAs that own O / down rows
   const int j = cta - H;
@@ -445,6 +448,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
   const int npair = p.QKV / 2, half = HD / 2;
   const int pr_lo = (int)((long long)cta * npair / ncta), pr_hi = (int)((long long)(cta + 1) * npair / ncta);
   const int G = H / KVH, kh = head ? cta / G : 0;
+  const int kv_pair_lo = H * half, kv_pair_hi = (H + 2 * KVH) * half;  // QKV row pairs of the k and v heads
+  const bool my_kv = pr_lo < kv_pair_hi && pr_hi > kv_pair_lo;
   const int seq = p.prm[P_SEQ];
   int pos = p.prm[P_POS0];
   int tok = p.prm[P_IDS];
@@ -490,6 +495,16 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
           const int pidx = pr_lo + (tid >> 1), row = (pidx / half) * HD + pidx % half + (tid & 1) * half;
           cp_async4(bsm + tid, p.bqkv + (size_t)l * p.QKV + row);
         }
+        if (head && E > (uint32_t)L) {
+          // acquire the KV-cache rows that the k/v owners released at this layer of earlier steps of this launch
+          // (rows of earlier launches are ordered by the launch boundary)
+          if (tid < ncta) {
+            const int c_lo = (int)((long long)tid * npair / ncta), c_hi = (int)((long long)(tid + 1) * npair / ncta);
+            if (c_lo < kv_pair_hi && c_hi > kv_pair_lo) wait_word<true>(p.kvdone + tid, E - L, p, 10 * l + 9, &abort_s);
+          }
+          compute_bar();
+          if (abort_s) goto out;
+        }
         if (staged) {  // a head CTA's earlier cache positions are final: stage them now
           const float* kb = p.kc + cbase;
           const float* vb = p.vc + cbase;
@@ -507,7 +522,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
       cp_async_wait_all();
       compute_bar();
       MK_TRACE(trow, 1);
-      mk_norm_quant(xf, nw1, D, p.eps, xq, xd, xs, red);
+      mk_norm_quant(xf, nw1, D, p.eps, xq, xd, xs, red, sqs);
       MK_TRACE(trow, 2);
       {
         const int R = 2 * (pr_hi - pr_lo);
@@ -531,19 +546,26 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
               const size_t base = ((((size_t)seq * L + l) * KVH + kk) * p.ctx + pos) * HD;
               p.kc[base + i] = r0;
               p.kc[base + i + half] = r1;
-              st_release64(p.kvw + kk * HD + i, __float_as_uint(r0), E);
-              st_release64(p.kvw + kk * HD + i + half, __float_as_uint(r1), E);
+              st_relaxed64(p.kvw + kk * HD + i, __float_as_uint(r0), E);
+              st_relaxed64(p.kvw + kk * HD + i + half, __float_as_uint(r1), E);
             }
           } else {  // v head: appended as is
             const int kk = hh - H - KVH;
             const size_t base = ((((size_t)seq * L + l) * KVH + kk) * p.ctx + pos) * HD;
             p.vc[base + i] = a;
             p.vc[base + i + half] = b;
-            st_release64(p.kvw + (KVH + kk) * HD + i, __float_as_uint(a), E);
-            st_release64(p.kvw + (KVH + kk) * HD + i + half, __float_as_uint(b), E);
+            st_relaxed64(p.kvw + (KVH + kk) * HD + i, __float_as_uint(a), E);
+            st_relaxed64(p.kvw + (KVH + kk) * HD + i + half, __float_as_uint(b), E);
           }
         }
         compute_bar();  // outv is reused below
+        // Release of this layer's KV-cache rows (read by the head CTAs from the next step on): one gpu-scope fence
+        // after the barrier that orders the CTA's cache stores, then the CTA's kvdone word. Off the critical path:
+        // the warp that fences next waits for other CTAs' results anyway.
+        if (my_kv && tid == 0) {
+          __threadfence();
+          st_relaxed64(p.kvdone + cta, E, E);
+        }
       }
       MK_TRACE(trow, 3);
 
@@ -647,7 +669,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
       // ---- D (all CTAs): norm + gate/up rows of whole act blocks, silu * up, quantize (kernels.c:385-397)
       if (!read_vec(p.xw, 2 * E, 10 * l + 3)) goto out;
       MK_TRACE(trow, 10);
-      mk_norm_quant(xf, nw2, D, p.eps, xq, xd, xs, red);
+      mk_norm_quant(xf, nw2, D, p.eps, xq, xd, xs, red, sqs);
       for (int ab = cta; ab < nbf; ab += ncta) {
         const uint8_t* t = next_tile(4, 64, nbd);
         if (!t) goto out;
@@ -656,7 +678,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
         if (tid < 32) {
           const float gt = outv[tid], up = outv[32 + tid];
           const float v = __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, fast_exp_ref(-gt))), up);
-          quant_block_warp(v, tid, actq, actd, acts);
+          quant_block_redux(v, tid, actq, actd, acts);
           __syncwarp();
           unsigned long long* dst = p.actw + (size_t)ab * MK_ACT_WORDS;
           if (tid < 8) st_relaxed64(dst + tid, reinterpret_cast<const uint32_t*>(actq)[tid], E);
@@ -697,7 +719,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
     MK_TRACE(lrow, 0);
     if (!read_vec(p.xw, 2 * E + 1, 9999)) goto out;
     MK_TRACE(lrow, 1);
-    mk_norm_quant(xf, onw, D, p.eps, xq, xd, xs, red);
+    mk_norm_quant(xf, onw, D, p.eps, xq, xd, xs, red, sqs);
     MK_TRACE(lrow, 2);
     {
       float bv = -INFINITY;

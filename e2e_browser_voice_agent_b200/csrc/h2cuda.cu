@@ -85,8 +85,8 @@ struct h2c_engine {
   MkTile* mk_tiles = nullptr;
   float *mk_attn_norm = nullptr, *mk_ffn_norm = nullptr, *mk_bqkv = nullptr;
   unsigned long long *mk_xw = nullptr, *mk_qw = nullptr, *mk_kvw = nullptr, *mk_attw = nullptr, *mk_actw = nullptr,
-                     *mk_lmw = nullptr;
-  size_t mk_tagged_words = 0;  // mk_xw .. mk_lmw are one allocation of this many words
+                     *mk_lmw = nullptr, *mk_kvdone = nullptr;
+  size_t mk_tagged_words = 0;  // mk_xw .. mk_kvdone are one allocation of this many words
   int32_t* mk_io = nullptr;   // device: [0] next token, [4..7] error words
   int* mk_tile_count = nullptr;
   int32_t* mk_io_h = nullptr; // pinned
@@ -541,7 +541,7 @@ int mk_build(h2c_engine* e) {
       off += b;
     }
   }
-  const size_t words = (size_t)D * 3 + (size_t)2 * KVH * HD + (size_t)nbf * MK_ACT_WORDS + (size_t)ncta * 2;
+  const size_t words = (size_t)D * 3 + (size_t)2 * KVH * HD + (size_t)nbf * MK_ACT_WORDS + (size_t)ncta * 3;
   unsigned long long* tagged = nullptr;
   if ((r = dalloc_t(e, &e->mk_stream, total)) || (r = dalloc_t(e, &e->mk_tiles, table.size())) ||
       (r = dalloc_t(e, &e->mk_attn_norm, (size_t)NL * D)) || (r = dalloc_t(e, &e->mk_ffn_norm, (size_t)NL * D)) ||
@@ -554,6 +554,7 @@ int mk_build(h2c_engine* e) {
   e->mk_kvw = tagged + 3 * D;
   e->mk_actw = e->mk_kvw + (size_t)2 * KVH * HD;
   e->mk_lmw = e->mk_actw + (size_t)nbf * MK_ACT_WORDS;
+  e->mk_kvdone = e->mk_lmw + (size_t)ncta * 2;
   e->mk_tagged_words = words;
   CUDA_TRY(e, cudaMallocHost(&e->mk_io_h, 8 * sizeof(int32_t)));
   CUDA_TRY(e, cudaMemcpy(e->mk_tile_count, counts.data(), counts.size() * sizeof(int), cudaMemcpyHostToDevice));
@@ -589,6 +590,7 @@ int mk_launch(h2c_engine* e, int steps, unsigned long long* trace = nullptr) {
   p.attn_norm = e->mk_attn_norm; p.ffn_norm = e->mk_ffn_norm; p.bqkv = e->mk_bqkv; p.out_norm = e->out_norm;
   p.rope = e->rope; p.embd_qs = e->embd.qs; p.embd_d = e->embd.d; p.kc = e->kc; p.vc = e->vc; p.logits = e->logits;
   p.xw = e->mk_xw; p.qw = e->mk_qw; p.kvw = e->mk_kvw; p.attw = e->mk_attw; p.actw = e->mk_actw; p.lmw = e->mk_lmw;
+  p.kvdone = e->mk_kvdone;
   p.err = e->mk_io + 4; p.prm = e->prm; p.toklog = e->toklog; p.next = e->mk_io; p.steps = steps;
   p.timeout_ns = 2000000000ull;
   p.trace = trace;

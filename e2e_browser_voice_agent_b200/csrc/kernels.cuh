@@ -96,6 +96,27 @@ __device__ __forceinline__ void quant_block_warp(float v, int lane, int8_t* q, f
   }
 }
 
+// The same quantization with warp reductions in hardware (redux.sync): amax is the integer max of the |x| bit
+// patterns (order-preserving for non-negative floats, and a max is exact in any order); the four lane sums are two
+// packed add-reductions of the biased values q + 128 (eight of them per lane sum fit 16 bits), lanes 0 and 1 in one
+// word, 2 and 3 in the other. Bit-identical to quant_block_warp.
+__device__ __forceinline__ void quant_block_redux(float v, int lane, int8_t* q, float* d, int4* s) {
+  const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v))));
+  const float dd = __fdiv_rn(amax, 127.0f);
+  const float id = dd != 0.0f ? __fdiv_rn(1.0f, dd) : 0.0f;
+  const int qi = max(-128, min(127, __float2int_rn(__fmul_rn(v, id))));
+  q[(lane & 16) | invperm16(lane & 15)] = (int8_t)qi;
+  const int dl = (lane & 7) >> 1;  // the dot lane that owns this element
+  const unsigned bq = (unsigned)(qi + 128) << ((dl & 1) * 16);
+  const unsigned s01 = __reduce_add_sync(0xffffffffu, dl < 2 ? bq : 0u);
+  const unsigned s23 = __reduce_add_sync(0xffffffffu, dl < 2 ? 0u : bq);
+  if (lane == 0) {
+    *d = dd;
+    *s = make_int4(MK_MAGIC - 8 * ((int)(s01 & 0xffffu) - 1024), MK_MAGIC - 8 * ((int)(s01 >> 16) - 1024),
+                   MK_MAGIC - 8 * ((int)(s23 & 0xffffu) - 1024), MK_MAGIC - 8 * ((int)(s23 >> 16) - 1024));
+  }
+}
+
 // Two blocks at once (v0 -> q0/d0/s0, v1 -> q1/d1/s1): the same arithmetic as quant_block_warp, written
 // interleaved so the shuffle and division latencies of the two blocks overlap.
 __device__ __forceinline__ void quant_block_warp2(float v0, float v1, int lane, int8_t* q0, float* d0, int4* s0,
