@@ -154,9 +154,14 @@ class CudaBackend:
         return {_lib.DECODE_GRAPH: "graph", _lib.DECODE_PERSISTENT: "persistent"}[n]
 
     def trace_decode(self, first_id: int, pos: int, steps: int, seq: int = 0) -> np.ndarray:
-        """Stage timestamps (ns) of the persistent kernel: array [2 CTAs][steps][layers + 1][16]."""
+        """Stage timestamps (ns) of the persistent kernel: array [CTAs][steps][layers + 1][16]."""
         L = self.cfg["layers"]
-        out = np.zeros((2, steps, L + 1, 16), dtype=np.uint64)
+        n = self._L.h2c_decode_ctas(self._h)
+        if n < 0:
+            _lib.check(n, self._h)
+        if n == 0:
+            raise RuntimeError("this model takes the graph decode path (no persistent kernel to trace)")
+        out = np.zeros((n, steps, L + 1, 16), dtype=np.uint64)
         _lib.check(self._L.h2c_trace_decode(self._h, int(seq), int(first_id), int(pos), int(steps), out.ctypes.data,
                                             out.size), self._h)
         return out

@@ -38,14 +38,21 @@
 namespace h2 {
 
 constexpr int MK_SLOT = 32768;                   // bytes per ring slot (one tile)
-constexpr int MK_NSLOT = 3;                      // ring depth
+constexpr int MK_NSLOT = 4;                      // ring depth (two tiles in use, two in flight)
 constexpr int MK_MAX_TILES = 256;                // per-CTA tile table kept in shared memory
 constexpr int MK_WARPS = 16;                     // compute warps
 constexpr int MK_NT = MK_WARPS * 32;             // compute threads
-constexpr int MK_THREADS = MK_NT + 32;           // + one producer warp
+constexpr int MK_THREADS = MK_NT;                // 16 warps: the 128-register limit of a 512-thread block
 constexpr int MK_TILE_ROWS = 64;                 // rows per tile (lm_head, q/k/v)
 constexpr int MK_TRACE_PTS = 16;
 constexpr int MK_ACT_WORDS = 16;                 // tagged words per act block: 8 int8 quads, d, 4 lane sums
+#ifndef MK_ACT_COPIES
+#define MK_ACT_COPIES 8                          // act blocks are stored in this many copies; CTA c reads copy c % 8,
+#endif                                           // so no L2 line is polled by every CTA
+#ifndef MK_ACT_GROUP
+#define MK_ACT_GROUP 16                          // act blocks one warp polls together in the down stage
+#endif
+
 #ifndef MK_POLL_NS
 #define MK_POLL_NS 0                             // back-off between polls of a tagged word
 #endif
@@ -81,27 +88,91 @@ struct MkParams {
   unsigned long long* qw;         // [D] tagged q (after bias and RoPE)
   unsigned long long* kvw;        // [2 KVH HD] tagged k then v of the current position
   unsigned long long* attw;       // [D] tagged att
-  unsigned long long* actw;       // [F/32][MK_ACT_WORDS] tagged act blocks
+  unsigned long long* actw;       // [MK_ACT_COPIES][F/32][MK_ACT_WORDS] tagged act blocks
   unsigned long long* lmw;        // [ncta][2] tagged lm_head partials (value, index)
   unsigned long long* kvdone;     // [ncta] epoch of the last layer whose KV-cache rows this CTA has released
+  unsigned long long* rawact;     // [nsplit][32] tagged act values of the split blocks
+  int nsplit;                     // act blocks beyond one per CTA, computed in 4 pieces of 16 gate/up rows by the
+                                  // last 4 nsplit CTAs and quantized by the consumers (0: whole blocks only)
   int* err;                       // [4]: code, cta, stage, abort flag
   int32_t* prm;                   // pass parameters (P_POS0, P_M, P_SEQ, P_IDS)
   int32_t* toklog;                // [seqs][ctx + 1]
   int32_t* next;
   int steps;
   unsigned long long timeout_ns;
-  unsigned long long* trace;      // optional: [2][steps * (L + 1)][MK_TRACE_PTS] %globaltimer stamps of CTA 0
-                                  // and of the last CTA (profiling)
+  unsigned long long* trace;      // optional: [ncta][steps * (L + 1)][MK_TRACE_PTS] %globaltimer stamps
+                                  // (profiling)
 };
 
 // dynamic shared memory of k_decode_persistent without the K/V staging area (must match the carve-up below)
 __host__ __device__ inline size_t mk_smem_base(int D, int F, int HD, int ctx, int prod_items) {
   const int nbf = F / 32;
-  const int outn = 3 * HD > 64 ? 3 * HD : 64;
+  const int outn = 3 * HD > 128 ? 3 * HD : 128;
+  const int nbp = ((D / 32) + 3) & ~3;
   return (size_t)MK_NSLOT * MK_SLOT + (size_t)prod_items * 16 + (size_t)((F + 127) & ~127) +
-         (size_t)((nbf + 3) & ~3) * 4 + (size_t)nbf * 16 + (size_t)D * 4 + 64 * 4 + (size_t)outn * 4 + 32 * 4 + 64 +
-         (size_t)MK_MAX_TILES * 16 + (size_t)D * 4 * 3 + (size_t)64 * 4 + (size_t)HD * 4 +
+         (size_t)((nbf + 3) & ~3) * 4 + (size_t)nbf * 16 + (size_t)D * 4 + 64 * 4 + (size_t)outn * 4 + 32 * 4 + 128 +
+         (size_t)MK_MAX_TILES * 16 + (size_t)D * 4 * 3 + (size_t)64 * 4 + (size_t)HD * 4 + (size_t)nbp * 13 * 4 +
          (size_t)((ctx + 3) & ~3) * 4;
+}
+
+// ---------------------------------------------------------------- chain tiles
+// QKV, O, gate/up and lm_head tiles use the "chain" layout: for R rows of nb blocks (nbp = nb rounded up to 4),
+// values [R][4 lanes][nbp] as 32-bit words (word (r, l, b) = the 4 bytes wasm lane l of block b consumes), then fp16
+// scales [R][nbp]; padding blocks are zero. Thread (r, l) reads its lane's words of 4 blocks with one 16-byte load
+// and keeps the lane's running sum in a register. The int8 input is in the matching per-lane layout (MkX).
+__host__ __device__ constexpr int mk_nbp(int nb) { return (nb + 3) & ~3; }
+
+struct MkX {       // int8 input of a chain tile, per lane: x0[l][b] = word l of block b's low half, x1 = high half,
+  int* x0;         // xs[l][b] = MK_MAGIC - 8 x (sum of lane l's values), dx[b] = scale; [4][nbp] ints, dx [nbp];
+  int* x1;         // padding blocks hold zeros, which make every padding product -0 (exact no-op in the sums)
+  int* xs;
+  float* dx;
+};
+
+// thread (r, l) of a chain tile: acc_l = (((0 + f32(p_0) * (dw_0 * dx_0)) + ...) over the blocks in order
+// (dot_q4_q8, kernels.c:121-139)
+__device__ __forceinline__ float mk_lane_chain(const uint8_t* tile, int R, int nbp, int r, int l, const MkX& x) {
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(tile) + (size_t)(r * 4 + l) * nbp;
+  const __half* d = reinterpret_cast<const __half*>(tile + (size_t)R * nbp * 16) + (size_t)r * nbp;
+  const int *x0 = x.x0 + l * nbp, *x1 = x.x1 + l * nbp, *xs = x.xs + l * nbp;
+  float acc = 0.f;
+  for (int b = 0; b < nbp; b += 4) {
+    const uint4 ww = *reinterpret_cast<const uint4*>(w + b);
+    const uint2 dd = *reinterpret_cast<const uint2*>(d + b);
+    const int4 a0 = *reinterpret_cast<const int4*>(x0 + b), a1 = *reinterpret_cast<const int4*>(x1 + b);
+    const int4 as = *reinterpret_cast<const int4*>(xs + b);
+    const float4 dx = *reinterpret_cast<const float4*>(x.dx + b);
+    const __half2 d01 = *reinterpret_cast<const __half2*>(&dd.x), d23 = *reinterpret_cast<const __half2*>(&dd.y);
+    const float p0 = q4_lane(ww.x, a0.x, a1.x, as.x), p1 = q4_lane(ww.y, a0.y, a1.y, as.y);
+    const float p2 = q4_lane(ww.z, a0.z, a1.z, as.z), p3 = q4_lane(ww.w, a0.w, a1.w, as.w);
+    acc = __fadd_rn(acc, __fmul_rn(p0, __fmul_rn(__low2float(d01), dx.x)));
+    acc = __fadd_rn(acc, __fmul_rn(p1, __fmul_rn(__high2float(d01), dx.y)));
+    acc = __fadd_rn(acc, __fmul_rn(p2, __fmul_rn(__low2float(d23), dx.z)));
+    acc = __fadd_rn(acc, __fmul_rn(p3, __fmul_rn(__high2float(d23), dx.w)));
+  }
+  return acc;
+}
+
+// quantize one 32-value block (one value per lane) into block b of a chain input: the arithmetic of
+// quant_block_redux, stored per lane
+__device__ __forceinline__ void mk_quant_chain(float v, int lane, int b, int nbp, const MkX& x) {
+  const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v))));
+  const float dd = __fdiv_rn(amax, 127.0f);
+  const float id = dd != 0.0f ? __fdiv_rn(1.0f, dd) : 0.0f;
+  const int qi = max(-128, min(127, __float2int_rn(__fmul_rn(v, id))));
+  const int pos = (lane & 16) | invperm16(lane & 15);  // byte of the permuted block (word pos / 4)
+  int8_t* dst = reinterpret_cast<int8_t*>(pos < 16 ? x.x0 : x.x1);
+  dst[((((pos & 15) >> 2) * nbp) + b) * 4 + (pos & 3)] = (int8_t)qi;
+  const int dl = (lane & 7) >> 1;
+  const unsigned bq = (unsigned)(qi + 128) << ((dl & 1) * 16);
+  const unsigned s01 = __reduce_add_sync(0xffffffffu, dl < 2 ? bq : 0u);
+  const unsigned s23 = __reduce_add_sync(0xffffffffu, dl < 2 ? 0u : bq);
+  if (lane < 4) {
+    const unsigned sw = lane < 2 ? s01 : s23;
+    const int t = (int)((lane & 1) ? (sw >> 16) : (sw & 0xffffu)) - 1024;
+    x.xs[lane * nbp + b] = MK_MAGIC - 8 * t;
+  }
+  if (lane == 0) x.dx[b] = dd;
 }
 
 // ---------------------------------------------------------------- PTX helpers
@@ -148,6 +219,13 @@ __device__ __forceinline__ unsigned long long ld_relaxed64(const unsigned long l
   unsigned long long v;
   asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
+}
+// four consecutive tagged words (32-byte aligned) in one request; each 64-bit element is read atomically
+__device__ __forceinline__ void ld_relaxed64x4(const unsigned long long* p, unsigned long long* v) {
+  asm volatile("ld.relaxed.gpu.global.v4.u64 {%0, %1, %2, %3}, [%4];"
+               : "=l"(v[0]), "=l"(v[1]), "=l"(v[2]), "=l"(v[3])
+               : "l"(p)
+               : "memory");
 }
 __device__ __forceinline__ void st_relaxed64(unsigned long long* p, uint32_t payload, uint32_t tag) {
   const unsigned long long v = ((unsigned long long)tag << 32) | payload;
@@ -209,6 +287,62 @@ __device__ __forceinline__ uint32_t wait_word(const unsigned long long* w, uint3
   return 0;
 }
 
+// Read `count` tagged words (word k at src(k)) that must carry epoch >= tag. Words are read in aligned quads
+// (src(4m) .. src(4m) + 3 contiguous and 32-byte aligned; words of the last quad beyond count are read but
+// ignored, so the allocation must extend to the quad's end): thread t takes quads t, t + MK_NT. A quad is one
+// 32-byte request, and strong loads are not merged across threads, so the request count per poll round, which
+// sets its latency, is a quarter of the word count. Stale quads are re-read together until every word carries
+// the tag (bounded like wait_word). sink(k, payload) stores each payload. On timeout or abort sets *abort_s and
+// returns early.
+template <typename Src, typename Sink>
+__device__ __forceinline__ void read_words(int count, Src src, uint32_t tag, Sink sink, const MkParams& p, int stage,
+                                           int* abort_s) {
+  const int nquad = (count + 3) >> 2;
+  for (int m0 = threadIdx.x; m0 < nquad; m0 += 2 * MK_NT) {
+    unsigned long long v[8];
+    unsigned pending = 0;  // bit 4 j + e: word e of quad j still to deliver
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+      const int m = m0 + j * MK_NT;
+      v[4 * j] = v[4 * j + 1] = v[4 * j + 2] = v[4 * j + 3] = 0;
+      if (m < nquad) {
+        ld_relaxed64x4(src(4 * m), v + 4 * j);
+#pragma unroll
+        for (int e = 0; e < 4; e++)
+          if (4 * m + e < count) pending |= 1u << (4 * j + e);
+      }
+    }
+    unsigned long long t0 = 0;
+    for (unsigned it = 0;; it++) {
+#pragma unroll
+      for (int j = 0; j < 2; j++)
+#pragma unroll
+        for (int e = 0; e < 4; e++)
+          if (((pending >> (4 * j + e)) & 1u) && (uint32_t)(v[4 * j + e] >> 32) >= tag) {
+            sink(4 * (m0 + j * MK_NT) + e, (uint32_t)v[4 * j + e]);
+            pending &= ~(1u << (4 * j + e));
+          }
+      if (!pending) break;
+      if (it == 0) {
+        t0 = gtimer();
+      } else if ((it & 31) == 31) {
+        if (*(volatile int*)abort_s || ld_volatile_i(p.err + 3)) {
+          *(volatile int*)abort_s = 1;
+          return;
+        }
+        if (gtimer() - t0 > p.timeout_ns) {
+          mk_fail(p, MK_TIMEOUT_WAIT, stage);
+          *(volatile int*)abort_s = 1;
+          return;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 2; j++)
+        if ((pending >> (4 * j)) & 15u) ld_relaxed64x4(src(4 * (m0 + j * MK_NT)), v + 4 * j);
+    }
+  }
+}
+
 // ---------------------------------------------------------------- shared building blocks
 
 // s = ((s + p[0]) + p[stride]) + ... over n terms in order. The shared-memory loads of the next 16 terms issue
@@ -253,14 +387,15 @@ __device__ __forceinline__ TileMap tile_map(int nb) {
 
 // quantization of nblk 32-value blocks: value i of block b is f(b * 32 + lane); two blocks per warp at a time
 template <typename Fn>
-__device__ __forceinline__ void mk_quant_blocks(int nblk, Fn f, int8_t* xq, float* xd, int4* xs) {
+__device__ __forceinline__ void mk_quant_blocks(int nblk, Fn f, const MkX& x) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nbp = mk_nbp(nblk);
   for (int b = warp; b < nblk; b += 2 * MK_WARPS) {
     const int b2 = b + MK_WARPS;
     const float v0 = f(b * 32 + lane);
     const float v1 = b2 < nblk ? f(b2 * 32 + lane) : 0.f;
-    quant_block_redux(v0, lane, xq + b * 32, xd + b, xs + b);
-    if (b2 < nblk) quant_block_redux(v1, lane, xq + b2 * 32, xd + b2, xs + b2);
+    mk_quant_chain(v0, lane, b, nbp, x);
+    if (b2 < nblk) mk_quant_chain(v1, lane, b2, nbp, x);
   }
   compute_bar();
 }
@@ -268,8 +403,8 @@ __device__ __forceinline__ void mk_quant_blocks(int nblk, Fn f, int8_t* xq, floa
 // RMSNorm of xf[0..D) (shared) into int8 blocks xq/xd/xs (shared), the reference's lane order (kernels.c:80-114):
 // the squares are formed by all threads into sq (shared, D floats), then thread l < 4 adds sq[4k + l] over k in
 // order and ((l0 + l1) + l2) + l3 combines the four chains.
-__device__ void mk_norm_quant(const float* xf, const float* w, int D, float eps, int8_t* xq, float* xd, int4* xs,
-                              float* red, float* sq) {
+__device__ __forceinline__ void mk_norm_quant(const float* xf, const float* w, int D, float eps, const MkX& x, float* red,
+                              float* sq) {
   const int tid = threadIdx.x;
   for (int i = tid; i < D; i += MK_NT) sq[i] = __fmul_rn(xf[i], xf[i]);
   compute_bar();
@@ -277,12 +412,12 @@ __device__ void mk_norm_quant(const float* xf, const float* w, int D, float eps,
   compute_bar();
   const float ss = __fadd_rn(__fadd_rn(__fadd_rn(red[0], red[1]), red[2]), red[3]);
   const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), eps)));
-  mk_quant_blocks(D / 32, [&](int i) { return __fmul_rn(__fmul_rn(xf[i], r), w[i]); }, xq, xd, xs);
+  mk_quant_blocks(D / 32, [&](int i) { return __fmul_rn(__fmul_rn(xf[i], r), w[i]); }, x);
 }
 
 // plain quantization of xf[0..K) (shared) into shared int8 blocks
-__device__ void mk_quant(const float* xf, int K, int8_t* xq, float* xd, int4* xs) {
-  mk_quant_blocks(K / 32, [&](int i) { return xf[i]; }, xq, xd, xs);
+__device__ __forceinline__ void mk_quant(const float* xf, int K, const MkX& x) {
+  mk_quant_blocks(K / 32, [&](int i) { return xf[i]; }, x);
 }
 
 // One tile (R rows, nb blocks; row-major: values [R][nb][16 B], then fp16 scales [R][nb]) against the shared
@@ -293,7 +428,7 @@ __device__ void mk_quant(const float* xf, int K, int8_t* xq, float* xd, int4* xs
 // Requires nb <= MK_NT.
 __device__ __forceinline__ int mk_prod_stride(int nb) { return 4 * nb + 4; }
 
-__device__ void mk_tile_dot(const uint8_t* tile, int R, int nb, const TileMap& m, const int8_t* xq, const float* xd,
+__device__ __forceinline__ void mk_tile_dot(const uint8_t* tile, int R, int nb, const TileMap& m, const int8_t* xq, const float* xd,
                             const int4* xs, float4* prod, float* out) {
   const int tid = threadIdx.x;
   const __half* wd = reinterpret_cast<const __half*>(tile + (((size_t)nb * R * 16 + 15) & ~(size_t)15));
@@ -326,44 +461,51 @@ __device__ void mk_tile_dot(const uint8_t* tile, int R, int nb, const TileMap& m
 }
 
 // ---------------------------------------------------------------- the kernel
+// Shape parameters TD (hidden), TF (ffn), TH (q heads), TKVH (kv heads), THD (head dim) fix the model shape at
+// compile time when non-zero, so buffer offsets and loop bounds are constants (fewer live registers in this
+// single large kernel); 0 takes the shape from MkParams.
+template <int TD, int TF, int TH, int TKVH, int THD>
 __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  const int D = p.D, F = p.F, H = p.H, KVH = p.KVH, HD = p.HD, L = p.L;
+  const int D = TD ? TD : p.D, F = TF ? TF : p.F, H = TH ? TH : p.H, KVH = TKVH ? TKVH : p.KVH,
+            HD = THD ? THD : p.HD, L = p.L;
   const int nbd = D / 32, nbf = F / 32;
+  const int QKV = D + 2 * KVH * HD;
+  // fixed-size regions first (constant offsets for a fixed shape), then the context-dependent ones
   uint8_t* ring = smem;                                                     // MK_NSLOT * MK_SLOT
-  float4* prod = reinterpret_cast<float4*>(ring + MK_NSLOT * MK_SLOT);      // p.prod_items
-  int8_t* xq = reinterpret_cast<int8_t*>(prod + p.prod_items);             // F int8
+  int8_t* xq = reinterpret_cast<int8_t*>(ring + MK_NSLOT * MK_SLOT);       // F int8
   float* xd = reinterpret_cast<float*>(xq + ((F + 127) & ~127));          // F/32
   int4* xs = reinterpret_cast<int4*>(xd + ((nbf + 3) & ~3));              // F/32
   float* xf = reinterpret_cast<float*>(xs + nbf);                          // D
   float* xown = xf + D;                                                    // 64 (this CTA's x rows)
-  float* outv = xown + 64;                                                 // max(3 HD, 64) (tile results)
-  float* red = outv + (3 * HD > 64 ? 3 * HD : 64);                         // 32
-  int8_t* actq = reinterpret_cast<int8_t*>(red + 32);                     // 32 B int8, 4 B d, 16 B sums
-  float* actd = reinterpret_cast<float*>(actq + 32);
-  int4* acts = reinterpret_cast<int4*>(actq + 48);
-  MkTile* tsm = reinterpret_cast<MkTile*>(actq + 64);                     // MK_MAX_TILES (this CTA's table)
+  float* outv = xown + 64;                                                 // max(3 HD, 128) (tile results)
+  float* red = outv + (3 * HD > 128 ? 3 * HD : 128);                       // 32
+  uint8_t* actb = reinterpret_cast<uint8_t*>(red + 32);                   // 2 x (32 B int8, 4 B d, 16 B sums, pad)
+  MkTile* tsm = reinterpret_cast<MkTile*>(actb + 128);                    // MK_MAX_TILES (this CTA's table)
   float* nw1 = reinterpret_cast<float*>(tsm + MK_MAX_TILES);              // D: attn_norm of the layer
   float* nw2 = nw1 + D;                                                    // D: ffn_norm of the layer
   float* onw = nw2 + D;                                                    // D: output norm
   float* bsm = onw + D;                                                    // 64: bias of this CTA's QKV rows
   float* rsm = bsm + 64;                                                   // HD: RoPE row of the position
-  float* sc = rsm + HD;                                                    // ctx (scores)
+  const int nbpd = mk_nbp(nbd);
+  int* xcw = reinterpret_cast<int*>(rsm + HD);                             // chain input: 13 nbpd words
+  const MkX xc{xcw, xcw + 4 * nbpd, xcw + 8 * nbpd, reinterpret_cast<float*>(xcw + 12 * nbpd)};
+  float4* prod = reinterpret_cast<float4*>(xcw + 13 * nbpd);              // p.prod_items
+  float* sc = reinterpret_cast<float*>(prod + p.prod_items);              // ctx (scores)
   const int HDP = HD + 4;                                                  // padded K rows: conflict-free dots
   float* kst = sc + ((p.ctx + 3) & ~3);                                    // kv_stage * HDP
   float* vst = kst + (size_t)p.kv_stage * HDP;                             // kv_stage * HD
-  __shared__ __align__(8) uint64_t full[MK_NSLOT], empty[MK_NSLOT];
+  __shared__ __align__(8) uint64_t full[MK_NSLOT];
   __shared__ int abort_s;
   __shared__ int tok_s;
+  __shared__ int ndone_s;       // act blocks whose down products are in prod
+  __shared__ __align__(16) uint8_t splitq_s[8][64];  // quantized split act blocks: 32 B int8, d, lane sums
 
   const int tid = threadIdx.x, cta = blockIdx.x, ncta = p.ncta;
   const MkTile* my_tiles = p.tiles + (size_t)cta * p.tile_stride;
 
   if (tid == 0) {
-    for (int s = 0; s < MK_NSLOT; s++) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
+    for (int s = 0; s < MK_NSLOT; s++) mbar_init(&full[s], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     abort_s = 0;
   }
@@ -374,78 +516,100 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
   // this CTA's tile table and the output norm go to shared memory once (no global load per tile)
   for (int i = tid; i < my_count; i += MK_THREADS) tsm[i] = my_tiles[i];
   for (int i = tid; i < D; i += MK_THREADS) onw[i] = p.out_norm[i];
+  for (int i = tid; i < 13 * nbpd; i += MK_THREADS) xcw[i] = 0;
   __syncthreads();
 
-  // ------------------------------------------------------------ producer warp: stream the CTA's tiles
-  if (tid >= MK_NT) {
-    if (tid == MK_NT) {
-      int issued = 0;
-      for (int i = 0; i < total_tiles; i++) {
-        const int s = i % MK_NSLOT;
-        if (i >= MK_NSLOT) {
-          if (!mbar_wait(&empty[s], ((i / MK_NSLOT) - 1) & 1, p)) {
-            if (!ld_volatile_i(p.err + 3)) mk_fail(p, MK_TIMEOUT_SLOT, -1);
-            break;
-          }
-        }
-        if (ld_volatile_i(p.err + 3)) break;
-        const MkTile t = tsm[i % my_count];
-        if (t.bytes == 0 || t.bytes > MK_SLOT || (t.bytes & 15) || (t.off & 15)) {
-          mk_fail(p, MK_ABORTED, -2);
-          break;
-        }
-        mbar_expect_tx(&full[s], t.bytes);
-        bulk_g2s(ring + (size_t)s * MK_SLOT, p.stream + t.off, t.bytes, &full[s]);
-        issued = i + 1;
-      }
-      // drain: every issued copy must land before the CTA exits (bounded; the source is valid memory)
-      for (int i = (issued > MK_NSLOT ? issued - MK_NSLOT : 0); i < issued; i++) {
-        const unsigned long long t0 = gtimer();
-        while (!mbar_try_wait(&full[i % MK_NSLOT], (i / MK_NSLOT) & 1))
-          if (gtimer() - t0 > p.timeout_ns) break;
-      }
-    }
-    return;
-  }
-
-  // ------------------------------------------------------------ compute warps
-  int tile_i = 0;
-  // wait for the next tile; the table entry must describe the rows and blocks this stage expects
-  auto next_tile = [&](int stage, int rows, int nb) -> const uint8_t* {
-    const int s = tile_i % MK_NSLOT;
-    if (tid == 0) {
-      const MkTile t = tsm[tile_i % my_count];
-      if (t.rows != rows || t.nb != nb) {
-        mk_fail(p, MK_ABORTED, stage);
+  // ------------------------------------------------------------ the weight ring
+  // Thread 0 streams the CTA's tiles into the ring with bulk copies: tile k goes to slot k % MK_NSLOT once tile
+  // k - MK_NSLOT has been released (after a CTA barrier, so no thread still reads the slot). Weight streaming
+  // competes with the cross-CTA exchanges for L2 and memory bandwidth, and slots free up at stage ends, right when
+  // results are exchanged; so inside the layers the refills wait for the start of the next RMSNorm, which reads no
+  // global memory, or for a stage that finds its tile not yet issued. The lm_head refills as soon as a slot frees.
+  int tile_i = 0;    // tiles consumed (every thread)
+  int issued = 0;    // tiles issued (thread 0)
+  bool pace = false; // thread 0: defer refills to the next RMSNorm
+  auto refill = [&]() {  // thread 0: issue every tile whose slot is free
+    const int lim = min(total_tiles, tile_i + MK_NSLOT);
+    if (issued < lim) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    while (issued < lim) {
+      const int s = issued % MK_NSLOT;
+      const MkTile t = tsm[issued % my_count];
+      if (t.bytes == 0 || t.bytes > MK_SLOT || (t.bytes & 15) || (t.off & 15)) {
+        mk_fail(p, MK_ABORTED, -2);
         abort_s = 1;
-      } else if (!mbar_wait(&full[s], (tile_i / MK_NSLOT) & 1, p)) {
-        if (!ld_volatile_i(p.err + 3)) mk_fail(p, MK_TIMEOUT_SLOT, stage);
-        abort_s = 1;
+        return;
       }
+      mbar_expect_tx(&full[s], t.bytes);
+      bulk_g2s(ring + (size_t)s * MK_SLOT, p.stream + t.off, t.bytes, &full[s]);
+      issued++;
     }
-    compute_bar();
-    return abort_s ? nullptr : ring + (size_t)s * MK_SLOT;
   };
-  auto release_tile = [&]() {
+  if (tid == 0) refill();
+
+  unsigned long long* trace = nullptr;
+  if (p.trace) trace = p.trace + (size_t)cta * p.steps * (L + 1) * MK_TRACE_PTS;
+  // wait for the next n (1 or 2) tiles; each table entry must describe the rows and blocks this stage expects
+  auto next_tiles = [&](int stage, int n, int rows0, int rows1, int nb) -> bool {
+    if (tid == 0) {
+      for (int h = 0; h < n && !abort_s; h++) {
+        const int ti = tile_i + h;
+        const MkTile t = tsm[ti % my_count];
+        if (ti >= issued) refill();  // not issued yet: refill now
+        if (t.rows != (h ? rows1 : rows0) || t.nb != nb) {
+          mk_fail(p, MK_ABORTED, stage);
+          abort_s = 1;
+        } else if (!mbar_wait(&full[ti % MK_NSLOT], (ti / MK_NSLOT) & 1, p)) {
+          if (!ld_volatile_i(p.err + 3)) mk_fail(p, MK_TIMEOUT_SLOT, stage);
+          abort_s = 1;
+        }
+      }
+    }
     compute_bar();
-    if (tid == 0) mbar_arrive(&empty[tile_i % MK_NSLOT]);
-    tile_i++;
+    return !abort_s;
+  };
+  auto release_tiles = [&](int n) {
+    compute_bar();
+    tile_i += n;
+    if (tid == 0 && !pace) refill();
+  };
+  // n chain tiles at once (tile h on warps 8h .. 8h + 7, thread (r, l) = (t / 4, t % 4)); row r of tile h lands in
+  // outv[64 h + r]
+  unsigned long long tw = 0, tc = 0;  // trace: time spent waiting for and computing chain tiles
+  auto chain_tiles = [&](int stage, int n, int rows0, int rows1, int nb) -> bool {
+    const unsigned long long c0 = trace ? gtimer() : 0;
+    if (!next_tiles(stage, n, rows0, rows1, nb)) return false;
+    const unsigned long long c1 = trace ? gtimer() : 0;
+    const int h = tid >> 8, t = tid & 255, R = h ? rows1 : rows0;
+    if (h < n && (t & ~31) < 4 * R) {  // whole warps: hsum4_quad shuffles over all 32 lanes
+      const uint8_t* tl = ring + (size_t)((tile_i + h) % MK_NSLOT) * MK_SLOT;
+      const int r = t >> 2;
+      const float a = r < R ? mk_lane_chain(tl, R, mk_nbp(nb), r, t & 3, xc) : 0.f;
+      const float v = hsum4_quad(a);
+      if (r < R && (t & 3) == 0) outv[64 * h + r] = v;
+    }
+    release_tiles(n);
+    if (trace) {
+      tw += c1 - c0;
+      tc += gtimer() - c1;
+    }
+    return true;
   };
   // read D tagged floats (x or att) into xf
   auto read_vec = [&](const unsigned long long* src, uint32_t tag, int stage) -> bool {
-    for (int i = tid; i < D; i += MK_NT) xf[i] = __uint_as_float(wait_word(src + i, tag, p, stage, &abort_s));
+    read_words(D, [&](int k) { return src + k; }, tag, [&](int k, uint32_t v) { xf[k] = __uint_as_float(v); }, p,
+               stage, &abort_s);
     compute_bar();
     return !abort_s;
   };
 
-  const TileMap map_d = tile_map(nbd), map_f = tile_map(nbf);
+  const TileMap map_f = tile_map(nbf);
   float* sqs = reinterpret_cast<float*>(prod);  // norm squares (prod is free between tiles)
   const bool head = cta < H;
   const int nh = ncta - H;                  // CTAs that own O / down rows
   const int j = cta - H;
   const int o_lo = head ? 0 : (int)((long long)j * D / nh), o_hi = head ? 0 : (int)((long long)(j + 1) * D / nh);
   const int v_lo = (int)((long long)cta * p.V / ncta), v_hi = (int)((long long)(cta + 1) * p.V / ncta);
-  const int npair = p.QKV / 2, half = HD / 2;
+  const int npair = QKV / 2, half = HD / 2;
   const int pr_lo = (int)((long long)cta * npair / ncta), pr_hi = (int)((long long)(cta + 1) * npair / ncta);
   const int G = H / KVH, kh = head ? cta / G : 0;
   const int kv_pair_lo = H * half, kv_pair_hi = (H + 2 * KVH) * half;  // QKV row pairs of the k and v heads
@@ -454,9 +618,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
   int pos = p.prm[P_POS0];
   int tok = p.prm[P_IDS];
   uint32_t E = 0;  // layer epoch (1-based within the launch)
-  unsigned long long* trace = nullptr;
-  if (p.trace && (cta == 0 || cta == ncta - 1))
-    trace = p.trace + (cta == 0 ? 0 : (size_t)p.steps * (L + 1) * MK_TRACE_PTS);
+
 #define MK_TRACE(row, k) \
   do { if (trace && tid == 0) trace[(size_t)(row) * MK_TRACE_PTS + (k)] = gtimer(); } while (0)
 
@@ -482,7 +644,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
       E++;
       const int trow = step * (L + 1) + l;
       MK_TRACE(trow, 0);
-      if (trace && tid == 0) trace[(size_t)trow * MK_TRACE_PTS + 15] = (unsigned long long)clock64();
+
       const size_t cbase = (((size_t)seq * L + l) * KVH + kh) * (size_t)p.ctx * HD;
       const bool staged = head && pos <= p.kv_stage;
       {
@@ -493,7 +655,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
         }
         if (tid < 2 * (pr_hi - pr_lo)) {
           const int pidx = pr_lo + (tid >> 1), row = (pidx / half) * HD + pidx % half + (tid & 1) * half;
-          cp_async4(bsm + tid, p.bqkv + (size_t)l * p.QKV + row);
+          cp_async4(bsm + tid, p.bqkv + (size_t)l * QKV + row);
         }
         if (head && E > (uint32_t)L) {
           // acquire the KV-cache rows that the k/v owners released at this layer of earlier steps of this launch
@@ -522,14 +684,15 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
       cp_async_wait_all();
       compute_bar();
       MK_TRACE(trow, 1);
-      mk_norm_quant(xf, nw1, D, p.eps, xq, xd, xs, red, sqs);
+      if (tid == 0) {
+        pace = true;
+        refill();
+      }
+      mk_norm_quant(xf, nw1, D, p.eps, xc, red, sqs);
       MK_TRACE(trow, 2);
       {
         const int R = 2 * (pr_hi - pr_lo);
-        const uint8_t* t = next_tile(1, R, nbd);
-        if (!t) goto out;
-        mk_tile_dot(t, R, nbd, map_d, xq, xd, xs, prod, outv);
-        release_tile();
+        if (!chain_tiles(1, 1, R, 0, nbd)) goto out;
         for (int jp = tid; jp < pr_hi - pr_lo; jp += MK_NT) {
           const int pidx = pr_lo + jp, hh = pidx / half, i = pidx % half;
           const float a = __fadd_rn(outv[2 * jp], bsm[2 * jp]);
@@ -575,13 +738,13 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
         float* q_s = outv;
         float* knew = outv + HD;
         float* vnew = outv + 2 * HD;
-        for (int i = tid; i < 3 * HD; i += MK_NT) {
-          float v;
-          if (i < HD) v = __uint_as_float(wait_word(p.qw + cta * HD + i, E, p, 10 * l + 1, &abort_s));
-          else if (i < 2 * HD) v = __uint_as_float(wait_word<true>(p.kvw + kh * HD + (i - HD), E, p, 10 * l + 1, &abort_s));
-          else v = __uint_as_float(wait_word<true>(p.kvw + (KVH + kh) * HD + (i - 2 * HD), E, p, 10 * l + 1, &abort_s));
-          outv[i] = v;
-        }
+        read_words(
+            3 * HD,
+            [&](int k) {
+              return k < HD ? p.qw + cta * HD + k
+                            : (k < 2 * HD ? p.kvw + kh * HD + (k - HD) : p.kvw + (KVH + kh) * HD + (k - 2 * HD));
+            },
+            E, [&](int k, uint32_t v) { outv[k] = __uint_as_float(v); }, p, 10 * l + 1, &abort_s);
         compute_bar();
         if (abort_s) goto out;
         MK_TRACE(trow, 4);
@@ -653,11 +816,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
         // ---- C: O rows with the residual (kernels.c:379-382)
         if (!read_vec(p.attw, E, 10 * l + 2)) goto out;
         MK_TRACE(trow, 8);
-        mk_quant(xf, D, xq, xd, xs);
-        const uint8_t* t = next_tile(3, o_hi - o_lo, nbd);
-        if (!t) goto out;
-        mk_tile_dot(t, o_hi - o_lo, nbd, map_d, xq, xd, xs, prod, outv);
-        release_tile();
+        mk_quant(xf, D, xc);
+        if (!chain_tiles(3, 1, o_hi - o_lo, 0, nbd)) goto out;
         for (int n = o_lo + tid; n < o_hi; n += MK_NT) {
           const float v = __fadd_rn(xown[n - o_lo], outv[n - o_lo]);
           xown[n - o_lo] = v;
@@ -669,42 +829,178 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
       // ---- D (all CTAs): norm + gate/up rows of whole act blocks, silu * up, quantize (kernels.c:385-397)
       if (!read_vec(p.xw, 2 * E, 10 * l + 3)) goto out;
       MK_TRACE(trow, 10);
-      mk_norm_quant(xf, nw2, D, p.eps, xq, xd, xs, red, sqs);
-      for (int ab = cta; ab < nbf; ab += ncta) {
-        const uint8_t* t = next_tile(4, 64, nbd);
-        if (!t) goto out;
-        mk_tile_dot(t, 64, nbd, map_d, xq, xd, xs, prod, outv);
-        release_tile();
-        if (tid < 32) {
-          const float gt = outv[tid], up = outv[32 + tid];
+      if (tid == 0) refill();
+      mk_norm_quant(xf, nw2, D, p.eps, xc, red, sqs);
+      MK_TRACE(trow, 14);
+      auto publish_act = [&](int h, int ab) {  // warp 8h: silu(gate) * up of tile h, quantized and published
+        const int lane = tid & 31;
+        const float gt = outv[64 * h + lane], up = outv[64 * h + 32 + lane];
+        const float v = __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, fast_exp_ref(-gt))), up);
+        int8_t* aq = reinterpret_cast<int8_t*>(actb + 64 * h);
+        float* ad = reinterpret_cast<float*>(actb + 64 * h + 32);
+        int4* as = reinterpret_cast<int4*>(actb + 64 * h + 48);
+        quant_block_redux(v, lane, aq, ad, as);
+        __syncwarp();
+        if (lane < 13) {
+          const uint32_t u = lane < 8 ? reinterpret_cast<const uint32_t*>(aq)[lane]
+                                      : (lane == 8 ? __float_as_uint(*ad) : reinterpret_cast<const uint32_t*>(as)[lane - 9]);
+#pragma unroll
+          for (int c = 0; c < MK_ACT_COPIES; c++)
+            st_relaxed64(p.actw + ((size_t)c * nbf + ab) * MK_ACT_WORDS + lane, u, E);
+        }
+        __syncwarp();
+      };
+      if (p.nsplit == 0) {
+        for (int ab0 = cta; ab0 < nbf; ab0 += 2 * ncta) {  // act blocks ab0 and ab0 + ncta: two tiles at once
+          const int n = ab0 + ncta < nbf ? 2 : 1;
+          if (!chain_tiles(4, n, 64, 64, nbd)) goto out;
+          const int h = tid >> 8;
+          if (h < n && (tid & 255) < 32) publish_act(h, ab0 + h * ncta);
+        }
+      } else {
+        // act block cta on warps 0-7; the last 4 nsplit CTAs also take piece q (8 gate + 8 up rows of block
+        // ncta + q / 4) on warps 8-9 and publish its 8 act values unquantized
+        const int q = cta - (ncta - 4 * p.nsplit);
+        if (!chain_tiles(4, q >= 0 ? 2 : 1, 64, 16, nbd)) goto out;
+        if (tid < 32) publish_act(0, cta);
+        if (q >= 0 && tid >= 256 && tid < 256 + 8) {
+          const int j = tid - 256;
+          const float gt = outv[64 + j], up = outv[64 + 8 + j];
           const float v = __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, fast_exp_ref(-gt))), up);
-          quant_block_redux(v, tid, actq, actd, acts);
-          __syncwarp();
-          unsigned long long* dst = p.actw + (size_t)ab * MK_ACT_WORDS;
-          if (tid < 8) st_relaxed64(dst + tid, reinterpret_cast<const uint32_t*>(actq)[tid], E);
-          else if (tid == 8) st_relaxed64(dst + 8, __float_as_uint(*actd), E);
-          else if (tid < 13) st_relaxed64(dst + tid, reinterpret_cast<const uint32_t*>(acts)[tid - 9], E);
-          __syncwarp();
+          st_relaxed64(p.rawact + (size_t)(q >> 2) * 32 + 8 * (q & 3) + j, __float_as_uint(v), E);
         }
       }
       MK_TRACE(trow, 11);
 
-      // ---- E (other CTAs): down rows over the quantized act, residual (kernels.c:399-400)
+      // ---- E (other CTAs): down rows over the quantized act, residual (kernels.c:399-400). Pipelined over the act
+      // blocks: thread b (warps 0-5) polls act block b and, as soon as it lands, forms its products for every down
+      // row of the CTA; warps 8.. quantize the split blocks the same way; warps 6-7 then add each (row, lane)
+      // chain in block order once all blocks are in.
       if (!head) {
-        for (int i = tid; i < nbf * 13; i += MK_NT) {
-          const int ab = i / 13, w = i - ab * 13;
-          const uint32_t v = wait_word(p.actw + (size_t)ab * MK_ACT_WORDS + w, E, p, 10 * l + 4, &abort_s);
-          if (w < 8) reinterpret_cast<uint32_t*>(xq)[ab * 8 + w] = v;
-          else if (w == 8) xd[ab] = __uint_as_float(v);
-          else reinterpret_cast<uint32_t*>(xs)[ab * 4 + (w - 9)] = v;
+        const int R = o_hi - o_lo, PS = mk_prod_stride(nbf);
+        const int nq = nbf - p.nsplit;  // blocks published quantized
+        if (tid == 0) ndone_s = 0;
+        if (!next_tiles(5, 1, R, 0, nbf)) goto out;
+        MK_TRACE(trow, 7);
+        const uint8_t* tl = ring + (size_t)(tile_i % MK_NSLOT) * MK_SLOT;
+        const __half* wdn = reinterpret_cast<const __half*>(tl + (((size_t)nbf * R * 16 + 15) & ~(size_t)15));
+        float* pf = reinterpret_cast<float*>(prod);
+        auto products = [&](int b, int r, const int4& x0, const int4& x1, const int4& xs4, float dx) {
+          const int it = r * nbf + b;
+          const uint4 w = *reinterpret_cast<const uint4*>(tl + (size_t)it * 16);
+          const float sc = __fmul_rn(__half2float(wdn[it]), dx);
+          *reinterpret_cast<float4*>(pf + r * PS + 4 * b) =
+              make_float4(__fmul_rn(q4_lane(w.x, x0.x, x1.x, xs4.x), sc), __fmul_rn(q4_lane(w.y, x0.y, x1.y, xs4.y), sc),
+                          __fmul_rn(q4_lane(w.z, x0.z, x1.z, xs4.z), sc), __fmul_rn(q4_lane(w.w, x0.w, x1.w, xs4.w), sc));
+        };
+        if (tid < 192) {
+          // warp w takes blocks 32 w + 192 k ...: its lanes poll the blocks' words together (each load instruction
+          // reads 256 contiguous bytes: lane j of round t holds word (32 t + j) % 16 of block (32 t + j) / 16), park
+          // the payloads in xq / xd / xs, then lane j forms the products of its block
+          const int warp = tid >> 5, lane = tid & 31;
+          constexpr int AT = MK_ACT_GROUP / 8;  // quad loads per lane per round
+          for (int b0 = MK_ACT_GROUP * warp; b0 < nq; b0 += 6 * MK_ACT_GROUP) {
+            const int nbw = min(MK_ACT_GROUP, nq - b0);
+            const unsigned long long* src = p.actw + ((size_t)(cta % MK_ACT_COPIES) * nbf + b0) * MK_ACT_WORDS;
+            // lane j of round t reads words 4 (32 t + j) .. + 3: quarter j % 4 of block (32 t + j) / 4
+            unsigned long long v[4 * AT];
+            unsigned pending = 0;
+#pragma unroll
+            for (int t = 0; t < AT; t++) {
+              const int u = 32 * t + lane, blk = u >> 2, j0 = 4 * (u & 3);
+              if (blk < nbw) {
+                ld_relaxed64x4(src + 4 * u, v + 4 * t);
+#pragma unroll
+                for (int e = 0; e < 4; e++)
+                  if (j0 + e < 13) pending |= 1u << (4 * t + e);
+              }
+            }
+            const unsigned long long t0 = gtimer();
+            unsigned poll_rounds = 0;
+            for (unsigned it = 0;; it++) {
+              poll_rounds = it + 1;
+#pragma unroll
+              for (int t = 0; t < AT; t++)
+#pragma unroll
+                for (int e = 0; e < 4; e++)
+                  if (((pending >> (4 * t + e)) & 1u) && (uint32_t)(v[4 * t + e] >> 32) >= E) {
+                    const int u = 32 * t + lane, blk = b0 + (u >> 2), j = 4 * (u & 3) + e;
+                    const uint32_t w = (uint32_t)v[4 * t + e];
+                    if (j < 8) reinterpret_cast<uint32_t*>(xq)[blk * 8 + j] = w;
+                    else if (j == 8) xd[blk] = __uint_as_float(w);
+                    else reinterpret_cast<uint32_t*>(xs)[blk * 4 + (j - 9)] = w;
+                    pending &= ~(1u << (4 * t + e));
+                  }
+              if (__all_sync(0xffffffffu, pending == 0)) break;
+              if ((it & 31) == 31) {
+                int bad = 0;
+                if (*(volatile int*)&abort_s || ld_volatile_i(p.err + 3)) bad = 1;
+                else if (gtimer() - t0 > p.timeout_ns) bad = 2;
+                if (__any_sync(0xffffffffu, bad != 0)) {
+                  if (bad == 2) mk_fail(p, MK_TIMEOUT_WAIT, 10 * l + 4);
+                  abort_s = 1;
+                  break;
+                }
+              }
+#pragma unroll
+              for (int t = 0; t < AT; t++)
+                if ((pending >> (4 * t)) & 15u) ld_relaxed64x4(src + 4 * (32 * t + lane), v + 4 * t);
+            }
+            if (*(volatile int*)&abort_s) break;
+            if (trace && lane == 0 && (warp == 0 || b0 + 32 >= nq))
+              trace[(size_t)trow * MK_TRACE_PTS + (warp == 0 ? 4 : 5)] = gtimer();
+            if (trace && lane == 0 && warp == 0) trace[(size_t)trow * MK_TRACE_PTS + 15] = poll_rounds;
+            __syncwarp();
+            if (lane < nbw) {
+              const int b = b0 + lane;
+              const int4 x0 = *reinterpret_cast<const int4*>(xq + b * 32);
+              const int4 x1 = *reinterpret_cast<const int4*>(xq + b * 32 + 16);
+              const int4 xs4 = xs[b];
+              const float dx = xd[b];
+              for (int r = 0; r < R; r++) products(b, r, x0, x1, xs4, dx);
+              __threadfence_block();
+              atomicAdd(&ndone_s, 1);
+            }
+            __syncwarp();
+          }
+        } else if (tid >= 256 && (tid >> 5) - 8 < p.nsplit) {
+          const int k = (tid >> 5) - 8, lane = tid & 31, b = nq + k;
+          const float v = __uint_as_float(wait_word(p.rawact + (size_t)k * 32 + lane, E, p, 10 * l + 5, &abort_s));
+          if (trace && k == 0 && lane == 0) trace[(size_t)trow * MK_TRACE_PTS + 6] = gtimer();
+          int8_t* sq8 = reinterpret_cast<int8_t*>(splitq_s[k]);
+          quant_block_redux(v, lane, sq8, reinterpret_cast<float*>(splitq_s[k] + 32), reinterpret_cast<int4*>(splitq_s[k] + 48));
+          __syncwarp();
+          if (lane < R)
+            products(b, lane, *reinterpret_cast<const int4*>(sq8), *reinterpret_cast<const int4*>(sq8 + 16),
+                     *reinterpret_cast<const int4*>(splitq_s[k] + 48), *reinterpret_cast<const float*>(splitq_s[k] + 32));
+          __syncwarp();
+          if (lane == 0) {
+            __threadfence_block();
+            atomicAdd(&ndone_s, 1);
+          }
+        } else if (tid >= 192 && tid < 192 + ((4 * R + 31) & ~31)) {
+          const int c = tid - 192;
+          const unsigned long long t0 = gtimer();
+          for (unsigned it = 0; *(volatile int*)&ndone_s < nbf; it++) {
+            if ((it & 63) == 63) {
+              if (*(volatile int*)&abort_s || ld_volatile_i(p.err + 3)) break;
+              if (gtimer() - t0 > p.timeout_ns) {
+                mk_fail(p, MK_TIMEOUT_WAIT, 10 * l + 6);
+                abort_s = 1;
+                break;
+              }
+            }
+          }
+          __threadfence_block();
+          if (trace && c == 0) trace[(size_t)trow * MK_TRACE_PTS + 12] = gtimer();
+          float acc = 0.f;
+          if (c < 4 * R && !*(volatile int*)&abort_s) acc = chain_sum(0.f, pf + (c >> 2) * PS + (c & 3), 4, nbf);
+          const float hv = hsum4_quad(acc);
+          if (c < 4 * R && (c & 3) == 0) outv[c >> 2] = hv;
         }
         compute_bar();
         if (abort_s) goto out;
-        MK_TRACE(trow, 12);
-        const uint8_t* t = next_tile(5, o_hi - o_lo, nbf);
-        if (!t) goto out;
-        mk_tile_dot(t, o_hi - o_lo, nbf, map_f, xq, xd, xs, prod, outv);
-        release_tile();
+        release_tiles(1);
         for (int n = o_lo + tid; n < o_hi; n += MK_NT) {
           const float v = __fadd_rn(xown[n - o_lo], outv[n - o_lo]);
           xown[n - o_lo] = v;
@@ -719,22 +1015,30 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
     MK_TRACE(lrow, 0);
     if (!read_vec(p.xw, 2 * E + 1, 9999)) goto out;
     MK_TRACE(lrow, 1);
-    mk_norm_quant(xf, onw, D, p.eps, xq, xd, xs, red, sqs);
+    if (tid == 0) {  // the lm_head streams freely
+      pace = false;
+      refill();
+    }
+    mk_norm_quant(xf, onw, D, p.eps, xc, red, sqs);
     MK_TRACE(lrow, 2);
+    tw = tc = 0;
     {
+      // two tiles at once; warp 8h keeps the argmax of tile h's rows (ties to the lowest index, cpu-worker.js:156-157;
+      // the merge is order-independent)
       float bv = -INFINITY;
       int bi = 0x7fffffff;
-      for (int r0 = v_lo; r0 < v_hi; r0 += MK_TILE_ROWS) {
-        const int R = v_hi - r0 < MK_TILE_ROWS ? v_hi - r0 : MK_TILE_ROWS;
-        const uint8_t* t = next_tile(8, R, nbd);
-        if (!t) goto out;
-        mk_tile_dot(t, R, nbd, map_d, xq, xd, xs, prod, outv);
-        release_tile();
-        for (int r = tid; r < R; r += MK_NT) p.logits[r0 + r] = outv[r];
-        if (tid < 32) {  // rows in increasing order, ties to the lowest index (cpu-worker.js:156-157)
+      for (int r0 = v_lo; r0 < v_hi; r0 += 2 * MK_TILE_ROWS) {
+        const int R0 = min(MK_TILE_ROWS, v_hi - r0);
+        const int R1 = min(MK_TILE_ROWS, max(0, v_hi - r0 - MK_TILE_ROWS));
+        const int n = R1 > 0 ? 2 : 1;
+        if (!chain_tiles(8, n, R0, R1, nbd)) goto out;
+        for (int i = tid; i < R0 + R1; i += MK_NT) p.logits[r0 + i] = outv[i < R0 ? i : 64 + (i - R0)];
+        const int h = tid >> 8, lane = tid & 31;
+        if (h < n && (tid & 255) < 32) {
+          const int R = h ? R1 : R0, rb = r0 + 64 * h;
           float v = -INFINITY;
           int idx = 0x7fffffff;
-          for (int r = tid; r < R; r += 32) amax_merge(v, idx, outv[r], r0 + r);
+          for (int r = lane; r < R; r += 32) amax_merge(v, idx, outv[64 * h + r], rb + r);
 #pragma unroll
           for (int o = 16; o; o >>= 1) {
             const float v2 = __shfl_xor_sync(0xffffffffu, v, o);
@@ -745,19 +1049,32 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
         }
       }
       MK_TRACE(lrow, 3);
+      if (trace && tid == 0) {
+        trace[(size_t)lrow * MK_TRACE_PTS + 5] = tw;
+        trace[(size_t)lrow * MK_TRACE_PTS + 6] = tc;
+      }
+      if (tid == 256) {  // warp 8's best joins warp 0's
+        red[0] = bv;
+        reinterpret_cast<int*>(red)[1] = bi;
+      }
+      compute_bar();
       if (tid == 0) {
+        if (v_hi - v_lo > MK_TILE_ROWS) amax_merge(bv, bi, red[0], reinterpret_cast<int*>(red)[1]);
         st_relaxed64(p.lmw + 2 * cta, __float_as_uint(bv), step + 1);
         st_relaxed64(p.lmw + 2 * cta + 1, (uint32_t)bi, step + 1);
       }
     }
+    {  // every CTA's (value, index) pair, all words read at once
+      uint32_t* lmv = reinterpret_cast<uint32_t*>(prod);
+      read_words(2 * ncta, [&](int k) { return p.lmw + k; }, step + 1, [&](int k, uint32_t v) { lmv[k] = v; }, p,
+                 9998, &abort_s);
+      compute_bar();
+    }
     if (tid < 32) {
+      const uint32_t* lmv = reinterpret_cast<const uint32_t*>(prod);
       float v = -INFINITY;
       int idx = 0x7fffffff;
-      for (int i = tid; i < ncta; i += 32) {
-        const float v2 = __uint_as_float(wait_word(p.lmw + 2 * i, step + 1, p, 9998, &abort_s));
-        const int i2 = (int)wait_word(p.lmw + 2 * i + 1, step + 1, p, 9998, &abort_s);
-        amax_merge(v, idx, v2, i2);
-      }
+      for (int i = tid; i < ncta; i += 32) amax_merge(v, idx, __uint_as_float(lmv[2 * i]), (int)lmv[2 * i + 1]);
 #pragma unroll
       for (int o = 16; o; o >>= 1) {
         const float v2 = __shfl_xor_sync(0xffffffffu, v, o);
@@ -779,6 +1096,12 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
     }
   }
 out:
+  if (tid == 0)  // every issued bulk copy must land before the CTA exits (bounded; the sources are valid memory)
+    for (int k = tile_i; k < issued; k++) {
+      const unsigned long long t0 = gtimer();
+      while (!mbar_try_wait(&full[k % MK_NSLOT], (k / MK_NSLOT) & 1))
+        if (gtimer() - t0 > p.timeout_ns) break;
+    }
   cp_async_wait_all();  // no shared-memory copy may still be in flight when the CTA exits
   return;
 #undef MK_TRACE

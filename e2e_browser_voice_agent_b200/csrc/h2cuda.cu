@@ -85,7 +85,9 @@ struct h2c_engine {
   MkTile* mk_tiles = nullptr;
   float *mk_attn_norm = nullptr, *mk_ffn_norm = nullptr, *mk_bqkv = nullptr;
   unsigned long long *mk_xw = nullptr, *mk_qw = nullptr, *mk_kvw = nullptr, *mk_attw = nullptr, *mk_actw = nullptr,
-                     *mk_lmw = nullptr, *mk_kvdone = nullptr;
+                     *mk_lmw = nullptr, *mk_kvdone = nullptr, *mk_rawact = nullptr;
+  int mk_nsplit = 0;
+  void* mk_kernel = nullptr;  // the k_decode_persistent instance for this model's shape
   size_t mk_tagged_words = 0;  // mk_xw .. mk_kvdone are one allocation of this many words
   int32_t* mk_io = nullptr;   // device: [0] next token, [4..7] error words
   int* mk_tile_count = nullptr;
@@ -400,20 +402,32 @@ struct TileSpec {
   const uint16_t* d;
   int nb;
   std::vector<int> rows;
+  bool chain;         // chain layout (QKV, O, gate/up, lm_head) or row-major (down)
 };
 
-size_t tile_bytes(int nb, int R) { return align_up((size_t)nb * R * 16, 16) + align_up((size_t)nb * R * 2, 16); }
+size_t tile_bytes(int nb, int R, bool chain) {
+  if (chain) return (size_t)R * mk_nbp(nb) * 16 + align_up((size_t)R * mk_nbp(nb) * 2, 16);
+  return align_up((size_t)nb * R * 16, 16) + align_up((size_t)nb * R * 2, 16);
+}
 
-// gather rows of a grouped-layout matrix into one row-major tile: values [R][nb][16], then scales [R][nb]
+// Gather rows of a grouped-layout matrix into one tile. Row-major: values [R][nb][16 B], then fp16 scales [R][nb].
+// Chain: values [R][4][nbp] 32-bit words (word l of every block of the row, lane by lane), then fp16 scales
+// [R][nbp]; the padding blocks up to nbp are zero.
 void gather_tile(const TileSpec& t, uint8_t* dst) {
-  const int R = (int)t.rows.size(), nb = t.nb;
-  uint16_t* dd = reinterpret_cast<uint16_t*>(dst + align_up((size_t)nb * R * 16, 16));
+  const int R = (int)t.rows.size(), nb = t.nb, nbp = mk_nbp(nb);
+  memset(dst, 0, tile_bytes(nb, R, t.chain));
+  uint16_t* dd = reinterpret_cast<uint16_t*>(dst + (t.chain ? (size_t)R * nbp * 16 : align_up((size_t)nb * R * 16, 16)));
   for (int j = 0; j < R; j++)
     for (int b = 0; b < nb; b++) {
       const int n = t.rows[j], g = n >> 5, r = n & 31;
       const size_t e = ((size_t)g * nb + b) * 32 + r;
-      memcpy(dst + ((size_t)j * nb + b) * 16, t.qs + e * 16, 16);
-      dd[(size_t)j * nb + b] = t.d[e];
+      if (t.chain) {
+        for (int l = 0; l < 4; l++) memcpy(dst + (((size_t)j * 4 + l) * nbp + b) * 4, t.qs + e * 16 + 4 * l, 4);
+        dd[(size_t)j * nbp + b] = t.d[e];
+      } else {
+        memcpy(dst + ((size_t)j * nb + b) * 16, t.qs + e * 16, 16);
+        dd[(size_t)j * nb + b] = t.d[e];
+      }
     }
 }
 
@@ -438,20 +452,24 @@ int mk_build(h2c_engine* e) {
   if (e->out_type == 8) return mk_unsupported(e, "Q8_0 output matrix (the persistent kernel streams Q4_0 tiles)");
   if (HD % MK_TILE_ROWS) return mk_unsupported(e, "head_dim not a multiple of 64");
   if (F < D) return mk_unsupported(e, "ffn narrower than the hidden size");
-  if (tile_bytes(nbd, MK_TILE_ROWS) > (size_t)MK_SLOT) return mk_unsupported(e, "rows too long for 64-row tiles");
+  if (tile_bytes(nbd, MK_TILE_ROWS, true) > (size_t)MK_SLOT) return mk_unsupported(e, "rows too long for 64-row tiles");
   const int nh = std::min(dev_sms - H, D / 4);  // CTAs owning O / down rows
   if (nh < 1) return mk_unsupported(e, "not enough SMs");
   const int ncta = H + nh;
   if (V < ncta) return mk_unsupported(e, "vocabulary smaller than the grid");
   const int o_max = (D + nh - 1) / nh;
-  if (o_max > 64 || tile_bytes(nbf, o_max) > (size_t)MK_SLOT)
+  if (o_max > 64 || tile_bytes(nbf, o_max, false) > (size_t)MK_SLOT)
     return mk_unsupported(e, "per-CTA O/down tiles larger than a ring slot");
+  if (o_max > 16) return mk_unsupported(e, "more than 16 O/down rows per CTA");
+  // act blocks beyond one per CTA: up to 8 are split into 16-row gate/up pieces on the last CTAs, else every CTA
+  // takes whole blocks, two at a time
+  const int nsplit = (nbf > ncta && nbf - ncta <= 8 && 4 * (nbf - ncta) <= nh) ? nbf - ncta : 0;
   const int npair = QKV / 2, pr_max = (npair + ncta - 1) / ncta;
   if (2 * pr_max > 64) return mk_unsupported(e, "more than 64 QKV rows per CTA");
   if (nbf > MK_NT) return mk_unsupported(e, "rows longer than the tile kernel's thread count");
-  // product buffer: R rows of (4 nb + 4) floats, in float4 units
-  const int prod_items =
-      std::max({MK_TILE_ROWS * (nbd + 1), o_max * (nbd + 1), o_max * (nbf + 1), 2 * pr_max * (nbd + 1)});
+  // product buffer of the row-major (down) tiles: R rows of (4 nb + 4) floats, in float4 units; it also holds the
+  // D squares of the RMSNorm
+  const int prod_items = std::max(o_max * (nbf + 1), D / 4 + 1);
   const size_t base = mk_smem_base(D, F, HD, c.ctx, prod_items);
   int max_optin = 0;
   CUDA_TRY(e, cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, e->dev));
@@ -460,9 +478,12 @@ int mk_build(h2c_engine* e) {
   // K rows are staged with 4 floats of padding (conflict-free dot products), V rows unpadded
   const int kv_stage = (int)std::min<size_t>((size_t)c.ctx, (budget - base) / ((size_t)(2 * HD + 4) * 4));
   const size_t smem = base + (size_t)kv_stage * (2 * HD + 4) * 4;
-  CUDA_TRY(e, cudaFuncSetAttribute(k_decode_persistent, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  // the Qwen2.5-0.5B shape has its own instance with the shape compiled in; other shapes take the generic one
+  e->mk_kernel = (D == 896 && F == 4864 && H == 14 && KVH == 2 && HD == 64) ? (void*)k_decode_persistent<896, 4864, 14, 2, 64>
+                                                                          : (void*)k_decode_persistent<0, 0, 0, 0, 0>;
+  CUDA_TRY(e, cudaFuncSetAttribute(e->mk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   int occ = 0;
-  CUDA_TRY(e, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_decode_persistent, MK_THREADS, smem));
+  CUDA_TRY(e, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, e->mk_kernel, MK_THREADS, smem));
   if (occ < 1) return mk_unsupported(e, "persistent kernel does not fit on an SM");
 
   // host copies of the packed (grouped) matrices
@@ -488,8 +509,8 @@ int mk_build(h2c_engine* e) {
   // per-CTA tile lists, in consumption order (must match k_decode_persistent)
   std::vector<std::vector<TileSpec>> specs(ncta);
   const int half = HD / 2;
-  auto rows_tile = [&](int mat, int nb, int first, int count) {
-    TileSpec t{hq[mat].data(), hd[mat].data(), nb, {}};
+  auto rows_tile = [&](int mat, int nb, int first, int count, bool chain) {
+    TileSpec t{hq[mat].data(), hd[mat].data(), nb, {}, chain};
     for (int n = first; n < first + count; n++) t.rows.push_back(n);
     return t;
   };
@@ -501,29 +522,36 @@ int mk_build(h2c_engine* e) {
     const int pr_lo = (int)((long long)cta * npair / ncta), pr_hi = (int)((long long)(cta + 1) * npair / ncta);
     auto& Lst = specs[cta];
     for (int l = 0; l < NL; l++) {
-      TileSpec a{hq[4 * l].data(), hd[4 * l].data(), nbd, {}};
+      TileSpec a{hq[4 * l].data(), hd[4 * l].data(), nbd, {}, true};
       for (int pi = pr_lo; pi < pr_hi; pi++) {  // QKV rows in RoPE pairs (i, i + HD/2) of a head
         const int hh = pi / half, i = pi % half;
         a.rows.push_back(hh * HD + i);
         a.rows.push_back(hh * HD + i + half);
       }
       Lst.push_back(a);
-      if (!head) Lst.push_back(rows_tile(4 * l + 1, nbd, o_lo, o_hi - o_lo));
-      for (int ab = cta; ab < nbf; ab += ncta) {
-        TileSpec g{hq[4 * l + 2].data(), hd[4 * l + 2].data(), nbd, {}};
+      if (!head) Lst.push_back(rows_tile(4 * l + 1, nbd, o_lo, o_hi - o_lo, true));
+      for (int ab = cta; ab < (nsplit ? ncta : nbf); ab += ncta) {
+        TileSpec g{hq[4 * l + 2].data(), hd[4 * l + 2].data(), nbd, {}, true};
         for (int q = 0; q < 32; q++) g.rows.push_back(32 * ab + q);
         for (int q = 0; q < 32; q++) g.rows.push_back(F + 32 * ab + q);
         Lst.push_back(g);
       }
-      if (!head) Lst.push_back(rows_tile(4 * l + 3, nbf, o_lo, o_hi - o_lo));
+      if (nsplit && cta >= ncta - 4 * nsplit) {  // piece q: act values 8 (q % 4) .. + 7 of block ncta + q / 4
+        const int q = cta - (ncta - 4 * nsplit), ab = ncta + q / 4;
+        TileSpec g{hq[4 * l + 2].data(), hd[4 * l + 2].data(), nbd, {}, true};
+        for (int j = 0; j < 8; j++) g.rows.push_back(32 * ab + 8 * (q % 4) + j);
+        for (int j = 0; j < 8; j++) g.rows.push_back(F + 32 * ab + 8 * (q % 4) + j);
+        Lst.push_back(g);
+      }
+      if (!head) Lst.push_back(rows_tile(4 * l + 3, nbf, o_lo, o_hi - o_lo, false));
     }
     for (int r0 = v_lo; r0 < v_hi; r0 += MK_TILE_ROWS)
-      Lst.push_back(rows_tile(4 * NL, nbd, r0, std::min(v_hi, r0 + MK_TILE_ROWS) - r0));
+      Lst.push_back(rows_tile(4 * NL, nbd, r0, std::min(v_hi, r0 + MK_TILE_ROWS) - r0, true));
   }
   size_t maxt = 0, total = 0;
   for (auto& Lst : specs) {
     maxt = std::max(maxt, Lst.size());
-    for (auto& t : Lst) total += tile_bytes(t.nb, (int)t.rows.size());
+    for (auto& t : Lst) total += tile_bytes(t.nb, (int)t.rows.size(), t.chain);
   }
   if (maxt > (size_t)MK_MAX_TILES) return mk_unsupported(e, "more tiles per token than the shared-memory table holds");
   std::vector<uint8_t> stream(total);
@@ -534,14 +562,18 @@ int mk_build(h2c_engine* e) {
     counts[cta] = (int)specs[cta].size();
     for (size_t i = 0; i < specs[cta].size(); i++) {
       const TileSpec& t = specs[cta][i];
-      const size_t b = tile_bytes(t.nb, (int)t.rows.size());
+      const size_t b = tile_bytes(t.nb, (int)t.rows.size(), t.chain);
       if (b > (size_t)MK_SLOT) return mk_unsupported(e, "tile larger than a ring slot");
       gather_tile(t, stream.data() + off);
       table[(size_t)cta * maxt + i] = MkTile{(uint64_t)off, (uint32_t)b, (uint16_t)t.rows.size(), (uint16_t)t.nb};
       off += b;
     }
   }
-  const size_t words = (size_t)D * 3 + (size_t)2 * KVH * HD + (size_t)nbf * MK_ACT_WORDS + (size_t)ncta * 3;
+  // tagged-word regions, each starting on a 4-word (32-byte) boundary for the quad reads, plus one spare quad
+  auto q4w = [](size_t n) { return (n + 3) & ~(size_t)3; };
+  const size_t lm_words = q4w((size_t)ncta * 2), kvd_words = q4w((size_t)ncta);
+  const size_t words = (size_t)D * 3 + (size_t)2 * KVH * HD + (size_t)MK_ACT_COPIES * nbf * MK_ACT_WORDS + lm_words +
+                       kvd_words + (size_t)nsplit * 32 + 4;
   unsigned long long* tagged = nullptr;
   if ((r = dalloc_t(e, &e->mk_stream, total)) || (r = dalloc_t(e, &e->mk_tiles, table.size())) ||
       (r = dalloc_t(e, &e->mk_attn_norm, (size_t)NL * D)) || (r = dalloc_t(e, &e->mk_ffn_norm, (size_t)NL * D)) ||
@@ -553,8 +585,10 @@ int mk_build(h2c_engine* e) {
   e->mk_attw = tagged + 2 * D;
   e->mk_kvw = tagged + 3 * D;
   e->mk_actw = e->mk_kvw + (size_t)2 * KVH * HD;
-  e->mk_lmw = e->mk_actw + (size_t)nbf * MK_ACT_WORDS;
-  e->mk_kvdone = e->mk_lmw + (size_t)ncta * 2;
+  e->mk_lmw = e->mk_actw + (size_t)MK_ACT_COPIES * nbf * MK_ACT_WORDS;
+  e->mk_kvdone = e->mk_lmw + lm_words;
+  e->mk_rawact = e->mk_kvdone + kvd_words;
+  e->mk_nsplit = nsplit;
   e->mk_tagged_words = words;
   CUDA_TRY(e, cudaMallocHost(&e->mk_io_h, 8 * sizeof(int32_t)));
   CUDA_TRY(e, cudaMemcpy(e->mk_tile_count, counts.data(), counts.size() * sizeof(int), cudaMemcpyHostToDevice));
@@ -591,13 +625,15 @@ int mk_launch(h2c_engine* e, int steps, unsigned long long* trace = nullptr) {
   p.rope = e->rope; p.embd_qs = e->embd.qs; p.embd_d = e->embd.d; p.kc = e->kc; p.vc = e->vc; p.logits = e->logits;
   p.xw = e->mk_xw; p.qw = e->mk_qw; p.kvw = e->mk_kvw; p.attw = e->mk_attw; p.actw = e->mk_actw; p.lmw = e->mk_lmw;
   p.kvdone = e->mk_kvdone;
+  p.rawact = e->mk_rawact;
+  p.nsplit = e->mk_nsplit;
   p.err = e->mk_io + 4; p.prm = e->prm; p.toklog = e->toklog; p.next = e->mk_io; p.steps = steps;
   p.timeout_ns = 2000000000ull;
   p.trace = trace;
   CUDA_TRY(e, cudaMemsetAsync(e->mk_xw, 0, e->mk_tagged_words * sizeof(unsigned long long), e->st));
   CUDA_TRY(e, cudaMemsetAsync(e->mk_io, 0, 8 * sizeof(int32_t), e->st));
   void* args[] = {&p};
-  CUDA_TRY(e, cudaLaunchCooperativeKernel((void*)k_decode_persistent, dim3(e->mk_ncta), dim3(MK_THREADS), args,
+  CUDA_TRY(e, cudaLaunchCooperativeKernel(e->mk_kernel, dim3(e->mk_ncta), dim3(MK_THREADS), args,
                                           e->mk_smem, e->st));
   return H2C_OK;
 }
@@ -890,8 +926,6 @@ int h2c_generate(h2c_engine* e, int seq, int32_t first_id, int32_t pos, int32_t 
 int h2c_trace_decode(h2c_engine* e, int seq, int32_t first_id, int32_t pos, int32_t steps, uint64_t* out, int64_t n) {
   if (!e || !out || steps < 1) return H2C_ERR_INVALID;
   const h2c_config& c = e->cfg;
-  const int64_t need = 2 * (int64_t)steps * (c.layers + 1) * MK_TRACE_PTS;
-  if (n < need) return e->fail(H2C_ERR_INVALID, "trace needs %lld entries", (long long)need);
   if (seq < 0 || seq >= c.max_seqs || pos < 0 || (int64_t)pos + steps >= c.ctx || first_id < 0 || first_id >= c.vocab)
     return e->fail(H2C_ERR_INVALID, "bad trace arguments");
   CUDA_TRY(e, cudaSetDevice(e->dev));
@@ -899,6 +933,8 @@ int h2c_trace_decode(h2c_engine* e, int seq, int32_t first_id, int32_t pos, int3
   if (r) return r;
   if ((r = mk_build(e))) return r;
   if (!e->mk_ok) return e->fail(H2C_ERR_INVALID, "persistent decode kernel unavailable: %s", e->mk_why.c_str());
+  const int64_t need = (int64_t)e->mk_ncta * steps * (c.layers + 1) * MK_TRACE_PTS;
+  if (n < need) return e->fail(H2C_ERR_INVALID, "trace needs %lld entries", (long long)need);
   unsigned long long* d = nullptr;
   CUDA_TRY(e, cudaMalloc(&d, need * 8));
   CUDA_TRY(e, cudaMemsetAsync(d, 0, need * 8, e->st));
@@ -914,6 +950,15 @@ int h2c_trace_decode(h2c_engine* e, int seq, int32_t first_id, int32_t pos, int3
   }
   cudaFree(d);
   return r;
+}
+
+int h2c_decode_ctas(h2c_engine* e) {
+  if (!e) return H2C_ERR_INVALID;
+  CUDA_TRY(e, cudaSetDevice(e->dev));
+  int r = check_ready(e);
+  if (r) return r;
+  if ((r = mk_build(e))) return r;
+  return e->mk_ok ? e->mk_ncta : 0;
 }
 
 int h2c_decode_kernels(h2c_engine* e) {

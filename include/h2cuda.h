@@ -109,11 +109,14 @@ int h2c_set_decode_mode(h2c_engine* e, int mode);
 int h2c_decode_path(h2c_engine* e);
 
 /* Profiling aid for the persistent decode kernel: runs h2c_generate's device-side greedy decode once with
- * %globaltimer stamps (nanoseconds) taken at the stage boundaries of CTA 0 (a head CTA) and of the last CTA.
- * out receives 2 * steps * (layers + 1) * 16 entries: [cta 0 | last cta][step][layer or lm_head][point], 0 where a
- * point does not apply. The per-operation profile of the reference (profile_start/get, kernels.c:481-483) for
- * this path. Allocates a temporary device buffer. */
+ * %globaltimer stamps (nanoseconds) taken at the stage boundaries of every CTA. out receives
+ * h2c_decode_ctas(e) * steps * (layers + 1) * 16 entries: [cta][step][layer or lm_head][point], 0 where a point
+ * does not apply. The per-operation profile of the reference (profile_start/get, kernels.c:481-483) for this
+ * path. Allocates a temporary device buffer. */
 int h2c_trace_decode(h2c_engine* e, int seq, int32_t first_id, int32_t pos, int32_t steps, uint64_t* out, int64_t n);
+
+/* Grid size (CTAs) of the persistent decode kernel, 0 when the model takes the graph path; < 0 on error. */
+int h2c_decode_ctas(h2c_engine* e);
 
 /* Number of kernels one decode step launches (the kernel nodes of the decode-step CUDA graph); < 0 on error. */
 int h2c_decode_kernels(h2c_engine* e);
