@@ -201,30 +201,26 @@ def main():
 
     import torch
     import torch.distributed as dist
-    from e2e_browser_voice_agent_b200 import backend, synth
+    from e2e_browser_voice_agent_b200 import backend, sessions, synth
 
     torch.cuda.set_device(local)
     if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        sessions.init("nccl")
     steps = args.steps if args.steps is not None else 3200
     warm = max(3, args.warmup)
 
     def barrier():
-        if world > 1:
-            dist.barrier()
+        sessions.barrier()
         torch.cuda.synchronize()
 
     def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return sessions.max_over_ranks(x, device="cuda")
 
     path = synth.ensure("qwen2-0.5b")
     be = backend.open_model(path, ctx=PROMPT + ROUND + 1, prefill_chunk=16, device=local)
-    prompt = synth.prompt_ids(151936, PROMPT, seed=1 + rank)
+    # one session per rank (weak scaling): rank r serves session r of a world-sized set
+    (sid,) = sessions.shard(world, world, rank)
+    prompt = synth.prompt_ids(151936, PROMPT, seed=sessions.session_seed(sid))
     first = be.forward(prompt, 0)
 
     def device_rounds(n):
