@@ -46,9 +46,9 @@ constexpr int MK_THREADS = MK_NT;                // 16 warps: the 128-register l
 constexpr int MK_TILE_ROWS = 64;                 // rows per tile (lm_head, q/k/v)
 constexpr int MK_TRACE_PTS = 16;
 constexpr int MK_ACT_WORDS = 16;                 // tagged words per act block: 8 int8 quads, d, 4 lane sums
-#ifndef MK_ACT_COPIES
-#define MK_ACT_COPIES 8                          // act blocks are stored in this many copies; CTA c reads copy c % 8,
-#endif                                           // so no L2 line is polled by every CTA
+#ifndef MK_PACE
+#define MK_PACE true                             // defer ring refills inside the layers to the next RMSNorm
+#endif
 #ifndef MK_ACT_GROUP
 #define MK_ACT_GROUP 16                          // act blocks one warp polls together in the down stage
 #endif
@@ -88,7 +88,7 @@ struct MkParams {
   unsigned long long* qw;         // [D] tagged q (after bias and RoPE)
   unsigned long long* kvw;        // [2 KVH HD] tagged k then v of the current position
   unsigned long long* attw;       // [D] tagged att
-  unsigned long long* actw;       // [MK_ACT_COPIES][F/32][MK_ACT_WORDS] tagged act blocks
+  unsigned long long* actw;       // [F/32][MK_ACT_WORDS] tagged act blocks
   unsigned long long* lmw;        // [ncta][2] tagged lm_head partials (value, index)
   unsigned long long* kvdone;     // [ncta] epoch of the last layer whose KV-cache rows this CTA has released
   unsigned long long* rawact;     // [nsplit][32] tagged act values of the split blocks
@@ -685,7 +685,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
       compute_bar();
       MK_TRACE(trow, 1);
       if (tid == 0) {
-        pace = true;
+        pace = MK_PACE;
         refill();
       }
       mk_norm_quant(xf, nw1, D, p.eps, xc, red, sqs);
@@ -844,9 +844,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
         if (lane < 13) {
           const uint32_t u = lane < 8 ? reinterpret_cast<const uint32_t*>(aq)[lane]
                                       : (lane == 8 ? __float_as_uint(*ad) : reinterpret_cast<const uint32_t*>(as)[lane - 9]);
-#pragma unroll
-          for (int c = 0; c < MK_ACT_COPIES; c++)
-            st_relaxed64(p.actw + ((size_t)c * nbf + ab) * MK_ACT_WORDS + lane, u, E);
+          st_relaxed64(p.actw + (size_t)ab * MK_ACT_WORDS + lane, u, E);
         }
         __syncwarp();
       };
@@ -901,7 +899,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
           constexpr int AT = MK_ACT_GROUP / 8;  // quad loads per lane per round
           for (int b0 = MK_ACT_GROUP * warp; b0 < nq; b0 += 6 * MK_ACT_GROUP) {
             const int nbw = min(MK_ACT_GROUP, nq - b0);
-            const unsigned long long* src = p.actw + ((size_t)(cta % MK_ACT_COPIES) * nbf + b0) * MK_ACT_WORDS;
+            const unsigned long long* src = p.actw + (size_t)b0 * MK_ACT_WORDS;
             // lane j of round t reads words 4 (32 t + j) .. + 3: quarter j % 4 of block (32 t + j) / 4
             unsigned long long v[4 * AT];
             unsigned pending = 0;

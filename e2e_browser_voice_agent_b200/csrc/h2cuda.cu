@@ -572,7 +572,7 @@ int mk_build(h2c_engine* e) {
   // tagged-word regions, each starting on a 4-word (32-byte) boundary for the quad reads, plus one spare quad
   auto q4w = [](size_t n) { return (n + 3) & ~(size_t)3; };
   const size_t lm_words = q4w((size_t)ncta * 2), kvd_words = q4w((size_t)ncta);
-  const size_t words = (size_t)D * 3 + (size_t)2 * KVH * HD + (size_t)MK_ACT_COPIES * nbf * MK_ACT_WORDS + lm_words +
+  const size_t words = (size_t)D * 3 + (size_t)2 * KVH * HD + (size_t)nbf * MK_ACT_WORDS + lm_words +
                        kvd_words + (size_t)nsplit * 32 + 4;
   unsigned long long* tagged = nullptr;
   if ((r = dalloc_t(e, &e->mk_stream, total)) || (r = dalloc_t(e, &e->mk_tiles, table.size())) ||
@@ -585,7 +585,7 @@ int mk_build(h2c_engine* e) {
   e->mk_attw = tagged + 2 * D;
   e->mk_kvw = tagged + 3 * D;
   e->mk_actw = e->mk_kvw + (size_t)2 * KVH * HD;
-  e->mk_lmw = e->mk_actw + (size_t)MK_ACT_COPIES * nbf * MK_ACT_WORDS;
+  e->mk_lmw = e->mk_actw + (size_t)nbf * MK_ACT_WORDS;
   e->mk_kvdone = e->mk_lmw + lm_words;
   e->mk_rawact = e->mk_kvdone + kvd_words;
   e->mk_nsplit = nsplit;
