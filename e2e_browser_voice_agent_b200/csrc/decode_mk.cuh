@@ -574,11 +574,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
   };
   // n chain tiles at once (tile h on warps 8h .. 8h + 7, thread (r, l) = (t / 4, t % 4)); row r of tile h lands in
   // outv[64 h + r]
-  unsigned long long tw = 0, tc = 0;  // trace: time spent waiting for and computing chain tiles
   auto chain_tiles = [&](int stage, int n, int rows0, int rows1, int nb) -> bool {
-    const unsigned long long c0 = trace ? gtimer() : 0;
     if (!next_tiles(stage, n, rows0, rows1, nb)) return false;
-    const unsigned long long c1 = trace ? gtimer() : 0;
     const int h = tid >> 8, t = tid & 255, R = h ? rows1 : rows0;
     if (h < n && (t & ~31) < 4 * R) {  // whole warps: hsum4_quad shuffles over all 32 lanes
       const uint8_t* tl = ring + (size_t)((tile_i + h) % MK_NSLOT) * MK_SLOT;
@@ -588,10 +585,6 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
       if (r < R && (t & 3) == 0) outv[64 * h + r] = v;
     }
     release_tiles(n);
-    if (trace) {
-      tw += c1 - c0;
-      tc += gtimer() - c1;
-    }
     return true;
   };
   // read D tagged floats (x or att) into xf
@@ -642,6 +635,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
 
     for (int l = 0; l < L; l++) {
       E++;
+
       const int trow = step * (L + 1) + l;
       MK_TRACE(trow, 0);
 
@@ -1019,45 +1013,47 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
     }
     mk_norm_quant(xf, onw, D, p.eps, xc, red, sqs);
     MK_TRACE(lrow, 2);
-    tw = tc = 0;
     {
-      // two tiles at once; warp 8h keeps the argmax of tile h's rows (ties to the lowest index, cpu-worker.js:156-157;
-      // the merge is order-independent)
+      // two tiles at once; the quad leader of each row stores its logit, and every warp keeps the running argmax
+      // of its rows (ties to the lowest index, cpu-worker.js:156-157; the merge is order-independent)
       float bv = -INFINITY;
       int bi = 0x7fffffff;
       for (int r0 = v_lo; r0 < v_hi; r0 += 2 * MK_TILE_ROWS) {
         const int R0 = min(MK_TILE_ROWS, v_hi - r0);
         const int R1 = min(MK_TILE_ROWS, max(0, v_hi - r0 - MK_TILE_ROWS));
         const int n = R1 > 0 ? 2 : 1;
-        if (!chain_tiles(8, n, R0, R1, nbd)) goto out;
-        for (int i = tid; i < R0 + R1; i += MK_NT) p.logits[r0 + i] = outv[i < R0 ? i : 64 + (i - R0)];
-        const int h = tid >> 8, lane = tid & 31;
-        if (h < n && (tid & 255) < 32) {
-          const int R = h ? R1 : R0, rb = r0 + 64 * h;
-          float v = -INFINITY;
-          int idx = 0x7fffffff;
-          for (int r = lane; r < R; r += 32) amax_merge(v, idx, outv[64 * h + r], rb + r);
-#pragma unroll
-          for (int o = 16; o; o >>= 1) {
-            const float v2 = __shfl_xor_sync(0xffffffffu, v, o);
-            const int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
-            amax_merge(v, idx, v2, i2);
+        if (!next_tiles(8, n, R0, R1, nbd)) goto out;
+        const int h = tid >> 8, t = tid & 255, R = h ? R1 : R0;
+        if (h < n && (t & ~31) < 4 * R) {  // whole warps (shuffles over all 32 lanes)
+          const uint8_t* tl = ring + (size_t)((tile_i + h) % MK_NSLOT) * MK_SLOT;
+          const int r = t >> 2;
+          const float a = r < R ? mk_lane_chain(tl, R, nbpd, r, t & 3, xc) : 0.f;
+          const float v = hsum4_quad(a);
+          float vv = -INFINITY;
+          int vi = 0x7fffffff;
+          if (r < R && (t & 3) == 0) {
+            p.logits[r0 + 64 * h + r] = v;
+            vv = v;
+            vi = r0 + 64 * h + r;
           }
-          amax_merge(bv, bi, v, idx);
+#pragma unroll
+          for (int o = 4; o < 32; o <<= 1) {  // the warp's 8 quad leaders
+            const float v2 = __shfl_xor_sync(0xffffffffu, vv, o);
+            const int i2 = __shfl_xor_sync(0xffffffffu, vi, o);
+            amax_merge(vv, vi, v2, i2);
+          }
+          amax_merge(bv, bi, vv, vi);
         }
+        release_tiles(n);
       }
       MK_TRACE(lrow, 3);
-      if (trace && tid == 0) {
-        trace[(size_t)lrow * MK_TRACE_PTS + 5] = tw;
-        trace[(size_t)lrow * MK_TRACE_PTS + 6] = tc;
-      }
-      if (tid == 256) {  // warp 8's best joins warp 0's
-        red[0] = bv;
-        reinterpret_cast<int*>(red)[1] = bi;
+      if ((tid & 31) == 0) {  // each warp's best
+        red[tid >> 5] = bv;
+        reinterpret_cast<int*>(red)[16 + (tid >> 5)] = bi;
       }
       compute_bar();
       if (tid == 0) {
-        if (v_hi - v_lo > MK_TILE_ROWS) amax_merge(bv, bi, red[0], reinterpret_cast<int*>(red)[1]);
+        for (int w = 1; w < MK_WARPS; w++) amax_merge(bv, bi, red[w], reinterpret_cast<const int*>(red)[16 + w]);
         st_relaxed64(p.lmw + 2 * cta, __float_as_uint(bv), step + 1);
         st_relaxed64(p.lmw + 2 * cta + 1, (uint32_t)bi, step + 1);
       }
