@@ -46,6 +46,9 @@ constexpr int MK_THREADS = MK_NT;                // 16 warps: the 128-register l
 constexpr int MK_TILE_ROWS = 64;                 // rows per tile (lm_head, q/k/v)
 constexpr int MK_TRACE_PTS = 16;
 constexpr int MK_ACT_WORDS = 16;                 // tagged words per act block: 8 int8 quads, d, 4 lane sums
+#ifndef MK_SQ_SINK
+#define MK_SQ_SINK true                          // the x reads also store x^2 for the RMSNorm
+#endif
 #ifndef MK_PACE
 #define MK_PACE true                             // defer ring refills inside the layers to the next RMSNorm
 #endif
@@ -386,6 +389,39 @@ __device__ __forceinline__ TileMap tile_map(int nb) {
 }
 
 // quantization of nblk 32-value blocks: value i of block b is f(b * 32 + lane); two blocks per warp at a time
+// two blocks at once (b0 and b1, one value per lane each): the arithmetic of mk_quant_chain, written interleaved
+// so that the reductions and divisions of the two blocks overlap
+__device__ __forceinline__ void mk_quant_chain2(float v0, float v1, int lane, int b0, int b1, int nbp, const MkX& x) {
+  const unsigned m0 = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v0)));
+  const unsigned m1 = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v1)));
+  const float d0 = __fdiv_rn(__uint_as_float(m0), 127.0f), d1 = __fdiv_rn(__uint_as_float(m1), 127.0f);
+  const float i0 = d0 != 0.0f ? __fdiv_rn(1.0f, d0) : 0.0f, i1 = d1 != 0.0f ? __fdiv_rn(1.0f, d1) : 0.0f;
+  const int q0 = max(-128, min(127, __float2int_rn(__fmul_rn(v0, i0))));
+  const int q1 = max(-128, min(127, __float2int_rn(__fmul_rn(v1, i1))));
+  const int pos = (lane & 16) | invperm16(lane & 15);
+  int8_t* dst = reinterpret_cast<int8_t*>(pos < 16 ? x.x0 : x.x1) + ((((pos & 15) >> 2) * nbp) * 4 + (pos & 3));
+  dst[b0 * 4] = (int8_t)q0;
+  dst[b1 * 4] = (int8_t)q1;
+  const int dl = (lane & 7) >> 1;
+  const unsigned sh = (dl & 1) * 16;
+  const unsigned a0 = (unsigned)(q0 + 128) << sh, a1 = (unsigned)(q1 + 128) << sh;
+  const unsigned s01a = __reduce_add_sync(0xffffffffu, dl < 2 ? a0 : 0u);
+  const unsigned s23a = __reduce_add_sync(0xffffffffu, dl < 2 ? 0u : a0);
+  const unsigned s01b = __reduce_add_sync(0xffffffffu, dl < 2 ? a1 : 0u);
+  const unsigned s23b = __reduce_add_sync(0xffffffffu, dl < 2 ? 0u : a1);
+  if (lane < 4) {
+    const unsigned wa = lane < 2 ? s01a : s23a, wb = lane < 2 ? s01b : s23b;
+    const int ta = (int)((lane & 1) ? (wa >> 16) : (wa & 0xffffu)) - 1024;
+    const int tb = (int)((lane & 1) ? (wb >> 16) : (wb & 0xffffu)) - 1024;
+    x.xs[lane * nbp + b0] = MK_MAGIC - 8 * ta;
+    x.xs[lane * nbp + b1] = MK_MAGIC - 8 * tb;
+  }
+  if (lane == 0) {
+    x.dx[b0] = d0;
+    x.dx[b1] = d1;
+  }
+}
+
 template <typename Fn>
 __device__ __forceinline__ void mk_quant_blocks(int nblk, Fn f, const MkX& x) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -393,9 +429,8 @@ __device__ __forceinline__ void mk_quant_blocks(int nblk, Fn f, const MkX& x) {
   for (int b = warp; b < nblk; b += 2 * MK_WARPS) {
     const int b2 = b + MK_WARPS;
     const float v0 = f(b * 32 + lane);
-    const float v1 = b2 < nblk ? f(b2 * 32 + lane) : 0.f;
-    mk_quant_chain(v0, lane, b, nbp, x);
-    if (b2 < nblk) mk_quant_chain(v1, lane, b2, nbp, x);
+    if (b2 < nblk) mk_quant_chain2(v0, f(b2 * 32 + lane), lane, b, b2, nbp, x);
+    else mk_quant_chain(v0, lane, b, nbp, x);
   }
   compute_bar();
 }
@@ -404,10 +439,12 @@ __device__ __forceinline__ void mk_quant_blocks(int nblk, Fn f, const MkX& x) {
 // the squares are formed by all threads into sq (shared, D floats), then thread l < 4 adds sq[4k + l] over k in
 // order and ((l0 + l1) + l2) + l3 combines the four chains.
 __device__ __forceinline__ void mk_norm_quant(const float* xf, const float* w, int D, float eps, const MkX& x, float* red,
-                              float* sq) {
+                                              float* sq, bool have_sq = false) {
   const int tid = threadIdx.x;
-  for (int i = tid; i < D; i += MK_NT) sq[i] = __fmul_rn(xf[i], xf[i]);
-  compute_bar();
+  if (!have_sq) {  // (the x reads can deliver the squares with x)
+    for (int i = tid; i < D; i += MK_NT) sq[i] = __fmul_rn(xf[i], xf[i]);
+    compute_bar();
+  }
   if (tid < 4) red[tid] = chain_sum(0.f, sq + tid, 4, D / 4);
   compute_bar();
   const float ss = __fadd_rn(__fadd_rn(__fadd_rn(red[0], red[1]), red[2]), red[3]);
@@ -588,15 +625,26 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
     return true;
   };
   // read D tagged floats (x or att) into xf
-  auto read_vec = [&](const unsigned long long* src, uint32_t tag, int stage) -> bool {
-    read_words(D, [&](int k) { return src + k; }, tag, [&](int k, uint32_t v) { xf[k] = __uint_as_float(v); }, p,
-               stage, &abort_s);
+  float* sqs = reinterpret_cast<float*>(prod);  // norm squares (prod is free between tiles)
+  // read D tagged floats into xf; with_sq also stores their squares into sqs for the RMSNorm that follows
+  auto read_vec = [&](const unsigned long long* src, uint32_t tag, int stage, bool with_sq = false) -> bool {
+    if (with_sq)
+      read_words(
+          D, [&](int k) { return src + k; }, tag,
+          [&](int k, uint32_t v) {
+            const float f = __uint_as_float(v);
+            xf[k] = f;
+            sqs[k] = __fmul_rn(f, f);
+          },
+          p, stage, &abort_s);
+    else
+      read_words(D, [&](int k) { return src + k; }, tag, [&](int k, uint32_t v) { xf[k] = __uint_as_float(v); }, p,
+                 stage, &abort_s);
     compute_bar();
     return !abort_s;
   };
 
   const TileMap map_f = tile_map(nbf);
-  float* sqs = reinterpret_cast<float*>(prod);  // norm squares (prod is free between tiles)
   const bool head = cta < H;
   const int nh = ncta - H;                  // CTAs that own O / down rows
   const int j = cta - H;
@@ -674,7 +722,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
       }
 
       // ---- A (all CTAs): norm, QKV pairs, bias, RoPE, KV append (kernels.c:328-352)
-      if (l > 0 && !read_vec(p.xw, 2 * (E - 1) + 1, 10 * l + 0)) goto out;
+      if (l > 0 && !read_vec(p.xw, 2 * (E - 1) + 1, 10 * l + 0, MK_SQ_SINK)) goto out;
       cp_async_wait_all();
       compute_bar();
       MK_TRACE(trow, 1);
@@ -682,7 +730,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
         pace = MK_PACE;
         refill();
       }
-      mk_norm_quant(xf, nw1, D, p.eps, xc, red, sqs);
+      mk_norm_quant(xf, nw1, D, p.eps, xc, red, sqs, MK_SQ_SINK && l > 0);
       MK_TRACE(trow, 2);
       {
         const int R = 2 * (pr_hi - pr_lo);
@@ -821,10 +869,10 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
       }
 
       // ---- D (all CTAs): norm + gate/up rows of whole act blocks, silu * up, quantize (kernels.c:385-397)
-      if (!read_vec(p.xw, 2 * E, 10 * l + 3)) goto out;
+      if (!read_vec(p.xw, 2 * E, 10 * l + 3, MK_SQ_SINK)) goto out;
       MK_TRACE(trow, 10);
       if (tid == 0) refill();
-      mk_norm_quant(xf, nw2, D, p.eps, xc, red, sqs);
+      mk_norm_quant(xf, nw2, D, p.eps, xc, red, sqs, MK_SQ_SINK);
       MK_TRACE(trow, 14);
       auto publish_act = [&](int h, int ab) {  // warp 8h: silu(gate) * up of tile h, quantized and published
         const int lane = tid & 31;
@@ -1005,13 +1053,13 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
     // ---- output norm, lm_head rows, argmax (kernels.c:404-414, cpu-worker.js:154-158)
     const int lrow = step * (L + 1) + L;
     MK_TRACE(lrow, 0);
-    if (!read_vec(p.xw, 2 * E + 1, 9999)) goto out;
+    if (!read_vec(p.xw, 2 * E + 1, 9999, MK_SQ_SINK)) goto out;
     MK_TRACE(lrow, 1);
     if (tid == 0) {  // the lm_head streams freely
       pace = false;
       refill();
     }
-    mk_norm_quant(xf, onw, D, p.eps, xc, red, sqs);
+    mk_norm_quant(xf, onw, D, p.eps, xc, red, sqs, MK_SQ_SINK);
     MK_TRACE(lrow, 2);
     {
       // two tiles at once; the quad leader of each row stores its logit, and every warp keeps the running argmax
