@@ -112,6 +112,33 @@ def test_device_generate_matches_stepwise_and_oracle(model, mode):
     be.destroy()
 
 
+@pytest.mark.parametrize("model,ctx,n_prompt", [("tiny", 1024, 700), ("gqa7", 1024, 600), ("qwen2-0.5b", 512, 200)])
+def test_long_context_decode(model, ctx, n_prompt):
+    """Contexts longer than the persistent kernel stages in shared memory: attention reads the older cached
+    positions from L2/HBM. Device greedy decode and its last logits equal the oracle's, bit for bit."""
+    path = synth.ensure(model)
+    be = open_mode(path, "persistent", ctx=ctx, prefill_chunk=16)
+    V = be.cfg["vocab"]
+    prompt = synth.prompt_ids(V, n_prompt, seed=ctx + n_prompt)
+    first = be.forward(prompt, 0)
+    steps = 8
+    dev, _ = be.generate(first, n_prompt, steps)
+    last = be.forward([int(dev[-1])], n_prompt + steps, want_logits=True)
+    ref = O.open_model("oracle", path, ctx=ctx, mt=16, threads=8)
+    r = ref.forward(prompt, 0)
+    assert r["next"] == first
+    want, nxt = [], r["next"]
+    for i in range(steps):
+        r = ref.forward([nxt], n_prompt + i)
+        nxt = r["next"]
+        want.append(nxt)
+    assert list(dev) == want
+    r = ref.forward([nxt], n_prompt + steps, want_logits=True)
+    assert last == r["next"]
+    assert np.array_equal(bits(be.read_logits()), bits(r["logits"]))
+    be.destroy()
+
+
 def test_full_size_qwen2_0_5b_bit_exact():
     """The benchmark model (24 layers, hidden 896, vocab 151936, tied Q4_0 lm_head): 32-token prompt, then
     teacher-forced steps and device-side greedy decode, bit-identical to the oracle in both decode paths."""
