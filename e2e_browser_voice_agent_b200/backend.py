@@ -166,6 +166,10 @@ class CudaBackend:
                                             out.size), self._h)
         return out
 
+    def set_decode_fault(self, stall_cta: int = -1, timeout_ns: int = 2_000_000_000) -> None:
+        """Test aid: make one CTA of the persistent kernel withhold its results so the bounded waits expire."""
+        _lib.check(self._L.h2c_set_decode_fault(self._h, int(stall_cta), int(timeout_ns)), self._h)
+
     def decode_kernels(self) -> int:
         n = self._L.h2c_decode_kernels(self._h)
         if n < 0:

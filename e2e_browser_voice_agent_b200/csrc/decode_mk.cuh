@@ -95,6 +95,7 @@ struct MkParams {
   unsigned long long* lmw;        // [ncta][2] tagged lm_head partials (value, index)
   unsigned long long* kvdone;     // [ncta] epoch of the last layer whose KV-cache rows this CTA has released
   unsigned long long* rawact;     // [nsplit][32] tagged act values of the split blocks
+  int stall_cta;                  // test aid: this CTA never publishes its QKV rows (-1: none), so waits expire
   int nsplit;                     // act blocks beyond one per CTA, computed in 4 pieces of 16 gate/up rows by the
                                   // last 4 nsplit CTAs and quantized by the consumers (0: whole blocks only)
   int* err;                       // [4]: code, cta, stage, abort flag
@@ -735,7 +736,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
       {
         const int R = 2 * (pr_hi - pr_lo);
         if (!chain_tiles(1, 1, R, 0, nbd)) goto out;
-        for (int jp = tid; jp < pr_hi - pr_lo; jp += MK_NT) {
+        const int npub = cta == p.stall_cta ? 0 : pr_hi - pr_lo;
+        for (int jp = tid; jp < npub; jp += MK_NT) {
           const int pidx = pr_lo + jp, hh = pidx / half, i = pidx % half;
           const float a = __fadd_rn(outv[2 * jp], bsm[2 * jp]);
           const float b = __fadd_rn(outv[2 * jp + 1], bsm[2 * jp + 1]);

@@ -87,6 +87,8 @@ struct h2c_engine {
   unsigned long long *mk_xw = nullptr, *mk_qw = nullptr, *mk_kvw = nullptr, *mk_attw = nullptr, *mk_actw = nullptr,
                      *mk_lmw = nullptr, *mk_kvdone = nullptr, *mk_rawact = nullptr;
   int mk_nsplit = 0;
+  int mk_stall_cta = -1;                          // h2c_set_decode_fault
+  unsigned long long mk_timeout_ns = 2000000000ull;
   void* mk_kernel = nullptr;  // the k_decode_persistent instance for this model's shape
   size_t mk_tagged_words = 0;  // mk_xw .. mk_kvdone are one allocation of this many words
   int32_t* mk_io = nullptr;   // device: [0] next token, [4..7] error words
@@ -628,7 +630,8 @@ int mk_launch(h2c_engine* e, int steps, unsigned long long* trace = nullptr) {
   p.rawact = e->mk_rawact;
   p.nsplit = e->mk_nsplit;
   p.err = e->mk_io + 4; p.prm = e->prm; p.toklog = e->toklog; p.next = e->mk_io; p.steps = steps;
-  p.timeout_ns = 2000000000ull;
+  p.timeout_ns = e->mk_timeout_ns;
+  p.stall_cta = e->mk_stall_cta;
   p.trace = trace;
   CUDA_TRY(e, cudaMemsetAsync(e->mk_xw, 0, e->mk_tagged_words * sizeof(unsigned long long), e->st));
   CUDA_TRY(e, cudaMemsetAsync(e->mk_io, 0, 8 * sizeof(int32_t), e->st));
@@ -950,6 +953,14 @@ int h2c_trace_decode(h2c_engine* e, int seq, int32_t first_id, int32_t pos, int3
   }
   cudaFree(d);
   return r;
+}
+
+int h2c_set_decode_fault(h2c_engine* e, int stall_cta, int64_t timeout_ns) {
+  if (!e || stall_cta < -1 || timeout_ns < 1000000 || timeout_ns > 10000000000ll)
+    return e ? e->fail(H2C_ERR_INVALID, "stall_cta must be >= -1 and timeout_ns in [1 ms, 10 s]") : H2C_ERR_INVALID;
+  e->mk_stall_cta = stall_cta;
+  e->mk_timeout_ns = (unsigned long long)timeout_ns;
+  return H2C_OK;
 }
 
 int h2c_decode_ctas(h2c_engine* e) {

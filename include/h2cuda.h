@@ -118,6 +118,13 @@ int h2c_trace_decode(h2c_engine* e, int seq, int32_t first_id, int32_t pos, int3
 /* Grid size (CTAs) of the persistent decode kernel, 0 when the model takes the graph path; < 0 on error. */
 int h2c_decode_ctas(h2c_engine* e);
 
+/* Test aid for the persistent kernel's failure detection (no reference counterpart): every bounded wait of the
+ * kernel gives up after timeout_ns (default 2 s), and with stall_cta >= 0 that CTA never publishes its QKV rows,
+ * so the CTAs that need them wait until the limit, record the error and every CTA returns; the next
+ * h2c_forward / h2c_generate then fails with H2C_ERR_TIMEOUT and the engine stays usable (the affected positions
+ * of the KV cache must be recomputed). stall_cta = -1 restores normal operation. No fault, trap or hang. */
+int h2c_set_decode_fault(h2c_engine* e, int stall_cta, int64_t timeout_ns);
+
 /* Number of kernels one decode step launches (the kernel nodes of the decode-step CUDA graph); < 0 on error. */
 int h2c_decode_kernels(h2c_engine* e);
 

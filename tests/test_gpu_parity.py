@@ -139,6 +139,31 @@ def test_long_context_decode(model, ctx, n_prompt):
     be.destroy()
 
 
+def test_bounded_wait_expires_and_engine_recovers():
+    """Failure detection without a GPU fault: one CTA withholds its QKV rows, so the CTAs that need them wait until
+    the (shortened) limit, record the error and return; the call reports H2C_ERR_TIMEOUT quickly, and after the
+    test aid is cleared the same engine decodes the same tokens as before."""
+    import time
+    path = synth.ensure("tiny")
+    be = open_mode(path, "persistent", ctx=64, prefill_chunk=8)
+    prompt = synth.prompt_ids(be.cfg["vocab"], 9, seed=5)
+    first = be.forward(prompt, 0)
+    good, _ = be.generate(first, len(prompt), 6)
+    ncta = be._L.h2c_decode_ctas(be._h)
+    assert ncta > 0
+    be.set_decode_fault(stall_cta=ncta - 1, timeout_ns=20_000_000)
+    t0 = time.perf_counter()
+    with pytest.raises(_lib.H2CError) as ei:
+        be.generate(first, len(prompt), 6)
+    assert ei.value.code == _lib.ERR_TIMEOUT
+    assert time.perf_counter() - t0 < 10
+    be.set_decode_fault(-1)
+    assert be.forward(prompt, 0) == first  # the aborted launch left cache rows to recompute
+    again, _ = be.generate(first, len(prompt), 6)
+    assert list(again) == list(good)
+    be.destroy()
+
+
 def test_full_size_qwen2_0_5b_bit_exact():
     """The benchmark model (24 layers, hidden 896, vocab 151936, tied Q4_0 lm_head): 32-token prompt, then
     teacher-forced steps and device-side greedy decode, bit-identical to the oracle in both decode paths."""
