@@ -45,15 +45,13 @@ constexpr int MK_NT = MK_WARPS * 32;             // compute threads
 constexpr int MK_THREADS = MK_NT;                // 16 warps: the 128-register limit of a 512-thread block
 constexpr int MK_TILE_ROWS = 64;                 // rows per tile (lm_head, q/k/v)
 constexpr int MK_TRACE_PTS = 16;
-constexpr int MK_ACT_WORDS = 16;                 // tagged words per act block: 8 int8 quads, d, 4 lane sums
+constexpr int MK_ACT_WORDS = 8;                  // words per act block: its 32 int8 values and scale (36 bytes) as six
+                                                 // 48-bit payloads under a 16-bit epoch tag (words 6, 7 unused)
 #ifndef MK_SQ_SINK
 #define MK_SQ_SINK true                          // the x reads also store x^2 for the RMSNorm
 #endif
 #ifndef MK_PACE
 #define MK_PACE true                             // defer ring refills inside the layers to the next RMSNorm
-#endif
-#ifndef MK_ACT_GROUP
-#define MK_ACT_GROUP 16                          // act blocks one warp polls together in the down stage
 #endif
 
 #ifndef MK_POLL_NS
@@ -91,7 +89,7 @@ struct MkParams {
   unsigned long long* qw;         // [D] tagged q (after bias and RoPE)
   unsigned long long* kvw;        // [2 KVH HD] tagged k then v of the current position
   unsigned long long* attw;       // [D] tagged att
-  unsigned long long* actw;       // [F/32][MK_ACT_WORDS] tagged act blocks
+  unsigned long long* actw;       // [F/32][MK_ACT_WORDS] act blocks, 48-bit payload | 16-bit epoch
   unsigned long long* lmw;        // [ncta][2] tagged lm_head partials (value, index)
   unsigned long long* kvdone;     // [ncta] epoch of the last layer whose KV-cache rows this CTA has released
   unsigned long long* rawact;     // [nsplit][32] tagged act values of the split blocks
@@ -377,18 +375,6 @@ __device__ __forceinline__ float chain_sum(float s, const float* p, int stride, 
   return s;
 }
 
-// the thread -> (block, first row, row step) map of mk_tile_dot for rows of nb blocks, computed once per stage
-struct TileMap {
-  int b, r0, rstep;
-};
-__device__ __forceinline__ TileMap tile_map(int nb) {
-  TileMap m;
-  m.rstep = MK_NT / nb;
-  m.b = threadIdx.x % nb;
-  m.r0 = threadIdx.x / nb;
-  return m;
-}
-
 // quantization of nblk 32-value blocks: value i of block b is f(b * 32 + lane); two blocks per warp at a time
 // two blocks at once (b0 and b1, one value per lane each): the arithmetic of mk_quant_chain, written interleaved
 // so that the reductions and divisions of the two blocks overlap
@@ -458,45 +444,9 @@ __device__ __forceinline__ void mk_quant(const float* xf, int K, const MkX& x) {
   mk_quant_blocks(K / 32, [&](int i) { return xf[i]; }, x);
 }
 
-// One tile (R rows, nb blocks; row-major: values [R][nb][16 B], then fp16 scales [R][nb]) against the shared
-// int8 input: out[r] = ((l0 + l1) + l2) + l3 of the reference's lane chains (kernels.c:121-139, 209-229).
-// Phase 1: a thread owns one 32-value block b (its activations stay in registers) and walks rows r, r + NT/nb, ...
-// computing the four exact lane dots and the products f32(p_l) * (dw * dx) into prod (rows padded to 4 nb + 4
-// floats so the phase-2 reads are conflict-free). Phase 2: thread (r, l) adds its lane's products in block order.
-// Requires nb <= MK_NT.
+// Down tiles are row-major (values [R][nb][16 B], then fp16 scales [R][nb]); their products go to a shared
+// buffer of R rows of 4 nb + 4 floats (the padding keeps the ordered chain reads conflict-free).
 __device__ __forceinline__ int mk_prod_stride(int nb) { return 4 * nb + 4; }
-
-__device__ __forceinline__ void mk_tile_dot(const uint8_t* tile, int R, int nb, const TileMap& m, const int8_t* xq, const float* xd,
-                            const int4* xs, float4* prod, float* out) {
-  const int tid = threadIdx.x;
-  const __half* wd = reinterpret_cast<const __half*>(tile + (((size_t)nb * R * 16 + 15) & ~(size_t)15));
-  const int PS = mk_prod_stride(nb);
-  float* pf = reinterpret_cast<float*>(prod);
-  if (m.r0 < m.rstep) {
-    const int b = m.b;
-    const int4 x0 = *reinterpret_cast<const int4*>(xq + b * 32);
-    const int4 x1 = *reinterpret_cast<const int4*>(xq + b * 32 + 16);
-    const int4 s = xs[b];
-    const float dx = xd[b];
-    for (int r = m.r0; r < R; r += m.rstep) {
-      const int it = r * nb + b;
-      const uint4 w = *reinterpret_cast<const uint4*>(tile + (size_t)it * 16);
-      const float sc = __fmul_rn(__half2float(wd[it]), dx);
-      *reinterpret_cast<float4*>(pf + r * PS + 4 * b) =
-          make_float4(__fmul_rn(q4_lane(w.x, x0.x, x1.x, s.x), sc), __fmul_rn(q4_lane(w.y, x0.y, x1.y, s.y), sc),
-                      __fmul_rn(q4_lane(w.z, x0.z, x1.z, s.z), sc), __fmul_rn(q4_lane(w.w, x0.w, x1.w, s.w), sc));
-    }
-  }
-  compute_bar();
-  const int chains = R * 4;
-  if (tid < ((chains + 31) & ~31)) {
-    float acc = 0.f;
-    if (tid < chains) acc = chain_sum(0.f, pf + (tid >> 2) * PS + (tid & 3), 4, nb);
-    const float v = hsum4_quad(acc);
-    if (tid < chains && (tid & 3) == 0) out[tid >> 2] = v;
-  }
-  compute_bar();
-}
 
 // ---------------------------------------------------------------- the kernel
 // Shape parameters TD (hidden), TF (ffn), TH (q heads), TKVH (kv heads), THD (head dim) fix the model shape at
@@ -645,7 +595,6 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
     return !abort_s;
   };
 
-  const TileMap map_f = tile_map(nbf);
   const bool head = cta < H;
   const int nh = ncta - H;                  // CTAs that own O / down rows
   const int j = cta - H;
@@ -885,10 +834,15 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
         int4* as = reinterpret_cast<int4*>(actb + 64 * h + 48);
         quant_block_redux(v, lane, aq, ad, as);
         __syncwarp();
-        if (lane < 13) {
-          const uint32_t u = lane < 8 ? reinterpret_cast<const uint32_t*>(aq)[lane]
-                                      : (lane == 8 ? __float_as_uint(*ad) : reinterpret_cast<const uint32_t*>(as)[lane - 9]);
-          st_relaxed64(p.actw + (size_t)ab * MK_ACT_WORDS + lane, u, E);
+        if (lane < 6) {  // bytes 6 lane .. 6 lane + 5 of the int8 block and its scale, under the epoch's low 16 bits
+          const uint8_t* bb = actb + 64 * h;
+          const int off = 6 * lane, a = off & ~7, sh = (off & 7) * 8;
+          const unsigned long long lo = *reinterpret_cast<const unsigned long long*>(bb + a);
+          const unsigned long long hi = *reinterpret_cast<const unsigned long long*>(bb + a + 8);
+          const unsigned long long v48 = (sh ? (lo >> sh) | (hi << (64 - sh)) : lo) & 0xFFFFFFFFFFFFull;
+          const unsigned long long wv = ((unsigned long long)(E & 0xFFFFu) << 48) | v48;
+          asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p.actw + (size_t)ab * MK_ACT_WORDS + lane), "l"(wv)
+                       : "memory");
         }
         __syncwarp();
       };
@@ -940,39 +894,23 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
           // reads 256 contiguous bytes: lane j of round t holds word (32 t + j) % 16 of block (32 t + j) / 16), park
           // the payloads in xq / xd / xs, then lane j forms the products of its block
           const int warp = tid >> 5, lane = tid & 31;
-          constexpr int AT = MK_ACT_GROUP / 8;  // quad loads per lane per round
-          for (int b0 = MK_ACT_GROUP * warp; b0 < nq; b0 += 6 * MK_ACT_GROUP) {
-            const int nbw = min(MK_ACT_GROUP, nq - b0);
+          // lane j reads words 4 j .. 4 j + 3: half j % 2 of block j / 2 (the six payload words of a block are words
+          // 0-3 and 4-5); every act word is rewritten each layer, so its 16-bit tag differs from the previous one
+          const uint16_t tg = (uint16_t)E;
+          for (int b0 = 16 * warp; b0 < nq; b0 += 6 * 16) {
+            const int nbw = min(16, nq - b0);
             const unsigned long long* src = p.actw + (size_t)b0 * MK_ACT_WORDS;
-            // lane j of round t reads words 4 (32 t + j) .. + 3: quarter j % 4 of block (32 t + j) / 4
-            unsigned long long v[4 * AT];
+            unsigned long long v[4] = {0, 0, 0, 0};
             unsigned pending = 0;
-#pragma unroll
-            for (int t = 0; t < AT; t++) {
-              const int u = 32 * t + lane, blk = u >> 2, j0 = 4 * (u & 3);
-              if (blk < nbw) {
-                ld_relaxed64x4(src + 4 * u, v + 4 * t);
-#pragma unroll
-                for (int e = 0; e < 4; e++)
-                  if (j0 + e < 13) pending |= 1u << (4 * t + e);
-              }
+            if ((lane >> 1) < nbw) {
+              ld_relaxed64x4(src + 4 * lane, v);
+              pending = (lane & 1) ? 0x3u : 0xFu;
             }
             const unsigned long long t0 = gtimer();
-            unsigned poll_rounds = 0;
             for (unsigned it = 0;; it++) {
-              poll_rounds = it + 1;
 #pragma unroll
-              for (int t = 0; t < AT; t++)
-#pragma unroll
-                for (int e = 0; e < 4; e++)
-                  if (((pending >> (4 * t + e)) & 1u) && (uint32_t)(v[4 * t + e] >> 32) >= E) {
-                    const int u = 32 * t + lane, blk = b0 + (u >> 2), j = 4 * (u & 3) + e;
-                    const uint32_t w = (uint32_t)v[4 * t + e];
-                    if (j < 8) reinterpret_cast<uint32_t*>(xq)[blk * 8 + j] = w;
-                    else if (j == 8) xd[blk] = __uint_as_float(w);
-                    else reinterpret_cast<uint32_t*>(xs)[blk * 4 + (j - 9)] = w;
-                    pending &= ~(1u << (4 * t + e));
-                  }
+              for (int e = 0; e < 4; e++)
+                if (((pending >> e) & 1u) && (uint16_t)(v[e] >> 48) == tg) pending &= ~(1u << e);
               if (__all_sync(0xffffffffu, pending == 0)) break;
               if ((it & 31) == 31) {
                 int bad = 0;
@@ -984,21 +922,32 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
                   break;
                 }
               }
-#pragma unroll
-              for (int t = 0; t < AT; t++)
-                if ((pending >> (4 * t)) & 15u) ld_relaxed64x4(src + 4 * (32 * t + lane), v + 4 * t);
+              if (pending) ld_relaxed64x4(src + 4 * lane, v);
             }
             if (*(volatile int*)&abort_s) break;
-            if (trace && lane == 0 && (warp == 0 || b0 + 32 >= nq))
+            if (trace && lane == 0 && (warp == 0 || b0 + 16 >= nq))
               trace[(size_t)trow * MK_TRACE_PTS + (warp == 0 ? 4 : 5)] = gtimer();
-            if (trace && lane == 0 && warp == 0) trace[(size_t)trow * MK_TRACE_PTS + 15] = poll_rounds;
-            __syncwarp();
+            // lane b (< 16) gathers block b's six payloads from lanes 2 b and 2 b + 1 and unpacks the 36 bytes
+            const unsigned long long M48 = 0xFFFFFFFFFFFFull;
+            const int s0 = 2 * (lane & 15);
+            const unsigned long long c0 = __shfl_sync(0xffffffffu, v[0], s0) & M48;
+            const unsigned long long c1 = __shfl_sync(0xffffffffu, v[1], s0) & M48;
+            const unsigned long long c2 = __shfl_sync(0xffffffffu, v[2], s0) & M48;
+            const unsigned long long c3 = __shfl_sync(0xffffffffu, v[3], s0) & M48;
+            const unsigned long long c4 = __shfl_sync(0xffffffffu, v[0], s0 + 1) & M48;
+            const unsigned long long c5 = __shfl_sync(0xffffffffu, v[1], s0 + 1) & M48;
             if (lane < nbw) {
               const int b = b0 + lane;
-              const int4 x0 = *reinterpret_cast<const int4*>(xq + b * 32);
-              const int4 x1 = *reinterpret_cast<const int4*>(xq + b * 32 + 16);
-              const int4 xs4 = xs[b];
-              const float dx = xd[b];
+              const unsigned long long w0 = c0 | (c1 << 48), w1 = (c1 >> 16) | (c2 << 32), w2 = (c2 >> 32) | (c3 << 16),
+                                       w3 = c4 | (c5 << 48);
+              const int4 x0 = make_int4((int)w0, (int)(w0 >> 32), (int)w1, (int)(w1 >> 32));
+              const int4 x1 = make_int4((int)w2, (int)(w2 >> 32), (int)w3, (int)(w3 >> 32));
+              const float dx = __uint_as_float((uint32_t)(c5 >> 16));
+              // lane l's accumulator start: MK_MAGIC - 8 x (sum of its eight int8 values, word l of each half)
+              const int4 xs4 = make_int4(MK_MAGIC - 8 * __dp4a(x0.x, 0x01010101, __dp4a(x1.x, 0x01010101, 0)),
+                                         MK_MAGIC - 8 * __dp4a(x0.y, 0x01010101, __dp4a(x1.y, 0x01010101, 0)),
+                                         MK_MAGIC - 8 * __dp4a(x0.z, 0x01010101, __dp4a(x1.z, 0x01010101, 0)),
+                                         MK_MAGIC - 8 * __dp4a(x0.w, 0x01010101, __dp4a(x1.w, 0x01010101, 0)));
               for (int r = 0; r < R; r++) products(b, r, x0, x1, xs4, dx);
               __threadfence_block();
               atomicAdd(&ndone_s, 1);
