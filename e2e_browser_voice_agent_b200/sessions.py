@@ -34,8 +34,12 @@ def env_rank():
 def init(backend: str, timeout_s: float = 120.0) -> None:
     """Join the process group (rendezvous from the environment, as torchrun sets it) with a short timeout, so ranks
     that wait for a missing peer end with an error instead of hanging."""
+    import torch
     import torch.distributed as dist
-    dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s))
+    kw = {}
+    if backend == "nccl":  # bind the group to this rank's GPU (set as current before init)
+        kw["device_id"] = torch.device("cuda", torch.cuda.current_device())
+    dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s), **kw)
 
 
 def max_over_ranks(x: float, device=None) -> float:
