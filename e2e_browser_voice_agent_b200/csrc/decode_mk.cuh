@@ -101,6 +101,9 @@ struct MkParams {
   int32_t* toklog;                // [seqs][ctx + 1]
   int32_t* next;
   int steps;
+  uint32_t epoch0;                // layer epoch before this launch: tags keep growing across launches, so words of
+                                  // earlier launches never read as fresh and need no clearing
+  uint32_t lm0;                   // decode steps before this launch (tags of the lm_head partials)
   unsigned long long timeout_ns;
   unsigned long long* trace;      // optional: [ncta][steps * (L + 1)][MK_TRACE_PTS] %globaltimer stamps
                                   // (profiling)
@@ -608,7 +611,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
   const int seq = p.prm[P_SEQ];
   int pos = p.prm[P_POS0];
   int tok = p.prm[P_IDS];
-  uint32_t E = 0;  // layer epoch (1-based within the launch)
+  uint32_t E = p.epoch0;  // layer epoch (grows by one per layer, across launches)
 
 #define MK_TRACE(row, k) \
   do { if (trace && tid == 0) trace[(size_t)(row) * MK_TRACE_PTS + (k)] = gtimer(); } while (0)
@@ -649,7 +652,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
           const int pidx = pr_lo + (tid >> 1), row = (pidx / half) * HD + pidx % half + (tid & 1) * half;
           cp_async4(bsm + tid, p.bqkv + (size_t)l * QKV + row);
         }
-        if (head && E > (uint32_t)L) {
+        if (head && E > p.epoch0 + (uint32_t)L) {
           // acquire the KV-cache rows that the k/v owners released at this layer of earlier steps of this launch
           // (rows of earlier launches are ordered by the launch boundary)
           if (tid < ncta) {
@@ -770,10 +773,12 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
           sc[t] = v;
           mx = fmaxf(mx, v);
         }
+        MK_TRACE(trow, 12);
         mx = warp_max(mx);
         if ((tid & 31) == 0) red[tid >> 5] = mx;
         compute_bar();
         mx = warp_max(red[tid & (MK_WARPS - 1)]);
+        MK_TRACE(trow, 13);
         for (int t = tid; t < T; t += MK_NT) sc[t] = fast_exp_ref(__fsub_rn(sc[t], mx));
         compute_bar();
         MK_TRACE(trow, 5);
@@ -1053,13 +1058,13 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
       compute_bar();
       if (tid == 0) {
         for (int w = 1; w < MK_WARPS; w++) amax_merge(bv, bi, red[w], reinterpret_cast<const int*>(red)[16 + w]);
-        st_relaxed64(p.lmw + 2 * cta, __float_as_uint(bv), step + 1);
-        st_relaxed64(p.lmw + 2 * cta + 1, (uint32_t)bi, step + 1);
+        st_relaxed64(p.lmw + 2 * cta, __float_as_uint(bv), p.lm0 + step + 1);
+        st_relaxed64(p.lmw + 2 * cta + 1, (uint32_t)bi, p.lm0 + step + 1);
       }
     }
     {  // every CTA's (value, index) pair, all words read at once
       uint32_t* lmv = reinterpret_cast<uint32_t*>(prod);
-      read_words(2 * ncta, [&](int k) { return p.lmw + k; }, step + 1, [&](int k, uint32_t v) { lmv[k] = v; }, p,
+      read_words(2 * ncta, [&](int k) { return p.lmw + k; }, p.lm0 + step + 1, [&](int k, uint32_t v) { lmv[k] = v; }, p,
                  9998, &abort_s);
       compute_bar();
     }

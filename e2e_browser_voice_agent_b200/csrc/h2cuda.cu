@@ -87,6 +87,8 @@ struct h2c_engine {
   unsigned long long *mk_xw = nullptr, *mk_qw = nullptr, *mk_kvw = nullptr, *mk_attw = nullptr, *mk_actw = nullptr,
                      *mk_lmw = nullptr, *mk_kvdone = nullptr, *mk_rawact = nullptr;
   int mk_nsplit = 0;
+  uint32_t mk_epoch = 0, mk_lm_epoch = 0;  // tag epochs used by earlier launches
+  bool mk_io_dirty = true;                   // error words must be cleared before the next launch
   int mk_stall_cta = -1;                          // h2c_set_decode_fault
   unsigned long long mk_timeout_ns = 2000000000ull;
   void* mk_kernel = nullptr;  // the k_decode_persistent instance for this model's shape
@@ -592,6 +594,7 @@ int mk_build(h2c_engine* e) {
   e->mk_rawact = e->mk_kvdone + kvd_words;
   e->mk_nsplit = nsplit;
   e->mk_tagged_words = words;
+  CUDA_TRY(e, cudaMemset(tagged, 0, words * sizeof(unsigned long long)));  // epoch 0: nothing published yet
   CUDA_TRY(e, cudaMallocHost(&e->mk_io_h, 8 * sizeof(int32_t)));
   CUDA_TRY(e, cudaMemcpy(e->mk_tile_count, counts.data(), counts.size() * sizeof(int), cudaMemcpyHostToDevice));
   CUDA_TRY(e, cudaMemcpy(e->mk_stream, stream.data(), total, cudaMemcpyHostToDevice));
@@ -633,8 +636,21 @@ int mk_launch(h2c_engine* e, int steps, unsigned long long* trace = nullptr) {
   p.timeout_ns = e->mk_timeout_ns;
   p.stall_cta = e->mk_stall_cta;
   p.trace = trace;
-  CUDA_TRY(e, cudaMemsetAsync(e->mk_xw, 0, e->mk_tagged_words * sizeof(unsigned long long), e->st));
-  CUDA_TRY(e, cudaMemsetAsync(e->mk_io, 0, 8 * sizeof(int32_t), e->st));
+  // Tags grow across launches (epoch0, lm0), so the exchange words are cleared only when the epoch counter nears
+  // its range (2^30 layers) and the error words only after a failed launch (they are written only on failure).
+  if (e->mk_epoch > (1u << 30) || e->mk_lm_epoch > (1u << 30)) {
+    CUDA_TRY(e, cudaMemsetAsync(e->mk_xw, 0, e->mk_tagged_words * sizeof(unsigned long long), e->st));
+    e->mk_epoch = e->mk_lm_epoch = 0;
+  }
+  if (e->mk_io_dirty) {
+    CUDA_TRY(e, cudaMemsetAsync(e->mk_io, 0, 8 * sizeof(int32_t), e->st));
+    e->mk_io_dirty = false;
+  }
+  p.epoch0 = e->mk_epoch;
+  p.lm0 = e->mk_lm_epoch;
+  e->mk_io_dirty = true;  // until mk_status reads this launch's error words back clean
+  e->mk_epoch += (uint32_t)steps * (uint32_t)c.layers;
+  e->mk_lm_epoch += (uint32_t)steps;
   void* args[] = {&p};
   CUDA_TRY(e, cudaLaunchCooperativeKernel(e->mk_kernel, dim3(e->mk_ncta), dim3(MK_THREADS), args,
                                           e->mk_smem, e->st));
@@ -644,6 +660,7 @@ int mk_launch(h2c_engine* e, int steps, unsigned long long* trace = nullptr) {
 // After a persistent launch has completed (stream synchronised): turn its error words into a status.
 int mk_status(h2c_engine* e) {
   const int32_t* io = e->mk_io_h;
+  e->mk_io_dirty = io[4] != 0;  // a launch whose status read back clean leaves the error words zero
   if (io[4] != 0)
     return e->fail(H2C_ERR_TIMEOUT, "persistent decode kernel: bounded wait expired (code %d, CTA %d, stage %d)", io[4],
                    io[5], io[6]);
