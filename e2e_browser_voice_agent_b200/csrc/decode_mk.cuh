@@ -93,6 +93,9 @@ struct MkParams {
   unsigned long long* lmw;        // [ncta][2] tagged lm_head partials (value, index)
   unsigned long long* kvdone;     // [ncta] epoch of the last layer whose KV-cache rows this CTA has released
   unsigned long long* rawact;     // [nsplit][32] tagged act values of the split blocks
+  unsigned long long* lcmax;      // [H][ncta rounded up to 4] long-context attention: members' partial score maxes
+  unsigned long long* lce;        // [H][ctx rounded up to 4] long-context attention: exp(s_t - max) per position
+  unsigned long long* lcsum;      // [H] long-context attention: the softmax sum
   int stall_cta;                  // test aid: this CTA never publishes its QKV rows (-1: none), so waits expire
   int nsplit;                     // act blocks beyond one per CTA, computed in 4 pieces of 16 gate/up rows by the
                                   // last 4 nsplit CTAs and quantized by the consumers (0: whole blocks only)
@@ -642,6 +645,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
 
       const size_t cbase = (((size_t)seq * L + l) * KVH + kh) * (size_t)p.ctx * HD;
       const bool staged = head && pos <= p.kv_stage;
+      // long context: more positions than a head CTA stages; every CTA then works on attention (below)
+      const bool lc = pos > p.kv_stage;
       {
         // this layer's norm weights and QKV bias arrive while the layer's inputs are in flight
         for (int i = tid; i < D / 4; i += MK_NT) {
@@ -652,7 +657,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
           const int pidx = pr_lo + (tid >> 1), row = (pidx / half) * HD + pidx % half + (tid & 1) * half;
           cp_async4(bsm + tid, p.bqkv + (size_t)l * QKV + row);
         }
-        if (head && E > p.epoch0 + (uint32_t)L) {
+        if ((head || lc) && E > p.epoch0 + (uint32_t)L) {
           // acquire the KV-cache rows that the k/v owners released at this layer of earlier steps of this launch
           // (rows of earlier launches are ordered by the launch boundary)
           if (tid < ncta) {
@@ -728,7 +733,125 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
       }
       MK_TRACE(trow, 3);
 
-      if (head) {
+      if (lc) {
+        // ---- B' (long context, all CTAs): the CTAs of head hg's group (the head CTA and every non-head CTA j with
+        // (j - H) % H == hg) split the positions for the scores and the head dims for the ordered p.v sums; the
+        // head CTA adds the softmax sum in position order (kernels.c:355-377, same arithmetic and order as B).
+        const int T = pos + 1;
+        const int hg = head ? cta : (cta - H) % H, khg = hg / G;
+        const int gcount = hg < nh ? (nh - 1 - hg) / H + 1 : 0;  // non-head members
+        const int GS = 1 + gcount, gi = head ? 0 : 1 + (cta - H) / H;
+        const int t0 = (int)((long long)gi * T / GS), t1 = (int)((long long)(gi + 1) * T / GS);
+        const int d0 = gi * HD / GS, d1 = (gi + 1) * HD / GS, nd = d1 - d0;
+        const size_t gbase = (((size_t)seq * L + l) * KVH + khg) * (size_t)p.ctx * HD;
+        // per-head rows of the exchange arrays start on 4-word boundaries (read_words reads aligned quads)
+        unsigned long long* lcm = p.lcmax + (size_t)hg * ((ncta + 3) & ~3);
+        unsigned long long* lce = p.lce + (size_t)hg * ((p.ctx + 3) & ~3);
+        float* q_s = outv;
+        float* knew = outv + HD;
+        float* vnew = outv + 2 * HD;
+        read_words(
+            3 * HD,
+            [&](int k) {
+              return k < HD ? p.qw + hg * HD + k
+                            : (k < 2 * HD ? p.kvw + khg * HD + (k - HD) : p.kvw + (KVH + khg) * HD + (k - 2 * HD));
+            },
+            E, [&](int k, uint32_t v) { outv[k] = __uint_as_float(v); }, p, 10 * l + 1, &abort_s);
+        compute_bar();
+        if (abort_s) goto out;
+        if (head) MK_TRACE(trow, 4);
+        const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
+        float mx = -1e30f;
+        for (int t = t0 + tid; t < t1; t += MK_NT) {  // this member's positions
+          float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+          const float4* kr = reinterpret_cast<const float4*>(t == pos ? knew : p.kc + gbase + (size_t)t * HD);
+#pragma unroll 16
+          for (int i = 0; i < HD / 4; i++) {
+            const float4 k4 = t == pos ? kr[i] : __ldcg(kr + i);
+            s0 = __fadd_rn(s0, __fmul_rn(q_s[4 * i], k4.x));
+            s1 = __fadd_rn(s1, __fmul_rn(q_s[4 * i + 1], k4.y));
+            s2 = __fadd_rn(s2, __fmul_rn(q_s[4 * i + 2], k4.z));
+            s3 = __fadd_rn(s3, __fmul_rn(q_s[4 * i + 3], k4.w));
+          }
+          const float v = __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(s0, s1), s2), s3), scale);
+          sc[t] = v;
+          mx = fmaxf(mx, v);
+        }
+        mx = warp_max(mx);
+        if ((tid & 31) == 0) red[tid >> 5] = mx;
+        compute_bar();
+        mx = warp_max(red[tid & (MK_WARPS - 1)]);
+        if (tid == 0) st_relaxed64(lcm + gi, __float_as_uint(mx), E);
+        // the group's max (exact in any order), then exp of this member's positions, published
+        read_words(GS, [&](int k) { return lcm + k; }, E,
+                   [&](int k, uint32_t v) { xf[k] = __uint_as_float(v); }, p, 10 * l + 6, &abort_s);  // (xf is free)
+        compute_bar();
+        if (abort_s) goto out;
+        mx = -1e30f;
+        for (int k = 0; k < GS; k++) mx = fmaxf(mx, xf[k]);
+        for (int t = t0 + tid; t < t1; t += MK_NT) {
+          const float e = fast_exp_ref(__fsub_rn(sc[t], mx));
+          st_relaxed64(lce + t, __float_as_uint(e), E);
+        }
+        // every member collects all T exponentials; the head CTA adds them in position order (kernels.c:368)
+        read_words(T, [&](int k) { return lce + k; }, E,
+                   [&](int k, uint32_t v) { sc[k] = __uint_as_float(v); }, p, 10 * l + 7, &abort_s);
+        compute_bar();
+        if (abort_s) goto out;
+        if (head) {
+          MK_TRACE(trow, 5);
+          if (tid == 0) st_relaxed64(p.lcsum + hg, __float_as_uint(chain_sum(0.f, sc, 1, T)), E);
+        }
+        if (tid == 0) red[16] = __uint_as_float(wait_word(p.lcsum + hg, E, p, 10 * l + 8, &abort_s));
+        compute_bar();
+        if (abort_s) goto out;
+        const float sum = red[16];
+        for (int t = tid; t < T; t += MK_NT) sc[t] = __fdiv_rn(sc[t], sum);
+        compute_bar();
+        if (head) MK_TRACE(trow, 6);
+        // o_d = sum_t p_t v_td in position order for this member's dims. Warps 1-15 form the products p_t v_td of the
+        // next chunk of positions straight from the cache into the staging area (double-buffered) while warp 0's
+        // threads d < nd add the current chunk's products in order: a step of the ordered sum is one add.
+        if (nd > 0) {
+          const int C = (int)((size_t)p.kv_stage * (2 * HD + 4) / (2 * nd));  // positions per chunk
+          float* pb = kst;                                                     // [2][nd][C] products
+          const float* vg = p.vc + gbase + d0;
+          auto make_chunk = [&](int c, int buf) {  // threads 32 ..: eight loads in flight per thread
+            const int ta = c * C, n = (min(pos, ta + C) - ta) * nd;
+            constexpr int U = 8, NL = MK_NT - 32;
+            for (int i0 = tid - 32; i0 < n; i0 += U * NL) {
+              float v[U];
+#pragma unroll
+              for (int u = 0; u < U; u++) {
+                const int i = i0 + u * NL, t = i / nd, dd = i - t * nd;
+                v[u] = i < n ? __ldcg(vg + (size_t)(ta + t) * HD + dd) : 0.f;
+              }
+#pragma unroll
+              for (int u = 0; u < U; u++) {
+                const int i = i0 + u * NL, t = i / nd, dd = i - t * nd;
+                if (i < n) pb[((size_t)buf * nd + dd) * C + t] = __fmul_rn(sc[ta + t], v[u]);
+              }
+            }
+          };
+          const int nch = (pos + C - 1) / C;  // chunks of cached positions 0 .. pos - 1
+          float o = 0.f;
+          if (tid >= 32 && nch > 0) make_chunk(0, 0);
+          for (int c = 0; c < nch; c++) {
+            compute_bar();  // chunk c's products are in place; the other buffer is free
+            if (tid >= 32) {
+              if (c + 1 < nch) make_chunk(c + 1, (c + 1) & 1);
+            } else if (tid < nd) {
+              o = chain_sum(o, pb + ((size_t)(c & 1) * nd + tid) * C, 1, min(pos, c * C + C) - c * C);
+            }
+          }
+          compute_bar();  // the product buffers are free again
+          if (tid < nd) {
+            o = __fadd_rn(o, __fmul_rn(sc[pos], vnew[d0 + tid]));
+            st_relaxed64(p.attw + (size_t)hg * HD + d0 + tid, __float_as_uint(o), E);
+          }
+        }
+        if (head) MK_TRACE(trow, 7);
+      } else if (head) {
         // ---- B: attention of head h over the cache (kernels.c:355-377)
         const int T = pos + 1;
         float* q_s = outv;
@@ -810,7 +933,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
           st_relaxed64(p.attw + (size_t)cta * HD + tid, __float_as_uint(o), E);
         }
         MK_TRACE(trow, 7);
-      } else {
+      }
+      if (!head) {
         // ---- C: O rows with the residual (kernels.c:379-382)
         if (!read_vec(p.attw, E, 10 * l + 2)) goto out;
         MK_TRACE(trow, 8);

@@ -85,7 +85,8 @@ struct h2c_engine {
   MkTile* mk_tiles = nullptr;
   float *mk_attn_norm = nullptr, *mk_ffn_norm = nullptr, *mk_bqkv = nullptr;
   unsigned long long *mk_xw = nullptr, *mk_qw = nullptr, *mk_kvw = nullptr, *mk_attw = nullptr, *mk_actw = nullptr,
-                     *mk_lmw = nullptr, *mk_kvdone = nullptr, *mk_rawact = nullptr;
+                     *mk_lmw = nullptr, *mk_kvdone = nullptr, *mk_rawact = nullptr, *mk_lcmax = nullptr,
+                     *mk_lce = nullptr, *mk_lcsum = nullptr;
   int mk_nsplit = 0;
   uint32_t mk_epoch = 0, mk_lm_epoch = 0;  // tag epochs used by earlier launches
   bool mk_io_dirty = true;                   // error words must be cleared before the next launch
@@ -481,6 +482,8 @@ int mk_build(h2c_engine* e) {
   if (base > budget) return mk_unsupported(e, "context too long for the shared-memory score buffer");
   // K rows are staged with 4 floats of padding (conflict-free dot products), V rows unpadded
   const int kv_stage = (int)std::min<size_t>((size_t)c.ctx, (budget - base) / ((size_t)(2 * HD + 4) * 4));
+  // beyond kv_stage positions attention streams the V columns through the same area: it must hold a few rows
+  if (kv_stage < std::min(16, c.ctx)) return mk_unsupported(e, "context too long for the shared-memory budget");
   const size_t smem = base + (size_t)kv_stage * (2 * HD + 4) * 4;
   // the Qwen2.5-0.5B shape has its own instance with the shape compiled in; other shapes take the generic one
   e->mk_kernel = (D == 896 && F == 4864 && H == 14 && KVH == 2 && HD == 64) ? (void*)k_decode_persistent<896, 4864, 14, 2, 64>
@@ -576,8 +579,10 @@ int mk_build(h2c_engine* e) {
   // tagged-word regions, each starting on a 4-word (32-byte) boundary for the quad reads, plus one spare quad
   auto q4w = [](size_t n) { return (n + 3) & ~(size_t)3; };
   const size_t lm_words = q4w((size_t)ncta * 2), kvd_words = q4w((size_t)ncta);
-  const size_t words = (size_t)D * 3 + (size_t)2 * KVH * HD + (size_t)nbf * MK_ACT_WORDS + lm_words +
-                       kvd_words + (size_t)nsplit * 32 + 4;
+  const size_t raw_words = q4w((size_t)nsplit * 32), lcm_words = (size_t)H * q4w((size_t)ncta),
+               lce_words = (size_t)H * q4w((size_t)c.ctx), lcs_words = q4w((size_t)H);
+  const size_t words = (size_t)D * 3 + (size_t)2 * KVH * HD + (size_t)nbf * MK_ACT_WORDS + lm_words + kvd_words +
+                       raw_words + lcm_words + lce_words + lcs_words + 4;
   unsigned long long* tagged = nullptr;
   if ((r = dalloc_t(e, &e->mk_stream, total)) || (r = dalloc_t(e, &e->mk_tiles, table.size())) ||
       (r = dalloc_t(e, &e->mk_attn_norm, (size_t)NL * D)) || (r = dalloc_t(e, &e->mk_ffn_norm, (size_t)NL * D)) ||
@@ -592,6 +597,9 @@ int mk_build(h2c_engine* e) {
   e->mk_lmw = e->mk_actw + (size_t)nbf * MK_ACT_WORDS;
   e->mk_kvdone = e->mk_lmw + lm_words;
   e->mk_rawact = e->mk_kvdone + kvd_words;
+  e->mk_lcmax = e->mk_rawact + raw_words;
+  e->mk_lce = e->mk_lcmax + lcm_words;
+  e->mk_lcsum = e->mk_lce + lce_words;
   e->mk_nsplit = nsplit;
   e->mk_tagged_words = words;
   CUDA_TRY(e, cudaMemset(tagged, 0, words * sizeof(unsigned long long)));  // epoch 0: nothing published yet
@@ -631,6 +639,7 @@ int mk_launch(h2c_engine* e, int steps, unsigned long long* trace = nullptr) {
   p.xw = e->mk_xw; p.qw = e->mk_qw; p.kvw = e->mk_kvw; p.attw = e->mk_attw; p.actw = e->mk_actw; p.lmw = e->mk_lmw;
   p.kvdone = e->mk_kvdone;
   p.rawact = e->mk_rawact;
+  p.lcmax = e->mk_lcmax; p.lce = e->mk_lce; p.lcsum = e->mk_lcsum;
   p.nsplit = e->mk_nsplit;
   p.err = e->mk_io + 4; p.prm = e->prm; p.toklog = e->toklog; p.next = e->mk_io; p.steps = steps;
   p.timeout_ns = e->mk_timeout_ns;
