@@ -274,10 +274,12 @@ def main():
     if persistent:  # one cooperative launch runs a whole generate call (up to 64 device-chained steps)
         kdesc = "k_decode_persistent (one cooperative launch per 64-step round, 1 CTA per SM)"
         launches = calls
-        d2h = 8 * 4  # next id + status words
+        h2d = 3 * 4  # sequence, position and token id, carried in the launch's parameter block
+        d2h = 5 * 4  # the record CTA 0 writes into mapped host memory: launch number, next id, 3 status words
     else:
         kdesc = f"decode step ({kernels} kernels in one CUDA graph)"
         launches = kernels * steps
+        h2d = 4 * 5  # pass parameters (position, length, sequence, pad, token id)
         d2h = 4
 
     cpu = None
@@ -303,7 +305,7 @@ def main():
                          "bytes_per_step": bytes_step,
                          "traffic": NCU_TRAFFIC_PER_STEP if persistent else None,
                          "traffic_note": "DRAM read+write bytes per decode step, ncu capture of k_decode_persistent"},
-            "e2e": {"value": round(e2e, 2), "unit": UNIT, "h2d_bytes_per_step": 4 * 5, "d2h_bytes_per_step": d2h},
+            "e2e": {"value": round(e2e, 2), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches,
             "clocks": ck,
             "cpu_baseline": cpu,

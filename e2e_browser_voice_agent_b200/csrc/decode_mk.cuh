@@ -101,8 +101,13 @@ struct MkParams {
                                   // last 4 nsplit CTAs and quantized by the consumers (0: whole blocks only)
   int* err;                       // [4]: code, cta, stage, abort flag
   int32_t* prm;                   // pass parameters (P_POS0, P_M, P_SEQ, P_IDS)
+  int arg_seq, arg_pos, arg_tok;  // the first step's sequence, position and token when args_given (else from prm)
+  int args_given;
   int32_t* toklog;                // [seqs][ctx + 1]
   int32_t* next;
+  int32_t* done;                  // optional record in mapped host memory, written by CTA 0 when it finishes:
+                                  // {launch_seq, next token, error code, error CTA, error stage}
+  int32_t launch_seq;
   int steps;
   uint32_t epoch0;                // layer epoch before this launch: tags keep growing across launches, so words of
                                   // earlier launches never read as fresh and need no clearing
@@ -267,6 +272,7 @@ __device__ __forceinline__ void mk_fail(const MkParams& p, int code, int stage) 
     p.err[1] = blockIdx.x;
     p.err[2] = stage;
   }
+  __threadfence();  // the code, CTA and stage words before the abort flag
   atomicExch(p.err + 3, 1);
   __threadfence();
 }
@@ -611,9 +617,9 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
   const int G = H / KVH, kh = head ? cta / G : 0;
   const int kv_pair_lo = H * half, kv_pair_hi = (H + 2 * KVH) * half;  // QKV row pairs of the k and v heads
   const bool my_kv = pr_lo < kv_pair_hi && pr_hi > kv_pair_lo;
-  const int seq = p.prm[P_SEQ];
-  int pos = p.prm[P_POS0];
-  int tok = p.prm[P_IDS];
+  const int seq = p.args_given ? p.arg_seq : p.prm[P_SEQ];
+  int pos = p.args_given ? p.arg_pos : p.prm[P_POS0];
+  int tok = p.args_given ? p.arg_tok : p.prm[P_IDS];
   uint32_t E = p.epoch0;  // layer epoch (grows by one per layer, across launches)
 
 #define MK_TRACE(row, k) \
@@ -1225,6 +1231,17 @@ out:
         if (gtimer() - t0 > p.timeout_ns) break;
     }
   cp_async_wait_all();  // no shared-memory copy may still be in flight when the CTA exits
+  if (p.done && cta == 0 && tid == 0) {
+    // CTA 0 finishes after every CTA has published its last lm_head partial, so the launch's outcome is known:
+    // the host polls this record instead of copying and synchronising
+    volatile int32_t* d = p.done;
+    d[1] = tok;
+    d[2] = ld_volatile_i(p.err);
+    d[3] = ld_volatile_i(p.err + 1);
+    d[4] = ld_volatile_i(p.err + 2);
+    __threadfence_system();
+    d[0] = p.launch_seq;
+  }
   return;
 #undef MK_TRACE
 }

@@ -7,6 +7,7 @@
 #include <cstdio>
 #include <cstring>
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -97,6 +98,9 @@ struct h2c_engine {
   int32_t* mk_io = nullptr;   // device: [0] next token, [4..7] error words
   int* mk_tile_count = nullptr;
   int32_t* mk_io_h = nullptr; // pinned
+  int32_t* mk_done_h = nullptr;  // mapped pinned record CTA 0 writes when a single-token launch finishes
+  int32_t* mk_done_d = nullptr;  // its device alias
+  int32_t mk_launch_seq = 0;
   bool mk_pending = false;    // the last pass of the current forward ran on the persistent kernel
 
   int fail(int code, const char* fmt, ...) {
@@ -604,6 +608,9 @@ int mk_build(h2c_engine* e) {
   e->mk_tagged_words = words;
   CUDA_TRY(e, cudaMemset(tagged, 0, words * sizeof(unsigned long long)));  // epoch 0: nothing published yet
   CUDA_TRY(e, cudaMallocHost(&e->mk_io_h, 8 * sizeof(int32_t)));
+  CUDA_TRY(e, cudaHostAlloc((void**)&e->mk_done_h, 8 * sizeof(int32_t), cudaHostAllocMapped));
+  CUDA_TRY(e, cudaHostGetDevicePointer((void**)&e->mk_done_d, e->mk_done_h, 0));
+  memset(e->mk_done_h, 0, 8 * sizeof(int32_t));
   CUDA_TRY(e, cudaMemcpy(e->mk_tile_count, counts.data(), counts.size() * sizeof(int), cudaMemcpyHostToDevice));
   CUDA_TRY(e, cudaMemcpy(e->mk_stream, stream.data(), total, cudaMemcpyHostToDevice));
   CUDA_TRY(e, cudaMemcpy(e->mk_tiles, table.data(), table.size() * sizeof(MkTile), cudaMemcpyHostToDevice));
@@ -627,7 +634,9 @@ bool use_persistent(h2c_engine* e) {
 }
 
 // Launch `steps` decode steps of the persistent kernel (parameters already in e->prm on the stream).
-int mk_launch(h2c_engine* e, int steps, unsigned long long* trace = nullptr) {
+// args (seq, pos, token) given: the first step's parameters travel in the launch's own parameter block and CTA 0
+// reports the outcome in the mapped host record (mk_wait_done polls it), so no copy is enqueued on either side.
+int mk_launch(h2c_engine* e, int steps, unsigned long long* trace = nullptr, const int32_t* args = nullptr) {
   const h2c_config& c = e->cfg;
   MkParams p{};
   p.D = c.dim; p.F = c.ffn; p.H = c.heads; p.KVH = c.kv_heads; p.HD = e->HD; p.QKV = e->QKV; p.L = c.layers;
@@ -641,7 +650,14 @@ int mk_launch(h2c_engine* e, int steps, unsigned long long* trace = nullptr) {
   p.rawact = e->mk_rawact;
   p.lcmax = e->mk_lcmax; p.lce = e->mk_lce; p.lcsum = e->mk_lcsum;
   p.nsplit = e->mk_nsplit;
-  p.err = e->mk_io + 4; p.prm = e->prm; p.toklog = e->toklog; p.next = e->mk_io; p.steps = steps;
+  p.err = e->mk_io + 4; p.prm = e->prm; p.toklog = e->toklog; p.next = e->mk_io;
+  p.steps = steps;
+  if (args) {
+    p.args_given = 1; p.arg_seq = args[0]; p.arg_pos = args[1]; p.arg_tok = args[2];
+    if (++e->mk_launch_seq <= 0) e->mk_launch_seq = 1;
+    p.done = e->mk_done_d;
+    p.launch_seq = e->mk_launch_seq;
+  }
   p.timeout_ns = e->mk_timeout_ns;
   p.stall_cta = e->mk_stall_cta;
   p.trace = trace;
@@ -660,8 +676,8 @@ int mk_launch(h2c_engine* e, int steps, unsigned long long* trace = nullptr) {
   e->mk_io_dirty = true;  // until mk_status reads this launch's error words back clean
   e->mk_epoch += (uint32_t)steps * (uint32_t)c.layers;
   e->mk_lm_epoch += (uint32_t)steps;
-  void* args[] = {&p};
-  CUDA_TRY(e, cudaLaunchCooperativeKernel(e->mk_kernel, dim3(e->mk_ncta), dim3(MK_THREADS), args,
+  void* kargs[] = {&p};
+  CUDA_TRY(e, cudaLaunchCooperativeKernel(e->mk_kernel, dim3(e->mk_ncta), dim3(MK_THREADS), kargs,
                                           e->mk_smem, e->st));
   return H2C_OK;
 }
@@ -673,6 +689,35 @@ int mk_status(h2c_engine* e) {
   if (io[4] != 0)
     return e->fail(H2C_ERR_TIMEOUT, "persistent decode kernel: bounded wait expired (code %d, CTA %d, stage %d)", io[4],
                    io[5], io[6]);
+  return H2C_OK;
+}
+
+// After a single-token launch with its arguments given: spin on the mapped record CTA 0 writes when the launch's
+// token is known (no device-to-host copy, no stream synchronisation). The spin ends when the record appears or the
+// stream reports the kernel finished (its own waits are bounded), so it cannot outlast the kernel.
+int mk_wait_done(h2c_engine* e, int32_t* next) {
+  volatile int32_t* d = e->mk_done_h;
+  const int32_t want = e->mk_launch_seq;
+  for (unsigned it = 1; d[0] != want; it++) {
+    if (it % 4096) continue;
+    const cudaError_t q = cudaStreamQuery(e->st);
+    if (q == cudaErrorNotReady) continue;
+    if (q != cudaSuccess) return e->fail(H2C_ERR_CUDA, "CUDA: %s", cudaGetErrorString(q));
+    if (d[0] == want) break;
+    // the kernel ended without writing its record (it cannot, short of a fault): read the device words instead
+    CUDA_TRY(e, cudaMemcpy(e->mk_io_h, e->mk_io, 8 * sizeof(int32_t), cudaMemcpyDeviceToHost));
+    int r = mk_status(e);
+    if (r) return r;
+    *next = e->mk_io_h[0];
+    return H2C_OK;
+  }
+  std::atomic_thread_fence(std::memory_order_acquire);
+  const int32_t code = d[2];
+  e->mk_io_dirty = code != 0;
+  if (code)
+    return e->fail(H2C_ERR_TIMEOUT, "persistent decode kernel: bounded wait expired (code %d, CTA %d, stage %d)", code,
+                   d[3], d[4]);
+  *next = d[1];
   return H2C_OK;
 }
 
@@ -701,14 +746,17 @@ int run_forward(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t p
     h[P_SEQ] = seq;
     h[3] = 0;
     memcpy(h + P_IDS, ids + c0, sizeof(int32_t) * mlen);
-    CUDA_TRY(e, cudaMemcpyAsync(e->prm, h, sizeof(int32_t) * (P_IDS + mlen), cudaMemcpyHostToDevice, e->st));
     if (mlen == 1 && !pf) {
       if (e->decode_mode != H2C_DECODE_GRAPH && (r = mk_build(e))) return r;
-      if (use_persistent(e)) {
-        if ((r = mk_launch(e, 1))) return r;
+      if (use_persistent(e)) {  // the token's parameters travel with the launch: nothing to copy first
+        const int32_t args[3] = {seq, pos + c0, ids[c0]};
+        if ((r = mk_launch(e, 1, nullptr, args))) return r;
         e->mk_pending = true;
         continue;
       }
+    }
+    CUDA_TRY(e, cudaMemcpyAsync(e->prm, h, sizeof(int32_t) * (P_IDS + mlen), cudaMemcpyHostToDevice, e->st));
+    if (mlen == 1 && !pf) {
       if (!e->gexec) {
         r = build_graph(e);
         if (r) return r;
@@ -899,10 +947,7 @@ int h2c_forward(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t p
     if (e->mk_pending && (r = mk_status(e))) return r;
     *next = sample_host(lg.data(), e->cfg.vocab, temperature, sseed);
   } else if (e->mk_pending) {
-    CUDA_TRY(e, cudaMemcpyAsync(e->mk_io_h, e->mk_io, 8 * sizeof(int32_t), cudaMemcpyDeviceToHost, e->st));
-    CUDA_TRY(e, cudaStreamSynchronize(e->st));
-    if ((r = mk_status(e))) return r;
-    *next = e->mk_io_h[0];
+    if ((r = mk_wait_done(e, next))) return r;
   } else {
     CUDA_TRY(e, cudaMemcpyAsync(e->next_h, e->next_d, 4, cudaMemcpyDeviceToHost, e->st));
     CUDA_TRY(e, cudaStreamSynchronize(e->st));
@@ -1085,6 +1130,7 @@ int h2c_destroy(h2c_engine* e) {
   for (void* p : e->dallocs) cudaFree(p);
   if (e->prm_h) cudaFreeHost(e->prm_h);
   if (e->mk_io_h) cudaFreeHost(e->mk_io_h);
+  if (e->mk_done_h) cudaFreeHost(e->mk_done_h);
   if (e->next_h) cudaFreeHost(e->next_h);
   if (e->ev0) cudaEventDestroy(e->ev0);
   if (e->ev1) cudaEventDestroy(e->ev1);
