@@ -24,7 +24,7 @@ PROFILE_NAMES = ["embed", "norm+quantize", "matvec qkv", "rope+kv", "attention",
 # the exported symbols of include/h2cuda.h
 EXPORTS = ["h2c_create", "h2c_set_tensor", "h2c_forward", "h2c_generate", "h2c_decode_kernels", "h2c_set_decode_mode",
            "h2c_decode_path", "h2c_trace_decode", "h2c_decode_ctas", "h2c_set_decode_fault", "h2c_read_logits",
-           "h2c_profile", "h2c_destroy",
+           "h2c_profile", "h2c_destroy", "h2c_selftest_math",
            "h2c_last_error", "h2c_device_bytes", "h2c_q4_matrix_bytes", "h2c_q4_pack", "h2c_q4_matvec_scratch_bytes",
            "h2c_q4_matvec", "h2c_q4_matvec_noalloc"]
 
@@ -63,6 +63,7 @@ def load(path: str = LIB_PATH) -> C.CDLL:
     L.h2c_trace_decode.argtypes = [p, C.c_int, i32, i32, i32, p, i64]
     L.h2c_decode_ctas.argtypes = [p]
     L.h2c_set_decode_fault.argtypes = [p, C.c_int, i64]
+    L.h2c_selftest_math.argtypes = [C.c_int, p]
     L.h2c_read_logits.argtypes = [p, C.c_int, p, i64]
     L.h2c_profile.argtypes = [p, C.c_int, p, i32, i32, C.POINTER(C.c_double)]
     L.h2c_destroy.argtypes = [p]
@@ -79,7 +80,7 @@ def load(path: str = LIB_PATH) -> C.CDLL:
     L.h2c_q4_matvec_noalloc.argtypes = [p, i32, i32, p, i32, p, i32, p, p]
     for name in ("h2c_create", "h2c_set_tensor", "h2c_forward", "h2c_generate", "h2c_decode_kernels", "h2c_set_decode_mode",
                  "h2c_decode_path", "h2c_trace_decode", "h2c_decode_ctas", "h2c_set_decode_fault", "h2c_read_logits",
-                 "h2c_profile",
+                 "h2c_profile", "h2c_selftest_math",
                  "h2c_destroy", "h2c_q4_pack", "h2c_q4_matvec", "h2c_q4_matvec_noalloc"):
         getattr(L, name).restype = C.c_int
     _lib = L

@@ -170,8 +170,8 @@ __device__ __forceinline__ float mk_lane_chain(const uint8_t* tile, int R, int n
 // quant_block_redux, stored per lane
 __device__ __forceinline__ void mk_quant_chain(float v, int lane, int b, int nbp, const MkX& x) {
   const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v))));
-  const float dd = __fdiv_rn(amax, 127.0f);
-  const float id = dd != 0.0f ? __fdiv_rn(1.0f, dd) : 0.0f;
+  const float dd = block_scale(amax);
+  const float id = block_iscale(dd);
   const int qi = max(-128, min(127, __float2int_rn(__fmul_rn(v, id))));
   const int pos = (lane & 16) | invperm16(lane & 15);  // byte of the permuted block (word pos / 4)
   int8_t* dst = reinterpret_cast<int8_t*>(pos < 16 ? x.x0 : x.x1);
@@ -359,31 +359,39 @@ __device__ __forceinline__ void read_words(int count, Src src, uint32_t tag, Sin
 
 // ---------------------------------------------------------------- shared building blocks
 
-// s = ((s + p[0]) + p[stride]) + ... over n terms in order. The shared-memory loads of the next 16 terms issue
-// before the adds of the current 16, so a step costs one add latency, not a load latency.
+// s = ((s + p[0]) + p[stride]) + ... over n terms in order. Two 16-register buffers alternate: the shared-memory
+// loads of the next 16 terms issue before the adds of the current 16, so a step costs one add latency, not a load
+// latency (and no register moves between the buffers).
 __device__ __forceinline__ float chain_sum(float s, const float* p, int stride, int n) {
-  float a[16], nx[16];
-  const int n16 = n & ~15;
-  if (n16) {
+  float a[16], b[16];
+  const int n32 = n & ~31;
+  if (n32) {
 #pragma unroll
     for (int u = 0; u < 16; u++) a[u] = p[u * stride];
-    for (int k = 16; k < n16; k += 16) {
+    for (int k = 0; k < n32; k += 32) {
 #pragma unroll
-      for (int u = 0; u < 16; u++) nx[u] = p[(k + u) * stride];
+      for (int u = 0; u < 16; u++) b[u] = p[(k + 16 + u) * stride];
 #pragma unroll
       for (int u = 0; u < 16; u++) s = __fadd_rn(s, a[u]);
+      if (k + 32 < n32) {
 #pragma unroll
-      for (int u = 0; u < 16; u++) a[u] = nx[u];
+        for (int u = 0; u < 16; u++) a[u] = p[(k + 32 + u) * stride];
+      }
+#pragma unroll
+      for (int u = 0; u < 16; u++) s = __fadd_rn(s, b[u]);
     }
-#pragma unroll
-    for (int u = 0; u < 16; u++) s = __fadd_rn(s, a[u]);
   }
-  const int rem = n - n16;
+  const int rem = n - n32;  // 0..31 trailing terms
 #pragma unroll
-  for (int u = 0; u < 16; u++) a[u] = u < rem ? p[(n16 + u) * stride] : 0.f;
+  for (int u = 0; u < 16; u++) a[u] = u < rem ? p[(n32 + u) * stride] : 0.f;
+#pragma unroll
+  for (int u = 0; u < 16; u++) b[u] = u + 16 < rem ? p[(n32 + 16 + u) * stride] : 0.f;
 #pragma unroll
   for (int u = 0; u < 16; u++)
     if (u < rem) s = __fadd_rn(s, a[u]);
+#pragma unroll
+  for (int u = 0; u < 16; u++)
+    if (u + 16 < rem) s = __fadd_rn(s, b[u]);
   return s;
 }
 
@@ -393,8 +401,8 @@ __device__ __forceinline__ float chain_sum(float s, const float* p, int stride, 
 __device__ __forceinline__ void mk_quant_chain2(float v0, float v1, int lane, int b0, int b1, int nbp, const MkX& x) {
   const unsigned m0 = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v0)));
   const unsigned m1 = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v1)));
-  const float d0 = __fdiv_rn(__uint_as_float(m0), 127.0f), d1 = __fdiv_rn(__uint_as_float(m1), 127.0f);
-  const float i0 = d0 != 0.0f ? __fdiv_rn(1.0f, d0) : 0.0f, i1 = d1 != 0.0f ? __fdiv_rn(1.0f, d1) : 0.0f;
+  const float d0 = block_scale(__uint_as_float(m0)), d1 = block_scale(__uint_as_float(m1));
+  const float i0 = block_iscale(d0), i1 = block_iscale(d1);
   const int q0 = max(-128, min(127, __float2int_rn(__fmul_rn(v0, i0))));
   const int q1 = max(-128, min(127, __float2int_rn(__fmul_rn(v1, i1))));
   const int pos = (lane & 16) | invperm16(lane & 15);
@@ -435,8 +443,9 @@ __device__ __forceinline__ void mk_quant_blocks(int nblk, Fn f, const MkX& x) {
 }
 
 // RMSNorm of xf[0..D) (shared) into int8 blocks xq/xd/xs (shared), the reference's lane order (kernels.c:80-114):
-// the squares are formed by all threads into sq (shared, D floats), then thread l < 4 adds sq[4k + l] over k in
-// order and ((l0 + l1) + l2) + l3 combines the four chains.
+// the squares are formed by all threads into sq (shared, D floats), then thread 32 + l (warp 1, so that thread 0
+// can issue weight copies meanwhile) adds sq[4k + l] over k in order and ((l0 + l1) + l2) + l3 combines the four
+// chains.
 __device__ __forceinline__ void mk_norm_quant(const float* xf, const float* w, int D, float eps, const MkX& x, float* red,
                                               float* sq, bool have_sq = false) {
   const int tid = threadIdx.x;
@@ -444,10 +453,11 @@ __device__ __forceinline__ void mk_norm_quant(const float* xf, const float* w, i
     for (int i = tid; i < D; i += MK_NT) sq[i] = __fmul_rn(xf[i], xf[i]);
     compute_bar();
   }
-  if (tid < 4) red[tid] = chain_sum(0.f, sq + tid, 4, D / 4);
+  if (tid >= 32 && tid < 36) red[tid - 32] = chain_sum(0.f, sq + (tid - 32), 4, D / 4);
   compute_bar();
   const float ss = __fadd_rn(__fadd_rn(__fadd_rn(red[0], red[1]), red[2]), red[3]);
-  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), eps)));
+  const float mean = D == 896 ? div896_rn(ss) : __fdiv_rn(ss, (float)D);
+  const float r = rcp_rn(sqrt_rn(__fadd_rn(mean, eps)));
   mk_quant_blocks(D / 32, [&](int i) { return __fmul_rn(__fmul_rn(xf[i], r), w[i]); }, x);
 }
 

@@ -1262,3 +1262,36 @@ extern "C" int h2c_q4_matvec_noalloc(const void* w, int32_t n_rows, int32_t k, c
   }
   return h2c_q4_matvec(w, n_rows, k, x, m, y, op, bias, scratch, stream);
 }
+
+// ---------------------------------------------------------------- self-test of the fast correctly rounded forms
+
+namespace {
+__global__ void k_selftest_math(unsigned long long* bad) {
+  unsigned long long n[4] = {0, 0, 0, 0};
+  const uint64_t step = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (1ull << 32); i += step) {
+    const float x = __uint_as_float((uint32_t)i);
+    n[0] += __float_as_uint(h2::div127_rn(x)) != __float_as_uint(__fdiv_rn(x, 127.0f));
+    n[1] += __float_as_uint(h2::div896_rn(x)) != __float_as_uint(__fdiv_rn(x, 896.0f));
+    n[2] += __float_as_uint(h2::rcp_rn(x)) != __float_as_uint(__fdiv_rn(1.0f, x));
+    n[3] += __float_as_uint(h2::sqrt_rn(x)) != __float_as_uint(__fsqrt_rn(x));
+  }
+  for (int k = 0; k < 4; k++)
+    if (n[k]) atomicAdd(bad + k, n[k]);
+}
+}  // namespace
+
+extern "C" int h2c_selftest_math(int device, uint64_t* mismatches) {
+  if (!mismatches) return H2C_ERR_INVALID;
+  if (cudaSetDevice(device) != cudaSuccess) return H2C_ERR_CUDA;
+  unsigned long long* d = nullptr;
+  if (cudaMalloc(&d, 4 * sizeof(unsigned long long)) != cudaSuccess) return H2C_ERR_NO_MEMORY;
+  cudaError_t c = cudaMemset(d, 0, 4 * sizeof(unsigned long long));
+  if (c == cudaSuccess) {
+    k_selftest_math<<<148 * 8, 256>>>(d);
+    c = cudaGetLastError();
+  }
+  if (c == cudaSuccess) c = cudaMemcpy(mismatches, d, 4 * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+  cudaFree(d);
+  return c == cudaSuccess ? H2C_OK : H2C_ERR_CUDA;
+}

@@ -66,6 +66,56 @@ __device__ __forceinline__ float hsum4_quad(float a) {
   return __fadd_rn(__fadd_rn(__fadd_rn(a, a1), a2), a3);
 }
 
+// Correctly rounded division by 127, division by 896 (the 0.5B hidden size), reciprocal and square root for the
+// latency-critical chains of the decode kernel (RMSNorm scale, int8 block scales). Each uses a short published
+// method inside an input range where a comparison with the IEEE-rounded intrinsics over every float of the range
+// found no difference on B200 (h2c_selftest_math repeats that comparison over all 2^32 inputs, fallbacks included),
+// and the intrinsic itself outside the range; so every result equals the intrinsic's, about 8-25 cycles instead of
+// 60-70 on the dependent path.
+//  - x / y with the divisor known in advance (N. Brisebarre, J.-M. Muller, S. K. Raina, "Accelerating correctly
+//    rounded floating-point division when the divisor is known in advance", IEEE Trans. Computers 53(8), 2004):
+//    zh = RN(1/y), zl = RN(1/y - zh), q = RN(x zh + RN(x zl)); exact here for x >= 2^-100.
+//  - 1/b and sqrt(a) (P. W. Markstein, "Computation of elementary functions on the IBM RISC System/6000
+//    processor", IBM J. Res. Dev. 34(1), 1990): the hardware approximation refined by one Newton step whose residual
+//    (1 - b y, resp. a - s^2) is exact through a fused multiply-add; exact here for normal b < 2^126, resp.
+//    a >= 2^-102.
+constexpr float H2_R127_HI = (float)(1.0 / 127.0);
+constexpr float H2_R127_LO = (float)((1.0 - 127.0 * (double)H2_R127_HI) / 127.0);
+constexpr float H2_R896_HI = (float)(1.0 / 896.0);
+constexpr float H2_R896_LO = (float)((1.0 - 896.0 * (double)H2_R896_HI) / 896.0);
+__device__ __forceinline__ float div127_rn(float x) {
+  const unsigned b = __float_as_uint(x);
+  if (b >= 0x0D800000u && b < 0x7F800000u) return __fmaf_rn(x, H2_R127_HI, __fmul_rn(x, H2_R127_LO));
+  return __fdiv_rn(x, 127.0f);
+}
+__device__ __forceinline__ float div896_rn(float x) {
+  const unsigned b = __float_as_uint(x);
+  if (b >= 0x0D800000u && b < 0x7F800000u) return __fmaf_rn(x, H2_R896_HI, __fmul_rn(x, H2_R896_LO));
+  return __fdiv_rn(x, 896.0f);
+}
+__device__ __forceinline__ float rcp_rn(float b) {
+  const unsigned u = __float_as_uint(b);
+  if (u >= 0x00800000u && u <= 0x7E800000u) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(b));
+    return __fmaf_rn(__fmaf_rn(-b, y, 1.0f), y, y);
+  }
+  return __fdiv_rn(1.0f, b);
+}
+__device__ __forceinline__ float sqrt_rn(float a) {
+  const unsigned u = __float_as_uint(a);
+  if (u >= 0x0C800000u && u < 0x7F800000u) {
+    float r;
+    asm("rsqrt.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(a));
+    const float s = __fmul_rn(a, r);
+    return __fmaf_rn(__fmaf_rn(-s, s, a), __fmul_rn(0.5f, r), s);
+  }
+  return __fsqrt_rn(a);
+}
+// the int8 block scale and its reciprocal: d = amax / 127, id = d ? 1 / d : 0 (kernels.c:96-97)
+__device__ __forceinline__ float block_scale(float amax) { return div127_rn(amax); }
+__device__ __forceinline__ float block_iscale(float d) { return d != 0.0f ? rcp_rn(d) : 0.0f; }
+
 // Integers |p| < 2^22 converted to float without the (quarter-rate) int->float instruction: the bit pattern
 // MK_MAGIC + p is the float 12582912 + p exactly, and subtracting 12582912 is exact. Block dots carry MK_MAGIC in
 // their accumulator, so f32(p) = __int_as_float(acc) - 12582912.0f.
@@ -102,8 +152,8 @@ __device__ __forceinline__ void quant_block_warp(float v, int lane, int8_t* q, f
 // word, 2 and 3 in the other. Bit-identical to quant_block_warp.
 __device__ __forceinline__ void quant_block_redux(float v, int lane, int8_t* q, float* d, int4* s) {
   const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v))));
-  const float dd = __fdiv_rn(amax, 127.0f);
-  const float id = dd != 0.0f ? __fdiv_rn(1.0f, dd) : 0.0f;
+  const float dd = block_scale(amax);
+  const float id = block_iscale(dd);
   const int qi = max(-128, min(127, __float2int_rn(__fmul_rn(v, id))));
   q[(lane & 16) | invperm16(lane & 15)] = (int8_t)qi;
   const int dl = (lane & 7) >> 1;  // the dot lane that owns this element

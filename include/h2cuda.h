@@ -125,6 +125,12 @@ int h2c_decode_ctas(h2c_engine* e);
  * of the KV cache must be recomputed). stall_cta = -1 restores normal operation. No fault, trap or hang. */
 int h2c_set_decode_fault(h2c_engine* e, int stall_cta, int64_t timeout_ns);
 
+/* Self-test of the decode kernels' correctly rounded arithmetic (no reference counterpart): compares the fast
+ * division by 127 and by 896, reciprocal and square root used on the quantization and RMSNorm paths with CUDA's
+ * IEEE-rounded __fdiv_rn / __fsqrt_rn over all 2^32 float bit patterns on `device` and writes the four mismatch
+ * counts (all 0 when the fast forms are exact on this GPU) to mismatches[0..3]. */
+int h2c_selftest_math(int device, uint64_t* mismatches);
+
 /* Number of kernels one decode step launches (the kernel nodes of the decode-step CUDA graph); < 0 on error. */
 int h2c_decode_kernels(h2c_engine* e);
 

@@ -321,3 +321,12 @@ def test_q4_matvec_microbench(N, K, M):
         ref = O.matvec_q4(blocks, N, K, x, op=op, bias=bias if op == 1 else None, y=y0, nth=8)
         got = y.cpu().numpy()
         assert np.array_equal(bits(got), bits(ref)), f"op {op}: {rel_err(got, ref):.3g}"
+
+
+def test_fast_correctly_rounded_math_is_exact():
+    """The decode kernel's fast division by 127 and 896, reciprocal and square root (RMSNorm scale, int8 block
+    scales) must equal CUDA's IEEE-rounded __fdiv_rn / __fsqrt_rn on every one of the 2^32 float inputs."""
+    L = _lib.load()
+    out = (C.c_uint64 * 4)()
+    assert L.h2c_selftest_math(0, out) == 0
+    assert list(out) == [0, 0, 0, 0], f"mismatches (x/127, x/896, 1/x, sqrt x): {list(out)}"
