@@ -22,7 +22,7 @@ from __future__ import annotations
 
 import ctypes as C
 import time
-from typing import Dict, Optional, Sequence
+from typing import Dict, List, Optional, Sequence
 
 import numpy as np
 
@@ -110,6 +110,49 @@ class CudaBackend:
         if want_logits or self.keep_logits:
             self._last_logits[seq] = self._read(seq)
         return int(self._next.value)
+
+    def forward_batch(self, seqs: Sequence[int], ids: Sequence[int], pos: Sequence[int], temperature: float = 0.0,
+                      seed: int = 1, want_logits: bool = False) -> List[int]:
+        """One decode step of several sessions at once: token ids[m] of sequence seqs[m] at position pos[m];
+        returns each session's next token (the same tokens and logits as separate forward calls)."""
+        if self._h is None:
+            raise RuntimeError("backend destroyed")
+        s = np.ascontiguousarray(np.asarray(seqs, dtype=np.int32).reshape(-1))
+        t = np.ascontiguousarray(np.asarray(ids, dtype=np.int32).reshape(-1))
+        p = np.ascontiguousarray(np.asarray(pos, dtype=np.int32).reshape(-1))
+        if not (s.size == t.size == p.size) or s.size == 0:
+            raise ValueError("seqs, ids and pos must have the same non-zero length")
+        if int(p.max()) + 1 >= self.ctx:
+            raise RuntimeError("context full")
+        out = np.empty(s.size, dtype=np.int32)
+        rc = self._L.h2c_forward_batch(self._h, int(s.size), s.ctypes.data, t.ctypes.data, p.ctypes.data,
+                                       float(temperature), int(seed) & 0xFFFFFFFF, out.ctypes.data)
+        if rc == _lib.ERR_CONTEXT_FULL:
+            raise RuntimeError("context full")
+        _lib.check(rc, self._h)
+        self._last_logits = {}
+        if want_logits or self.keep_logits:
+            for q in s.tolist():
+                self._last_logits[q] = self._read(q)
+        return out.tolist()
+
+    def generate_batch(self, seqs: Sequence[int], ids: Sequence[int], pos: Sequence[int], steps: int):
+        """Greedy decode of `steps` tokens of every session on the device (batched steps chained without the
+        host). Returns ([n][steps] token array, device milliseconds)."""
+        s = np.ascontiguousarray(np.asarray(seqs, dtype=np.int32).reshape(-1))
+        t = np.ascontiguousarray(np.asarray(ids, dtype=np.int32).reshape(-1))
+        p = np.ascontiguousarray(np.asarray(pos, dtype=np.int32).reshape(-1))
+        if not (s.size == t.size == p.size) or s.size == 0:
+            raise ValueError("seqs, ids and pos must have the same non-zero length")
+        out = np.empty((s.size, int(steps)), dtype=np.int32)
+        ms = C.c_float()
+        rc = self._L.h2c_generate_batch(self._h, int(s.size), s.ctypes.data, t.ctypes.data, p.ctypes.data, int(steps),
+                                        out.ctypes.data, C.byref(ms))
+        if rc == _lib.ERR_CONTEXT_FULL:
+            raise RuntimeError("context full")
+        _lib.check(rc, self._h)
+        self._last_logits = {}
+        return out, float(ms.value)
 
     def _read(self, seq: int) -> np.ndarray:
         out = np.empty(self.cfg["vocab"], dtype=np.float32)

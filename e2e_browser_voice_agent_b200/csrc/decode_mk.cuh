@@ -189,7 +189,6 @@ __device__ __forceinline__ void mk_quant_chain(float v, int lane, int b, int nbp
 }
 
 // ---------------------------------------------------------------- PTX helpers
-__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 __device__ __forceinline__ void mbar_init(uint64_t* b, unsigned count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count));
 }
@@ -213,11 +212,6 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned by
                "l"(src), "r"(bytes), "r"(smem_u32(bar))
                : "memory");
 }
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 __device__ __forceinline__ unsigned long long gtimer() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
@@ -243,9 +237,6 @@ __device__ __forceinline__ void ld_relaxed64x4(const unsigned long long* p, unsi
 __device__ __forceinline__ void st_relaxed64(unsigned long long* p, uint32_t payload, uint32_t tag) {
   const unsigned long long v = ((unsigned long long)tag << 32) | payload;
   asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
 __device__ __forceinline__ void st_release64(unsigned long long* p, uint32_t payload, uint32_t tag) {
   const unsigned long long v = ((unsigned long long)tag << 32) | payload;
@@ -536,14 +527,16 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
   // results are exchanged; so inside the layers the refills wait for the start of the next RMSNorm, which reads no
   // global memory, or for a stage that finds its tile not yet issued. The lm_head refills as soon as a slot frees.
   int tile_i = 0;    // tiles consumed (every thread)
+  int tpos = 0;      // tile_i % my_count: table entry of the next tile to consume
   int issued = 0;    // tiles issued (thread 0)
+  int ipos = 0;      // issued % my_count (thread 0)
   bool pace = false; // thread 0: defer refills to the next RMSNorm
   auto refill = [&]() {  // thread 0: issue every tile whose slot is free
     const int lim = min(total_tiles, tile_i + MK_NSLOT);
     if (issued < lim) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     while (issued < lim) {
       const int s = issued % MK_NSLOT;
-      const MkTile t = tsm[issued % my_count];
+      const MkTile t = tsm[ipos];
       if (t.bytes == 0 || t.bytes > MK_SLOT || (t.bytes & 15) || (t.off & 15)) {
         mk_fail(p, MK_ABORTED, -2);
         abort_s = 1;
@@ -552,6 +545,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
       mbar_expect_tx(&full[s], t.bytes);
       bulk_g2s(ring + (size_t)s * MK_SLOT, p.stream + t.off, t.bytes, &full[s]);
       issued++;
+      if (++ipos == my_count) ipos = 0;
     }
   };
   if (tid == 0) refill();
@@ -563,7 +557,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
     if (tid == 0) {
       for (int h = 0; h < n && !abort_s; h++) {
         const int ti = tile_i + h;
-        const MkTile t = tsm[ti % my_count];
+        const MkTile t = tsm[tpos + h < my_count ? tpos + h : tpos + h - my_count];
         if (ti >= issued) refill();  // not issued yet: refill now
         if (t.rows != (h ? rows1 : rows0) || t.nb != nb) {
           mk_fail(p, MK_ABORTED, stage);
@@ -580,6 +574,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
   auto release_tiles = [&](int n) {
     compute_bar();
     tile_i += n;
+    tpos += n;
+    while (tpos >= my_count) tpos -= my_count;
     if (tid == 0 && !pace) refill();
   };
   // n chain tiles at once (tile h on warps 8h .. 8h + 7, thread (r, l) = (t / 4, t % 4)); row r of tile h lands in

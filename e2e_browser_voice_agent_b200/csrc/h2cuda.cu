@@ -59,7 +59,7 @@ struct h2c_engine {
   float* am_v = nullptr;
   int* am_i = nullptr;
   int am_np = 0;
-  int32_t* prm = nullptr;      // device params [P_IDS + max_chunk]
+  int32_t* prm = nullptr;      // device params [P_WORDS]
   int32_t* next_d = nullptr;   // device next token
   int32_t* toklog = nullptr;   // device token log [max_seqs][ctx + 1]
   int graph_kernels = 0;       // kernel nodes in the decode-step graph
@@ -70,6 +70,15 @@ struct h2c_engine {
   cudaStream_t st = nullptr;
   cudaGraphExec_t gexec = nullptr;
   cudaGraph_t graph = nullptr;
+  // batched decode steps (h2c_forward_batch): logits of every token, per-token argmax partials, the tokens, and
+  // one CUDA graph per batch size
+  float* logits_b = nullptr;
+  float* am_vb = nullptr;
+  int* am_ib = nullptr;
+  int32_t* next_b = nullptr;
+  int32_t* prm_bh = nullptr;   // pinned [P_WORDS]
+  int32_t* next_bh = nullptr;  // pinned [P_CAP]
+  std::vector<cudaGraphExec_t> bexec;
   std::string err;
   int64_t dev_bytes = 0;
   std::vector<void*> dallocs;
@@ -218,8 +227,8 @@ int upload_f32(h2c_engine* e, float** p, int64_t count, const void* data, uint64
 
 // ---------------------------------------------------------------- launch helpers
 
-// Launch shapes: decode (M == 1) uses 32-row tiles (16 for long rows, to bound shared memory); prefill runs
-// sub-batches of up to 4 tokens on 8-row tiles.
+// Launch shapes: one token (the graph decode step) runs k_matvec on 32-row tiles (16 for long rows, to bound
+// shared memory); passes of several tokens run k_matmul (below).
 template <int WT, int ROWS, int MB>
 void launch_mv_t(int op, const uint8_t* qs, const __half* d, int N, int K, const int8_t* xq, const float* xd,
                  const int4* xs, int M, float* y, int ldy, const float* bias, cudaStream_t st) {
@@ -228,6 +237,37 @@ void launch_mv_t(int op, const uint8_t* qs, const __half* d, int N, int K, const
   if (op == OP_STORE) k_matvec<WT, ROWS, MB, OP_STORE><<<blocks, 256, smem, st>>>(qs, d, N, K, xq, xd, xs, M, y, ldy, bias);
   else if (op == OP_BIAS) k_matvec<WT, ROWS, MB, OP_BIAS><<<blocks, 256, smem, st>>>(qs, d, N, K, xq, xd, xs, M, y, ldy, bias);
   else k_matvec<WT, ROWS, MB, OP_ADD><<<blocks, 256, smem, st>>>(qs, d, N, K, xq, xd, xs, M, y, ldy, bias);
+}
+
+// Several tokens (prompt chunks, batched decode steps): k_matmul with token groups of 32, 16 or 8 (the largest whose
+// activations fit next to the weight ring) and row ranges that give about two CTAs per SM.
+constexpr size_t MM_SMEM = 160 * 1024;
+template <int WT, int TG, int RT>
+size_t mm_smem(int nb) { return (size_t)mm_act_bytes(TG, nb) + 2 * (size_t)mm_chunk_bytes(WT, (256 / (4 * TG)) * RT); }
+
+template <int WT, int TG, int RT>
+void launch_mm_t(int op, const uint8_t* qs, const __half* d, int N, int K, const int8_t* xq, const float* xd,
+                 const int4* xs, int M, float* y, int ldy, const float* bias, cudaStream_t st) {
+  constexpr int SR = (256 / (4 * TG)) * RT;
+  const int ntg = (M + TG - 1) / TG;
+  const int nrr = std::max(1, 2 * 148 / ntg);
+  const int rows = (int)align_up((size_t)((N + nrr - 1) / nrr), SR);
+  const int grid = ntg * ((N + rows - 1) / rows);
+  const size_t smem = mm_smem<WT, TG, RT>(K / 32);
+  if (op == OP_STORE) k_matmul<WT, TG, RT, OP_STORE><<<grid, 256, smem, st>>>(qs, d, N, K, xq, xd, xs, M, rows, y, ldy, bias);
+  else if (op == OP_BIAS) k_matmul<WT, TG, RT, OP_BIAS><<<grid, 256, smem, st>>>(qs, d, N, K, xq, xd, xs, M, rows, y, ldy, bias);
+  else k_matmul<WT, TG, RT, OP_ADD><<<grid, 256, smem, st>>>(qs, d, N, K, xq, xd, xs, M, rows, y, ldy, bias);
+}
+
+// 8 rows per thread when the matrix is tall enough to keep every SM busy with them, else 2
+template <int WT, int TG>
+void launch_mm(int op, const uint8_t* qs, const __half* d, int N, int K, const int8_t* xq, const float* xd,
+               const int4* xs, int M, float* y, int ldy, const float* bias, cudaStream_t st) {
+  const int ntg = (M + TG - 1) / TG;
+  if ((size_t)N * ntg >= (size_t)2 * 148 * (256 / (4 * TG)) * 8)
+    launch_mm_t<WT, TG, 8>(op, qs, d, N, K, xq, xd, xs, M, y, ldy, bias, st);
+  else
+    launch_mm_t<WT, TG, 2>(op, qs, d, N, K, xq, xd, xs, M, y, ldy, bias, st);
 }
 
 template <int WT>
@@ -239,17 +279,12 @@ void matvec_w(int op, const uint8_t* qs, const __half* d, int N, int K, const in
     else launch_mv_t<WT, 16, 1>(op, qs, d, N, K, xq, xd, xs, 1, y, ldy, bias, st);
     return;
   }
-  if ((size_t)8 * 4 * nb * 16 > 200 * 1024) {  // very long rows: one token per launch
-    for (int m0 = 0; m0 < M; m0++)
-      launch_mv_t<WT, 16, 1>(op, qs, d, N, K, xq + (size_t)m0 * K, xd + (size_t)m0 * nb, xs + (size_t)m0 * nb, 1,
-                             y + (size_t)m0 * ldy, ldy, bias, st);
-    return;
-  }
-  for (int m0 = 0; m0 < M; m0 += 4) {
-    const int mm = M - m0 < 4 ? M - m0 : 4;
-    launch_mv_t<WT, 8, 4>(op, qs, d, N, K, xq + (size_t)m0 * K, xd + (size_t)m0 * nb, xs + (size_t)m0 * nb, mm,
-                          y + (size_t)m0 * ldy, ldy, bias, st);
-  }
+  if (M > 16 && mm_smem<WT, 32, 8>(nb) <= MM_SMEM) return launch_mm<WT, 32>(op, qs, d, N, K, xq, xd, xs, M, y, ldy, bias, st);
+  if (M > 8 && mm_smem<WT, 16, 8>(nb) <= MM_SMEM) return launch_mm<WT, 16>(op, qs, d, N, K, xq, xd, xs, M, y, ldy, bias, st);
+  if (mm_smem<WT, 8, 8>(nb) <= MM_SMEM) return launch_mm<WT, 8>(op, qs, d, N, K, xq, xd, xs, M, y, ldy, bias, st);
+  for (int m0 = 0; m0 < M; m0++)  // rows too long for a staged token group: one token per launch
+    launch_mv_t<WT, 16, 1>(op, qs, d, N, K, xq + (size_t)m0 * K, xd + (size_t)m0 * nb, xs + (size_t)m0 * nb, 1,
+                           y + (size_t)m0 * ldy, ldy, bias, st);
 }
 
 void matvec(int op, const Q4Mat& W, const int8_t* xq, const float* xd, const int4* xs, int M, float* y, int ldy,
@@ -266,14 +301,33 @@ cudaError_t mv_attr(int max_smem) {
   return c;
 }
 
+template <int WT, int TG, int RT>
+cudaError_t mm_attr() {
+  const int smem = (int)MM_SMEM;
+  cudaError_t c = cudaFuncSetAttribute(k_matmul<WT, TG, RT, OP_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (c == cudaSuccess) c = cudaFuncSetAttribute(k_matmul<WT, TG, RT, OP_BIAS>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (c == cudaSuccess) c = cudaFuncSetAttribute(k_matmul<WT, TG, RT, OP_ADD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  return c;
+}
+template <int WT, int TG>
+cudaError_t mm_attr_mt() {
+  cudaError_t c = mm_attr<WT, TG, 8>();
+  if (c == cudaSuccess) c = mm_attr<WT, TG, 2>();
+  return c;
+}
+
 cudaError_t set_kernel_attrs(int ctx) {
   const int big = 200 * 1024;
   cudaError_t c = mv_attr<WQ4, 32, 1>(big);
   if (c == cudaSuccess) c = mv_attr<WQ4, 16, 1>(big);
-  if (c == cudaSuccess) c = mv_attr<WQ4, 8, 4>(big);
   if (c == cudaSuccess) c = mv_attr<WQ8, 32, 1>(big);
   if (c == cudaSuccess) c = mv_attr<WQ8, 16, 1>(big);
-  if (c == cudaSuccess) c = mv_attr<WQ8, 8, 4>(big);
+  if (c == cudaSuccess) c = mm_attr_mt<WQ4, 8>();
+  if (c == cudaSuccess) c = mm_attr_mt<WQ4, 16>();
+  if (c == cudaSuccess) c = mm_attr_mt<WQ4, 32>();
+  if (c == cudaSuccess) c = mm_attr_mt<WQ8, 8>();
+  if (c == cudaSuccess) c = mm_attr_mt<WQ8, 16>();
+  if (c == cudaSuccess) c = mm_attr_mt<WQ8, 32>();
   const int att = ctx * 4 > 48 * 1024 ? ctx * 4 : 48 * 1024;
   if (c == cudaSuccess) c = cudaFuncSetAttribute(k_attention<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, att);
   if (c == cudaSuccess) c = cudaFuncSetAttribute(k_attention<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, att);
@@ -296,7 +350,7 @@ inline void mark(Prof* p, int op, cudaStream_t st) {
 
 // Enqueue one pass of M tokens (positions and ids are read from e->prm on the device). logits: compute the
 // last token's logits and the greedy next token into e->next_d.
-void enqueue_pass(h2c_engine* e, int M, bool logits, Prof* pf) {
+void enqueue_pass(h2c_engine* e, int M, bool logits, Prof* pf, bool batch = false) {
   const h2c_config& c = e->cfg;
   const int D = c.dim, F = c.ffn, H = c.heads, KVH = c.kv_heads, HD = e->HD, QKV = e->QKV, NL = c.layers;
   cudaStream_t st = e->st;
@@ -335,7 +389,18 @@ void enqueue_pass(h2c_engine* e, int M, bool logits, Prof* pf) {
     matvec(OP_ADD, W.down, e->xq, e->xd, e->xs, M, e->x, D, nullptr, st);
     mark(pf, 9, st);
   }
-  if (logits) {
+  if (batch) {  // every token of a batched decode step is the last of its sequence: logits and a token for each
+    k_norm_quant<<<M, 256, D * 4, st>>>(e->x, 0, e->out_norm, D, c.eps, e->xq, e->xd, e->xs);
+    if (e->out_type == 8) {
+      matvec_w<WQ8>(OP_STORE, (const uint8_t*)e->out8.qs, e->out8.d, c.vocab, D, e->xq, e->xd, e->xs, M, e->logits_b,
+                    c.vocab, nullptr, st);
+    } else {
+      matvec(OP_STORE, e->out_type == 2 ? e->out4 : e->embd, e->xq, e->xd, e->xs, M, e->logits_b, c.vocab, nullptr, st);
+    }
+    k_argmax1<<<dim3(e->am_np, M), 256, 0, st>>>(e->logits_b, c.vocab, e->am_vb, e->am_ib);
+    k_argmax2_batch<<<M, 32, 0, st>>>(e->am_vb, e->am_ib, e->am_np, e->prm, e->toklog, e->cfg.ctx, e->next_b);
+    mark(pf, 10, st);
+  } else if (logits) {
     k_norm_quant<<<1, 256, D * 4, st>>>(e->x, M - 1, e->out_norm, D, c.eps, e->xq, e->xd, e->xs);
     if (e->out_type == 8) {
       matvec_w<WQ8>(OP_STORE, (const uint8_t*)e->out8.qs, e->out8.d, c.vocab, D, e->xq, e->xd, e->xs, 1, e->logits,
@@ -835,7 +900,7 @@ int h2c_create(int device, const h2c_config* cfg, h2c_engine** out) {
       (r = dalloc_t(e, &e->xq, (size_t)MT * KQ)) || (r = dalloc_t(e, &e->xd, (size_t)MT * KQ / 32)) ||
       (r = dalloc_t(e, &e->xs, (size_t)MT * KQ / 32)) ||
       (r = dalloc_t(e, &e->am_v, (size_t)e->am_np)) || (r = dalloc_t(e, &e->am_i, (size_t)e->am_np)) ||
-      (r = dalloc_t(e, &e->prm, (size_t)(P_IDS + MT))) || (r = dalloc_t(e, &e->next_d, 1)) ||
+      (r = dalloc_t(e, &e->prm, (size_t)P_WORDS)) || (r = dalloc_t(e, &e->next_d, 1)) ||
       (r = dalloc_t(e, &e->toklog, (size_t)c.max_seqs * (c.ctx + 1))) ||
       (r = dalloc_t(e, &e->rope, (size_t)c.ctx * HD)))
     return bail(r);
@@ -955,6 +1020,98 @@ int h2c_forward(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t p
   }
   e->last_logits_valid.assign(e->cfg.max_seqs, 0);
   e->last_logits_valid[seq] = 1;
+  return H2C_OK;
+}
+
+// Validate a batch, allocate the batch buffers on first use, write the pass parameters (mode 1) and launch the
+// batch graph for n tokens `steps` times (each launch's argmax feeds the next).
+int batch_launch(h2c_engine* e, int32_t n, const int32_t* seqs, const int32_t* ids, const int32_t* pos, int steps,
+                 cudaEvent_t before = nullptr) {
+  const h2c_config& c = e->cfg;
+  const int cap = c.max_chunk < P_CAP ? c.max_chunk : P_CAP;
+  if (n < 1 || n > cap) return e->fail(H2C_ERR_INVALID, "batch of %d sequences (1 .. %d per step)", n, cap);
+  std::vector<char> seen(c.max_seqs, 0);
+  for (int m = 0; m < n; m++) {
+    if (seqs[m] < 0 || seqs[m] >= c.max_seqs) return e->fail(H2C_ERR_INVALID, "sequence %d out of range [0, %d)", seqs[m], c.max_seqs);
+    if (seen[seqs[m]]) return e->fail(H2C_ERR_INVALID, "sequence %d appears twice in one batch", seqs[m]);
+    seen[seqs[m]] = 1;
+    if (pos[m] < 0) return e->fail(H2C_ERR_INVALID, "negative position");
+    if ((int64_t)pos[m] + steps >= c.ctx) return e->fail(H2C_ERR_CONTEXT_FULL, "context full (sequence %d)", seqs[m]);
+    if (ids[m] < 0 || ids[m] >= c.vocab) return e->fail(H2C_ERR_INVALID, "token id %d out of range", ids[m]);
+  }
+  CUDA_TRY(e, cudaSetDevice(e->dev));
+  int r = check_ready(e);
+  if (r) return r;
+  if (!e->logits_b) {
+    if ((r = dalloc_t(e, &e->logits_b, (size_t)cap * c.vocab)) || (r = dalloc_t(e, &e->am_vb, (size_t)cap * e->am_np)) ||
+        (r = dalloc_t(e, &e->am_ib, (size_t)cap * e->am_np)) || (r = dalloc_t(e, &e->next_b, (size_t)P_CAP)))
+      return r;
+    CUDA_TRY(e, cudaMallocHost(&e->prm_bh, sizeof(int32_t) * P_WORDS));
+    CUDA_TRY(e, cudaMallocHost(&e->next_bh, sizeof(int32_t) * P_CAP));
+    memset(e->prm_bh, 0, sizeof(int32_t) * P_WORDS);
+    e->bexec.assign(cap + 1, nullptr);
+  }
+  int32_t* h = e->prm_bh;
+  h[P_POS0] = 0; h[P_M] = n; h[P_SEQ] = 0; h[P_MODE] = 1;
+  for (int m = 0; m < n; m++) {
+    h[P_IDS + m] = ids[m];
+    h[P_IDS + P_CAP + m] = pos[m];
+    h[P_IDS + 2 * P_CAP + m] = seqs[m];
+  }
+  CUDA_TRY(e, cudaMemcpyAsync(e->prm, h, sizeof(int32_t) * P_WORDS, cudaMemcpyHostToDevice, e->st));
+  if (!e->bexec[n]) {  // one graph per batch size, captured on first use
+    cudaGraph_t g = nullptr;
+    CUDA_TRY(e, cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal));
+    enqueue_pass(e, n, false, nullptr, true);
+    cudaError_t ce = cudaStreamEndCapture(e->st, &g);
+    if (ce != cudaSuccess) return e->fail(H2C_ERR_CUDA, "graph capture: %s", cudaGetErrorString(ce));
+    ce = cudaGraphInstantiate(&e->bexec[n], g, 0);
+    cudaGraphDestroy(g);
+    if (ce != cudaSuccess) return e->fail(H2C_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(ce));
+  }
+  if (before) CUDA_TRY(e, cudaEventRecord(before, e->st));
+  for (int i = 0; i < steps; i++) CUDA_TRY(e, cudaGraphLaunch(e->bexec[n], e->st));
+  return H2C_OK;
+}
+
+int h2c_forward_batch(h2c_engine* e, int32_t n, const int32_t* seqs, const int32_t* ids, const int32_t* pos,
+                      float temperature, uint32_t seed, int32_t* next) {
+  if (!e || !seqs || !ids || !pos || !next) return H2C_ERR_INVALID;
+  const h2c_config& c = e->cfg;
+  int r = batch_launch(e, n, seqs, ids, pos, 1);
+  if (r) return r;
+  if (temperature > 0) {
+    std::vector<float> lg((size_t)n * c.vocab);
+    CUDA_TRY(e, cudaMemcpyAsync(lg.data(), e->logits_b, lg.size() * 4, cudaMemcpyDeviceToHost, e->st));
+    CUDA_TRY(e, cudaStreamSynchronize(e->st));
+    for (int m = 0; m < n; m++)
+      next[m] = sample_host(lg.data() + (size_t)m * c.vocab, c.vocab, temperature, seed + (uint32_t)pos[m]);
+  } else {
+    CUDA_TRY(e, cudaMemcpyAsync(e->next_bh, e->next_b, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, e->st));
+    CUDA_TRY(e, cudaStreamSynchronize(e->st));
+    memcpy(next, e->next_bh, sizeof(int32_t) * n);
+  }
+  e->last_logits_valid.assign(c.max_seqs, 0);
+  for (int m = 0; m < n; m++) e->last_logits_valid[seqs[m]] = 2 + m;  // row m of the batch logits
+  return H2C_OK;
+}
+
+int h2c_generate_batch(h2c_engine* e, int32_t n, const int32_t* seqs, const int32_t* ids, const int32_t* pos,
+                       int32_t steps, int32_t* out_tokens, float* device_ms) {
+  if (!e || !seqs || !ids || !pos || steps < 1) return H2C_ERR_INVALID;
+  const h2c_config& c = e->cfg;
+  CUDA_TRY(e, cudaSetDevice(e->dev));
+  int r = batch_launch(e, n, seqs, ids, pos, steps, e->ev0);  // ev0: after the parameter copy and graph build
+  if (r) return r;
+  CUDA_TRY(e, cudaEventRecord(e->ev1, e->st));
+  if (out_tokens)
+    for (int m = 0; m < n; m++)
+      CUDA_TRY(e, cudaMemcpyAsync(out_tokens + (size_t)m * steps, e->toklog + (size_t)seqs[m] * (c.ctx + 1) + pos[m] + 1,
+                                  sizeof(int32_t) * steps, cudaMemcpyDeviceToHost, e->st));
+  CUDA_TRY(e, cudaStreamSynchronize(e->st));
+  if (device_ms) CUDA_TRY(e, cudaEventElapsedTime(device_ms, e->ev0, e->ev1));
+  e->last_logits_valid.assign(c.max_seqs, 0);
+  for (int m = 0; m < n; m++) e->last_logits_valid[seqs[m]] = 2 + m;
   return H2C_OK;
 }
 
@@ -1088,7 +1245,9 @@ int h2c_read_logits(h2c_engine* e, int seq, float* out, int64_t n) {
     return e->fail(H2C_ERR_INVALID, "no logits for sequence %d (its last forward was not the latest)", seq);
   if (n < e->cfg.vocab) return e->fail(H2C_ERR_INVALID, "output holds %lld floats, vocab is %d", (long long)n, e->cfg.vocab);
   CUDA_TRY(e, cudaSetDevice(e->dev));
-  CUDA_TRY(e, cudaMemcpyAsync(out, e->logits, (size_t)e->cfg.vocab * 4, cudaMemcpyDeviceToHost, e->st));
+  const int v = e->last_logits_valid[seq];
+  const float* src = v >= 2 ? e->logits_b + (size_t)(v - 2) * e->cfg.vocab : e->logits;
+  CUDA_TRY(e, cudaMemcpyAsync(out, src, (size_t)e->cfg.vocab * 4, cudaMemcpyDeviceToHost, e->st));
   CUDA_TRY(e, cudaStreamSynchronize(e->st));
   return H2C_OK;
 }
@@ -1126,6 +1285,10 @@ int h2c_destroy(h2c_engine* e) {
   cudaSetDevice(e->dev);
   if (e->st) cudaStreamSynchronize(e->st);
   if (e->gexec) cudaGraphExecDestroy(e->gexec);
+  for (cudaGraphExec_t g : e->bexec)
+    if (g) cudaGraphExecDestroy(g);
+  if (e->prm_bh) cudaFreeHost(e->prm_bh);
+  if (e->next_bh) cudaFreeHost(e->next_bh);
   if (e->graph) cudaGraphDestroy(e->graph);
   for (void* p : e->dallocs) cudaFree(p);
   if (e->prm_h) cudaFreeHost(e->prm_h);

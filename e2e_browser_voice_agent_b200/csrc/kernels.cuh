@@ -31,8 +31,17 @@
 
 namespace h2 {
 
-// device-resident parameters of one pass, written by the host with one copy before each pass
-enum { P_POS0 = 0, P_M = 1, P_SEQ = 2, P_IDS = 4 };
+// device-resident parameters of one pass, written by the host with one copy before each pass:
+// [P_POS0] first position, [P_M] tokens, [P_SEQ] sequence, [P_MODE] 0 = the tokens are positions pos0 .. pos0+M-1 of
+// one sequence (a prompt chunk or one decode step), 1 = one decode token of each of M sequences (a batched decode
+// step: token m is at position prm[P_IDS + P_CAP + m] of sequence prm[P_IDS + 2 P_CAP + m]); then the ids.
+enum { P_POS0 = 0, P_M = 1, P_SEQ = 2, P_MODE = 3, P_IDS = 4, P_CAP = 256, P_WORDS = P_IDS + 3 * P_CAP };
+__device__ __forceinline__ int tok_pos(const int32_t* prm, int m) {
+  return prm[P_MODE] ? prm[P_IDS + P_CAP + m] : prm[P_POS0] + m;
+}
+__device__ __forceinline__ int tok_seq(const int32_t* prm, int m) {
+  return prm[P_MODE] ? prm[P_IDS + 2 * P_CAP + m] : prm[P_SEQ];
+}
 
 // byte p of a permuted 16-byte block holds GGUF byte PERM[p]
 __host__ __device__ constexpr int perm16(int p) { return ((p & 3) >> 1) * 8 + (p >> 2) * 2 + (p & 1); }
@@ -282,6 +291,18 @@ __global__ void k_swiglu_quant(const float* __restrict__ gu, int F, int M, int8_
 enum { OP_STORE = 0, OP_BIAS = 1, OP_ADD = 2 };
 enum { WQ4 = 0, WQ8 = 1 };
 
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {  // weights are read once per pass: no L1 allocation
   uint4 v;
   asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
@@ -346,18 +367,18 @@ __global__ void __launch_bounds__(256) k_matvec(const uint8_t* __restrict__ qs, 
     }
   }
   __syncthreads();
-  const int t = threadIdx.x;
-  const int l = t & 3, r = (t >> 2) % ROWS, m = (t >> 2) / ROWS;
-  if (m < MB) {
+  // (MB * ROWS * 4 is a multiple of 32 or below 256, so whole warps take part in hsum4_quad)
+  for (int t = threadIdx.x; t < ((MB * ROWS * 4 + 255) & ~255); t += blockDim.x) {
+    const int l = t & 3, r = (t >> 2) % ROWS, m = (t >> 2) / ROWS;
     float acc = 0.f;
-    if (m < M) {
+    if (m < M && m < MB) {
       const float* pp = reinterpret_cast<const float*>(prod) + ((size_t)m * nb * ROWS + r) * 4 + l;
 #pragma unroll 8
       for (int b = 0; b < nb; b++) acc = __fadd_rn(acc, pp[(size_t)b * ROWS * 4]);
     }
     const float v = hsum4_quad(acc);
     const int n = n0 + r;
-    if (l == 0 && m < M && n < N) {
+    if (l == 0 && m < M && m < MB && n < N) {
       float* o = y + (size_t)m * ldy + n;
       if (OP == OP_ADD) *o = __fadd_rn(*o, v);
       else if (OP == OP_BIAS) *o = __fadd_rn(v, bias[n]);
@@ -366,13 +387,138 @@ __global__ void __launch_bounds__(256) k_matvec(const uint8_t* __restrict__ qs, 
   }
 }
 
+// y[m][n] (op)= the reference's lane arithmetic for several tokens at once (matmul_q4 M > 1 / dot_q8_q8,
+// kernels.c:121-273), each weight byte read once per token group. CTA (token group, row range): the group's TG
+// tokens' int8 activations, lane sums and scales stay in shared memory for the whole CTA; the range's weights stream
+// through a double-buffered cp.async ring in chunks of MC_BC blocks x RT * H rows (a sub-range). Thread
+// (m, h, l) keeps the running lane-l sums of token m for rows h, h + H, ... of the sub-range (H = 256 / (4 TG)) in
+// registers and adds each block's product in block order: acc = (((0 + p_0 (dw_0 dx_0)) + p_1 (dw_1 dx_1)) + ...);
+// at the sub-range's last block ((l0 + l1) + l2) + l3 and the epilogue (put(), kernels.c:190-194).
+constexpr int MC_BC = 16;  // blocks per weight chunk
+__host__ __device__ constexpr int mm_wb(int wt) { return wt == 0 ? 16 : 32; }
+__host__ __device__ constexpr int mm_xq_stride(int nb) { return nb * 32 + 16; }  // bytes per token (padded)
+__host__ __device__ constexpr int mm_xs_stride(int nb) { return nb * 16 + 16; }
+__host__ __device__ constexpr int mm_xd_stride(int nb) { return nb + 1; }       // floats
+__host__ __device__ constexpr int mm_act_bytes(int tg, int nb) {
+  return tg * (mm_xq_stride(nb) + mm_xs_stride(nb)) + ((tg * mm_xd_stride(nb) * 4 + 15) & ~15);
+}
+__host__ __device__ constexpr int mm_chunk_bytes(int wt, int sr) {
+  return sr * MC_BC * mm_wb(wt) + ((sr * MC_BC * 2 + 15) & ~15);
+}
+template <int WT, int TG, int RT, int OP>
+__global__ void __launch_bounds__(256) k_matmul(const uint8_t* __restrict__ qs, const __half* __restrict__ dsc, int N,
+                                                int K, const int8_t* __restrict__ xq, const float* __restrict__ xd,
+                                                const int4* __restrict__ xs, int M, int rows_per_cta, float* __restrict__ y,
+                                                int ldy, const float* __restrict__ bias) {
+  constexpr int WB = mm_wb(WT), H = 256 / (TG * 4), SR = H * RT, CH = mm_chunk_bytes(WT, SR);
+  constexpr int WSZ = SR * MC_BC * WB;
+  extern __shared__ __align__(16) uint8_t msm[];
+  const int nb = K / 32, ntg = (M + TG - 1) / TG;
+  const int tg = blockIdx.x % ntg, m0 = tg * TG, mt = min(TG, M - m0);
+  const int row_lo = (blockIdx.x / ntg) * rows_per_cta, row_hi = min(N, row_lo + rows_per_cta);
+  const int tid = threadIdx.x, l = tid & 3, hp = (tid >> 2) % H, m = tid / (4 * H);
+  uint8_t* axq = msm;
+  uint8_t* axs = axq + TG * mm_xq_stride(nb);
+  float* axd = reinterpret_cast<float*>(axs + TG * mm_xs_stride(nb));
+  uint8_t* ring = msm + mm_act_bytes(TG, nb);
+  // the token group's activations, once
+  for (int i = tid; i < mt * nb * 2; i += 256) {
+    const int hf = i & 1, b = (i >> 1) % nb, mm = (i >> 1) / nb;
+    cp_async16(axq + mm * mm_xq_stride(nb) + b * 32 + hf * 16, xq + (size_t)(m0 + mm) * K + (size_t)b * 32 + hf * 16);
+  }
+  for (int i = tid; i < mt * nb; i += 256) {
+    const int b = i % nb, mm = i / nb;
+    if (WT == WQ4) cp_async16(axs + mm * mm_xs_stride(nb) + b * 16, xs + (size_t)(m0 + mm) * nb + b);
+    cp_async4(axd + mm * mm_xd_stride(nb) + b, xd + (size_t)(m0 + mm) * nb + b);
+  }
+  const int nkc = (nb + MC_BC - 1) / MC_BC;
+  const int nsub = (row_hi - row_lo + SR - 1) / SR;
+  const int nchunk = nsub * nkc;
+  auto stage = [&](int c) {  // chunk c: sub-range c / nkc, blocks (c % nkc) * MC_BC ..
+    uint8_t* ws = ring + (c & 1) * CH;
+    __half* ds = reinterpret_cast<__half*>(ws + WSZ);
+    const int rb = row_lo + (c / nkc) * SR, b0 = (c % nkc) * MC_BC, bc = min(MC_BC, nb - b0);
+    for (int i = tid; i < bc * SR * (WB / 16); i += 256) {
+      const int piece = i % (WB / 16), r = (i / (WB / 16)) % SR, b = i / (WB / 16) / SR;
+      const int n = rb + r;  // rows past N read the zero padding of their 32-row group, or are skipped
+      if (n < ((N + 31) & ~31)) {
+        const size_t e = ((size_t)(n >> 5) * nb + b0 + b) * 32 + (n & 31);
+        cp_async16(ws + (b * SR + r) * WB + piece * 16, qs + e * WB + piece * 16);
+      }
+    }
+    for (int i = tid; i < bc * (SR / 2); i += 256) {  // scales of two adjacent rows (same 32-row group) per copy
+      const int rp = i % (SR / 2), b = i / (SR / 2), n = rb + 2 * rp;
+      if (n < ((N + 31) & ~31))
+        cp_async4(ds + b * SR + 2 * rp, dsc + ((size_t)(n >> 5) * nb + b0 + b) * 32 + (n & 31));
+    }
+    cp_async_commit();
+  };
+  float acc[RT];
+#pragma unroll
+  for (int j = 0; j < RT; j++) acc[j] = 0.f;
+  if (nchunk > 0) stage(0);  // (committed together with the activations)
+  for (int c = 0; c < nchunk; c++) {
+    if (c + 1 < nchunk) {
+      stage(c + 1);
+      cp_async_wait_group<1>();
+    } else {
+      cp_async_wait_group<0>();
+    }
+    __syncthreads();
+    const int kc = c % nkc, b0 = kc * MC_BC, bc = min(MC_BC, nb - b0);
+    if (m < mt) {
+      const uint8_t* ws = ring + (c & 1) * CH;
+      const __half* ds = reinterpret_cast<const __half*>(ws + WSZ);
+      const uint8_t* xqm = axq + m * mm_xq_stride(nb) + b0 * 32;
+      const uint8_t* xsm = axs + m * mm_xs_stride(nb) + b0 * 16;
+      const float* xdm = axd + m * mm_xd_stride(nb) + b0;
+      for (int b = 0; b < bc; b++) {
+        const int x0 = *reinterpret_cast<const int*>(xqm + b * 32 + 4 * l);
+        const int x1 = *reinterpret_cast<const int*>(xqm + b * 32 + 16 + 4 * l);
+        const int xsl = WT == WQ4 ? *reinterpret_cast<const int*>(xsm + b * 16 + 4 * l) : 0;
+        const float dx = xdm[b];
+#pragma unroll
+        for (int j = 0; j < RT; j++) {
+          const int r = hp + H * j;
+          const uint8_t* wr = ws + (b * SR + r) * WB + 4 * l;
+          float p;
+          if (WT == WQ4) {
+            p = q4_lane(*reinterpret_cast<const uint32_t*>(wr), x0, x1, xsl);
+          } else {
+            const int w0 = *reinterpret_cast<const int*>(wr), w1 = *reinterpret_cast<const int*>(wr + 16);
+            p = magic_to_float(__dp4a(w0, x0, __dp4a(w1, x1, MK_MAGIC)));
+          }
+          acc[j] = __fadd_rn(acc[j], __fmul_rn(p, __fmul_rn(__half2float(ds[b * SR + r]), dx)));
+        }
+      }
+    }
+    if (kc == nkc - 1) {  // the sub-range's rows are complete
+      const int rb = row_lo + (c / nkc) * SR;
+#pragma unroll
+      for (int j = 0; j < RT; j++) {
+        const float v = hsum4_quad(acc[j]);
+        acc[j] = 0.f;
+        const int n = rb + hp + H * j;
+        if (l == 0 && m < mt && n < row_hi) {
+          float* o = y + (size_t)(m0 + m) * ldy + n;
+          if (OP == OP_ADD) *o = __fadd_rn(*o, v);
+          else if (OP == OP_BIAS) *o = __fadd_rn(v, bias[n]);
+          else *o = v;
+        }
+      }
+    }
+    __syncthreads();  // the buffer is refilled by the next iteration's stage()
+  }
+  cp_async_wait_all();
+}
+
 // RoPE on the Q and K heads of each token (pairs (i, i + HD/2), table cos/sin), then K and V appended to the
 // cache of (seq, layer) (kernels.c:337-352). One CTA per token.
 __global__ void k_rope_kv(const int32_t* __restrict__ prm, float* __restrict__ qkv, int QKV, const float* __restrict__ rope,
                           float* __restrict__ kc, float* __restrict__ vc, int H, int KVH, int HD, int ctx, int layers,
                           int layer) {
   const int m = blockIdx.x;
-  const int pos = prm[P_POS0] + m, seq = prm[P_SEQ];
+  const int pos = tok_pos(prm, m), seq = tok_seq(prm, m);
   const int D = H * HD, half = HD / 2;
   float* row = qkv + (size_t)m * QKV;
   const float* cs = rope + (size_t)pos * HD;
@@ -410,7 +556,7 @@ __global__ void __launch_bounds__(128) k_attention(const int32_t* __restrict__ p
   __shared__ float red[4];
   __shared__ float sum_s;
   const int h = blockIdx.x, m = blockIdx.y, tid = threadIdx.x;
-  const int T = prm[P_POS0] + m + 1, seq = prm[P_SEQ];
+  const int T = tok_pos(prm, m) + 1, seq = tok_seq(prm, m);
   const int kh = h / (H / KVH);
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
   for (int i = tid; i < HD; i += blockDim.x) q_s[i] = qkv[(size_t)m * QKV + (size_t)h * HD + i];
@@ -467,6 +613,9 @@ __device__ __forceinline__ void amax_merge(float& v, int& i, float v2, int i2) {
 __global__ void k_argmax1(const float* __restrict__ logits, int V, float* __restrict__ pv, int* __restrict__ pi) {
   __shared__ float sv[32];
   __shared__ int si[32];
+  logits += (size_t)blockIdx.y * V;  // row blockIdx.y (one row per token of a batched step)
+  pv += (size_t)blockIdx.y * gridDim.x;
+  pi += (size_t)blockIdx.y * gridDim.x;
   float v = -INFINITY;
   int idx = 0x7fffffff;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < V; i += gridDim.x * blockDim.x) amax_merge(v, idx, logits[i], i);
@@ -508,6 +657,34 @@ __global__ void k_argmax2(const float* __restrict__ pv, const int* __restrict__ 
     prm[P_POS0] = next_pos;
     prm[P_M] = 1;
     prm[P_IDS] = tok;
+  }
+}
+
+// stage 2 of a batched decode step: block m merges row m's partials; the token of sequence seq_m (at position pos_m)
+// goes to out[m], is logged at tokens[seq_m][pos_m + 1] and becomes token m of the next step at pos_m + 1 (so
+// steps can be chained on the device, as k_argmax2 does for one sequence).
+__global__ void k_argmax2_batch(const float* __restrict__ pv, const int* __restrict__ pi, int np,
+                                int32_t* __restrict__ prm, int32_t* __restrict__ toklog, int ctx,
+                                int32_t* __restrict__ out) {
+  const int m = blockIdx.x;
+  pv += (size_t)m * np;
+  pi += (size_t)m * np;
+  float v = -INFINITY;
+  int idx = 0x7fffffff;
+  for (int i = threadIdx.x; i < np; i += 32) amax_merge(v, idx, pv[i], pi[i]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const float v2 = __shfl_xor_sync(0xffffffffu, v, o);
+    const int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
+    amax_merge(v, idx, v2, i2);
+  }
+  if (threadIdx.x == 0) {
+    const int tok = idx == 0x7fffffff ? 0 : idx;
+    const int next_pos = tok_pos(prm, m) + 1;
+    out[m] = tok;
+    if (next_pos <= ctx) toklog[(size_t)tok_seq(prm, m) * (ctx + 1) + next_pos] = tok;
+    prm[P_IDS + m] = tok;
+    prm[P_IDS + P_CAP + m] = next_pos;
   }
 }
 

@@ -89,6 +89,21 @@ int h2c_set_tensor(h2c_engine* e, int kind, int layer, int ggml_type, const void
 int h2c_forward(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t pos, float temperature,
                 uint32_t seed, int32_t* next);
 
+/* One decode step of n sessions at once (the multi-session serving form, forwardBatch of the CUDA backend; no
+ * reference counterpart: the reference serves one session per backend, cpu.js:33-50). Token ids[m] of sequence
+ * seqs[m] (distinct) is processed at position pos[m]; next[m] receives its next token, chosen as by h2c_forward
+ * (greedy, or sampled with seed + pos[m]). Each weight byte is read once for the whole batch; every token's
+ * arithmetic is the single-token arithmetic, so the results equal n separate h2c_forward calls bit for bit.
+ * 1 <= n <= min(max_chunk, 256). h2c_read_logits(seqs[m]) returns token m's logits afterwards. */
+int h2c_forward_batch(h2c_engine* e, int32_t n, const int32_t* seqs, const int32_t* ids, const int32_t* pos,
+                      float temperature, uint32_t seed, int32_t* next);
+
+/* Greedy decode of `steps` tokens of each of n sessions entirely on the device: batched steps as h2c_forward_batch,
+ * each step's tokens fed to the next without a host round trip. out_tokens (nullable) receives [n][steps] ids;
+ * device_ms (nullable) the CUDA-event time of the steps. Needs pos[m] + steps < ctx. */
+int h2c_generate_batch(h2c_engine* e, int32_t n, const int32_t* seqs, const int32_t* ids, const int32_t* pos,
+                       int32_t steps, int32_t* out_tokens, float* device_ms);
+
 /* Greedy decode of `steps` tokens of sequence `seq` entirely on the device: first_id is processed at `pos`, each
  * step's argmax becomes the next step's input without a host round trip (the WebGPU backend keeps its sampled
  * token on the GPU the same way, webgpu.js:391, 553-574). out_tokens (nullable) receives the `steps` generated

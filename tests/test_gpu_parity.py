@@ -330,3 +330,86 @@ def test_fast_correctly_rounded_math_is_exact():
     out = (C.c_uint64 * 4)()
     assert L.h2c_selftest_math(0, out) == 0
     assert list(out) == [0, 0, 0, 0], f"mismatches (x/127, x/896, 1/x, sqrt x): {list(out)}"
+
+
+@pytest.mark.parametrize("model", ["tiny", "gqa7", "small-q8", "qwen2-0.5b"])
+def test_forward_batch_matches_separate_sessions(model):
+    """A batched decode step of several sessions (each at its own position, ragged membership across steps) gives
+    every session the logits and token that its own single-token forward gives, bit for bit; on the small models
+    also the oracle's, session by session."""
+    path = synth.ensure(model)
+    n_seq, steps, ctx = 6, 8, 64
+    bat = backend.open_model(path, ctx=ctx, prefill_chunk=8, max_seqs=n_seq)
+    sep = backend.open_model(path, ctx=ctx, prefill_chunk=8, max_seqs=n_seq)
+    V = bat.cfg["vocab"]
+    refs = [O.open_model("oracle", path, ctx=ctx, mt=8, threads=4) for _ in range(n_seq)] if model != "qwen2-0.5b" else []
+    pos, tok = [], []
+    for s in range(n_seq):
+        prompt = synth.prompt_ids(V, 3 + 2 * s, seed=300 + s)
+        a = bat.forward(prompt, 0, seq=s)
+        b = sep.forward(prompt, 0, seq=s)
+        assert a == b
+        if refs:
+            assert refs[s].forward(prompt, 0)["next"] == a
+        pos.append(len(prompt))
+        tok.append(a)
+    for k in range(steps):
+        members = [s for s in range(n_seq) if (s + k) % 4 != 3]  # a different subset each step
+        out = bat.forward_batch(members, [tok[s] for s in members], [pos[s] for s in members], want_logits=True)
+        for s, nb in zip(members, out):
+            ns = sep.forward([tok[s]], pos[s], seq=s, want_logits=True)
+            lb, ls = bat.read_logits(s), sep.read_logits(s)
+            assert np.array_equal(bits(lb), bits(ls)), f"{model} step {k} seq {s}: batch logits differ from single"
+            assert nb == ns, f"{model} step {k} seq {s}: token {nb} vs {ns}"
+            if refs:
+                r = refs[s].forward([tok[s]], pos[s], want_logits=True)
+                assert np.array_equal(bits(lb), bits(r["logits"])), f"{model} step {k} seq {s}: differs from oracle"
+                assert nb == r["next"]
+            tok[s], pos[s] = nb, pos[s] + 1
+    bat.destroy()
+    sep.destroy()
+
+
+def test_forward_batch_errors():
+    path = synth.ensure("tiny")
+    be = backend.open_model(path, ctx=16, prefill_chunk=4, max_seqs=4)
+    L, h = be._L, be._h
+
+    def call(seqs, ids, pos):
+        s, t, p = (np.ascontiguousarray(np.asarray(v, dtype=np.int32)) for v in (seqs, ids, pos))
+        out = np.zeros(max(len(seqs), 1), dtype=np.int32)
+        return L.h2c_forward_batch(h, len(seqs), s.ctypes.data, t.ctypes.data, p.ctypes.data, C.c_float(0.0),
+                                   C.c_uint32(1), out.ctypes.data)
+
+    assert call([0, 0], [1, 2], [0, 0]) == _lib.ERR_INVALID           # a sequence twice
+    assert call([0, 1, 2, 3, 0], [1] * 5, [0] * 5) == _lib.ERR_INVALID  # more than max_chunk
+    assert call([4], [1], [0]) == _lib.ERR_INVALID                     # sequence out of range
+    assert call([1], [1], [15]) == _lib.ERR_CONTEXT_FULL
+    assert call([1], [be.cfg["vocab"]], [0]) == _lib.ERR_INVALID        # token id out of range
+    assert call([0, 1], [1, 2], [0, 3]) == 0                            # and the engine still works
+    be.destroy()
+
+
+@pytest.mark.parametrize("model", ["tiny", "qwen2-0.5b"])
+def test_generate_batch_matches_forward_batch(model):
+    """Batched steps chained on the device give the tokens of host-driven batched steps."""
+    path = synth.ensure(model)
+    n_seq, steps = 5, 12
+    a = backend.open_model(path, ctx=48, prefill_chunk=8, max_seqs=n_seq)
+    b = backend.open_model(path, ctx=48, prefill_chunk=8, max_seqs=n_seq)
+    V = a.cfg["vocab"]
+    first, pos = [], []
+    for s in range(n_seq):
+        prompt = synth.prompt_ids(V, 2 + 3 * s, seed=400 + s)
+        first.append(a.forward(prompt, 0, seq=s))
+        assert b.forward(prompt, 0, seq=s) == first[-1]
+        pos.append(len(prompt))
+    toks, ms = a.generate_batch(list(range(n_seq)), first, pos, steps)
+    assert toks.shape == (n_seq, steps) and ms > 0
+    cur, p = list(first), list(pos)
+    for k in range(steps):
+        cur = b.forward_batch(list(range(n_seq)), cur, p)
+        p = [x + 1 for x in p]
+        assert toks[:, k].tolist() == cur, f"{model} step {k}"
+    a.destroy()
+    b.destroy()
