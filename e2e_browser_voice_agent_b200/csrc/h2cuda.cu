@@ -240,8 +240,10 @@ void launch_mv_t(int op, const uint8_t* qs, const __half* d, int N, int K, const
 }
 
 // Several tokens (prompt chunks, batched decode steps): k_matmul with token groups of 32, 16 or 8 (the largest whose
-// activations fit next to the weight ring) and row ranges that give about two CTAs per SM.
-constexpr size_t MM_SMEM = 160 * 1024;
+// activations fit next to the weight ring in a third of an SM's shared memory, so three CTAs share an SM) and row
+// ranges that give about four CTAs per SM.
+constexpr size_t MM_SMEM = 160 * 1024;   // attribute limit (long rows)
+constexpr size_t MM_SMEM_FAST = 72 * 1024;
 template <int WT, int TG, int RT>
 size_t mm_smem(int nb) { return (size_t)mm_act_bytes(TG, nb) + 2 * (size_t)mm_chunk_bytes(WT, (256 / (4 * TG)) * RT); }
 
@@ -250,8 +252,8 @@ void launch_mm_t(int op, const uint8_t* qs, const __half* d, int N, int K, const
                  const int4* xs, int M, float* y, int ldy, const float* bias, cudaStream_t st) {
   constexpr int SR = (256 / (4 * TG)) * RT;
   const int ntg = (M + TG - 1) / TG;
-  const int nrr = std::max(1, 2 * 148 / ntg);
-  const int rows = (int)align_up((size_t)((N + nrr - 1) / nrr), SR);
+  const int nrr = std::max(1, 4 * 148 / ntg);
+  const int rows = std::max(SR, N / nrr / SR * SR);
   const int grid = ntg * ((N + rows - 1) / rows);
   const size_t smem = mm_smem<WT, TG, RT>(K / 32);
   if (op == OP_STORE) k_matmul<WT, TG, RT, OP_STORE><<<grid, 256, smem, st>>>(qs, d, N, K, xq, xd, xs, M, rows, y, ldy, bias);
@@ -264,7 +266,7 @@ template <int WT, int TG>
 void launch_mm(int op, const uint8_t* qs, const __half* d, int N, int K, const int8_t* xq, const float* xd,
                const int4* xs, int M, float* y, int ldy, const float* bias, cudaStream_t st) {
   const int ntg = (M + TG - 1) / TG;
-  if ((size_t)N * ntg >= (size_t)2 * 148 * (256 / (4 * TG)) * 8)
+  if ((size_t)N * ntg >= (size_t)4 * 148 * (256 / (4 * TG)) * 8)
     launch_mm_t<WT, TG, 8>(op, qs, d, N, K, xq, xd, xs, M, y, ldy, bias, st);
   else
     launch_mm_t<WT, TG, 2>(op, qs, d, N, K, xq, xd, xs, M, y, ldy, bias, st);
@@ -279,8 +281,8 @@ void matvec_w(int op, const uint8_t* qs, const __half* d, int N, int K, const in
     else launch_mv_t<WT, 16, 1>(op, qs, d, N, K, xq, xd, xs, 1, y, ldy, bias, st);
     return;
   }
-  if (M > 16 && mm_smem<WT, 32, 8>(nb) <= MM_SMEM) return launch_mm<WT, 32>(op, qs, d, N, K, xq, xd, xs, M, y, ldy, bias, st);
-  if (M > 8 && mm_smem<WT, 16, 8>(nb) <= MM_SMEM) return launch_mm<WT, 16>(op, qs, d, N, K, xq, xd, xs, M, y, ldy, bias, st);
+  if (M > 16 && mm_smem<WT, 32, 8>(nb) <= MM_SMEM_FAST) return launch_mm<WT, 32>(op, qs, d, N, K, xq, xd, xs, M, y, ldy, bias, st);
+  if (M > 8 && mm_smem<WT, 16, 8>(nb) <= MM_SMEM_FAST) return launch_mm<WT, 16>(op, qs, d, N, K, xq, xd, xs, M, y, ldy, bias, st);
   if (mm_smem<WT, 8, 8>(nb) <= MM_SMEM) return launch_mm<WT, 8>(op, qs, d, N, K, xq, xd, xs, M, y, ldy, bias, st);
   for (int m0 = 0; m0 < M; m0++)  // rows too long for a staged token group: one token per launch
     launch_mv_t<WT, 16, 1>(op, qs, d, N, K, xq + (size_t)m0 * K, xd + (size_t)m0 * nb, xs + (size_t)m0 * nb, 1,
@@ -316,6 +318,13 @@ cudaError_t mm_attr_mt() {
   return c;
 }
 
+// the grouped attention kernel holds G score rows of ctx floats: usable up to ATTG_SMEM bytes
+constexpr size_t ATTG_SMEM = 100 * 1024;
+bool attg_ok(int G, int HD, int ctx) {
+  if (G > 16 || G * HD > 1024) return false;
+  return (HD == 64 ? attg_smem_bytes<64>(G, ctx) : attg_smem_bytes<128>(G, ctx)) <= ATTG_SMEM;
+}
+
 cudaError_t set_kernel_attrs(int ctx) {
   const int big = 200 * 1024;
   cudaError_t c = mv_attr<WQ4, 32, 1>(big);
@@ -330,6 +339,10 @@ cudaError_t set_kernel_attrs(int ctx) {
   if (c == cudaSuccess) c = mm_attr_mt<WQ8, 32>();
   const int att = ctx * 4 > 48 * 1024 ? ctx * 4 : 48 * 1024;
   if (c == cudaSuccess) c = cudaFuncSetAttribute(k_attention<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, att);
+  if (c == cudaSuccess)
+    c = cudaFuncSetAttribute(k_attention_gqa<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATTG_SMEM);
+  if (c == cudaSuccess)
+    c = cudaFuncSetAttribute(k_attention_gqa<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATTG_SMEM);
   if (c == cudaSuccess) c = cudaFuncSetAttribute(k_attention<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, att);
   return c;
 }
@@ -365,10 +378,18 @@ void enqueue_pass(h2c_engine* e, int M, bool logits, Prof* pf, bool batch = fals
     mark(pf, 2, st);
     k_rope_kv<<<M, 256, 0, st>>>(e->prm, e->qkv, QKV, e->rope, e->kc, e->vc, H, KVH, HD, c.ctx, NL, l);
     mark(pf, 3, st);
-    if (HD == 64)
+    if (M > 1 && attg_ok(H / KVH, HD, c.ctx)) {  // several tokens: one CTA per (kv head, token)
+      if (HD == 64)
+        k_attention_gqa<64><<<dim3(KVH, M), 256, attg_smem_bytes<64>(H / KVH, c.ctx), st>>>(
+            e->prm, e->qkv, QKV, e->kc, e->vc, H, KVH, c.ctx, NL, l, e->att, D);
+      else
+        k_attention_gqa<128><<<dim3(KVH, M), 256, attg_smem_bytes<128>(H / KVH, c.ctx), st>>>(
+            e->prm, e->qkv, QKV, e->kc, e->vc, H, KVH, c.ctx, NL, l, e->att, D);
+    } else if (HD == 64) {
       k_attention<64><<<dim3(H, M), 128, (size_t)c.ctx * 4, st>>>(e->prm, e->qkv, QKV, e->kc, e->vc, H, KVH, c.ctx, NL, l, e->att, D);
-    else
+    } else {
       k_attention<128><<<dim3(H, M), 128, (size_t)c.ctx * 4, st>>>(e->prm, e->qkv, QKV, e->kc, e->vc, H, KVH, c.ctx, NL, l, e->att, D);
+    }
     mark(pf, 4, st);
     {
       const int warps = M * (D / 32);

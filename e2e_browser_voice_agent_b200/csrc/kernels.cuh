@@ -605,6 +605,118 @@ __global__ void __launch_bounds__(128) k_attention(const int32_t* __restrict__ p
   }
 }
 
+// The same attention for the G = H / KVH query heads that share kv head kh, one CTA per (kv head, token): each K row
+// is loaded once for the G heads (scores one position per thread), the G softmax sums run as G chains in position
+// order, and the G * HD ordered p.v chains advance together over chunks of AV_VC V rows staged in shared memory.
+// grid (KVH, M), 256 threads; dynamic smem: attg_smem_bytes(G, ctx).
+constexpr int AV_VC = 32;
+template <int HD>
+__host__ __device__ constexpr size_t attg_smem_bytes(int G, int ctx) {
+  return ((size_t)G * HD + (size_t)G * ((ctx + 3) & ~3) + (size_t)AV_VC * HD + 8 * 16 + 16) * 4;
+}
+template <int HD>
+__global__ void __launch_bounds__(256) k_attention_gqa(const int32_t* __restrict__ prm, const float* __restrict__ qkv,
+                                                       int QKV, const float* __restrict__ kc,
+                                                       const float* __restrict__ vc, int H, int KVH, int ctx,
+                                                       int layers, int layer, float* __restrict__ att, int D) {
+  extern __shared__ __align__(16) float asm_[];
+  const int kh = blockIdx.x, m = blockIdx.y, tid = threadIdx.x, G = H / KVH;
+  const int ctxp = (ctx + 3) & ~3;
+  float* q_s = asm_;                     // [G][HD]
+  float* sc = q_s + G * HD;              // [G][ctxp]
+  float* vst = sc + (size_t)G * ctxp;    // [AV_VC][HD]
+  float* red = vst + AV_VC * HD;         // [8 warps][<= 16 heads]
+  float* sum_s = red + 8 * 16;           // [G]
+  const int T = tok_pos(prm, m) + 1, seq = tok_seq(prm, m);
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
+  for (int i = tid; i < G * HD; i += 256) q_s[i] = qkv[(size_t)m * QKV + (size_t)kh * G * HD + i];
+  __syncthreads();
+  const size_t cbase = (((size_t)seq * layers + layer) * KVH + kh) * (size_t)ctx * HD;
+  const float* kb = kc + cbase;
+  const float* vb = vc + cbase;
+  float mx[16];
+#pragma unroll
+  for (int g = 0; g < 16; g++) mx[g] = -1e30f;
+  for (int t = tid; t < T; t += 256) {
+    float4 kr[HD / 4];
+    const float4* kp = reinterpret_cast<const float4*>(kb + (size_t)t * HD);
+#pragma unroll
+    for (int i = 0; i < HD / 4; i++) kr[i] = __ldg(kp + i);
+#pragma unroll
+    for (int g = 0; g < 16; g++) {
+      if (g < G) {
+        const float* qg = q_s + g * HD;
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+        for (int i = 0; i < HD / 4; i++) {
+          s0 = __fadd_rn(s0, __fmul_rn(qg[4 * i], kr[i].x));
+          s1 = __fadd_rn(s1, __fmul_rn(qg[4 * i + 1], kr[i].y));
+          s2 = __fadd_rn(s2, __fmul_rn(qg[4 * i + 2], kr[i].z));
+          s3 = __fadd_rn(s3, __fmul_rn(qg[4 * i + 3], kr[i].w));
+        }
+        const float v = __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(s0, s1), s2), s3), scale);
+        sc[g * ctxp + t] = v;
+        mx[g] = fmaxf(mx[g], v);
+      }
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < 16; g++) {
+    if (g < G) {
+      const float w = warp_max(mx[g]);
+      if ((tid & 31) == 0) red[(tid >> 5) * 16 + g] = w;
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < G * T; i += 256) {
+    const int g = i / T, t = i - g * T;
+    float w = red[g];
+    for (int k = 1; k < 8; k++) w = fmaxf(w, red[k * 16 + g]);
+    sc[g * ctxp + t] = fast_exp_ref(__fsub_rn(sc[g * ctxp + t], w));
+  }
+  __syncthreads();
+  if (tid < G) {  // softmax sums in position order (kernels.c:368)
+    const float* e = sc + tid * ctxp;
+    float s = 0.f;
+#pragma unroll 8
+    for (int t = 0; t < T; t++) s = __fadd_rn(s, e[t]);
+    sum_s[tid] = s;
+  }
+  __syncthreads();
+  for (int i = tid; i < G * T; i += 256) {
+    const int g = i / T, t = i - g * T;
+    sc[g * ctxp + t] = __fdiv_rn(sc[g * ctxp + t], sum_s[g]);
+  }
+  // o[g][d] = sum_t p[g][t] v[t][d] in position order (kernels.c:372-375); chains c = tid, tid + 256, ...
+  constexpr int NC = 4;  // chains per thread (G * HD <= 1024)
+  float o[NC];
+#pragma unroll
+  for (int k = 0; k < NC; k++) o[k] = 0.f;
+  for (int t0 = 0; t0 < T; t0 += AV_VC) {
+    const int tc = min(AV_VC, T - t0);
+    __syncthreads();  // (also orders the p writes above before their first use)
+    for (int i = tid; i < tc * (HD / 4); i += 256)
+      reinterpret_cast<float4*>(vst)[i] = __ldg(reinterpret_cast<const float4*>(vb + (size_t)t0 * HD) + i);
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < NC; k++) {
+      const int c = tid + 256 * k;
+      if (c < G * HD) {
+        const int g = c / HD, d = c - g * HD;
+        const float* p = sc + g * ctxp + t0;
+        float acc = o[k];
+        for (int t = 0; t < tc; t++) acc = __fadd_rn(acc, __fmul_rn(p[t], vst[t * HD + d]));
+        o[k] = acc;
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < NC; k++) {
+    const int c = tid + 256 * k;
+    if (c < G * HD) att[(size_t)m * D + (size_t)kh * G * HD + c] = o[k];
+  }
+}
+
 // Greedy argmax, stage 1: per-CTA (value, index) with ties to the lowest index (cpu-worker.js:156-157 scans
 // with a strict >).
 __device__ __forceinline__ void amax_merge(float& v, int& i, float v2, int i2) {
