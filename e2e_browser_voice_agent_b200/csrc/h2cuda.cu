@@ -272,6 +272,42 @@ void launch_mm(int op, const uint8_t* qs, const __half* d, int N, int K, const i
     launch_mm_t<WT, TG, 2>(op, qs, d, N, K, xq, xd, xs, M, y, ldy, bias, st);
 }
 
+// The tensor-core form: 32-row sub-ranges; token groups of 32, 16 or 8, the largest that still gives one CTA per SM
+// and fits two CTAs' shared memory per SM.
+constexpr size_t MMTC_SMEM_FAST = 110 * 1024;
+template <int WT, int TG>
+size_t mmtc_smem(int nb) { return (size_t)mt_smem_bytes(WT, TG, nb); }
+
+template <int WT, int TG>
+void launch_mmtc(int op, const uint8_t* qs, const __half* d, int N, int K, const int8_t* xq, const float* xd,
+                 const int4* xs, int M, float* y, int ldy, const float* bias, cudaStream_t st) {
+  const int ntg = (M + TG - 1) / TG;
+  const int groups = (N + 31) / 32;
+  const int nrr = std::max(1, 4 * 148 / ntg);
+  const int rows = 32 * std::max(1, groups / nrr);
+  const int grid = ntg * ((N + rows - 1) / rows);
+  const size_t smem = mmtc_smem<WT, TG>(K / 32);
+  if (op == OP_STORE) k_matmul_tc<WT, TG, OP_STORE><<<grid, 256, smem, st>>>(qs, d, N, K, xq, xd, xs, M, rows, y, ldy, bias);
+  else if (op == OP_BIAS) k_matmul_tc<WT, TG, OP_BIAS><<<grid, 256, smem, st>>>(qs, d, N, K, xq, xd, xs, M, rows, y, ldy, bias);
+  else k_matmul_tc<WT, TG, OP_ADD><<<grid, 256, smem, st>>>(qs, d, N, K, xq, xd, xs, M, rows, y, ldy, bias);
+}
+
+template <int WT>
+bool matmul_tc(int op, const uint8_t* qs, const __half* d, int N, int K, const int8_t* xq, const float* xd,
+               const int4* xs, int M, float* y, int ldy, const float* bias, cudaStream_t st) {
+  const int nb = K / 32, groups = (N + 31) / 32;
+  auto enough = [&](int tg) { return (size_t)((M + tg - 1) / tg) * groups >= 148; };
+  if (M > 16 && enough(32) && mmtc_smem<WT, 32>(nb) <= MMTC_SMEM_FAST)
+    launch_mmtc<WT, 32>(op, qs, d, N, K, xq, xd, xs, M, y, ldy, bias, st);
+  else if (M > 8 && enough(16) && mmtc_smem<WT, 16>(nb) <= MMTC_SMEM_FAST)
+    launch_mmtc<WT, 16>(op, qs, d, N, K, xq, xd, xs, M, y, ldy, bias, st);
+  else if (mmtc_smem<WT, 8>(nb) <= MM_SMEM)
+    launch_mmtc<WT, 8>(op, qs, d, N, K, xq, xd, xs, M, y, ldy, bias, st);
+  else
+    return false;
+  return true;
+}
+
 template <int WT>
 void matvec_w(int op, const uint8_t* qs, const __half* d, int N, int K, const int8_t* xq, const float* xd,
               const int4* xs, int M, float* y, int ldy, const float* bias, cudaStream_t st) {
@@ -281,6 +317,8 @@ void matvec_w(int op, const uint8_t* qs, const __half* d, int N, int K, const in
     else launch_mv_t<WT, 16, 1>(op, qs, d, N, K, xq, xd, xs, 1, y, ldy, bias, st);
     return;
   }
+  if (matmul_tc<WT>(op, qs, d, N, K, xq, xd, xs, M, y, ldy, bias, st)) return;
+  // (token groups too large for the tensor-core form's shared memory: the CUDA-core form below)
   if (M > 16 && mm_smem<WT, 32, 8>(nb) <= MM_SMEM_FAST) return launch_mm<WT, 32>(op, qs, d, N, K, xq, xd, xs, M, y, ldy, bias, st);
   if (M > 8 && mm_smem<WT, 16, 8>(nb) <= MM_SMEM_FAST) return launch_mm<WT, 16>(op, qs, d, N, K, xq, xd, xs, M, y, ldy, bias, st);
   if (mm_smem<WT, 8, 8>(nb) <= MM_SMEM) return launch_mm<WT, 8>(op, qs, d, N, K, xq, xd, xs, M, y, ldy, bias, st);
@@ -315,6 +353,10 @@ template <int WT, int TG>
 cudaError_t mm_attr_mt() {
   cudaError_t c = mm_attr<WT, TG, 8>();
   if (c == cudaSuccess) c = mm_attr<WT, TG, 2>();
+  const int smem = (int)MM_SMEM;
+  if (c == cudaSuccess) c = cudaFuncSetAttribute(k_matmul_tc<WT, TG, OP_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (c == cudaSuccess) c = cudaFuncSetAttribute(k_matmul_tc<WT, TG, OP_BIAS>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (c == cudaSuccess) c = cudaFuncSetAttribute(k_matmul_tc<WT, TG, OP_ADD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   return c;
 }
 

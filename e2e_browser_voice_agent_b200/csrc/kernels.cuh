@@ -512,6 +512,209 @@ __global__ void __launch_bounds__(256) k_matmul(const uint8_t* __restrict__ qs, 
   cp_async_wait_all();
 }
 
+// The same arithmetic with the exact integer block dots on the tensor cores (mma.sync m16n8k32, u8 x s8 for Q4_0
+// nibbles, s8 x s8 for Q8_0). In the permuted block layout lane l of the reference's dot owns bytes 4l .. 4l+3 of
+// each 16-byte half, which are the k = 4t .. 4t+3 and 16+4t .. 16+4t+3 slices of the MMA's A fragment of thread
+// t = l; so an A tile whose row 4 r + l keeps only lane l's weights of weight row r gives, in one MMA, the four lane
+// dots of 4 weight rows x 8 tokens for one block. The accumulator input is the lane's MK_MAGIC - 8 x (sum of its
+// int8 activations) (Q4) or MK_MAGIC (Q8), so each result is the float bit pattern of 12582912 + dot, exactly the
+// value q4_lane / dot_q8 form with dp4a. The float epilogue per block, in block order, is the reference's:
+// acc_l += f32(dot_l) * (dw * dx), the conversion and the two products for two tokens at a time with the packed
+// f32x2 forms (each half rounded as the scalar op). CTA: 8 warps x 4 weight rows = one 32-row group per sub-range; warp w holds the lane sums of rows 4w + (g / 4)
+// and 4w + 2 + (g / 4) (lane g % 4) for tokens 8 j + 2 t, 8 j + 2 t + 1 (g = laneid / 4, t = laneid % 4). The token
+// group's activations stay in shared memory (int8 blocks per token; lane sums as [block][lane][token]; scales as
+// [block][token], so each thread's token pair is one 8-byte load); the weights stream through an MT_ST-stage
+// cp.async ring of MC_BC-block chunks.
+constexpr int MT_ST = 4;
+__host__ __device__ constexpr int mt_xs_lane(int tg) { return tg + 8; }  // ints per lane row (padded)
+__host__ __device__ constexpr int mt_act_bytes(int tg, int nb) {
+  return tg * mm_xq_stride(nb) + nb * 4 * mt_xs_lane(tg) * 4 + nb * tg * 4;
+}
+__host__ __device__ constexpr int mt_smem_bytes(int wt, int tg, int nb) {
+  return mt_act_bytes(tg, nb) + MT_ST * mm_chunk_bytes(wt, 32);
+}
+__device__ __forceinline__ unsigned long long f2(float a, float b) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ unsigned long long f2_mul(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float f2_lo(unsigned long long v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float f2_hi(unsigned long long v) { return __uint_as_float((uint32_t)(v >> 32)); }
+
+template <int WT, int TG, int OP>
+__global__ void __launch_bounds__(256) k_matmul_tc(const uint8_t* __restrict__ qs, const __half* __restrict__ dsc,
+                                                   int N, int K, const int8_t* __restrict__ xq,
+                                                   const float* __restrict__ xd, const int4* __restrict__ xs, int M,
+                                                   int rows_per_cta, float* __restrict__ y, int ldy,
+                                                   const float* __restrict__ bias) {
+  constexpr int WB = mm_wb(WT), SR = 32, CH = mm_chunk_bytes(WT, SR), NT = TG / 8, XL = mt_xs_lane(TG);
+  constexpr int WSZ = SR * MC_BC * WB;
+  extern __shared__ __align__(16) uint8_t msm[];
+  const int nb = K / 32, ntg = (M + TG - 1) / TG, xqs = mm_xq_stride(nb);
+  const int tg = blockIdx.x % ntg, m0 = tg * TG, mt = min(TG, M - m0);
+  const int row_lo = (blockIdx.x / ntg) * rows_per_cta, row_hi = min(N, row_lo + rows_per_cta);
+  const int tid = threadIdx.x, warp = tid >> 5, lid = tid & 31, g = lid >> 2, t = lid & 3, ln = g & 3;
+  const int ra = 4 * warp + (g >> 2), rbw = ra + 2;  // the thread's two weight rows (sub-range local)
+  uint8_t* axq = msm;                                                  // [TG][xqs]
+  int* axs = reinterpret_cast<int*>(axq + TG * xqs);                   // [nb][4][XL]
+  float* axd = reinterpret_cast<float*>(axs + nb * 4 * XL);            // [nb][TG]
+  uint8_t* ring = msm + mt_act_bytes(TG, nb);
+  // the token group's activations, once (tokens past M read as zeros)
+  for (int i = tid; i < TG * nb * 2; i += 256) {
+    const int hf = i & 1, b = (i >> 1) % nb, mm = (i >> 1) / nb;
+    uint8_t* dst = axq + mm * xqs + b * 32 + hf * 16;
+    if (mm < mt) cp_async16(dst, xq + (size_t)(m0 + mm) * K + (size_t)b * 32 + hf * 16);
+    else *reinterpret_cast<int4*>(dst) = make_int4(0, 0, 0, 0);
+  }
+  for (int i = tid; i < TG * nb; i += 256) {
+    const int mm = i % TG, b = i / TG;
+    int4 s4 = make_int4(0, 0, 0, 0);
+    float d = 0.f;
+    if (mm < mt) {
+      if (WT == WQ4) s4 = xs[(size_t)(m0 + mm) * nb + b];
+      d = xd[(size_t)(m0 + mm) * nb + b];
+    }
+    int* sp = axs + (b * 4) * XL + mm;
+    sp[0] = s4.x;
+    sp[XL] = s4.y;
+    sp[2 * XL] = s4.z;
+    sp[3 * XL] = s4.w;
+    axd[b * TG + mm] = d;
+  }
+  const int nkc = (nb + MC_BC - 1) / MC_BC;
+  const int nsub = (row_hi - row_lo + SR - 1) / SR;
+  const int nchunk = nsub * nkc;
+  auto stage = [&](int c) {
+    if (c < nchunk) {
+      uint8_t* ws = ring + (c % MT_ST) * CH;
+      __half* ds = reinterpret_cast<__half*>(ws + WSZ);
+      const int rb = row_lo + (c / nkc) * SR, b0 = (c % nkc) * MC_BC, bc = min(MC_BC, nb - b0);
+      for (int i = tid; i < bc * SR * (WB / 16); i += 256) {
+        const int piece = i % (WB / 16), r = (i / (WB / 16)) % SR, b = i / (WB / 16) / SR;
+        const int n = rb + r;
+        if (n < ((N + 31) & ~31)) {
+          const size_t e = ((size_t)(n >> 5) * nb + b0 + b) * 32 + (n & 31);
+          cp_async16(ws + (b * SR + r) * WB + piece * 16, qs + e * WB + piece * 16);
+        }
+      }
+      for (int i = tid; i < bc * (SR / 2); i += 256) {
+        const int rp = i % (SR / 2), b = i / (SR / 2), n = rb + 2 * rp;
+        if (n < ((N + 31) & ~31))
+          cp_async4(ds + b * SR + 2 * rp, dsc + ((size_t)(n >> 5) * nb + b0 + b) * 32 + (n & 31));
+      }
+    }
+    cp_async_commit();  // (an empty group past the last chunk keeps the group count uniform)
+  };
+  unsigned long long acc[NT][2];  // (row ra: tokens ta, tb), (row rbw: tokens ta, tb)
+#pragma unroll
+  for (int j = 0; j < NT; j++) acc[j][0] = acc[j][1] = 0ull;
+  const unsigned long long magic2 = f2(-12582912.0f, -12582912.0f);
+#pragma unroll
+  for (int s = 0; s < MT_ST - 1; s++) stage(s);
+  for (int c = 0; c < nchunk; c++) {
+    stage(c + MT_ST - 1);
+    cp_async_wait_group<MT_ST - 1>();
+    __syncthreads();
+    const int kc = c % nkc, b0 = kc * MC_BC, bc = min(MC_BC, nb - b0);
+    const uint8_t* ws = ring + (c % MT_ST) * CH;
+    const __half* ds = reinterpret_cast<const __half*>(ws + WSZ);
+    const uint8_t* wa = ws + ra * WB + 4 * t;
+    const uint8_t* wbp = ws + rbw * WB + 4 * t;
+    const uint8_t* xb = axq + g * xqs + b0 * 32 + 4 * t;
+    const int* cs = axs + (b0 * 4 + ln) * XL + 2 * t;
+    const float* dxp = axd + b0 * TG + 2 * t;
+    const bool own = t == ln;
+#pragma unroll
+    for (int b = 0; b < MC_BC; b++) {
+      if (b < bc) {
+        uint32_t a0, a1, a2, a3;
+        if (WT == WQ4) {
+          const uint32_t u0 = own ? *reinterpret_cast<const uint32_t*>(wa + b * SR * WB) : 0u;
+          const uint32_t u1 = own ? *reinterpret_cast<const uint32_t*>(wbp + b * SR * WB) : 0u;
+          a0 = u0 & 0x0f0f0f0fu;
+          a2 = (u0 >> 4) & 0x0f0f0f0fu;
+          a1 = u1 & 0x0f0f0f0fu;
+          a3 = (u1 >> 4) & 0x0f0f0f0fu;
+        } else {
+          a0 = own ? *reinterpret_cast<const uint32_t*>(wa + b * SR * WB) : 0u;
+          a2 = own ? *reinterpret_cast<const uint32_t*>(wa + b * SR * WB + 16) : 0u;
+          a1 = own ? *reinterpret_cast<const uint32_t*>(wbp + b * SR * WB) : 0u;
+          a3 = own ? *reinterpret_cast<const uint32_t*>(wbp + b * SR * WB + 16) : 0u;
+        }
+        const float dw0 = __half2float(ds[b * SR + ra]), dw1 = __half2float(ds[b * SR + rbw]);
+        const unsigned long long w0 = f2(dw0, dw0), w1 = f2(dw1, dw1);
+#pragma unroll
+        for (int j = 0; j < NT; j++) {
+          const uint8_t* xj = xb + 8 * j * xqs + b * 32;
+          const uint32_t b0r = *reinterpret_cast<const uint32_t*>(xj), b1r = *reinterpret_cast<const uint32_t*>(xj + 16);
+          int c0, c1;
+          if (WT == WQ4) {
+            const int2 cc = *reinterpret_cast<const int2*>(cs + b * 4 * XL + 8 * j);
+            c0 = cc.x;
+            c1 = cc.y;
+          } else {
+            c0 = c1 = MK_MAGIC;
+          }
+          int d0, d1, d2, d3;
+          if (WT == WQ4)
+            asm volatile(
+                "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+                "{%10, %11, %12, %13};"
+                : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3)
+                : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0r), "r"(b1r), "r"(c0), "r"(c1), "r"(c0), "r"(c1));
+          else
+            asm volatile(
+                "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+                "{%10, %11, %12, %13};"
+                : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3)
+                : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0r), "r"(b1r), "r"(c0), "r"(c1), "r"(c0), "r"(c1));
+          const unsigned long long dx = *reinterpret_cast<const unsigned long long*>(dxp + b * TG + 8 * j);
+          const unsigned long long p01 = f2_add(f2(__int_as_float(d0), __int_as_float(d1)), magic2);
+          const unsigned long long p23 = f2_add(f2(__int_as_float(d2), __int_as_float(d3)), magic2);
+          const unsigned long long q01 = f2_mul(p01, f2_mul(w0, dx)), q23 = f2_mul(p23, f2_mul(w1, dx));
+          // the running sums are added as scalars: a packed multiply feeding a packed add may be fused into one
+          // packed fused multiply-add by the compiler (one rounding instead of two), which the reference never does
+          acc[j][0] = f2(__fadd_rn(f2_lo(acc[j][0]), f2_lo(q01)), __fadd_rn(f2_hi(acc[j][0]), f2_hi(q01)));
+          acc[j][1] = f2(__fadd_rn(f2_lo(acc[j][1]), f2_lo(q23)), __fadd_rn(f2_hi(acc[j][1]), f2_hi(q23)));
+        }
+      }
+    }
+    if (kc == nkc - 1) {  // the sub-range's rows are complete: ((l0 + l1) + l2) + l3 across g, g + 1, g + 2, g + 3
+      const int rb = row_lo + (c / nkc) * SR;
+#pragma unroll
+      for (int j = 0; j < NT; j++) {
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          const float v0 = (q & 1) ? f2_hi(acc[j][q >> 1]) : f2_lo(acc[j][q >> 1]);
+          const float v1 = __shfl_down_sync(0xffffffffu, v0, 4), v2 = __shfl_down_sync(0xffffffffu, v0, 8),
+                      v3 = __shfl_down_sync(0xffffffffu, v0, 12);
+          const float v = __fadd_rn(__fadd_rn(__fadd_rn(v0, v1), v2), v3);
+          const int mm = 8 * j + 2 * t + (q & 1), n = rb + ((q & 2) ? rbw : ra);
+          if (ln == 0 && mm < mt && n < row_hi) {
+            float* o = y + (size_t)(m0 + mm) * ldy + n;
+            if (OP == OP_ADD) *o = __fadd_rn(*o, v);
+            else if (OP == OP_BIAS) *o = __fadd_rn(v, bias[n]);
+            else *o = v;
+          }
+        }
+        acc[j][0] = acc[j][1] = 0ull;
+      }
+    }
+    __syncthreads();
+  }
+  cp_async_wait_all();
+}
+
 // RoPE on the Q and K heads of each token (pairs (i, i + HD/2), table cos/sin), then K and V appended to the
 // cache of (seq, layer) (kernels.c:337-352). One CTA per token.
 __global__ void k_rope_kv(const int32_t* __restrict__ prm, float* __restrict__ qkv, int QKV, const float* __restrict__ rope,
