@@ -50,8 +50,8 @@ KV_BYTES_PER_POS = 24 * 2 * 64 * 4 * 2
 
 
 # DRAM bytes (read + write) of one decode step of k_decode_persistent, from the ncu capture of a 4-step launch at
-# positions 32..35 (profiles/k_decode_persistent_qwen2-0.5b_full.md): 1,122,512,656 B / 4
-NCU_TRAFFIC_PER_STEP = 280_628_164
+# positions 32..35 (profiles/k_decode_persistent_qwen2-0.5b_full.md): 1,123,237,928 B / 4
+NCU_TRAFFIC_PER_STEP = 280_809_482
 
 
 def step_bytes(pos: int) -> int:
@@ -252,7 +252,7 @@ def bench_c4(args, world, rank, local):
     bytes_step = WEIGHT_BYTES + S * (KV_BYTES_PER_POS * (int(round(mean_pos)) + 2) + 504)
     peak, peak_kind = measured_peaks()
     achieved = bytes_step / (ms / steps / 1e3) / 1e9
-    kernels = be.decode_kernels()
+    kernels = be.batch_kernels(S)
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
         try:
@@ -272,7 +272,7 @@ def bench_c4(args, world, rank, local):
                        "global_batch": S * world, "seq_len": C4_PROMPT + steps, "parallelism": f"sessions x{world}",
                        "l2": "no flush: 278 MB of weights per step > 126 MB L2"},
             "roofline": {"bound": "hbm", "kernel": f"batched decode step ({kernels} kernels in one CUDA graph; "
-                                                   "k_matvec with 32 tokens per weight load)",
+                                                   "k_matmul_tc: int8 tensor-core block dots, 32 tokens per weight load)",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind, "bytes_per_step": bytes_step,
                          "traffic": None},

@@ -22,7 +22,7 @@ PROFILE_NAMES = ["embed", "norm+quantize", "matvec qkv", "rope+kv", "attention",
                  "matvec gate+up", "swiglu+quantize", "matvec down", "matvec output"]  # cpu-worker.js:32
 
 # the exported symbols of include/h2cuda.h
-EXPORTS = ["h2c_create", "h2c_set_tensor", "h2c_forward", "h2c_forward_batch", "h2c_generate_batch", "h2c_generate", "h2c_decode_kernels", "h2c_set_decode_mode",
+EXPORTS = ["h2c_create", "h2c_set_tensor", "h2c_forward", "h2c_forward_batch", "h2c_generate_batch", "h2c_batch_kernels", "h2c_generate", "h2c_decode_kernels", "h2c_set_decode_mode",
            "h2c_decode_path", "h2c_trace_decode", "h2c_decode_ctas", "h2c_set_decode_fault", "h2c_read_logits",
            "h2c_profile", "h2c_destroy", "h2c_selftest_math",
            "h2c_last_error", "h2c_device_bytes", "h2c_q4_matrix_bytes", "h2c_q4_pack", "h2c_q4_matvec_scratch_bytes",
@@ -58,6 +58,7 @@ def load(path: str = LIB_PATH) -> C.CDLL:
     L.h2c_forward.argtypes = [p, C.c_int, p, i32, i32, C.c_float, u32, C.POINTER(i32)]
     L.h2c_forward_batch.argtypes = [p, i32, p, p, p, C.c_float, u32, p]
     L.h2c_generate_batch.argtypes = [p, i32, p, p, p, i32, p, C.POINTER(C.c_float)]
+    L.h2c_batch_kernels.argtypes = [p, i32]
     L.h2c_generate.argtypes = [p, C.c_int, i32, i32, i32, p, C.POINTER(C.c_float)]
     L.h2c_decode_kernels.argtypes = [p]
     L.h2c_set_decode_mode.argtypes = [p, C.c_int]
@@ -80,7 +81,7 @@ def load(path: str = LIB_PATH) -> C.CDLL:
     L.h2c_q4_matvec_scratch_bytes.restype = u64
     L.h2c_q4_matvec.argtypes = [p, i32, i32, p, i32, p, i32, p, p, p]
     L.h2c_q4_matvec_noalloc.argtypes = [p, i32, i32, p, i32, p, i32, p, p]
-    for name in ("h2c_create", "h2c_set_tensor", "h2c_forward", "h2c_forward_batch", "h2c_generate_batch", "h2c_generate", "h2c_decode_kernels", "h2c_set_decode_mode",
+    for name in ("h2c_create", "h2c_set_tensor", "h2c_forward", "h2c_forward_batch", "h2c_generate_batch", "h2c_batch_kernels", "h2c_generate", "h2c_decode_kernels", "h2c_set_decode_mode",
                  "h2c_decode_path", "h2c_trace_decode", "h2c_decode_ctas", "h2c_set_decode_fault", "h2c_read_logits",
                  "h2c_profile", "h2c_selftest_math",
                  "h2c_destroy", "h2c_q4_pack", "h2c_q4_matvec", "h2c_q4_matvec_noalloc"):

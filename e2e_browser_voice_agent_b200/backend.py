@@ -213,6 +213,13 @@ class CudaBackend:
         """Test aid: make one CTA of the persistent kernel withhold its results so the bounded waits expire."""
         _lib.check(self._L.h2c_set_decode_fault(self._h, int(stall_cta), int(timeout_ns)), self._h)
 
+    def batch_kernels(self, n: int) -> int:
+        """Kernels one batched decode step of n sessions launches (0 before the first such step)."""
+        k = self._L.h2c_batch_kernels(self._h, int(n))
+        if k < 0:
+            _lib.check(k, self._h)
+        return k
+
     def decode_kernels(self) -> int:
         n = self._L.h2c_decode_kernels(self._h)
         if n < 0:

@@ -79,6 +79,7 @@ struct h2c_engine {
   int32_t* prm_bh = nullptr;   // pinned [P_WORDS]
   int32_t* next_bh = nullptr;  // pinned [P_CAP]
   std::vector<cudaGraphExec_t> bexec;
+  std::vector<int> bkernels;   // kernel nodes of each batch graph
   std::string err;
   int64_t dev_bytes = 0;
   std::vector<void*> dallocs;
@@ -1113,6 +1114,7 @@ int batch_launch(h2c_engine* e, int32_t n, const int32_t* seqs, const int32_t* i
     CUDA_TRY(e, cudaMallocHost(&e->next_bh, sizeof(int32_t) * P_CAP));
     memset(e->prm_bh, 0, sizeof(int32_t) * P_WORDS);
     e->bexec.assign(cap + 1, nullptr);
+    e->bkernels.assign(cap + 1, 0);
   }
   int32_t* h = e->prm_bh;
   h[P_POS0] = 0; h[P_M] = n; h[P_SEQ] = 0; h[P_MODE] = 1;
@@ -1129,6 +1131,15 @@ int batch_launch(h2c_engine* e, int32_t n, const int32_t* seqs, const int32_t* i
     cudaError_t ce = cudaStreamEndCapture(e->st, &g);
     if (ce != cudaSuccess) return e->fail(H2C_ERR_CUDA, "graph capture: %s", cudaGetErrorString(ce));
     ce = cudaGraphInstantiate(&e->bexec[n], g, 0);
+    size_t nn = 0;
+    if (ce == cudaSuccess) ce = cudaGraphGetNodes(g, nullptr, &nn);
+    std::vector<cudaGraphNode_t> nodes(nn);
+    if (ce == cudaSuccess && nn) ce = cudaGraphGetNodes(g, nodes.data(), &nn);
+    for (size_t i = 0; ce == cudaSuccess && i < nn; i++) {
+      cudaGraphNodeType ty;
+      ce = cudaGraphNodeGetType(nodes[i], &ty);
+      if (ce == cudaSuccess && ty == cudaGraphNodeTypeKernel) e->bkernels[n]++;
+    }
     cudaGraphDestroy(g);
     if (ce != cudaSuccess) return e->fail(H2C_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(ce));
   }
@@ -1261,6 +1272,12 @@ int h2c_decode_ctas(h2c_engine* e) {
   if (r) return r;
   if ((r = mk_build(e))) return r;
   return e->mk_ok ? e->mk_ncta : 0;
+}
+
+int h2c_batch_kernels(h2c_engine* e, int32_t n) {
+  if (!e) return H2C_ERR_INVALID;
+  if (n < 1 || n >= (int)e->bexec.size() || !e->bexec[n]) return 0;
+  return e->bkernels[n];
 }
 
 int h2c_decode_kernels(h2c_engine* e) {

@@ -146,6 +146,10 @@ int h2c_set_decode_fault(h2c_engine* e, int stall_cta, int64_t timeout_ns);
  * counts (all 0 when the fast forms are exact on this GPU) to mismatches[0..3]. */
 int h2c_selftest_math(int device, uint64_t* mismatches);
 
+/* Number of kernels one batched decode step of n sessions launches (the kernel nodes of its CUDA graph, which the
+ * first h2c_forward_batch / h2c_generate_batch of that size builds); 0 before that; < 0 on error. */
+int h2c_batch_kernels(h2c_engine* e, int32_t n);
+
 /* Number of kernels one decode step launches (the kernel nodes of the decode-step CUDA graph); < 0 on error. */
 int h2c_decode_kernels(h2c_engine* e);
 
