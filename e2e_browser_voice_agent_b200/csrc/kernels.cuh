@@ -133,32 +133,12 @@ __device__ __forceinline__ float magic_to_float(int acc) { return __fsub_rn(__in
 
 // Quantize the 32 values held one per lane (kernels.c:90-114): amax over the block (a max is exact in any order),
 // d = amax / 127, q = nearest-even(x * (1 / d)) saturated to int8. Stores the permuted int8 block, the scale and,
-// per lane, MK_MAGIC - 8 x (sum of the lane's int8 values): the accumulator start of the lane's Q4_0 block dot
-// (the -8 nibble offset and the float-conversion constant folded in).
-__device__ __forceinline__ void quant_block_warp(float v, int lane, int8_t* q, float* d, int4* s) {
-  const float amax = warp_max(fabsf(v));
-  const float dd = __fdiv_rn(amax, 127.0f);
-  const float id = dd != 0.0f ? __fdiv_rn(1.0f, dd) : 0.0f;
-  int qi = __float2int_rn(__fmul_rn(v, id));
-  qi = max(-128, min(127, qi));
-  q[(lane & 16) | invperm16(lane & 15)] = (int8_t)qi;
-  // lane l of the dot owns elements {2l, 2l+1, 8+2l, 9+2l} of each half: after the three butterflies below, lane
-  // 2l holds the sum over those eight elements
-  int t = qi + __shfl_xor_sync(0xffffffffu, qi, 1);
-  t += __shfl_xor_sync(0xffffffffu, t, 8);
-  t += __shfl_xor_sync(0xffffffffu, t, 16);
-  const int s1 = __shfl_sync(0xffffffffu, t, 2), s2 = __shfl_sync(0xffffffffu, t, 4),
-            s3 = __shfl_sync(0xffffffffu, t, 6);
-  if (lane == 0) {
-    *d = dd;
-    *s = make_int4(MK_MAGIC - 8 * t, MK_MAGIC - 8 * s1, MK_MAGIC - 8 * s2, MK_MAGIC - 8 * s3);
-  }
-}
-
-// The same quantization with warp reductions in hardware (redux.sync): amax is the integer max of the |x| bit
-// patterns (order-preserving for non-negative floats, and a max is exact in any order); the four lane sums are two
+// per lane l of the reference's dot (the owner of elements {2l, 2l+1, 8+2l, 9+2l} of each half),
+// MK_MAGIC - 8 x (sum of the lane's int8 values): the accumulator start of the lane's Q4_0 block dot (the -8 nibble
+// offset and the float-conversion constant folded in). The warp reductions run in hardware (redux.sync): amax is
+// the integer max of the |x| bit patterns (order-preserving for non-negative floats); the four lane sums are two
 // packed add-reductions of the biased values q + 128 (eight of them per lane sum fit 16 bits), lanes 0 and 1 in one
-// word, 2 and 3 in the other. Bit-identical to quant_block_warp.
+// word, 2 and 3 in the other.
 __device__ __forceinline__ void quant_block_redux(float v, int lane, int8_t* q, float* d, int4* s) {
   const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v))));
   const float dd = block_scale(amax);
@@ -173,42 +153,6 @@ __device__ __forceinline__ void quant_block_redux(float v, int lane, int8_t* q, 
     *d = dd;
     *s = make_int4(MK_MAGIC - 8 * ((int)(s01 & 0xffffu) - 1024), MK_MAGIC - 8 * ((int)(s01 >> 16) - 1024),
                    MK_MAGIC - 8 * ((int)(s23 & 0xffffu) - 1024), MK_MAGIC - 8 * ((int)(s23 >> 16) - 1024));
-  }
-}
-
-// Two blocks at once (v0 -> q0/d0/s0, v1 -> q1/d1/s1): the same arithmetic as quant_block_warp, written
-// interleaved so the shuffle and division latencies of the two blocks overlap.
-__device__ __forceinline__ void quant_block_warp2(float v0, float v1, int lane, int8_t* q0, float* d0, int4* s0,
-                                                  int8_t* q1, float* d1, int4* s1) {
-  float a0 = fabsf(v0), a1 = fabsf(v1);
-#pragma unroll
-  for (int o = 16; o; o >>= 1) {
-    const float b0 = __shfl_xor_sync(0xffffffffu, a0, o), b1 = __shfl_xor_sync(0xffffffffu, a1, o);
-    a0 = fmaxf(a0, b0);
-    a1 = fmaxf(a1, b1);
-  }
-  const float dd0 = __fdiv_rn(a0, 127.0f), dd1 = __fdiv_rn(a1, 127.0f);
-  const float id0 = dd0 != 0.0f ? __fdiv_rn(1.0f, dd0) : 0.0f, id1 = dd1 != 0.0f ? __fdiv_rn(1.0f, dd1) : 0.0f;
-  const int i0 = max(-128, min(127, __float2int_rn(__fmul_rn(v0, id0))));
-  const int i1 = max(-128, min(127, __float2int_rn(__fmul_rn(v1, id1))));
-  const int pos = (lane & 16) | invperm16(lane & 15);
-  q0[pos] = (int8_t)i0;
-  q1[pos] = (int8_t)i1;
-  int t0 = i0 + __shfl_xor_sync(0xffffffffu, i0, 1), t1 = i1 + __shfl_xor_sync(0xffffffffu, i1, 1);
-  t0 += __shfl_xor_sync(0xffffffffu, t0, 8);
-  t1 += __shfl_xor_sync(0xffffffffu, t1, 8);
-  t0 += __shfl_xor_sync(0xffffffffu, t0, 16);
-  t1 += __shfl_xor_sync(0xffffffffu, t1, 16);
-  // lane 0 gathers the lane sums held by lanes 0, 2, 4, 6 (see quant_block_warp)
-  const int u1 = __shfl_sync(0xffffffffu, t0, 2), u2 = __shfl_sync(0xffffffffu, t0, 4),
-            u3 = __shfl_sync(0xffffffffu, t0, 6);
-  const int w1 = __shfl_sync(0xffffffffu, t1, 2), w2 = __shfl_sync(0xffffffffu, t1, 4),
-            w3 = __shfl_sync(0xffffffffu, t1, 6);
-  if (lane == 0) {
-    *d0 = dd0;
-    *d1 = dd1;
-    *s0 = make_int4(MK_MAGIC - 8 * t0, MK_MAGIC - 8 * u1, MK_MAGIC - 8 * u2, MK_MAGIC - 8 * u3);
-    *s1 = make_int4(MK_MAGIC - 8 * t1, MK_MAGIC - 8 * w1, MK_MAGIC - 8 * w2, MK_MAGIC - 8 * w3);
   }
 }
 
@@ -229,7 +173,8 @@ __global__ void k_embed(const int32_t* __restrict__ prm, const uint8_t* __restri
   }
 }
 
-// RMSNorm (kernels.c:80-86) of row (row0 + blockIdx.x) of x, then int8 quantization into slot blockIdx.x.
+// RMSNorm (kernels.c:80-86) of row (row0 + blockIdx.x) of x, then int8 quantization into slot blockIdx.x (the
+// scale with the exact fast division / square root / reciprocal, the blocks with quant_block_redux).
 // The sum of squares runs as the reference's four lane chains (threads 0..3), in element order.
 // dynamic smem: D floats
 __global__ void k_norm_quant(const float* __restrict__ x, int row0, const float* __restrict__ w, int D, float eps,
@@ -251,7 +196,7 @@ __global__ void k_norm_quant(const float* __restrict__ x, int row0, const float*
   __syncthreads();
   if (threadIdx.x == 0) {
     const float ss = __fadd_rn(__fadd_rn(__fadd_rn(part[0], part[1]), part[2]), part[3]);
-    rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), eps)));
+    rs = rcp_rn(sqrt_rn(__fadd_rn(D == 896 ? div896_rn(ss) : __fdiv_rn(ss, (float)D), eps)));
   }
   __syncthreads();
   const float r = rs;
@@ -259,7 +204,7 @@ __global__ void k_norm_quant(const float* __restrict__ x, int row0, const float*
   for (int b = warp; b < nb; b += nw) {
     const int i = b * 32 + lane;
     const float v = __fmul_rn(__fmul_rn(xsm[i], r), w[i]);
-    quant_block_warp(v, lane, xq + (size_t)slot * D + b * 32, xd + (size_t)slot * nb + b, xs + (size_t)slot * nb + b);
+    quant_block_redux(v, lane, xq + (size_t)slot * D + b * 32, xd + (size_t)slot * nb + b, xs + (size_t)slot * nb + b);
   }
 }
 
@@ -272,7 +217,7 @@ __global__ void k_quant(const float* __restrict__ x, int K, int M, int8_t* __res
   if (gw >= M * nb) return;
   const int m = gw / nb, b = gw % nb;
   const float v = x[(size_t)m * K + b * 32 + lane];
-  quant_block_warp(v, lane, xq + (size_t)m * K + b * 32, xd + (size_t)m * nb + b, xs + (size_t)m * nb + b);
+  quant_block_redux(v, lane, xq + (size_t)m * K + b * 32, xd + (size_t)m * nb + b, xs + (size_t)m * nb + b);
 }
 
 // act = silu(gate) * up, then int8 quantization (kernels.c:393-397); one warp per 32-value block of act.
@@ -285,7 +230,7 @@ __global__ void k_swiglu_quant(const float* __restrict__ gu, int F, int M, int8_
   const float* g = gu + (size_t)m * 2 * F;
   const float gt = g[b * 32 + lane], up = g[F + b * 32 + lane];
   const float v = __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, fast_exp_ref(-gt))), up);
-  quant_block_warp(v, lane, xq + (size_t)m * F + b * 32, xd + (size_t)m * nb + b, xs + (size_t)m * nb + b);
+  quant_block_redux(v, lane, xq + (size_t)m * F + b * 32, xd + (size_t)m * nb + b, xs + (size_t)m * nb + b);
 }
 
 enum { OP_STORE = 0, OP_BIAS = 1, OP_ADD = 2 };
@@ -810,12 +755,13 @@ __global__ void __launch_bounds__(128) k_attention(const int32_t* __restrict__ p
 
 // The same attention for the G = H / KVH query heads that share kv head kh, one CTA per (kv head, token): each K row
 // is loaded once for the G heads (scores one position per thread), the G softmax sums run as G chains in position
-// order, and the G * HD ordered p.v chains advance together over chunks of AV_VC V rows staged in shared memory.
+// order, and the G * HD ordered p.v chains advance together over chunks of AV_VC V rows, double-buffered in shared
+// memory with cp.async (the first two chunks are requested before the scores, so they arrive meanwhile).
 // grid (KVH, M), 256 threads; dynamic smem: attg_smem_bytes(G, ctx).
 constexpr int AV_VC = 32;
 template <int HD>
 __host__ __device__ constexpr size_t attg_smem_bytes(int G, int ctx) {
-  return ((size_t)G * HD + (size_t)G * ((ctx + 3) & ~3) + (size_t)AV_VC * HD + 8 * 16 + 16) * 4;
+  return ((size_t)G * HD + (size_t)G * ((ctx + 3) & ~3) + (size_t)2 * AV_VC * HD + 8 * 16 + 16) * 4;
 }
 template <int HD>
 __global__ void __launch_bounds__(256) k_attention_gqa(const int32_t* __restrict__ prm, const float* __restrict__ qkv,
@@ -827,8 +773,8 @@ __global__ void __launch_bounds__(256) k_attention_gqa(const int32_t* __restrict
   const int ctxp = (ctx + 3) & ~3;
   float* q_s = asm_;                     // [G][HD]
   float* sc = q_s + G * HD;              // [G][ctxp]
-  float* vst = sc + (size_t)G * ctxp;    // [AV_VC][HD]
-  float* red = vst + AV_VC * HD;         // [8 warps][<= 16 heads]
+  float* vst = sc + (size_t)G * ctxp;    // [2][AV_VC][HD]
+  float* red = vst + 2 * AV_VC * HD;     // [8 warps][<= 16 heads]
   float* sum_s = red + 8 * 16;           // [G]
   const int T = tok_pos(prm, m) + 1, seq = tok_seq(prm, m);
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
@@ -837,6 +783,17 @@ __global__ void __launch_bounds__(256) k_attention_gqa(const int32_t* __restrict
   const size_t cbase = (((size_t)seq * layers + layer) * KVH + kh) * (size_t)ctx * HD;
   const float* kb = kc + cbase;
   const float* vb = vc + cbase;
+  const int nvc = (T + AV_VC - 1) / AV_VC;
+  auto stage_v = [&](int c) {  // V rows of chunk c into buffer c & 1 (an empty group past the last chunk)
+    if (c < nvc) {
+      const int t0 = c * AV_VC, tc = min(AV_VC, T - t0);
+      float* dst = vst + (c & 1) * AV_VC * HD;
+      for (int i = tid; i < tc * (HD / 4); i += 256) cp_async16(dst + 4 * i, vb + (size_t)t0 * HD + 4 * i);
+    }
+    cp_async_commit();
+  };
+  stage_v(0);
+  stage_v(1);
   float mx[16];
 #pragma unroll
   for (int g = 0; g < 16; g++) mx[g] = -1e30f;
@@ -895,12 +852,11 @@ __global__ void __launch_bounds__(256) k_attention_gqa(const int32_t* __restrict
   float o[NC];
 #pragma unroll
   for (int k = 0; k < NC; k++) o[k] = 0.f;
-  for (int t0 = 0; t0 < T; t0 += AV_VC) {
-    const int tc = min(AV_VC, T - t0);
-    __syncthreads();  // (also orders the p writes above before their first use)
-    for (int i = tid; i < tc * (HD / 4); i += 256)
-      reinterpret_cast<float4*>(vst)[i] = __ldg(reinterpret_cast<const float4*>(vb + (size_t)t0 * HD) + i);
-    __syncthreads();
+  for (int cc = 0; cc < nvc; cc++) {
+    const int t0 = cc * AV_VC, tc = min(AV_VC, T - t0);
+    cp_async_wait_group<1>();  // chunk cc has landed (chunk cc + 1 may still be in flight)
+    __syncthreads();           // (also orders the p writes above before their first use)
+    const float* vbuf = vst + (cc & 1) * AV_VC * HD;
 #pragma unroll
     for (int k = 0; k < NC; k++) {
       const int c = tid + 256 * k;
@@ -908,11 +864,14 @@ __global__ void __launch_bounds__(256) k_attention_gqa(const int32_t* __restrict
         const int g = c / HD, d = c - g * HD;
         const float* p = sc + g * ctxp + t0;
         float acc = o[k];
-        for (int t = 0; t < tc; t++) acc = __fadd_rn(acc, __fmul_rn(p[t], vst[t * HD + d]));
+        for (int t = 0; t < tc; t++) acc = __fadd_rn(acc, __fmul_rn(p[t], vbuf[t * HD + d]));
         o[k] = acc;
       }
     }
+    __syncthreads();  // buffer cc & 1 is free again
+    stage_v(cc + 2);
   }
+  cp_async_wait_all();
 #pragma unroll
   for (int k = 0; k < NC; k++) {
     const int c = tid + 256 * k;
