@@ -552,21 +552,31 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
 
   unsigned long long* trace = nullptr;
   if (p.trace) trace = p.trace + (size_t)cta * p.steps * (L + 1) * MK_TRACE_PTS;
+  // thread 0: the next n (1 or 2) tiles have landed and their table entries describe the rows and blocks the stage
+  // expects. A stage's thread 0 may do this ahead (during the RMSNorm before it, whose chains run on warp 1), so
+  // that the stage itself only passes the barrier.
+  int prewaited = 0;  // thread 0: tiles already waited for ahead of their stage
+  auto wait_tiles = [&](int stage, int n, int rows0, int rows1, int nb) {
+    if (prewaited == n) return;
+    prewaited = n;
+    for (int h = 0; h < n && !abort_s; h++) {
+      const int ti = tile_i + h;
+      const MkTile t = tsm[tpos + h < my_count ? tpos + h : tpos + h - my_count];
+      if (ti >= issued) refill();  // not issued yet: refill now
+      if (t.rows != (h ? rows1 : rows0) || t.nb != nb) {
+        mk_fail(p, MK_ABORTED, stage);
+        abort_s = 1;
+      } else if (!mbar_wait(&full[ti % MK_NSLOT], (ti / MK_NSLOT) & 1, p)) {
+        if (!ld_volatile_i(p.err + 3)) mk_fail(p, MK_TIMEOUT_SLOT, stage);
+        abort_s = 1;
+      }
+    }
+  };
   // wait for the next n (1 or 2) tiles; each table entry must describe the rows and blocks this stage expects
   auto next_tiles = [&](int stage, int n, int rows0, int rows1, int nb) -> bool {
     if (tid == 0) {
-      for (int h = 0; h < n && !abort_s; h++) {
-        const int ti = tile_i + h;
-        const MkTile t = tsm[tpos + h < my_count ? tpos + h : tpos + h - my_count];
-        if (ti >= issued) refill();  // not issued yet: refill now
-        if (t.rows != (h ? rows1 : rows0) || t.nb != nb) {
-          mk_fail(p, MK_ABORTED, stage);
-          abort_s = 1;
-        } else if (!mbar_wait(&full[ti % MK_NSLOT], (ti / MK_NSLOT) & 1, p)) {
-          if (!ld_volatile_i(p.err + 3)) mk_fail(p, MK_TIMEOUT_SLOT, stage);
-          abort_s = 1;
-        }
-      }
+      wait_tiles(stage, n, rows0, rows1, nb);
+      prewaited = 0;
     }
     compute_bar();
     return !abort_s;
@@ -699,6 +709,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
       if (tid == 0) {
         pace = MK_PACE;
         refill();
+        wait_tiles(1, 1, 2 * (pr_hi - pr_lo), 0, nbd);  // the QKV tile, while warp 1 runs the norm's chains
       }
       mk_norm_quant(xf, nw1, D, p.eps, xc, red, sqs, MK_SQ_SINK && l > 0);
       MK_TRACE(trow, 2);
@@ -963,7 +974,13 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
       // ---- D (all CTAs): norm + gate/up rows of whole act blocks, silu * up, quantize (kernels.c:385-397)
       if (!read_vec(p.xw, 2 * E, 10 * l + 3, MK_SQ_SINK)) goto out;
       MK_TRACE(trow, 10);
-      if (tid == 0) refill();
+      if (tid == 0) {
+        refill();
+        if (p.nsplit == 0) {  // the gate/up tiles of the first (or only) pair of act blocks, ahead as above
+          if (cta < nbf) wait_tiles(4, cta + ncta < nbf ? 2 : 1, 64, 64, nbd);
+        } else
+          wait_tiles(4, cta >= ncta - 4 * p.nsplit ? 2 : 1, 64, 16, nbd);
+      }
       mk_norm_quant(xf, nw2, D, p.eps, xc, red, sqs, MK_SQ_SINK);
       MK_TRACE(trow, 14);
       auto publish_act = [&](int h, int ab) {  // warp 8h: silu(gate) * up of tile h, quantized and published
