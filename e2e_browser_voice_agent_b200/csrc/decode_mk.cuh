@@ -555,13 +555,14 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
   // thread 0: the next n (1 or 2) tiles have landed and their table entries describe the rows and blocks the stage
   // expects. A stage's thread 0 may do this ahead (during the RMSNorm before it, whose chains run on warp 1), so
   // that the stage itself only passes the barrier.
-  int prewaited = 0;  // thread 0: tiles already waited for ahead of their stage
-  auto wait_tiles = [&](int stage, int n, int rows0, int rows1, int nb) {
-    if (prewaited == n) return;
-    prewaited = n;
+  int verified = 0;  // thread 0: tiles [0, verified) have landed and were checked (in consumption order)
+  auto wait_tiles = [&](int stage, int ahead, int n, int rows0, int rows1, int nb) {  // tiles tile_i + ahead + h
     for (int h = 0; h < n && !abort_s; h++) {
-      const int ti = tile_i + h;
-      const MkTile t = tsm[tpos + h < my_count ? tpos + h : tpos + h - my_count];
+      const int ti = tile_i + ahead + h;
+      if (ti < verified) continue;
+      int tp = tpos + ahead + h;
+      while (tp >= my_count) tp -= my_count;
+      const MkTile t = tsm[tp];
       if (ti >= issued) refill();  // not issued yet: refill now
       if (t.rows != (h ? rows1 : rows0) || t.nb != nb) {
         mk_fail(p, MK_ABORTED, stage);
@@ -570,14 +571,12 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
         if (!ld_volatile_i(p.err + 3)) mk_fail(p, MK_TIMEOUT_SLOT, stage);
         abort_s = 1;
       }
+      if (!abort_s) verified = ti + 1;
     }
   };
   // wait for the next n (1 or 2) tiles; each table entry must describe the rows and blocks this stage expects
   auto next_tiles = [&](int stage, int n, int rows0, int rows1, int nb) -> bool {
-    if (tid == 0) {
-      wait_tiles(stage, n, rows0, rows1, nb);
-      prewaited = 0;
-    }
+    if (tid == 0) wait_tiles(stage, 0, n, rows0, rows1, nb);
     compute_bar();
     return !abort_s;
   };
@@ -709,7 +708,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
       if (tid == 0) {
         pace = MK_PACE;
         refill();
-        wait_tiles(1, 1, 2 * (pr_hi - pr_lo), 0, nbd);  // the QKV tile, while warp 1 runs the norm's chains
+        wait_tiles(1, 0, 1, 2 * (pr_hi - pr_lo), 0, nbd);  // the QKV tile, while warp 1 runs the norm's chains
       }
       mk_norm_quant(xf, nw1, D, p.eps, xc, red, sqs, MK_SQ_SINK && l > 0);
       MK_TRACE(trow, 2);
@@ -755,6 +754,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
         }
       }
       MK_TRACE(trow, 3);
+      if (!head && !lc && tid == 0) wait_tiles(3, 0, 1, o_hi - o_lo, 0, nbd);  // the O tile, while attention runs
 
       if (lc) {
         // ---- B' (long context, all CTAs): the CTAs of head hg's group (the head CTA and every non-head CTA j with
@@ -976,10 +976,13 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
       MK_TRACE(trow, 10);
       if (tid == 0) {
         refill();
-        if (p.nsplit == 0) {  // the gate/up tiles of the first (or only) pair of act blocks, ahead as above
-          if (cta < nbf) wait_tiles(4, cta + ncta < nbf ? 2 : 1, 64, 64, nbd);
-        } else
-          wait_tiles(4, cta >= ncta - 4 * p.nsplit ? 2 : 1, 64, 16, nbd);
+        // the gate/up tiles of the first (or only) pair of act blocks, ahead as above (waiting for the down tile
+        // here as well measured 36 us per step slower)
+        if (p.nsplit == 0) {
+          if (cta < nbf) wait_tiles(4, 0, cta + ncta < nbf ? 2 : 1, 64, 64, nbd);
+        } else {
+          wait_tiles(4, 0, cta >= ncta - 4 * p.nsplit ? 2 : 1, 64, 16, nbd);
+        }
       }
       mk_norm_quant(xf, nw2, D, p.eps, xc, red, sqs, MK_SQ_SINK);
       MK_TRACE(trow, 14);
