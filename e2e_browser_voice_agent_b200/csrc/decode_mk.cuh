@@ -433,18 +433,58 @@ __device__ __forceinline__ void mk_quant_blocks(int nblk, Fn f, const MkX& x) {
   compute_bar();
 }
 
+// The squares of the RMSNorm are kept lane-major: the square of element k is at sq[(k % 4) * mk_sq_stride(D) + k / 4],
+// so lane chain l's terms are contiguous (16-byte loads) and the four lane rows start in different banks.
+__host__ __device__ constexpr int mk_sq_stride(int D) { return D / 4 + 4; }
+__device__ __forceinline__ int mk_sq_index(int k, int D) { return (k & 3) * mk_sq_stride(D) + (k >> 2); }
+
+// s = ((s + p[0]) + p[1]) + ... over n terms in order, p 16-byte aligned and n a multiple of 4: four float4 loads
+// of the next 16 terms issue before the adds of the current 16 (alternating buffers).
+__device__ __forceinline__ float chain_sum4(float s, const float* p, int n) {
+  const float4* q = reinterpret_cast<const float4*>(p);
+  const int n4 = n >> 2;
+  float4 a[4], b[4];
+#pragma unroll
+  for (int u = 0; u < 4; u++) a[u] = u < n4 ? q[u] : make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int k = 0; k < n4; k += 8) {
+#pragma unroll
+    for (int u = 0; u < 4; u++)
+      if (k + 4 + u < n4) b[u] = q[k + 4 + u];
+#pragma unroll
+    for (int u = 0; u < 4; u++)
+      if (k + u < n4) {
+        s = __fadd_rn(s, a[u].x);
+        s = __fadd_rn(s, a[u].y);
+        s = __fadd_rn(s, a[u].z);
+        s = __fadd_rn(s, a[u].w);
+      }
+#pragma unroll
+    for (int u = 0; u < 4; u++)
+      if (k + 8 + u < n4) a[u] = q[k + 8 + u];
+#pragma unroll
+    for (int u = 0; u < 4; u++)
+      if (k + 4 + u < n4) {
+        s = __fadd_rn(s, b[u].x);
+        s = __fadd_rn(s, b[u].y);
+        s = __fadd_rn(s, b[u].z);
+        s = __fadd_rn(s, b[u].w);
+      }
+  }
+  return s;
+}
+
 // RMSNorm of xf[0..D) (shared) into int8 blocks xq/xd/xs (shared), the reference's lane order (kernels.c:80-114):
-// the squares are formed by all threads into sq (shared, D floats), then thread 32 + l (warp 1, so that thread 0
-// can issue weight copies meanwhile) adds sq[4k + l] over k in order and ((l0 + l1) + l2) + l3 combines the four
-// chains.
+// the squares are formed by all threads into sq (shared, lane-major as above), then thread 32 + l (warp 1, so that
+// thread 0 can issue weight copies meanwhile) adds the squares of elements 4k + l over k in order and
+// ((l0 + l1) + l2) + l3 combines the four chains.
 __device__ __forceinline__ void mk_norm_quant(const float* xf, const float* w, int D, float eps, const MkX& x, float* red,
                                               float* sq, bool have_sq = false) {
   const int tid = threadIdx.x;
   if (!have_sq) {  // (the x reads can deliver the squares with x)
-    for (int i = tid; i < D; i += MK_NT) sq[i] = __fmul_rn(xf[i], xf[i]);
+    for (int i = tid; i < D; i += MK_NT) sq[mk_sq_index(i, D)] = __fmul_rn(xf[i], xf[i]);
     compute_bar();
   }
-  if (tid >= 32 && tid < 36) red[tid - 32] = chain_sum(0.f, sq + (tid - 32), 4, D / 4);
+  if (tid >= 32 && tid < 36) red[tid - 32] = chain_sum4(0.f, sq + (tid - 32) * mk_sq_stride(D), D / 4);
   compute_bar();
   const float ss = __fadd_rn(__fadd_rn(__fadd_rn(red[0], red[1]), red[2]), red[3]);
   const float mean = D == 896 ? div896_rn(ss) : __fdiv_rn(ss, (float)D);
@@ -612,7 +652,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
           [&](int k, uint32_t v) {
             const float f = __uint_as_float(v);
             xf[k] = f;
-            sqs[k] = __fmul_rn(f, f);
+            sqs[mk_sq_index(k, D)] = __fmul_rn(f, f);
           },
           p, stage, &abort_s);
     else
