@@ -497,9 +497,10 @@ __device__ __forceinline__ void mk_quant(const float* xf, int K, const MkX& x) {
   mk_quant_blocks(K / 32, [&](int i) { return xf[i]; }, x);
 }
 
-// Down tiles are row-major (values [R][nb][16 B], then fp16 scales [R][nb]); their products go to a shared
-// buffer of R rows of 4 nb + 4 floats (the padding keeps the ordered chain reads conflict-free).
-__device__ __forceinline__ int mk_prod_stride(int nb) { return 4 * nb + 4; }
+// Down tiles are row-major (values [R][nb][16 B], then fp16 scales [R][nb]); their products go to a shared buffer,
+// lane-major: row r's lane-l products of blocks 0 .. nb-1 are contiguous at (4 r + l) * mk_prod_lane_stride(nb)
+// (16-byte aligned; the padding spreads the 4 R chain threads' 16-byte reads over the banks).
+__host__ __device__ constexpr int mk_prod_lane_stride(int nb) { return ((nb + 3) & ~3) + 4; }
 
 // ---------------------------------------------------------------- the kernel
 // Shape parameters TD (hidden), TF (ffn), TH (q heads), TKVH (kv heads), THD (head dim) fix the model shape at
@@ -1074,7 +1075,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
       // row of the CTA; warps 8.. quantize the split blocks the same way; warps 6-7 then add each (row, lane)
       // chain in block order once all blocks are in.
       if (!head) {
-        const int R = o_hi - o_lo, PS = mk_prod_stride(nbf);
+        const int R = o_hi - o_lo, LS = mk_prod_lane_stride(nbf);
         const int nq = nbf - p.nsplit;  // blocks published quantized
         if (tid == 0) ndone_s = 0;
         if (!next_tiles(5, 1, R, 0, nbf)) goto out;
@@ -1086,9 +1087,11 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
           const int it = r * nbf + b;
           const uint4 w = *reinterpret_cast<const uint4*>(tl + (size_t)it * 16);
           const float sc = __fmul_rn(__half2float(wdn[it]), dx);
-          *reinterpret_cast<float4*>(pf + r * PS + 4 * b) =
-              make_float4(__fmul_rn(q4_lane(w.x, x0.x, x1.x, xs4.x), sc), __fmul_rn(q4_lane(w.y, x0.y, x1.y, xs4.y), sc),
-                          __fmul_rn(q4_lane(w.z, x0.z, x1.z, xs4.z), sc), __fmul_rn(q4_lane(w.w, x0.w, x1.w, xs4.w), sc));
+          float* o = pf + (size_t)(4 * r) * LS + b;
+          o[0] = __fmul_rn(q4_lane(w.x, x0.x, x1.x, xs4.x), sc);
+          o[LS] = __fmul_rn(q4_lane(w.y, x0.y, x1.y, xs4.y), sc);
+          o[2 * LS] = __fmul_rn(q4_lane(w.z, x0.z, x1.z, xs4.z), sc);
+          o[3 * LS] = __fmul_rn(q4_lane(w.w, x0.w, x1.w, xs4.w), sc);
         };
         if (tid < 192) {
           // warp w takes blocks 32 w + 192 k ...: its lanes poll the blocks' words together (each load instruction
@@ -1186,7 +1189,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
           __threadfence_block();
           if (trace && c == 0) trace[(size_t)trow * MK_TRACE_PTS + 12] = gtimer();
           float acc = 0.f;
-          if (c < 4 * R && !*(volatile int*)&abort_s) acc = chain_sum(0.f, pf + (c >> 2) * PS + (c & 3), 4, nbf);
+          if (c < 4 * R && !*(volatile int*)&abort_s)
+            acc = (nbf & 3) == 0 ? chain_sum4(0.f, pf + (size_t)c * LS, nbf) : chain_sum(0.f, pf + (size_t)c * LS, 1, nbf);
           const float hv = hsum4_quad(acc);
           if (c < 4 * R && (c & 3) == 0) outv[c >> 2] = hv;
         }

@@ -605,9 +605,9 @@ int mk_build(h2c_engine* e) {
   const int npair = QKV / 2, pr_max = (npair + ncta - 1) / ncta;
   if (2 * pr_max > 64) return mk_unsupported(e, "more than 64 QKV rows per CTA");
   if (nbf > MK_NT) return mk_unsupported(e, "rows longer than the tile kernel's thread count");
-  // product buffer of the row-major (down) tiles: R rows of (4 nb + 4) floats, in float4 units; it also holds the
-  // D squares of the RMSNorm
-  const int prod_items = std::max(o_max * (nbf + 1), D / 4 + 4);  // (RMSNorm squares: 4 lane rows of D / 4 + 4)
+  // product buffer (float4 units) of the row-major (down) tiles: 4 lane rows per row; it also holds the squares of
+  // the RMSNorm (4 lane rows of D / 4 + 4 floats)
+  const int prod_items = std::max(o_max * mk_prod_lane_stride(nbf), D / 4 + 4);
   const size_t base = mk_smem_base(D, F, HD, c.ctx, prod_items);
   int max_optin = 0;
   CUDA_TRY(e, cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, e->dev));
