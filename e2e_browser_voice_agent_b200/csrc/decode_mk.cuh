@@ -501,6 +501,8 @@ __device__ __forceinline__ void mk_quant(const float* xf, int K, const MkX& x) {
 // lane-major: row r's lane-l products of blocks 0 .. nb-1 are contiguous at (4 r + l) * mk_prod_lane_stride(nb)
 // (16-byte aligned; the padding spreads the 4 R chain threads' 16-byte reads over the banks).
 __host__ __device__ constexpr int mk_prod_lane_stride(int nb) { return ((nb + 3) & ~3) + 4; }
+// row stride (floats) of the products of a few-row chain tile: at least nbp, 16-byte aligned, 4 banks apart
+__host__ __device__ constexpr int mk_small_stride(int nbp) { return (nbp + 27) / 32 * 32 + 4; }
 
 // ---------------------------------------------------------------- the kernel
 // Shape parameters TD (hidden), TF (ffn), TH (q heads), TKVH (kv heads), THD (head dim) fix the model shape at
@@ -643,6 +645,33 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
     release_tiles(n);
     return true;
   };
+  // One chain tile of few rows (QKV, O: 4 R lane chains would leave 15 of 16 warps idle): all warps form the
+  // R x 4 x nb lane products into shared memory (prod, one padded row per (r, l)), then thread (r, l) adds its
+  // lane's products in block order; the same arithmetic and order as mk_lane_chain. Row r lands in outv[r].
+  auto small_tile = [&](int stage, int R, int nb) -> bool {
+    const int nbp = mk_nbp(nb), PSS = mk_small_stride(nbp);
+    if (4 * R > MK_NT || 4 * R * PSS > 4 * p.prod_items) return chain_tiles(stage, 1, R, 0, nb);
+    if (!next_tiles(stage, 1, R, 0, nb)) return false;
+    const uint8_t* tl = ring + (size_t)(tile_i % MK_NSLOT) * MK_SLOT;
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(tl);
+    const __half* dws = reinterpret_cast<const __half*>(tl + (size_t)R * nbp * 16);
+    float* pp = reinterpret_cast<float*>(prod);
+    for (int i = tid; i < 4 * R * nb; i += MK_NT) {
+      const int rl = i / nb, b = i - rl * nb, l = rl & 3;
+      const float q = q4_lane(w[(size_t)rl * nbp + b], xc.x0[l * nbp + b], xc.x1[l * nbp + b], xc.xs[l * nbp + b]);
+      pp[rl * PSS + b] = __fmul_rn(q, __fmul_rn(__half2float(dws[(rl >> 2) * nbp + b]), xc.dx[b]));
+    }
+    compute_bar();
+    if ((tid & ~31) < 4 * R) {  // whole warps: hsum4_quad shuffles over all 32 lanes
+      const int r = tid >> 2;
+      float a = 0.f;
+      if (r < R) a = (nb & 3) == 0 ? chain_sum4(0.f, pp + tid * PSS, nb) : chain_sum(0.f, pp + tid * PSS, 1, nb);
+      const float v = hsum4_quad(a);
+      if (r < R && (tid & 3) == 0) outv[r] = v;
+    }
+    release_tiles(1);
+    return true;
+  };
   // read D tagged floats (x or att) into xf
   float* sqs = reinterpret_cast<float*>(prod);  // norm squares (prod is free between tiles)
   // read D tagged floats into xf; with_sq also stores their squares into sqs for the RMSNorm that follows
@@ -755,7 +784,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
       MK_TRACE(trow, 2);
       {
         const int R = 2 * (pr_hi - pr_lo);
-        if (!chain_tiles(1, 1, R, 0, nbd)) goto out;
+        if (!small_tile(1, R, nbd)) goto out;
         const int npub = cta == p.stall_cta ? 0 : pr_hi - pr_lo;
         for (int jp = tid; jp < npub; jp += MK_NT) {
           const int pidx = pr_lo + jp, hh = pidx / half, i = pidx % half;
@@ -1003,7 +1032,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
         if (!read_vec(p.attw, E, 10 * l + 2)) goto out;
         MK_TRACE(trow, 8);
         mk_quant(xf, D, xc);
-        if (!chain_tiles(3, 1, o_hi - o_lo, 0, nbd)) goto out;
+        if (!small_tile(3, o_hi - o_lo, nbd)) goto out;
         for (int n = o_lo + tid; n < o_hi; n += MK_NT) {
           const float v = __fadd_rn(xown[n - o_lo], outv[n - o_lo]);
           xown[n - o_lo] = v;
