@@ -170,8 +170,8 @@ __device__ __forceinline__ float mk_lane_chain(const uint8_t* tile, int R, int n
 // quant_block_redux, stored per lane
 __device__ __forceinline__ void mk_quant_chain(float v, int lane, int b, int nbp, const MkX& x) {
   const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v))));
-  const float dd = block_scale(amax);
-  const float id = block_iscale(dd);
+  float dd, id;
+  block_scales(amax, dd, id);
   const int qi = max(-128, min(127, __float2int_rn(__fmul_rn(v, id))));
   const int pos = (lane & 16) | invperm16(lane & 15);  // byte of the permuted block (word pos / 4)
   int8_t* dst = reinterpret_cast<int8_t*>(pos < 16 ? x.x0 : x.x1);
@@ -392,8 +392,8 @@ __device__ __forceinline__ float chain_sum(float s, const float* p, int stride, 
 __device__ __forceinline__ void mk_quant_chain2(float v0, float v1, int lane, int b0, int b1, int nbp, const MkX& x) {
   const unsigned m0 = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v0)));
   const unsigned m1 = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v1)));
-  const float d0 = block_scale(__uint_as_float(m0)), d1 = block_scale(__uint_as_float(m1));
-  const float i0 = block_iscale(d0), i1 = block_iscale(d1);
+  float d0, d1, i0, i1;
+  block_scales2(__uint_as_float(m0), __uint_as_float(m1), d0, d1, i0, i1);
   const int q0 = max(-128, min(127, __float2int_rn(__fmul_rn(v0, i0))));
   const int q1 = max(-128, min(127, __float2int_rn(__fmul_rn(v1, i1))));
   const int pos = (lane & 16) | invperm16(lane & 15);
@@ -487,8 +487,7 @@ __device__ __forceinline__ void mk_norm_quant(const float* xf, const float* w, i
   if (tid >= 32 && tid < 36) red[tid - 32] = chain_sum4(0.f, sq + (tid - 32) * mk_sq_stride(D), D / 4);
   compute_bar();
   const float ss = __fadd_rn(__fadd_rn(__fadd_rn(red[0], red[1]), red[2]), red[3]);
-  const float mean = D == 896 ? div896_rn(ss) : __fdiv_rn(ss, (float)D);
-  const float r = rcp_rn(sqrt_rn(__fadd_rn(mean, eps)));
+  const float r = norm_scale(ss, D, eps);
   mk_quant_blocks(D / 32, [&](int i) { return __fmul_rn(__fmul_rn(xf[i], r), w[i]); }, x);
 }
 

@@ -92,38 +92,61 @@ constexpr float H2_R127_HI = (float)(1.0 / 127.0);
 constexpr float H2_R127_LO = (float)((1.0 - 127.0 * (double)H2_R127_HI) / 127.0);
 constexpr float H2_R896_HI = (float)(1.0 / 896.0);
 constexpr float H2_R896_LO = (float)((1.0 - 896.0 * (double)H2_R896_HI) / 896.0);
-__device__ __forceinline__ float div127_rn(float x) {
-  const unsigned b = __float_as_uint(x);
-  if (b >= 0x0D800000u && b < 0x7F800000u) return __fmaf_rn(x, H2_R127_HI, __fmul_rn(x, H2_R127_LO));
-  return __fdiv_rn(x, 127.0f);
+// The fast forms themselves (branch-free) and their input ranges. Callers that need several results test all the
+// ranges once and fall back to the intrinsics together, so the common path has one branch instead of one per
+// operation (each branch around a possible call to the intrinsics' slow path costs a warp re-convergence).
+__device__ __forceinline__ bool div_fast_ok(float x) { return __float_as_uint(x) - 0x0D800000u < 0x72000000u; }
+__device__ __forceinline__ float div127_fast(float x) { return __fmaf_rn(x, H2_R127_HI, __fmul_rn(x, H2_R127_LO)); }
+__device__ __forceinline__ float div896_fast(float x) { return __fmaf_rn(x, H2_R896_HI, __fmul_rn(x, H2_R896_LO)); }
+__device__ __forceinline__ bool rcp_fast_ok(float b) { return __float_as_uint(b) - 0x00800000u <= 0x7E000000u; }
+__device__ __forceinline__ float rcp_fast(float b) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(b));
+  return __fmaf_rn(__fmaf_rn(-b, y, 1.0f), y, y);
 }
-__device__ __forceinline__ float div896_rn(float x) {
-  const unsigned b = __float_as_uint(x);
-  if (b >= 0x0D800000u && b < 0x7F800000u) return __fmaf_rn(x, H2_R896_HI, __fmul_rn(x, H2_R896_LO));
-  return __fdiv_rn(x, 896.0f);
+__device__ __forceinline__ bool sqrt_fast_ok(float a) { return __float_as_uint(a) - 0x0C800000u < 0x73000000u; }
+__device__ __forceinline__ float sqrt_fast(float a) {
+  float r;
+  asm("rsqrt.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(a));
+  const float s = __fmul_rn(a, r);
+  return __fmaf_rn(__fmaf_rn(-s, s, a), __fmul_rn(0.5f, r), s);
 }
-__device__ __forceinline__ float rcp_rn(float b) {
-  const unsigned u = __float_as_uint(b);
-  if (u >= 0x00800000u && u <= 0x7E800000u) {
-    float y;
-    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(b));
-    return __fmaf_rn(__fmaf_rn(-b, y, 1.0f), y, y);
+__device__ __forceinline__ float div127_rn(float x) { return div_fast_ok(x) ? div127_fast(x) : __fdiv_rn(x, 127.0f); }
+__device__ __forceinline__ float div896_rn(float x) { return div_fast_ok(x) ? div896_fast(x) : __fdiv_rn(x, 896.0f); }
+__device__ __forceinline__ float rcp_rn(float b) { return rcp_fast_ok(b) ? rcp_fast(b) : __fdiv_rn(1.0f, b); }
+__device__ __forceinline__ float sqrt_rn(float a) { return sqrt_fast_ok(a) ? sqrt_fast(a) : __fsqrt_rn(a); }
+// the int8 block scale and its reciprocal: d = amax / 127, id = d ? 1 / d : 0 (kernels.c:96-97), for one block and
+// for two blocks at once
+__device__ __forceinline__ void block_scales(float amax, float& d, float& id) {
+  d = div127_fast(amax);
+  id = rcp_fast(d);
+  if (!(div_fast_ok(amax) && rcp_fast_ok(d))) {
+    d = __fdiv_rn(amax, 127.0f);
+    id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
   }
-  return __fdiv_rn(1.0f, b);
 }
-__device__ __forceinline__ float sqrt_rn(float a) {
-  const unsigned u = __float_as_uint(a);
-  if (u >= 0x0C800000u && u < 0x7F800000u) {
-    float r;
-    asm("rsqrt.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(a));
-    const float s = __fmul_rn(a, r);
-    return __fmaf_rn(__fmaf_rn(-s, s, a), __fmul_rn(0.5f, r), s);
+__device__ __forceinline__ void block_scales2(float a0, float a1, float& d0, float& d1, float& i0, float& i1) {
+  d0 = div127_fast(a0);
+  d1 = div127_fast(a1);
+  i0 = rcp_fast(d0);
+  i1 = rcp_fast(d1);
+  if (!(div_fast_ok(a0) && div_fast_ok(a1) && rcp_fast_ok(d0) && rcp_fast_ok(d1))) {
+    d0 = __fdiv_rn(a0, 127.0f);
+    d1 = __fdiv_rn(a1, 127.0f);
+    i0 = d0 != 0.0f ? __fdiv_rn(1.0f, d0) : 0.0f;
+    i1 = d1 != 0.0f ? __fdiv_rn(1.0f, d1) : 0.0f;
   }
-  return __fsqrt_rn(a);
 }
-// the int8 block scale and its reciprocal: d = amax / 127, id = d ? 1 / d : 0 (kernels.c:96-97)
-__device__ __forceinline__ float block_scale(float amax) { return div127_rn(amax); }
-__device__ __forceinline__ float block_iscale(float d) { return d != 0.0f ? rcp_rn(d) : 0.0f; }
+// the RMSNorm scale 1 / sqrt(ss / D + eps) (kernels.c:84), every step correctly rounded
+__device__ __forceinline__ float norm_scale(float ss, int D, float eps) {
+  if (D == 896) {
+    const float m = __fadd_rn(div896_fast(ss), eps);
+    const float q = sqrt_fast(m);
+    const float r = rcp_fast(q);
+    if (div_fast_ok(ss) && sqrt_fast_ok(m) && rcp_fast_ok(q)) return r;
+  }
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), eps)));
+}
 
 // Integers |p| < 2^22 converted to float without the (quarter-rate) int->float instruction: the bit pattern
 // MK_MAGIC + p is the float 12582912 + p exactly, and subtracting 12582912 is exact. Block dots carry MK_MAGIC in
@@ -141,8 +164,8 @@ __device__ __forceinline__ float magic_to_float(int acc) { return __fsub_rn(__in
 // word, 2 and 3 in the other.
 __device__ __forceinline__ void quant_block_redux(float v, int lane, int8_t* q, float* d, int4* s) {
   const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v))));
-  const float dd = block_scale(amax);
-  const float id = block_iscale(dd);
+  float dd, id;
+  block_scales(amax, dd, id);
   const int qi = max(-128, min(127, __float2int_rn(__fmul_rn(v, id))));
   q[(lane & 16) | invperm16(lane & 15)] = (int8_t)qi;
   const int dl = (lane & 7) >> 1;  // the dot lane that owns this element
@@ -196,7 +219,7 @@ __global__ void k_norm_quant(const float* __restrict__ x, int row0, const float*
   __syncthreads();
   if (threadIdx.x == 0) {
     const float ss = __fadd_rn(__fadd_rn(__fadd_rn(part[0], part[1]), part[2]), part[3]);
-    rs = rcp_rn(sqrt_rn(__fadd_rn(D == 896 ? div896_rn(ss) : __fdiv_rn(ss, (float)D), eps)));
+    rs = norm_scale(ss, D, eps);
   }
   __syncthreads();
   const float r = rs;
