@@ -176,14 +176,10 @@ __device__ __forceinline__ void mk_quant_chain(float v, int lane, int b, int nbp
   const int pos = (lane & 16) | invperm16(lane & 15);  // byte of the permuted block (word pos / 4)
   int8_t* dst = reinterpret_cast<int8_t*>(pos < 16 ? x.x0 : x.x1);
   dst[((((pos & 15) >> 2) * nbp) + b) * 4 + (pos & 3)] = (int8_t)qi;
-  const int dl = (lane & 7) >> 1;
-  const unsigned bq = (unsigned)(qi + 128) << ((dl & 1) * 16);
-  const unsigned s01 = __reduce_add_sync(0xffffffffu, dl < 2 ? bq : 0u);
-  const unsigned s23 = __reduce_add_sync(0xffffffffu, dl < 2 ? 0u : bq);
-  if (lane < 4) {
-    const unsigned sw = lane < 2 ? s01 : s23;
-    const int t = (int)((lane & 1) ? (sw >> 16) : (sw & 0xffffu)) - 1024;
-    x.xs[lane * nbp + b] = MK_MAGIC - 8 * t;
+  __syncwarp();
+  if (lane < 4) {  // lane l's sum: its words of the two halves, just stored (dp4a against ones)
+    const int i = lane * nbp + b;
+    x.xs[i] = MK_MAGIC - 8 * __dp4a(x.x0[i], 0x01010101, __dp4a(x.x1[i], 0x01010101, 0));
   }
   if (lane == 0) x.dx[b] = dd;
 }
@@ -400,19 +396,10 @@ __device__ __forceinline__ void mk_quant_chain2(float v0, float v1, int lane, in
   int8_t* dst = reinterpret_cast<int8_t*>(pos < 16 ? x.x0 : x.x1) + ((((pos & 15) >> 2) * nbp) * 4 + (pos & 3));
   dst[b0 * 4] = (int8_t)q0;
   dst[b1 * 4] = (int8_t)q1;
-  const int dl = (lane & 7) >> 1;
-  const unsigned sh = (dl & 1) * 16;
-  const unsigned a0 = (unsigned)(q0 + 128) << sh, a1 = (unsigned)(q1 + 128) << sh;
-  const unsigned s01a = __reduce_add_sync(0xffffffffu, dl < 2 ? a0 : 0u);
-  const unsigned s23a = __reduce_add_sync(0xffffffffu, dl < 2 ? 0u : a0);
-  const unsigned s01b = __reduce_add_sync(0xffffffffu, dl < 2 ? a1 : 0u);
-  const unsigned s23b = __reduce_add_sync(0xffffffffu, dl < 2 ? 0u : a1);
-  if (lane < 4) {
-    const unsigned wa = lane < 2 ? s01a : s23a, wb = lane < 2 ? s01b : s23b;
-    const int ta = (int)((lane & 1) ? (wa >> 16) : (wa & 0xffffu)) - 1024;
-    const int tb = (int)((lane & 1) ? (wb >> 16) : (wb & 0xffffu)) - 1024;
-    x.xs[lane * nbp + b0] = MK_MAGIC - 8 * ta;
-    x.xs[lane * nbp + b1] = MK_MAGIC - 8 * tb;
+  __syncwarp();
+  if (lane < 8) {  // lane l of block b0 (lanes 0-3) / b1 (lanes 4-7): its words of the two halves, dp4a against ones
+    const int i = (lane & 3) * nbp + (lane < 4 ? b0 : b1);
+    x.xs[i] = MK_MAGIC - 8 * __dp4a(x.x0[i], 0x01010101, __dp4a(x.x1[i], 0x01010101, 0));
   }
   if (lane == 0) {
     x.dx[b0] = d0;
@@ -1061,8 +1048,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
         const float v = __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, fast_exp_ref(-gt))), up);
         int8_t* aq = reinterpret_cast<int8_t*>(actb + 64 * h);
         float* ad = reinterpret_cast<float*>(actb + 64 * h + 32);
-        int4* as = reinterpret_cast<int4*>(actb + 64 * h + 48);
-        quant_block_redux(v, lane, aq, ad, as);
+        quant_block_nosum(v, lane, aq, ad);  // (the consumers form the lane sums themselves)
         __syncwarp();
         if (lane < 6) {  // bytes 6 lane .. 6 lane + 5 of the int8 block and its scale, under the epoch's low 16 bits
           const uint8_t* bb = actb + 64 * h;

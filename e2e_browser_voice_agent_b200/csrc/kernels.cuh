@@ -179,6 +179,15 @@ __device__ __forceinline__ void quant_block_redux(float v, int lane, int8_t* q, 
   }
 }
 
+// quant_block_redux without the lane sums (for blocks whose consumers form them from the int8 values)
+__device__ __forceinline__ void quant_block_nosum(float v, int lane, int8_t* q, float* d) {
+  const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v))));
+  float dd, id;
+  block_scales(amax, dd, id);
+  q[(lane & 16) | invperm16(lane & 15)] = (int8_t)max(-128, min(127, __float2int_rn(__fmul_rn(v, id))));
+  if (lane == 0) *d = dd;
+}
+
 // x[m] = dequant(embedding row ids[m]) (kernels.c:313-322), from the grouped / permuted Q4_0 layout
 __global__ void k_embed(const int32_t* __restrict__ prm, const uint8_t* __restrict__ qs, const __half* __restrict__ dsc,
                         int D, float* __restrict__ x) {
