@@ -618,9 +618,11 @@ int mk_build(h2c_engine* e) {
   // beyond kv_stage positions attention streams the V columns through the same area: it must hold a few rows
   if (kv_stage < std::min(16, c.ctx)) return mk_unsupported(e, "context too long for the shared-memory budget");
   const size_t smem = base + (size_t)kv_stage * (2 * HD + 4) * 4;
-  // the Qwen2.5-0.5B shape has its own instance with the shape compiled in; other shapes take the generic one
-  e->mk_kernel = (D == 896 && F == 4864 && H == 14 && KVH == 2 && HD == 64) ? (void*)k_decode_persistent<896, 4864, 14, 2, 64>
-                                                                          : (void*)k_decode_persistent<0, 0, 0, 0, 0>;
+  // the Qwen2.5-0.5B shape has its own instance with the shape compiled in (and without the chain-tile fallback
+  // of the QKV and O tiles, so its QKV and O tiles must fit the two-phase form); other shapes take the generic one
+  const bool fixed = D == 896 && F == 4864 && H == 14 && KVH == 2 && HD == 64 &&
+                     mk_small_tile_fits(2 * pr_max, nbd, prod_items) && mk_small_tile_fits(o_max, nbd, prod_items);
+  e->mk_kernel = fixed ? (void*)k_decode_persistent<896, 4864, 14, 2, 64> : (void*)k_decode_persistent<0, 0, 0, 0, 0>;
   CUDA_TRY(e, cudaFuncSetAttribute(e->mk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   int occ = 0;
   CUDA_TRY(e, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, e->mk_kernel, MK_THREADS, smem));
