@@ -492,6 +492,11 @@ __device__ __forceinline__ void mk_quant(const float* xf, int K, const MkX& x) {
 __host__ __device__ constexpr int mk_prod_lane_stride(int nb) { return ((nb + 3) & ~3) + 4; }
 // row stride (floats) of the products of a few-row chain tile: at least nbp, 16-byte aligned, 4 banks apart
 __host__ __device__ constexpr int mk_small_stride(int nbp) { return (nbp + 27) / 32 * 32 + 4; }
+// act blocks beyond one per CTA (nbf blocks over ncta CTAs, nh of which own O / down rows): up to 8 are split into
+// 16-row gate/up pieces on the last 4 nsplit CTAs (returns nsplit), else (0) every CTA takes whole blocks
+__host__ __device__ constexpr int mk_nsplit(int nbf, int ncta, int nh) {
+  return (nbf > ncta && nbf - ncta <= 8 && 4 * (nbf - ncta) <= nh) ? nbf - ncta : 0;
+}
 // a few-row chain tile of R rows and nb blocks fits the two-phase form: 4 R chain threads, products in prod
 __host__ __device__ constexpr bool mk_small_tile_fits(int R, int nb, int prod_items) {
   return 4 * R <= MK_NT && 4 * R * mk_small_stride(mk_nbp(nb)) <= 4 * prod_items;
@@ -500,8 +505,10 @@ __host__ __device__ constexpr bool mk_small_tile_fits(int R, int nb, int prod_it
 // ---------------------------------------------------------------- the kernel
 // Shape parameters TD (hidden), TF (ffn), TH (q heads), TKVH (kv heads), THD (head dim) fix the model shape at
 // compile time when non-zero, so buffer offsets and loop bounds are constants (fewer live registers in this
-// single large kernel); 0 takes the shape from MkParams.
-template <int TD, int TF, int TH, int TKVH, int THD>
+// single large kernel); 0 takes the shape from MkParams. TNCTA likewise fixes the grid size (and with it the
+// split of the act blocks) when non-zero. TR compiles in the optional timestamp trace (p.trace):
+// the untraced instance carries none of its code (the kernel's code exceeds the instruction cache).
+template <int TD, int TF, int TH, int TKVH, int THD, int TNCTA, bool TR>
 __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int D = TD ? TD : p.D, F = TF ? TF : p.F, H = TH ? TH : p.H, KVH = TKVH ? TKVH : p.KVH,
@@ -538,7 +545,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
   __shared__ int ndone_s;       // act blocks whose down products are in prod
   __shared__ __align__(16) uint8_t splitq_s[8][64];  // quantized split act blocks: 32 B int8, d, lane sums
 
-  const int tid = threadIdx.x, cta = blockIdx.x, ncta = p.ncta;
+  const int tid = threadIdx.x, cta = blockIdx.x, ncta = TNCTA ? TNCTA : p.ncta;
+  const int nsplit = TNCTA ? mk_nsplit(nbf, TNCTA, TNCTA - H) : p.nsplit;
   const MkTile* my_tiles = p.tiles + (size_t)cta * p.tile_stride;
 
   if (tid == 0) {
@@ -587,7 +595,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
   if (tid == 0) refill();
 
   unsigned long long* trace = nullptr;
-  if (p.trace) trace = p.trace + (size_t)cta * p.steps * (L + 1) * MK_TRACE_PTS;
+  if (TR && p.trace) trace = p.trace + (size_t)cta * p.steps * (L + 1) * MK_TRACE_PTS;
   // thread 0: the next n (1 or 2) tiles have landed and their table entries describe the rows and blocks the stage
   // expects. A stage's thread 0 may do this ahead (during the RMSNorm before it, whose chains run on warp 1), so
   // that the stage itself only passes the barrier.
@@ -1042,10 +1050,10 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
         refill();
         // the gate/up tiles of the first (or only) pair of act blocks, ahead as above (waiting for the down tile
         // here as well measured 36 us per step slower)
-        if (p.nsplit == 0) {
+        if (nsplit == 0) {
           if (cta < nbf) wait_tiles(4, 0, cta + ncta < nbf ? 2 : 1, 64, 64, nbd);
         } else {
-          wait_tiles(4, 0, cta >= ncta - 4 * p.nsplit ? 2 : 1, 64, 16, nbd);
+          wait_tiles(4, 0, cta >= ncta - 4 * nsplit ? 2 : 1, 64, 16, nbd);
         }
       }
       mk_norm_quant(xf, nw2, D, p.eps, xc, red, sqs, MK_SQ_SINK);
@@ -1070,7 +1078,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
         }
         __syncwarp();
       };
-      if (p.nsplit == 0) {
+      if (nsplit == 0) {
         for (int ab0 = cta; ab0 < nbf; ab0 += 2 * ncta) {  // act blocks ab0 and ab0 + ncta: two tiles at once
           const int n = ab0 + ncta < nbf ? 2 : 1;
           if (!chain_tiles(4, n, 64, 64, nbd)) goto out;
@@ -1080,7 +1088,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
       } else {
         // act block cta on warps 0-7; the last 4 nsplit CTAs also take piece q (8 gate + 8 up rows of block
         // ncta + q / 4) on warps 8-9 and publish its 8 act values unquantized
-        const int q = cta - (ncta - 4 * p.nsplit);
+        const int q = cta - (ncta - 4 * nsplit);
         if (!chain_tiles(4, q >= 0 ? 2 : 1, 64, 16, nbd)) goto out;
         if (tid < 32) publish_act(0, cta);
         if (q >= 0 && tid >= 256 && tid < 256 + 8) {
@@ -1098,7 +1106,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
       // chain in block order once all blocks are in.
       if (!head) {
         const int R = o_hi - o_lo, LS = mk_prod_lane_stride(nbf);
-        const int nq = nbf - p.nsplit;  // blocks published quantized
+        const int nq = nbf - nsplit;  // blocks published quantized
         if (tid == 0) ndone_s = 0;
         if (!next_tiles(5, 1, R, 0, nbf)) goto out;
         MK_TRACE(trow, 7);
@@ -1180,7 +1188,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
             }
             __syncwarp();
           }
-        } else if (tid >= 256 && (tid >> 5) - 8 < p.nsplit) {
+        } else if (tid >= 256 && (tid >> 5) - 8 < nsplit) {
           const int k = (tid >> 5) - 8, lane = tid & 31, b = nq + k;
           const float v = __uint_as_float(wait_word(p.rawact + (size_t)k * 32 + lane, E, p, 10 * l + 5, &abort_s));
           if (trace && k == 0 && lane == 0) trace[(size_t)trow * MK_TRACE_PTS + 6] = gtimer();

@@ -103,7 +103,8 @@ struct h2c_engine {
   bool mk_io_dirty = true;                   // error words must be cleared before the next launch
   int mk_stall_cta = -1;                          // h2c_set_decode_fault
   unsigned long long mk_timeout_ns = 2000000000ull;
-  void* mk_kernel = nullptr;  // the k_decode_persistent instance for this model's shape
+  void* mk_kernel = nullptr;        // the k_decode_persistent instance for this model's shape
+  void* mk_kernel_trace = nullptr;  // the same with the timestamp trace compiled in
   size_t mk_tagged_words = 0;  // mk_xw .. mk_kvdone are one allocation of this many words
   int32_t* mk_io = nullptr;   // device: [0] next token, [4..7] error words
   int* mk_tile_count = nullptr;
@@ -599,9 +600,7 @@ int mk_build(h2c_engine* e) {
   if (o_max > 64 || tile_bytes(nbf, o_max, false) > (size_t)MK_SLOT)
     return mk_unsupported(e, "per-CTA O/down tiles larger than a ring slot");
   if (o_max > 16) return mk_unsupported(e, "more than 16 O/down rows per CTA");
-  // act blocks beyond one per CTA: up to 8 are split into 16-row gate/up pieces on the last CTAs, else every CTA
-  // takes whole blocks, two at a time
-  const int nsplit = (nbf > ncta && nbf - ncta <= 8 && 4 * (nbf - ncta) <= nh) ? nbf - ncta : 0;
+  const int nsplit = mk_nsplit(nbf, ncta, nh);
   const int npair = QKV / 2, pr_max = (npair + ncta - 1) / ncta;
   if (2 * pr_max > 64) return mk_unsupported(e, "more than 64 QKV rows per CTA");
   if (nbf > MK_NT) return mk_unsupported(e, "rows longer than the tile kernel's thread count");
@@ -618,15 +617,22 @@ int mk_build(h2c_engine* e) {
   // beyond kv_stage positions attention streams the V columns through the same area: it must hold a few rows
   if (kv_stage < std::min(16, c.ctx)) return mk_unsupported(e, "context too long for the shared-memory budget");
   const size_t smem = base + (size_t)kv_stage * (2 * HD + 4) * 4;
-  // the Qwen2.5-0.5B shape has its own instance with the shape compiled in (and without the chain-tile fallback
-  // of the QKV and O tiles, so its QKV and O tiles must fit the two-phase form); other shapes take the generic one
-  const bool fixed = D == 896 && F == 4864 && H == 14 && KVH == 2 && HD == 64 &&
+  // the Qwen2.5-0.5B shape on a 148-SM B200 has its own instance with the shape and grid compiled in (and without
+  // the chain-tile fallback of the QKV and O tiles, so its QKV and O tiles must fit the two-phase form); other shapes
+  // and grids take the generic one
+  const bool fixed = D == 896 && F == 4864 && H == 14 && KVH == 2 && HD == 64 && ncta == 148 &&
                      mk_small_tile_fits(2 * pr_max, nbd, prod_items) && mk_small_tile_fits(o_max, nbd, prod_items);
-  e->mk_kernel = fixed ? (void*)k_decode_persistent<896, 4864, 14, 2, 64> : (void*)k_decode_persistent<0, 0, 0, 0, 0>;
+  // (the generic instance keeps the trace code: it serves both)
+  e->mk_kernel = fixed ? (void*)k_decode_persistent<896, 4864, 14, 2, 64, 148, false>
+                       : (void*)k_decode_persistent<0, 0, 0, 0, 0, 0, true>;
+  e->mk_kernel_trace = fixed ? (void*)k_decode_persistent<896, 4864, 14, 2, 64, 148, true> : e->mk_kernel;
   CUDA_TRY(e, cudaFuncSetAttribute(e->mk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  CUDA_TRY(e, cudaFuncSetAttribute(e->mk_kernel_trace, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   int occ = 0;
   CUDA_TRY(e, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, e->mk_kernel, MK_THREADS, smem));
-  if (occ < 1) return mk_unsupported(e, "persistent kernel does not fit on an SM");
+  int occ_trace = 0;
+  CUDA_TRY(e, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_trace, e->mk_kernel_trace, MK_THREADS, smem));
+  if (occ < 1 || occ_trace < 1) return mk_unsupported(e, "persistent kernel does not fit on an SM");
 
   // host copies of the packed (grouped) matrices
   auto fetch = [&](const Q4Mat& m, std::vector<uint8_t>& qs, std::vector<uint16_t>& d) -> int {
@@ -808,8 +814,8 @@ int mk_launch(h2c_engine* e, int steps, unsigned long long* trace = nullptr, con
   e->mk_epoch += (uint32_t)steps * (uint32_t)c.layers;
   e->mk_lm_epoch += (uint32_t)steps;
   void* kargs[] = {&p};
-  CUDA_TRY(e, cudaLaunchCooperativeKernel(e->mk_kernel, dim3(e->mk_ncta), dim3(MK_THREADS), kargs,
-                                          e->mk_smem, e->st));
+  void* kern = trace ? e->mk_kernel_trace : e->mk_kernel;
+  CUDA_TRY(e, cudaLaunchCooperativeKernel(kern, dim3(e->mk_ncta), dim3(MK_THREADS), kargs, e->mk_smem, e->st));
   return H2C_OK;
 }
 
