@@ -166,24 +166,6 @@ __device__ __forceinline__ float mk_lane_chain(const uint8_t* tile, int R, int n
   return acc;
 }
 
-// quantize one 32-value block (one value per lane) into block b of a chain input: the arithmetic of
-// quant_block_redux, stored per lane
-__device__ __forceinline__ void mk_quant_chain(float v, int lane, int b, int nbp, const MkX& x) {
-  const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v))));
-  float dd, id;
-  block_scales(amax, dd, id);
-  const int qi = max(-128, min(127, __float2int_rn(__fmul_rn(v, id))));
-  const int pos = (lane & 16) | invperm16(lane & 15);  // byte of the permuted block (word pos / 4)
-  int8_t* dst = reinterpret_cast<int8_t*>(pos < 16 ? x.x0 : x.x1);
-  dst[((((pos & 15) >> 2) * nbp) + b) * 4 + (pos & 3)] = (int8_t)qi;
-  __syncwarp();
-  if (lane < 4) {  // lane l's sum: its words of the two halves, just stored (dp4a against ones)
-    const int i = lane * nbp + b;
-    x.xs[i] = MK_MAGIC - 8 * __dp4a(x.x0[i], 0x01010101, __dp4a(x.x1[i], 0x01010101, 0));
-  }
-  if (lane == 0) x.dx[b] = dd;
-}
-
 // ---------------------------------------------------------------- PTX helpers
 __device__ __forceinline__ void mbar_init(uint64_t* b, unsigned count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count));
@@ -385,9 +367,10 @@ __device__ __forceinline__ float chain_sum(float s, const float* p, int stride, 
   return s;
 }
 
-// quantization of nblk 32-value blocks: value i of block b is f(b * 32 + lane); two blocks per warp at a time
-// two blocks at once (b0 and b1, one value per lane each): the arithmetic of mk_quant_chain, written interleaved
-// so that the reductions and divisions of the two blocks overlap
+// Quantize two 32-value blocks b0 and b1 (one value of each per lane) into a chain input, the arithmetic of
+// quant_block_redux (kernels.c:90-114) for each, written interleaved so that the reductions and divisions of the
+// two blocks overlap; the int8 values are stored per lane, then lanes 0-3 (b0) and 4-7 (b1) form their lane sums
+// and lane 0 stores the scales.
 __device__ __forceinline__ void mk_quant_chain2(float v0, float v1, int lane, int b0, int b1, int nbp, const MkX& x) {
   const unsigned m0 = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v0)));
   const unsigned m1 = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v1)));
@@ -410,15 +393,16 @@ __device__ __forceinline__ void mk_quant_chain2(float v0, float v1, int lane, in
   }
 }
 
+// quantization of nblk 32-value blocks: value i of block b is f(b * 32 + lane); two blocks per warp at a time
 template <typename Fn>
 __device__ __forceinline__ void mk_quant_blocks(int nblk, Fn f, const MkX& x) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nbp = mk_nbp(nblk);
   for (int b = warp; b < nblk; b += 2 * MK_WARPS) {
-    const int b2 = b + MK_WARPS;
-    const float v0 = f(b * 32 + lane);
-    if (b2 < nblk) mk_quant_chain2(v0, f(b2 * 32 + lane), lane, b, b2, nbp, x);
-    else mk_quant_chain(v0, lane, b, nbp, x);
+    // a warp without a second block quantizes its block twice into the same place (the same values and stores):
+    // one code path instead of a one-block variant beside the two-block one
+    const int b2 = b + MK_WARPS < nblk ? b + MK_WARPS : b;
+    mk_quant_chain2(f(b * 32 + lane), f(b2 * 32 + lane), lane, b, b2, nbp, x);
   }
   compute_bar();
 }
@@ -506,9 +490,11 @@ __host__ __device__ constexpr bool mk_small_tile_fits(int R, int nb, int prod_it
 // Shape parameters TD (hidden), TF (ffn), TH (q heads), TKVH (kv heads), THD (head dim) fix the model shape at
 // compile time when non-zero, so buffer offsets and loop bounds are constants (fewer live registers in this
 // single large kernel); 0 takes the shape from MkParams. TNCTA likewise fixes the grid size (and with it the
-// split of the act blocks) when non-zero. TR compiles in the optional timestamp trace (p.trace):
-// the untraced instance carries none of its code (the kernel's code exceeds the instruction cache).
-template <int TD, int TF, int TH, int TKVH, int THD, int TNCTA, bool TR>
+// split of the act blocks) when non-zero. TR compiles in the optional timestamp trace (p.trace), TLC the
+// long-context attention (positions beyond kv_stage; a TLC = false instance serves launches whose positions all stay
+// within kv_stage): the instances without them carry none of their code (the kernel's code exceeds the instruction
+// cache).
+template <int TD, int TF, int TH, int TKVH, int THD, int TNCTA, bool TR, bool TLC>
 __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int D = TD ? TD : p.D, F = TF ? TF : p.F, H = TH ? TH : p.H, KVH = TKVH ? TKVH : p.KVH,
@@ -739,7 +725,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
       const size_t cbase = (((size_t)seq * L + l) * KVH + kh) * (size_t)p.ctx * HD;
       const bool staged = head && pos <= p.kv_stage;
       // long context: more positions than a head CTA stages; every CTA then works on attention (below)
-      const bool lc = pos > p.kv_stage;
+      const bool lc = TLC && pos > p.kv_stage;
       {
         // this layer's norm weights and QKV bias arrive while the layer's inputs are in flight
         for (int i = tid; i < D / 4; i += MK_NT) {

@@ -105,6 +105,7 @@ struct h2c_engine {
   unsigned long long mk_timeout_ns = 2000000000ull;
   void* mk_kernel = nullptr;        // the k_decode_persistent instance for this model's shape
   void* mk_kernel_trace = nullptr;  // the same with the timestamp trace compiled in
+  void* mk_kernel_lc = nullptr;     // for launches that reach positions beyond mk_kv_stage (long-context attention)
   size_t mk_tagged_words = 0;  // mk_xw .. mk_kvdone are one allocation of this many words
   int32_t* mk_io = nullptr;   // device: [0] next token, [4..7] error words
   int* mk_tile_count = nullptr;
@@ -622,17 +623,17 @@ int mk_build(h2c_engine* e) {
   // and grids take the generic one
   const bool fixed = D == 896 && F == 4864 && H == 14 && KVH == 2 && HD == 64 && ncta == 148 &&
                      mk_small_tile_fits(2 * pr_max, nbd, prod_items) && mk_small_tile_fits(o_max, nbd, prod_items);
-  // (the generic instance keeps the trace code: it serves both)
-  e->mk_kernel = fixed ? (void*)k_decode_persistent<896, 4864, 14, 2, 64, 148, false>
-                       : (void*)k_decode_persistent<0, 0, 0, 0, 0, 0, true>;
-  e->mk_kernel_trace = fixed ? (void*)k_decode_persistent<896, 4864, 14, 2, 64, 148, true> : e->mk_kernel;
-  CUDA_TRY(e, cudaFuncSetAttribute(e->mk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  CUDA_TRY(e, cudaFuncSetAttribute(e->mk_kernel_trace, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  int occ = 0;
-  CUDA_TRY(e, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, e->mk_kernel, MK_THREADS, smem));
-  int occ_trace = 0;
-  CUDA_TRY(e, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_trace, e->mk_kernel_trace, MK_THREADS, smem));
-  if (occ < 1 || occ_trace < 1) return mk_unsupported(e, "persistent kernel does not fit on an SM");
+  // (the generic instance keeps the trace and long-context code: it serves every launch)
+  e->mk_kernel = fixed ? (void*)k_decode_persistent<896, 4864, 14, 2, 64, 148, false, false>
+                       : (void*)k_decode_persistent<0, 0, 0, 0, 0, 0, true, true>;
+  e->mk_kernel_lc = fixed ? (void*)k_decode_persistent<896, 4864, 14, 2, 64, 148, false, true> : e->mk_kernel;
+  e->mk_kernel_trace = fixed ? (void*)k_decode_persistent<896, 4864, 14, 2, 64, 148, true, true> : e->mk_kernel;
+  for (void* kern : {e->mk_kernel, e->mk_kernel_lc, e->mk_kernel_trace}) {
+    CUDA_TRY(e, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    int occ = 0;
+    CUDA_TRY(e, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, MK_THREADS, smem));
+    if (occ < 1) return mk_unsupported(e, "persistent kernel does not fit on an SM");
+  }
 
   // host copies of the packed (grouped) matrices
   auto fetch = [&](const Q4Mat& m, std::vector<uint8_t>& qs, std::vector<uint16_t>& d) -> int {
@@ -773,7 +774,9 @@ bool use_persistent(h2c_engine* e) {
 // Launch `steps` decode steps of the persistent kernel (parameters already in e->prm on the stream).
 // args (seq, pos, token) given: the first step's parameters travel in the launch's own parameter block and CTA 0
 // reports the outcome in the mapped host record (mk_wait_done polls it), so no copy is enqueued on either side.
-int mk_launch(h2c_engine* e, int steps, unsigned long long* trace = nullptr, const int32_t* args = nullptr) {
+// last_pos: the last position the launch decodes (it selects the instance with or without long-context attention)
+int mk_launch(h2c_engine* e, int steps, int last_pos, unsigned long long* trace = nullptr,
+              const int32_t* args = nullptr) {
   const h2c_config& c = e->cfg;
   MkParams p{};
   p.D = c.dim; p.F = c.ffn; p.H = c.heads; p.KVH = c.kv_heads; p.HD = e->HD; p.QKV = e->QKV; p.L = c.layers;
@@ -814,7 +817,7 @@ int mk_launch(h2c_engine* e, int steps, unsigned long long* trace = nullptr, con
   e->mk_epoch += (uint32_t)steps * (uint32_t)c.layers;
   e->mk_lm_epoch += (uint32_t)steps;
   void* kargs[] = {&p};
-  void* kern = trace ? e->mk_kernel_trace : e->mk_kernel;
+  void* kern = trace ? e->mk_kernel_trace : last_pos > e->mk_kv_stage ? e->mk_kernel_lc : e->mk_kernel;
   CUDA_TRY(e, cudaLaunchCooperativeKernel(kern, dim3(e->mk_ncta), dim3(MK_THREADS), kargs, e->mk_smem, e->st));
   return H2C_OK;
 }
@@ -887,7 +890,7 @@ int run_forward(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t p
       if (e->decode_mode != H2C_DECODE_GRAPH && (r = mk_build(e))) return r;
       if (use_persistent(e)) {  // the token's parameters travel with the launch: nothing to copy first
         const int32_t args[3] = {seq, pos + c0, ids[c0]};
-        if ((r = mk_launch(e, 1, nullptr, args))) return r;
+        if ((r = mk_launch(e, 1, pos + c0, nullptr, args))) return r;
         e->mk_pending = true;
         continue;
       }
@@ -1219,7 +1222,7 @@ int h2c_generate(h2c_engine* e, int seq, int32_t first_id, int32_t pos, int32_t 
   const bool mk = use_persistent(e);
   CUDA_TRY(e, cudaEventRecord(e->ev0, e->st));
   if (mk) {
-    if ((r = mk_launch(e, steps))) return r;
+    if ((r = mk_launch(e, steps, pos + steps - 1))) return r;
   } else {
     for (int i = 0; i < steps; i++) CUDA_TRY(e, cudaGraphLaunch(e->gexec, e->st));
   }
@@ -1254,7 +1257,7 @@ int h2c_trace_decode(h2c_engine* e, int seq, int32_t first_id, int32_t pos, int3
   int32_t* h = e->prm_h;
   h[P_POS0] = pos; h[P_M] = 1; h[P_SEQ] = seq; h[3] = 0; h[P_IDS] = first_id;
   CUDA_TRY(e, cudaMemcpyAsync(e->prm, h, sizeof(int32_t) * (P_IDS + 1), cudaMemcpyHostToDevice, e->st));
-  r = mk_launch(e, steps, d);
+  r = mk_launch(e, steps, pos + steps - 1, d);
   if (!r) {
     CUDA_TRY(e, cudaMemcpyAsync(e->mk_io_h, e->mk_io, 8 * sizeof(int32_t), cudaMemcpyDeviceToHost, e->st));
     CUDA_TRY(e, cudaMemcpyAsync(out, d, need * 8, cudaMemcpyDeviceToHost, e->st));
