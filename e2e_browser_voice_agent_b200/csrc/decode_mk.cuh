@@ -57,6 +57,12 @@ constexpr int MK_ACT_WORDS = 8;                  // words per act block: its 32 
 #ifndef MK_POLL_NS
 #define MK_POLL_NS 0                             // back-off between polls of a tagged word
 #endif
+#ifndef MK_SETTLE_O
+#define MK_SETTLE_O 1000                         // cycles the O owners pause after publishing x before polling it
+#endif
+#ifndef MK_SETTLE_QKV
+#define MK_SETTLE_QKV 0                          // cycles the head CTAs pause after the QKV publish
+#endif
 
 enum { MK_OK = 0, MK_TIMEOUT_WAIT = 1, MK_TIMEOUT_SLOT = 2, MK_ABORTED = 3 };
 
@@ -219,6 +225,12 @@ __device__ __forceinline__ void st_relaxed64(unsigned long long* p, uint32_t pay
 __device__ __forceinline__ void st_release64(unsigned long long* p, uint32_t payload, uint32_t tag) {
   const unsigned long long v = ((unsigned long long)tag << 32) | payload;
   asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// A local pause (no memory traffic) of the given number of SM cycles.
+__device__ __forceinline__ void mk_settle(long long cycles) {
+  const long long c0 = clock64();
+  while (clock64() - c0 < cycles) {
+  }
 }
 __device__ __forceinline__ int ld_volatile_i(const int* p) { return *(const volatile int*)p; }
 __device__ __forceinline__ void compute_bar() { asm volatile("bar.sync 1, %0;" ::"n"(MK_NT) : "memory"); }
@@ -812,6 +824,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
         }
       }
       MK_TRACE(trow, 3);
+      if (MK_SETTLE_QKV > 0 && head) mk_settle(MK_SETTLE_QKV);
       if (!head && !lc && tid == 0) wait_tiles(3, 0, 1, o_hi - o_lo, 0, nbd);  // the O tile, while attention runs
 
       if (lc) {
@@ -1027,6 +1040,11 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
           st_relaxed64(p.xw + n, __float_as_uint(v), 2 * E);
         }
         MK_TRACE(trow, 9);
+        // The O owners pause before polling x (the next stage's read), which includes the rows they just stored:
+        // polled at once, the last owners' rows became visible about 1.2 us later than after a 1000-cycle pause
+        // (measured 17-26 us per decode step). The down -> x exchange needs none: the next layer's start (the
+        // weight copies it issues) already separates the publish from the first poll.
+        if (MK_SETTLE_O > 0) mk_settle(MK_SETTLE_O);
       }
 
       // ---- D (all CTAs): norm + gate/up rows of whole act blocks, silu * up, quantize (kernels.c:385-397)
