@@ -50,8 +50,8 @@ KV_BYTES_PER_POS = 24 * 2 * 64 * 4 * 2
 
 
 # DRAM bytes (read + write) of one decode step of k_decode_persistent, from the ncu capture of a 4-step launch at
-# positions 32..35 (profiles/k_decode_persistent_qwen2-0.5b_full.md): 1,123,037,440 B / 4
-NCU_TRAFFIC_PER_STEP = 280_759_360
+# positions 32..35 (profiles/k_decode_persistent_qwen2-0.5b_full.md): 1,123,380,992 B / 4
+NCU_TRAFFIC_PER_STEP = 280_845_248
 
 
 def step_bytes(pos: int) -> int:
