@@ -60,6 +60,9 @@ constexpr int MK_ACT_WORDS = 8;                  // words per act block: its 32 
 #ifndef MK_SETTLE_O
 #define MK_SETTLE_O 1000                         // cycles the O owners pause after publishing x before polling it
 #endif
+#ifndef MK_SETTLE_LM
+#define MK_SETTLE_LM 1000                        // cycles every CTA pauses after the lm_head partial publish
+#endif
 #ifndef MK_SETTLE_QKV
 #define MK_SETTLE_QKV 0                          // cycles the head CTAs pause after the QKV publish
 #endif
@@ -1296,6 +1299,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(const MkPar
         st_relaxed64(p.lmw + 2 * cta + 1, (uint32_t)bi, p.lm0 + step + 1);
       }
     }
+    // (a pause before polling the words just published, as after the O publish: 1.3 us per step)
+    if (MK_SETTLE_LM > 0) mk_settle(MK_SETTLE_LM);
     {  // every CTA's (value, index) pair, all words read at once
       uint32_t* lmv = reinterpret_cast<uint32_t*>(prod);
       read_words(2 * ncta, [&](int k) { return p.lmw + k; }, p.lm0 + step + 1, [&](int k, uint32_t v) { lmv[k] = v; }, p,
