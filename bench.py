@@ -9,19 +9,23 @@ The weights (278 MB) exceed the 126 MB L2, so no L2 flush is needed between step
   value  tokens/s over all ranks, device-timed with CUDA events around K device-chained decode steps (the next
          token never leaves the GPU; inputs resident in HBM).
   e2e    the same K steps through the reference-facing per-token call (h2c_forward, as LLM.generateIds drives
-         be.forward): each step copies its token id and position host -> device and reads the next id back.
+         be.forward): each step passes its token id and position from the host and reads the next id back.
 
-Multi-GPU (torchrun, one rank per GPU): independent sessions, one per rank, weights replicated, no collective on
-the data path ("weak" scaling); timing barriers and the max-over-ranks reduction use NCCL.
+The same line carries the other configurations of the hot path as nested records, measured in the same process on
+every rank (so a multi-GPU run records each at every N):
+  multi_session  32 concurrent sessions per GPU (128-token prompts, then batched greedy decode steps: every weight
+                 byte read once per step for all 32 tokens), device-timed; e2e through the per-step batched call;
+  prefill        prompt passes of 32 (the C1 prompt), 128, 512 and 4096 tokens through h2c_forward;
+  microbench     the Q4_0 matvec shapes (one token), with weight copies rotated so that bytes come from HBM, and
+                 the two small shapes also L2-resident;
+  long_context   a 4096-token prompt, then device-chained greedy decode at positions 4096..
+Multi-GPU (torchrun, one rank per GPU): independent sessions per rank, weights replicated, no collective on the
+data path ("weak" scaling); timing barriers and the max-over-ranks reduction use NCCL.
 
---workload c4: multi-session serving, 32 concurrent sessions per GPU (128-token prompts, then greedy decode) in
-batched steps (h2c_forward_batch / h2c_generate_batch: every weight byte read once per step for all 32 tokens).
-A step is one batched decode step (32 tokens); value = tokens/s over all ranks, device-timed around K device-chained
-batched steps; e2e = the same steps through the host-driven per-step call (ids and positions copied in, 32 next
-ids read back).
-
+--workload c4 prints the multi-session record alone as the line.
 --impl reference: the reference's own CPU kernels (kernels.c, compiled natively through oracle/shim into
-oracle/_ref, driven like cpu-worker.js) on this host's cores, same workload, rank 0 only.
+oracle/_ref, driven like cpu-worker.js) on this host's cores, same workload and config, rank 0 only (one CPU
+process whatever N is; the other ranks exit without work).
 """
 from __future__ import annotations
 
@@ -30,9 +34,7 @@ import json
 import math
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
 import threading
 import time
 
@@ -45,75 +47,98 @@ PROMPT = 32
 ROUND = 64
 # algorithmic bytes of one decode step at the 0.5B configuration (tied Q4_0 lm_head): layer weights, norms and
 # biases, lm_head, plus 24,576 B of fp32 KV read per cached position and 24,576 B written per step
-WEIGHT_BYTES = 201_277_440 + 286_208 + 76_575_744
+LAYER_WEIGHT_BYTES = 201_277_440
+NORM_BIAS_BYTES = 286_208
+LM_HEAD_BYTES = 76_575_744
+WEIGHT_BYTES = LAYER_WEIGHT_BYTES + NORM_BIAS_BYTES + LM_HEAD_BYTES
 KV_BYTES_PER_POS = 24 * 2 * 64 * 4 * 2
-
+EMBED_ROW_BYTES = 504
+# multiply-accumulates per token of the 0.5B layers (Q4_0: 18 bytes per 32 weights)
+LAYER_MACS = LAYER_WEIGHT_BYTES // 18 * 32
 
 # DRAM bytes (read + write) of one decode step of k_decode_persistent, from the ncu capture of a 4-step launch at
-# positions 32..35 (profiles/k_decode_persistent_qwen2-0.5b_full.md): 1,123,380,992 B / 4
+# positions 32..35: 1,123,380,992 B / 4
 NCU_TRAFFIC_PER_STEP = 280_845_248
+
+C1_CONFIG = {"workload": "qwen2-0.5b Q4_0 tied lm_head, batch 1, 32-token prompt then greedy decode rounds of 64 "
+                         "(positions 32..95)",
+             "l2": "no flush: 278 MB of weights per step > 126 MB L2"}
+
+C4_SESSIONS = 32
+C4_PROMPT = 128
+C4_DECODE = 128
+C4_METRIC = "decode tok/s multi-session (32 concurrent per GPU) Qwen2-0.5B Q4_0"
+C3_PROMPT = 4096
+C3_DECODE = 64
+C2_SHAPES = [(896, 896), (128, 896), (4864, 896), (896, 4864), (151936, 896)]
 
 
 def step_bytes(pos: int) -> int:
     """Bytes one decode step at position pos must move (T = pos + 1 cached positions read, one written)."""
-    return WEIGHT_BYTES + KV_BYTES_PER_POS * (pos + 1) + KV_BYTES_PER_POS + 504
+    return WEIGHT_BYTES + KV_BYTES_PER_POS * (pos + 1) + KV_BYTES_PER_POS + EMBED_ROW_BYTES
 
 
-def measured_peaks():
+def c1_positions(steps: int):
+    """Positions of K timed C1 steps (rounds of the 64-token decode starting at the prompt's end)."""
+    return [PROMPT + (k % ROUND) for k in range(steps)]
+
+
+def peaks():
+    """(HBM GB/s, bf16 TFLOP/s burst, source) from MEASURED_PEAKS.json, else the documented fallback."""
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             p = json.load(f)
-        return float(p["hbm_gbs"]), "measured"
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
     except Exception:
-        return 6650.0, "fallback"
+        return 6650.0, 1590.0, "fallback"
 
 
 class Clocks:
-    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    """SM clocks and throttle reasons sampled through NVML by a thread while the timed region runs (every 2 ms, so
+    short regions get samples too)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown", 0x4: "sw_power_cap"}
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
-        self.proc = None
-        self.out = None
+        self.samples = []
+        self.stop_ev = threading.Event()
+        self.th = None
+        self.ok = False
+
+    def _run(self, h, N):
+        while True:
+            try:
+                self.samples.append((N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM),
+                                     N.nvmlDeviceGetCurrentClocksEventReasons(h)))
+            except Exception:
+                pass
+            if self.stop_ev.wait(0.002):
+                break
 
     def start(self):
         try:
-            self.out = tempfile.TemporaryFile(mode="w+")
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "100", "-i", str(self.gpu)], stdout=self.out,
-                                         stderr=subprocess.DEVNULL)
+            import pynvml as N
+            N.nvmlInit()
+            dev = os.environ.get("CUDA_VISIBLE_DEVICES")
+            idx = int(dev.split(",")[self.gpu]) if dev and dev.split(",")[0].isdigit() else self.gpu
+            h = N.nvmlDeviceGetHandleByIndex(idx)
+            self.max = N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM)
+            self.th = threading.Thread(target=self._run, args=(h, N), daemon=True)
+            self.th.start()
+            self.ok = True
         except Exception:
-            self.proc = None
+            self.ok = False
 
     def stop(self):
-        if not self.proc:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        self.out.seek(0)
-        sm, mx, reasons, n = [], None, set(), 0
-        for line in self.out.read().splitlines():
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            n += 1
-            for name, v in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"), f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": n}
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
+        self.stop_ev.set()
+        self.th.join(timeout=2)
+        sm = [s for s, _ in self.samples]
+        reasons = sorted({name for _, r in self.samples for bit, name in self.REASONS.items() if r & bit})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max, "reasons": reasons,
+                "samples": len(sm), "source": "NVML, every 2 ms during the timed region"}
 
 
 def dist_setup(n_gpus: int):
@@ -125,8 +150,16 @@ def dist_setup(n_gpus: int):
     return world, rank, local
 
 
+def host_cores():
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+
+
+def c1_config(world: int):
+    return dict(C1_CONFIG, global_batch=world, seq_len=PROMPT + ROUND, parallelism=f"sessions x{world}")
+
+
 def reference_arm(args, world, rank):
-    """The reference's CPU path (oracle/_ref) on this host: rank 0 only."""
+    """The reference's CPU path (oracle/_ref) on this host: rank 0 only, one CPU process whatever N is."""
     if rank != 0:
         return
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
@@ -134,7 +167,7 @@ def reference_arm(args, world, rank):
     from e2e_browser_voice_agent_b200 import synth
 
     kind = "ref_mt" if O.available("ref_mt") else "oracle"
-    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    cores = host_cores()
     decode_threads = max(1, math.ceil(cores / 2))  # cpu.js:23 default for generation
     path = synth.ensure("qwen2-0.5b")
     eng = O.open_model(kind, path, ctx=PROMPT + ROUND + 1, mt=16, threads=cores, decode_threads=decode_threads)
@@ -161,13 +194,14 @@ def reference_arm(args, world, rank):
     v = steps / t
     line = {"metric": METRIC, "value": round(v, 3), "unit": UNIT, "impl": "reference", "n_gpus": world,
             "steps": steps, "warmup": warm, "ms_per_step": round(t / steps * 1e3, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8 dot / f32", "data": "synthetic (seeded GGUF)",
-            "config": {"workload": "qwen2-0.5b Q4_0 tied, batch 1, 32 prompt + greedy decode rounds of 64",
-                       "prompt": PROMPT, "decode_round": ROUND},
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8 dot / f32 accumulate (Q4_0 weights)",
+            "data": "synthetic: seeded GGUF, N(0,0.02) weights quantised to Q4_0, uniform-random prompt ids",
+            "config": c1_config(world),
             "cpu_baseline": {"value": round(v, 3), "unit": UNIT, "cores": decode_threads,
                              "kind": "reference" if kind == "ref_mt" else "port",
                              "sample": f"{steps} decode steps (positions 32..95), {cores} host cores visible, "
-                                       f"{decode_threads} decode threads (cpu.js:23 default)"},
+                                       f"{decode_threads} decode threads (cpu.js:23 default); one CPU process on "
+                                       f"rank 0's host for any number of GPUs"},
             "e2e": {"value": round(v, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -178,7 +212,7 @@ def cpu_baseline_sample():
     import oracle as O
     from e2e_browser_voice_agent_b200 import synth
     kind = "ref_mt" if O.available("ref_mt") else "oracle"
-    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    cores = host_cores()
     dt = max(1, math.ceil(cores / 2))
     eng = O.open_model(kind, synth.ensure("qwen2-0.5b"), ctx=PROMPT + ROUND + 1, mt=16, threads=cores,
                        decode_threads=dt)
@@ -193,46 +227,48 @@ def cpu_baseline_sample():
                       f"{dt} decode threads of {cores} host cores (cpu.js:23 default)"}
 
 
-C4_SESSIONS = 32
-C4_PROMPT = 128
-C4_DECODE = 128
-C4_METRIC = "decode tok/s multi-session (32 concurrent per GPU) Qwen2-0.5B Q4_0"
+class Ctx:
+    """Per-process benchmark context: rank, world, barrier and max-over-ranks."""
 
+    def __init__(self, world, rank, local):
+        self.world, self.rank, self.local = world, rank, local
 
-def bench_c4(args, world, rank, local):
-    import torch
-    import torch.distributed as dist
-    from e2e_browser_voice_agent_b200 import backend, sessions, synth
-
-    torch.cuda.set_device(local)
-    if world > 1:
-        sessions.init("nccl")
-    steps = min(args.steps if args.steps is not None else C4_DECODE, C4_DECODE)
-    warm = max(3, args.warmup)
-    S = C4_SESSIONS
-    path = synth.ensure("qwen2-0.5b")
-    be = backend.open_model(path, ctx=C4_PROMPT + C4_DECODE + 1, prefill_chunk=S, max_seqs=S, device=local)
-    # rank r serves sessions r, r + world, ... of a 32 x world set (weak scaling), 32 at a time
-    sids = sessions.shard(S * world, world, rank)
-    first = []
-    for i, sid in enumerate(sids):
-        first.append(be.forward(synth.prompt_ids(151936, C4_PROMPT, seed=sessions.session_seed(sid)), 0, seq=i))
-    seqs = list(range(S))
-    pos = [C4_PROMPT] * S
-
-    def barrier():
+    def barrier(self):
+        import torch
+        from e2e_browser_voice_agent_b200 import sessions
         sessions.barrier()
         torch.cuda.synchronize()
 
+    def max(self, x: float) -> float:
+        from e2e_browser_voice_agent_b200 import sessions
+        return sessions.max_over_ranks(x, device="cuda")
+
+
+def measure_c4(cx: Ctx, steps: int, warm: int):
+    """Multi-session serving: 32 sessions per GPU in batched decode steps. Returns the record."""
+    from e2e_browser_voice_agent_b200 import backend, sessions, synth
+    S = C4_SESSIONS
+    steps = min(steps, C4_DECODE)
+    be = backend.open_model(synth.ensure("qwen2-0.5b"), ctx=C4_PROMPT + C4_DECODE + 1, prefill_chunk=S, max_seqs=S,
+                            device=cx.local)
+    sids = sessions.shard(S * cx.world, cx.world, cx.rank)  # rank r serves sessions r, r + world, ...
+    prompts = [synth.prompt_ids(151936, C4_PROMPT, seed=sessions.session_seed(sid)) for sid in sids]
+    # prefill of the 32 prompts (one h2c_forward each, 4 chunks of 32 tokens), wall clock
+    cx.barrier()
+    t0 = time.perf_counter()
+    first = [be.forward(p, 0, seq=i) for i, p in enumerate(prompts)]
+    prefill_s = cx.max(time.perf_counter() - t0)
+    seqs = list(range(S))
+    pos = [C4_PROMPT] * S
     be.generate_batch(seqs, first, pos, warm)
-    clocks = Clocks(local)
-    barrier()
+    clocks = Clocks(cx.local)
+    cx.barrier()
     clocks.start()
     _, ms = be.generate_batch(seqs, first, pos, steps)
-    barrier()
+    cx.barrier()
     ck = clocks.stop()
-    ms = sessions.max_over_ranks(ms, device="cuda")
-    value = world * S * steps / (ms / 1e3)
+    ms = cx.max(ms)
+    value = cx.world * S * steps / (ms / 1e3)
 
     def host_steps(n):
         cur, p = list(first), list(pos)
@@ -241,51 +277,140 @@ def bench_c4(args, world, rank, local):
             p = [x + 1 for x in p]
 
     host_steps(warm)
-    barrier()
+    cx.barrier()
     t0 = time.perf_counter()
     host_steps(steps)
-    barrier()
-    e2e_s = sessions.max_over_ranks(time.perf_counter() - t0, device="cuda")
-    e2e = world * S * steps / e2e_s
-
-    mean_pos = C4_PROMPT + (steps - 1) / 2
-    bytes_step = WEIGHT_BYTES + S * (KV_BYTES_PER_POS * (int(round(mean_pos)) + 2) + 504)
-    peak, peak_kind = measured_peaks()
+    cx.barrier()
+    e2e_s = cx.max(time.perf_counter() - t0)
+    e2e = cx.world * S * steps / e2e_s
+    # bytes: weights once per step + every session's KV (positions C4_PROMPT .. C4_PROMPT + steps - 1)
+    tot = sum(WEIGHT_BYTES + S * (KV_BYTES_PER_POS * (p + 2) + EMBED_ROW_BYTES)
+              for p in range(C4_PROMPT, C4_PROMPT + steps))
+    bytes_step = tot / steps
+    hbm, _, src = peaks()
     achieved = bytes_step / (ms / steps / 1e3) / 1e9
     kernels = be.batch_kernels(S)
-    cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
-        try:
-            cpu = cpu_baseline_sample()
-            cpu["sample"] += "; sessions run one after another on the CPU, so its multi-session rate is the same"
-        except Exception as ex:
-            cpu = {"value": None, "unit": UNIT, "cores": 0, "kind": "reference", "sample": f"failed: {ex}"}
     be.destroy()
-    if rank == 0:
-        line = {
-            "metric": C4_METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": steps,
-            "warmup": warm, "ms_per_step": round(ms / steps, 5), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "int8 dot / f32 accumulate (Q4_0 weights)",
-            "data": "synthetic: seeded GGUF, N(0,0.02) weights quantised to Q4_0, uniform-random prompt ids",
-            "config": {"workload": f"c4: {S} concurrent sessions per GPU, {C4_PROMPT}-token prompts, batched greedy "
-                                   f"decode steps (positions {C4_PROMPT}..{C4_PROMPT + steps - 1})",
-                       "global_batch": S * world, "seq_len": C4_PROMPT + steps, "parallelism": f"sessions x{world}",
-                       "l2": "no flush: 278 MB of weights per step > 126 MB L2"},
-            "roofline": {"bound": "hbm", "kernel": f"batched decode step ({kernels} kernels in one CUDA graph; "
-                                                   "k_matmul_tc: int8 tensor-core block dots, 32 tokens per weight load)",
-                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "peak_source": peak_kind, "bytes_per_step": bytes_step,
-                         "traffic": None},
-            "e2e": {"value": round(e2e, 2), "unit": UNIT, "h2d_bytes_per_step": 4 * 4 + 3 * 4 * 256,
-                    "d2h_bytes_per_step": 4 * S},
-            "gpu_launches": kernels * steps,
-            "clocks": ck,
-            "cpu_baseline": cpu,
-        }
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    return {
+        "metric": C4_METRIC, "value": round(value, 2), "unit": UNIT, "steps": steps, "warmup": warm,
+        "ms_per_step": round(ms / steps, 5), "higher_is_better": True, "scaling": "weak",
+        "config": {"workload": f"c4: {S} concurrent sessions per GPU, {C4_PROMPT}-token prompts, batched greedy "
+                               f"decode steps (positions {C4_PROMPT}..{C4_PROMPT + steps - 1})",
+                   "global_batch": S * cx.world, "seq_len": C4_PROMPT + steps, "parallelism": f"sessions x{cx.world}",
+                   "l2": "no flush: 278 MB of weights per step > 126 MB L2"},
+        "roofline": {"bound": "hbm", "kernel": f"batched decode step ({kernels} kernels in one CUDA graph)",
+                     "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                     "peak_source": src, "bytes_per_step": round(bytes_step), "traffic": None},
+        "e2e": {"value": round(e2e, 2), "unit": UNIT, "h2d_bytes_per_step": 4 * 4 + 3 * 4 * 256,
+                "d2h_bytes_per_step": 4 * S},
+        "prompt_prefill_ms": round(prefill_s * 1e3, 2),
+        "gpu_launches": kernels * steps, "clocks": ck,
+    }
+
+
+def measure_prefill_and_c3(cx: Ctx, decode_steps: int):
+    """Prompt passes of 128, 512 and 4096 tokens (one engine with 256-token chunks), then the long-context decode
+    after the 4096-token prompt. Returns (prefill records, long-context record)."""
+    import torch
+    from e2e_browser_voice_agent_b200 import backend, synth
+    _, bf16, src = peaks()
+    int8_peak = 2 * bf16  # the dense int8 tensor rate is twice the bf16 rate
+    be = backend.open_model(synth.ensure("qwen2-0.5b"), ctx=C3_PROMPT + C3_DECODE + 2, prefill_chunk=256,
+                            device=cx.local)
+    pre = {}
+    for n in (128, 512, 4096):
+        prompt = synth.prompt_ids(151936, n, seed=7 + n)
+        reps = 3 if n < 4096 else 1
+        be.forward(prompt[:64], 0)  # warm-up
+        ts = []
+        for _ in range(reps):
+            cx.barrier()
+            t0 = time.perf_counter()
+            first = be.forward(prompt, 0)
+            torch.cuda.synchronize()
+            ts.append(time.perf_counter() - t0)
+        t = cx.max(min(ts))
+        ops = 2 * LAYER_MACS * n
+        pre[str(n)] = {"tokens": n, "ms": round(t * 1e3, 3), "tok_per_s": round(n / t, 1),
+                       "roofline": {"bound": "tensor", "achieved": round(ops / t / 1e12, 2), "peak": int8_peak,
+                                    "unit": "int8 TOP/s", "frac": round(ops / t / 1e12 / int8_peak, 5),
+                                    "peak_source": f"2 x {src} bf16 (dense int8 rate)",
+                                    "ops": ops, "ops_note": "2 x layer weights x tokens (attention excluded)"}}
+    # long context: device-chained greedy decode after the 4096-token prompt (first = that prompt's next token)
+    be.generate(first, C3_PROMPT, 4)
+    clocks = Clocks(cx.local)
+    cx.barrier()
+    clocks.start()
+    _, ms = be.generate(first, C3_PROMPT, decode_steps)
+    cx.barrier()
+    ck = clocks.stop()
+    ms = cx.max(ms)
+    hbm, _, src = peaks()
+    tot = sum(step_bytes(p) for p in range(C3_PROMPT, C3_PROMPT + decode_steps))
+    achieved = tot / (ms / 1e3) / 1e9
+    lc = {"metric": "decode tok/s long context (4096-token prompt) Qwen2-0.5B Q4_0",
+          "value": round(cx.world * decode_steps / (ms / 1e3), 2), "unit": UNIT, "steps": decode_steps,
+          "ms_per_step": round(ms / decode_steps, 5), "positions": [C3_PROMPT, C3_PROMPT + decode_steps - 1],
+          "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                       "frac": round(achieved / hbm, 4), "peak_source": src,
+                       "bytes_per_step": round(tot / decode_steps)},
+          "kernel": be.decode_path, "clocks": ck}
+    be.destroy()
+    return pre, lc
+
+
+def measure_c2(cx: Ctx):
+    """The Q4_0 matvec shapes (one token): us per call and GB/s with weight copies rotated (>= 256 MB in rotation,
+    so the bytes come from HBM), and the two small shapes also L2-resident (the same copy back to back)."""
+    import numpy as np
+    import torch
+    from e2e_browser_voice_agent_b200 import _lib
+    from e2e_browser_voice_agent_b200 import gguf as G
+    L = _lib.load()
+    hbm, _, src = peaks()
+    dev = torch.device("cuda", cx.local)
+    stream = torch.cuda.current_stream(dev)
+    out = {}
+    rng = np.random.default_rng(0)
+    for N, K in C2_SHAPES:
+        blocks = G.q4_0_quantize(rng.standard_normal(N * K, dtype=np.float32) * np.float32(0.02))
+        packed = np.zeros(L.h2c_q4_matrix_bytes(N, K), np.uint8)
+        assert L.h2c_q4_pack(blocks.ctypes.data, N, K, packed.ctypes.data) == 0
+        w0 = torch.from_numpy(packed).to(dev)
+        copies = max(1, math.ceil(256e6 / packed.nbytes))
+        ws = [w0] + [w0.clone() for _ in range(copies - 1)]
+        x = torch.from_numpy(rng.standard_normal(K, dtype=np.float32)).to(dev)
+        y = torch.zeros(N, dtype=torch.float32, device=dev)
+        scratch = torch.zeros(L.h2c_q4_matvec_scratch_bytes(1, K), dtype=torch.uint8, device=dev)
+        algo = N * K // 32 * 18 + 4 * K + 4 * N
+
+        def run(seq):
+            for w in seq:
+                rc = L.h2c_q4_matvec(w.data_ptr(), N, K, x.data_ptr(), 1, y.data_ptr(), 0, None, scratch.data_ptr(),
+                                     stream.cuda_stream)
+                if rc:
+                    _lib.check(rc)
+
+        rec = {"bytes": algo}
+        for mode, seq in (("hbm", ws * max(1, 200 // len(ws))), ("l2", [w0] * 200)):
+            if mode == "l2" and N * K > 4864 * 896:
+                continue
+            run(seq[:20])
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record(stream)
+            run(seq)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / len(seq)
+            gbs = algo / (us * 1e-6) / 1e9
+            rec[mode] = {"us_per_call": round(us, 3), "gbs": round(gbs, 1), "frac": round(gbs / hbm, 4),
+                         "calls": len(seq)}
+        out[f"{N}x{K}"] = rec
+        del ws
+    return {"note": "h2c_q4_matvec, one token: quantize_row kernel + matvec kernel per call (2 launches), CUDA events "
+                    "on the launching stream; 'hbm' rotates weight copies (>= 256 MB), 'l2' repeats one copy",
+            "peak": hbm, "peak_source": src, "shapes": out}
 
 
 def main():
@@ -295,13 +420,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="C1 only, without the nested records")
     ap.add_argument("--workload", default="c1", choices=["c1", "c4"])
     args = ap.parse_args()
     world, rank, local = dist_setup(args.gpus)
     if args.impl == "reference":
         return reference_arm(args, world, rank)
-    if args.workload == "c4":
-        return bench_c4(args, world, rank, local)
 
     import torch
     import torch.distributed as dist
@@ -310,16 +434,20 @@ def main():
     torch.cuda.set_device(local)
     if world > 1:
         sessions.init("nccl")
-    steps = args.steps if args.steps is not None else 3200
+    cx = Ctx(world, rank, local)
     warm = max(3, args.warmup)
+    if args.workload == "c4":
+        rec = measure_c4(cx, args.steps if args.steps is not None else C4_DECODE, warm)
+        if rank == 0:
+            rec.update({"n_gpus": world, "vs_baseline": None, "dtype": "int8 dot / f32 accumulate (Q4_0 weights)",
+                        "data": "synthetic: seeded GGUF, N(0,0.02) weights quantised to Q4_0, uniform-random prompt ids"})
+            print(json.dumps(rec), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
 
-    def barrier():
-        sessions.barrier()
-        torch.cuda.synchronize()
-
-    def max_over_ranks(x: float) -> float:
-        return sessions.max_over_ranks(x, device="cuda")
-
+    steps = args.steps if args.steps is not None else 3200
     path = synth.ensure("qwen2-0.5b")
     be = backend.open_model(path, ctx=PROMPT + ROUND + 1, prefill_chunk=16, device=local)
     # one session per rank (weak scaling): rank r serves session r of a world-sized set
@@ -341,15 +469,15 @@ def main():
     # ---- value: device-chained decode, device time
     device_rounds(warm)
     clocks = Clocks(local)
-    barrier()
+    cx.barrier()
     clocks.start()
     ms, calls = device_rounds(steps)
-    barrier()
+    cx.barrier()
     ck = clocks.stop()
-    ms = max_over_ranks(ms)
+    ms = cx.max(ms)
     value = world * steps / (ms / 1e3)
 
-    # ---- e2e: the per-token reference-facing call, host buffers, host<->device copies in the timed region
+    # ---- e2e: the per-token reference-facing call, host buffers, host<->device transfers in the timed region
     def host_rounds(n):
         k, nxt = 0, first
         while k < n:
@@ -361,17 +489,16 @@ def main():
 
     e2e_steps = min(steps, 640)
     host_rounds(warm)
-    barrier()
+    cx.barrier()
     t0 = time.perf_counter()
     host_rounds(e2e_steps)
-    barrier()
-    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    cx.barrier()
+    e2e_s = cx.max(time.perf_counter() - t0)
     e2e = world * e2e_steps / e2e_s
 
-    # ---- roofline of the decode step (the unit the kernels of one step form), from the device-timed region
-    mean_pos = PROMPT + (ROUND - 1) / 2
-    bytes_step = step_bytes(int(round(mean_pos)))
-    peak, peak_kind = measured_peaks()
+    # ---- roofline of the decode step, from the device-timed region and the positions it actually ran
+    bytes_step = sum(step_bytes(p) for p in c1_positions(steps)) / steps
+    hbm, _, src = peaks()
     achieved = bytes_step / (ms / steps / 1e3) / 1e9
     kernels = be.decode_kernels()
     persistent = be.decode_path == "persistent"
@@ -385,6 +512,15 @@ def main():
         launches = kernels * steps
         h2d = 4 * 5  # pass parameters (position, length, sequence, pad, token id)
         d2h = 4
+    be.destroy()
+
+    extra = {}
+    if not args.no_extra:
+        t_extra = time.perf_counter()
+        extra["multi_session"] = measure_c4(cx, steps, warm)
+        extra["prefill"], extra["long_context"] = measure_prefill_and_c3(cx, C3_DECODE)
+        extra["microbench"] = measure_c2(cx)
+        extra["extra_wall_s"] = round(time.perf_counter() - t_extra, 1)
 
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
@@ -392,27 +528,24 @@ def main():
             cpu = cpu_baseline_sample()
         except Exception as ex:  # the baseline is reported, never required
             cpu = {"value": None, "unit": UNIT, "cores": 0, "kind": "reference", "sample": f"failed: {ex}"}
-    be.destroy()
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": steps,
             "warmup": warm, "ms_per_step": round(ms / steps, 5), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8 dot / f32 accumulate (Q4_0 weights)",
             "data": "synthetic: seeded GGUF, N(0,0.02) weights quantised to Q4_0, uniform-random prompt ids",
-            "config": {"workload": "qwen2-0.5b Q4_0 tied lm_head, batch 1, 32-token prompt then greedy decode "
-                                   "rounds of 64 (positions 32..95)",
-                       "global_batch": world, "seq_len": PROMPT + ROUND, "parallelism": f"sessions x{world}",
-                       "l2": "no flush: 278 MB of weights per step > 126 MB L2"},
+            "config": c1_config(world),
             "roofline": {"bound": "hbm", "kernel": kdesc,
-                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                         "bytes_per_step": bytes_step,
+                         "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(achieved / hbm, 4), "peak_source": src,
+                         "bytes_per_step": round(bytes_step),
                          "traffic": NCU_TRAFFIC_PER_STEP if persistent else None,
                          "traffic_note": "DRAM read+write bytes per decode step, ncu capture of k_decode_persistent"},
             "e2e": {"value": round(e2e, 2), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches,
             "clocks": ck,
             "cpu_baseline": cpu,
+            **extra,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -55,8 +55,8 @@ def load(path: str = LIB_PATH) -> C.CDLL:
     p, i32, u32, u64, i64 = C.c_void_p, C.c_int32, C.c_uint32, C.c_uint64, C.c_int64
     L.h2c_create.argtypes = [C.c_int, C.POINTER(Config), C.POINTER(p)]
     L.h2c_set_tensor.argtypes = [p, C.c_int, C.c_int, C.c_int, p, u64]
-    L.h2c_forward.argtypes = [p, C.c_int, p, i32, i32, C.c_float, u32, C.POINTER(i32)]
-    L.h2c_forward_batch.argtypes = [p, i32, p, p, p, C.c_float, u32, p]
+    L.h2c_forward.argtypes = [p, C.c_int, p, i32, i32, C.c_double, u32, C.POINTER(i32)]
+    L.h2c_forward_batch.argtypes = [p, i32, p, p, p, C.c_double, u32, p]
     L.h2c_generate_batch.argtypes = [p, i32, p, p, p, i32, p, C.POINTER(C.c_float)]
     L.h2c_batch_kernels.argtypes = [p, i32]
     L.h2c_generate.argtypes = [p, C.c_int, i32, i32, i32, p, C.POINTER(C.c_float)]

@@ -15,6 +15,7 @@
 #include "../../include/h2cuda.h"
 #include "decode_mk.cuh"
 #include "kernels.cuh"
+#include "sample.cuh"
 
 using namespace h2;
 
@@ -77,6 +78,10 @@ struct h2c_engine {
   int* am_ib = nullptr;
   int32_t* next_b = nullptr;
   int32_t* prm_bh = nullptr;   // pinned [P_WORDS]
+  // temperature sampling on the device (sample.cu): scratch for up to P_CAP rows, per-token seeds
+  void* samp = nullptr;
+  uint32_t* seeds_d = nullptr;  // [P_CAP]
+  uint32_t* seeds_h = nullptr;  // pinned [P_CAP]
   int32_t* next_bh = nullptr;  // pinned [P_CAP]
   std::vector<cudaGraphExec_t> bexec;
   std::vector<int> bkernels;   // kernel nodes of each batch graph
@@ -370,7 +375,12 @@ bool attg_ok(int G, int HD, int ctx) {
   return (HD == 64 ? attg_smem_bytes<64>(G, ctx) : attg_smem_bytes<128>(G, ctx)) <= ATTG_SMEM;
 }
 
-cudaError_t set_kernel_attrs(int ctx) {
+// The largest context h2c_create accepts: k_attention keeps one float score per position in shared memory.
+constexpr int MAX_CTX = 50000;
+
+// The attributes are per device and only ever raised to fixed maxima (a launch's own size decides its occupancy),
+// so engines with different contexts on one device never lower each other's limits.
+cudaError_t set_kernel_attrs() {
   const int big = 200 * 1024;
   cudaError_t c = mv_attr<WQ4, 32, 1>(big);
   if (c == cudaSuccess) c = mv_attr<WQ4, 16, 1>(big);
@@ -382,7 +392,7 @@ cudaError_t set_kernel_attrs(int ctx) {
   if (c == cudaSuccess) c = mm_attr_mt<WQ8, 8>();
   if (c == cudaSuccess) c = mm_attr_mt<WQ8, 16>();
   if (c == cudaSuccess) c = mm_attr_mt<WQ8, 32>();
-  const int att = ctx * 4 > 48 * 1024 ? ctx * 4 : 48 * 1024;
+  const int att = MAX_CTX * 4;
   if (c == cudaSuccess) c = cudaFuncSetAttribute(k_attention<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, att);
   if (c == cudaSuccess)
     c = cudaFuncSetAttribute(k_attention_gqa<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATTG_SMEM);
@@ -390,6 +400,29 @@ cudaError_t set_kernel_attrs(int ctx) {
     c = cudaFuncSetAttribute(k_attention_gqa<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATTG_SMEM);
   if (c == cudaSuccess) c = cudaFuncSetAttribute(k_attention<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, att);
   return c;
+}
+
+// set_kernel_attrs once per device, for the device current on the calling thread (any thread may call).
+constexpr int ATTR_MAX_DEVICES = 64;
+bool g_attrs_done[ATTR_MAX_DEVICES];
+std::mutex g_attrs_mutex;
+bool kernel_attrs_on_current_device(std::string* why) {
+  int dev = -1;
+  cudaError_t c = cudaGetDevice(&dev);
+  if (c != cudaSuccess || dev < 0 || dev >= ATTR_MAX_DEVICES) {
+    *why = std::string("cudaGetDevice: ") + (c != cudaSuccess ? cudaGetErrorString(c) : "device index out of range");
+    return false;
+  }
+  std::lock_guard<std::mutex> lock(g_attrs_mutex);
+  if (!g_attrs_done[dev]) {
+    c = set_kernel_attrs();
+    if (c != cudaSuccess) {
+      *why = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(c);
+      return false;
+    }
+    g_attrs_done[dev] = true;
+  }
+  return true;
 }
 
 struct Prof {
@@ -507,32 +540,6 @@ int build_graph(h2c_engine* e) {
   }
   e->graph_kernels = k;
   return H2C_OK;
-}
-
-// mulberry32 + softmax sampling in double precision, cpu-worker.js:154-167
-double mulberry32(uint32_t* s) {
-  *s = *s + 0x6d2b79f5u;
-  uint32_t t = *s;
-  t = (t ^ (t >> 15)) * (t | 1u);
-  t ^= t + (t ^ (t >> 7)) * (t | 61u);
-  return (double)(t ^ (t >> 14)) / 4294967296.0;
-}
-
-int sample_host(const float* lg, int n, double temperature, uint32_t seed) {
-  int best = 0;
-  for (int i = 1; i < n; i++)
-    if (lg[i] > lg[best]) best = i;
-  if (!(temperature > 0)) return best;
-  uint32_t s = seed;
-  const double mx = (double)lg[best] / temperature;
-  double sum = 0;
-  for (int i = 0; i < n; i++) sum += std::exp((double)lg[i] / temperature - mx);
-  double r = mulberry32(&s) * sum;
-  for (int i = 0; i < n; i++) {
-    r -= std::exp((double)lg[i] / temperature - mx);
-    if (r <= 0) return i;
-  }
-  return best;
 }
 
 // ---------------------------------------------------------------- persistent decode kernel: layout and launch
@@ -958,15 +965,11 @@ int h2c_create(int device, const h2c_config* cfg, h2c_engine** out) {
   const int MT = c.max_chunk, D = c.dim, F = c.ffn;
   const size_t kv = (size_t)c.max_seqs * c.layers * c.kv_heads * c.ctx * HD;
   e->am_np = 296;
-  if (c.ctx > 50000) {
+  if (c.ctx > MAX_CTX) {
     e->err = "ctx above 50000 positions (attention keeps one score per position in shared memory)";
     return bail(H2C_ERR_INVALID);
   }
-  ce = set_kernel_attrs(c.ctx);
-  if (ce != cudaSuccess) {
-    e->err = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(ce);
-    return bail(H2C_ERR_CUDA);
-  }
+  if (!kernel_attrs_on_current_device(&e->err)) return bail(H2C_ERR_CUDA);
   int r = 0;
   const int KQ = F > D ? F : D;
   if ((r = dalloc_t(e, &e->kc, kv)) || (r = dalloc_t(e, &e->vc, kv)) || (r = dalloc_t(e, &e->x, (size_t)MT * D)) ||
@@ -977,7 +980,8 @@ int h2c_create(int device, const h2c_config* cfg, h2c_engine** out) {
       (r = dalloc_t(e, &e->am_v, (size_t)e->am_np)) || (r = dalloc_t(e, &e->am_i, (size_t)e->am_np)) ||
       (r = dalloc_t(e, &e->prm, (size_t)P_WORDS)) || (r = dalloc_t(e, &e->next_d, 1)) ||
       (r = dalloc_t(e, &e->toklog, (size_t)c.max_seqs * (c.ctx + 1))) ||
-      (r = dalloc_t(e, &e->rope, (size_t)c.ctx * HD)))
+      (r = dalloc_t(e, &e->rope, (size_t)c.ctx * HD)) || (r = dalloc(e, &e->samp, sample_scratch_bytes(P_CAP))) ||
+      (r = dalloc_t(e, &e->seeds_d, (size_t)P_CAP)))
     return bail(r);
   // RoPE table in double precision, cpu-worker.js:131-135
   {
@@ -998,7 +1002,8 @@ int h2c_create(int device, const h2c_config* cfg, h2c_engine** out) {
   }
   e->prm_slots = (c.ctx + MT - 1) / MT + 1;
   ce = cudaMallocHost(&e->prm_h, sizeof(int32_t) * (size_t)(P_IDS + MT) * e->prm_slots);
-  if (ce == cudaSuccess) ce = cudaMallocHost(&e->next_h, sizeof(int32_t));
+  if (ce == cudaSuccess) ce = cudaMallocHost(&e->next_h, sizeof(int32_t) * P_CAP);
+  if (ce == cudaSuccess) ce = cudaMallocHost(&e->seeds_h, sizeof(uint32_t) * P_CAP);
   if (ce != cudaSuccess) {
     e->err = std::string("pinned allocation: ") + cudaGetErrorString(ce);
     return bail(H2C_ERR_NO_MEMORY);
@@ -1071,21 +1076,21 @@ int h2c_set_tensor(h2c_engine* e, int kind, int layer, int ggml_type, const void
   return r;
 }
 
-int h2c_forward(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t pos, float temperature, uint32_t seed,
+int h2c_forward(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t pos, double temperature, uint32_t seed,
                 int32_t* next) {
   if (!e || !next) return H2C_ERR_INVALID;
   CUDA_TRY(e, cudaSetDevice(e->dev));
   int r = run_forward(e, seq, ids, n, pos, nullptr);
   if (r) return r;
-  const uint32_t sseed = seed + (uint32_t)pos;
-  if (temperature > 0) {
-    std::vector<float> lg(e->cfg.vocab);
-    CUDA_TRY(e, cudaMemcpyAsync(lg.data(), e->logits, lg.size() * 4, cudaMemcpyDeviceToHost, e->st));
+  if (temperature > 0) {  // the draw runs on the device (sample.cu) over the logits of the last token
+    CUDA_TRY(e, launch_sample(e->logits, e->cfg.vocab, 1, temperature, nullptr, seed + (uint32_t)pos, e->next_d,
+                              e->samp, e->st));
+    CUDA_TRY(e, cudaMemcpyAsync(e->next_h, e->next_d, 4, cudaMemcpyDeviceToHost, e->st));
     if (e->mk_pending)
       CUDA_TRY(e, cudaMemcpyAsync(e->mk_io_h, e->mk_io, 8 * sizeof(int32_t), cudaMemcpyDeviceToHost, e->st));
     CUDA_TRY(e, cudaStreamSynchronize(e->st));
     if (e->mk_pending && (r = mk_status(e))) return r;
-    *next = sample_host(lg.data(), e->cfg.vocab, temperature, sseed);
+    *next = *e->next_h;
   } else if (e->mk_pending) {
     if ((r = mk_wait_done(e, next))) return r;
   } else {
@@ -1160,17 +1165,18 @@ int batch_launch(h2c_engine* e, int32_t n, const int32_t* seqs, const int32_t* i
 }
 
 int h2c_forward_batch(h2c_engine* e, int32_t n, const int32_t* seqs, const int32_t* ids, const int32_t* pos,
-                      float temperature, uint32_t seed, int32_t* next) {
+                      double temperature, uint32_t seed, int32_t* next) {
   if (!e || !seqs || !ids || !pos || !next) return H2C_ERR_INVALID;
   const h2c_config& c = e->cfg;
   int r = batch_launch(e, n, seqs, ids, pos, 1);
   if (r) return r;
-  if (temperature > 0) {
-    std::vector<float> lg((size_t)n * c.vocab);
-    CUDA_TRY(e, cudaMemcpyAsync(lg.data(), e->logits_b, lg.size() * 4, cudaMemcpyDeviceToHost, e->st));
+  if (temperature > 0) {  // each token's draw on the device, seeded by seed + its position
+    for (int m = 0; m < n; m++) e->seeds_h[m] = seed + (uint32_t)pos[m];
+    CUDA_TRY(e, cudaMemcpyAsync(e->seeds_d, e->seeds_h, sizeof(uint32_t) * n, cudaMemcpyHostToDevice, e->st));
+    CUDA_TRY(e, launch_sample(e->logits_b, c.vocab, n, temperature, e->seeds_d, 0, e->next_b, e->samp, e->st));
+    CUDA_TRY(e, cudaMemcpyAsync(e->next_bh, e->next_b, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, e->st));
     CUDA_TRY(e, cudaStreamSynchronize(e->st));
-    for (int m = 0; m < n; m++)
-      next[m] = sample_host(lg.data() + (size_t)m * c.vocab, c.vocab, temperature, seed + (uint32_t)pos[m]);
+    memcpy(next, e->next_bh, sizeof(int32_t) * n);
   } else {
     CUDA_TRY(e, cudaMemcpyAsync(e->next_bh, e->next_b, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, e->st));
     CUDA_TRY(e, cudaStreamSynchronize(e->st));
@@ -1386,6 +1392,7 @@ int h2c_destroy(h2c_engine* e) {
   if (e->mk_io_h) cudaFreeHost(e->mk_io_h);
   if (e->mk_done_h) cudaFreeHost(e->mk_done_h);
   if (e->next_h) cudaFreeHost(e->next_h);
+  if (e->seeds_h) cudaFreeHost(e->seeds_h);
   if (e->ev0) cudaEventDestroy(e->ev0);
   if (e->ev1) cudaEventDestroy(e->ev1);
   if (e->st) cudaStreamDestroy(e->st);
@@ -1420,13 +1427,18 @@ uint64_t h2c_q4_matvec_scratch_bytes(int32_t m, int32_t k) {
 
 int h2c_q4_matvec(const void* w, int32_t n_rows, int32_t k, const float* x, int32_t m, float* y, int32_t op,
                   const float* bias, void* scratch, void* stream) {
-  if (!w || !x || !y || !scratch || n_rows <= 0 || k <= 0 || k % 32 || m < 1 || op < 0 || op > 2 || (op == 1 && !bias))
+  if (!w || !x || !y || !scratch || n_rows <= 0 || k <= 0 || k % 32 || m < 1 || op < 0 || op > 2 || (op == 1 && !bias)) {
+    g_create_error = "h2c_q4_matvec: invalid argument";
     return H2C_ERR_INVALID;
-  if (((uintptr_t)w | (uintptr_t)scratch | (uintptr_t)x) & 15) return H2C_ERR_INVALID;
-  static bool attrs_set = false;
-  if (!attrs_set) {
-    if (set_kernel_attrs(2) != cudaSuccess) return H2C_ERR_CUDA;
-    attrs_set = true;
+  }
+  if (((uintptr_t)w | (uintptr_t)scratch | (uintptr_t)x) & 15) {
+    g_create_error = "h2c_q4_matvec: w, x and scratch must be 16-byte aligned";
+    return H2C_ERR_INVALID;
+  }
+  std::string why;
+  if (!kernel_attrs_on_current_device(&why)) {
+    g_create_error = "h2c_q4_matvec: " + why;
+    return H2C_ERR_CUDA;
   }
   cudaStream_t st = (cudaStream_t)stream;
   const size_t nbp = padded_rows(n_rows) * (k / 32);
@@ -1444,7 +1456,11 @@ int h2c_q4_matvec(const void* w, int32_t n_rows, int32_t k, const float* x, int3
   k_quant<<<(warps + 7) / 8, 256, 0, st>>>(x, k, m, xq, xd, xs);
   matvec(op, W, xq, xd, xs, m, y, n_rows, bias, st);
   cudaError_t c = cudaGetLastError();
-  return c == cudaSuccess ? H2C_OK : H2C_ERR_CUDA;
+  if (c != cudaSuccess) {
+    g_create_error = std::string("h2c_q4_matvec: launch failed: ") + cudaGetErrorString(c);
+    return H2C_ERR_CUDA;
+  }
+  return H2C_OK;
 }
 
 }  // extern "C"
@@ -1514,7 +1530,9 @@ extern "C" int h2c_q4_matvec_noalloc(const void* w, int32_t n_rows, int32_t k, c
     g_create_error = "h2c_q4_matvec_noalloc: " + why;
     return H2C_ERR_CUDA;
   }
-  return h2c_q4_matvec(w, n_rows, k, x, m, y, op, bias, scratch, stream);
+  const int r = h2c_q4_matvec(w, n_rows, k, x, m, y, op, bias, scratch, stream);
+  if (r != H2C_OK) g_create_error = "h2c_q4_matvec_noalloc: " + g_create_error;  // (the inner call's message)
+  return r;
 }
 
 // ---------------------------------------------------------------- self-test of the fast correctly rounded forms

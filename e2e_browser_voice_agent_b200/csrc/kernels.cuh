@@ -202,7 +202,7 @@ __device__ __forceinline__ void quant_block_nosum(float v, int lane, int8_t* q, 
 }
 
 // x[m] = dequant(embedding row ids[m]) (kernels.c:313-322), from the grouped / permuted Q4_0 layout
-__global__ void k_embed(const int32_t* __restrict__ prm, const uint8_t* __restrict__ qs, const __half* __restrict__ dsc,
+static __global__ void k_embed(const int32_t* __restrict__ prm, const uint8_t* __restrict__ qs, const __half* __restrict__ dsc,
                         int D, float* __restrict__ x) {
   const int m = blockIdx.x;
   const int t = prm[P_IDS + m];
@@ -222,7 +222,7 @@ __global__ void k_embed(const int32_t* __restrict__ prm, const uint8_t* __restri
 // scale with the exact fast division / square root / reciprocal, the blocks with quant_block_redux).
 // The sum of squares runs as the reference's four lane chains (threads 0..3), in element order.
 // dynamic smem: D floats
-__global__ void k_norm_quant(const float* __restrict__ x, int row0, const float* __restrict__ w, int D, float eps,
+static __global__ void k_norm_quant(const float* __restrict__ x, int row0, const float* __restrict__ w, int D, float eps,
                              int8_t* __restrict__ xq, float* __restrict__ xd, int4* __restrict__ xs) {
   extern __shared__ float xsm[];
   __shared__ float part[4];
@@ -255,7 +255,7 @@ __global__ void k_norm_quant(const float* __restrict__ x, int row0, const float*
 
 // int8 quantization of M rows of length K (the attention output before the O projection, kernels.c:379):
 // one warp per 32-value block.
-__global__ void k_quant(const float* __restrict__ x, int K, int M, int8_t* __restrict__ xq, float* __restrict__ xd,
+static __global__ void k_quant(const float* __restrict__ x, int K, int M, int8_t* __restrict__ xq, float* __restrict__ xd,
                         int4* __restrict__ xs) {
   const int nb = K / 32;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
@@ -266,7 +266,7 @@ __global__ void k_quant(const float* __restrict__ x, int K, int M, int8_t* __res
 }
 
 // act = silu(gate) * up, then int8 quantization (kernels.c:393-397); one warp per 32-value block of act.
-__global__ void k_swiglu_quant(const float* __restrict__ gu, int F, int M, int8_t* __restrict__ xq,
+static __global__ void k_swiglu_quant(const float* __restrict__ gu, int F, int M, int8_t* __restrict__ xq,
                                float* __restrict__ xd, int4* __restrict__ xs) {
   const int nb = F / 32;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
@@ -707,7 +707,7 @@ __global__ void __launch_bounds__(256) k_matmul_tc(const uint8_t* __restrict__ q
 
 // RoPE on the Q and K heads of each token (pairs (i, i + HD/2), table cos/sin), then K and V appended to the
 // cache of (seq, layer) (kernels.c:337-352). One CTA per token.
-__global__ void k_rope_kv(const int32_t* __restrict__ prm, float* __restrict__ qkv, int QKV, const float* __restrict__ rope,
+static __global__ void k_rope_kv(const int32_t* __restrict__ prm, float* __restrict__ qkv, int QKV, const float* __restrict__ rope,
                           float* __restrict__ kc, float* __restrict__ vc, int H, int KVH, int HD, int ctx, int layers,
                           int layer) {
   const int m = blockIdx.x;
@@ -929,7 +929,7 @@ __global__ void __launch_bounds__(256) k_attention_gqa(const int32_t* __restrict
 __device__ __forceinline__ void amax_merge(float& v, int& i, float v2, int i2) {
   if (v2 > v || (v2 == v && i2 < i)) { v = v2; i = i2; }
 }
-__global__ void k_argmax1(const float* __restrict__ logits, int V, float* __restrict__ pv, int* __restrict__ pi) {
+static __global__ void k_argmax1(const float* __restrict__ logits, int V, float* __restrict__ pv, int* __restrict__ pi) {
   __shared__ float sv[32];
   __shared__ int si[32];
   logits += (size_t)blockIdx.y * V;  // row blockIdx.y (one row per token of a batched step)
@@ -957,7 +957,7 @@ __global__ void k_argmax1(const float* __restrict__ logits, int V, float* __rest
 // stage 2: one warp merges the partials and stores the token. Like the WebGPU backend (webgpu.js:391), the token
 // stays on the device: it is logged at tokens[seq][pos0 + M] and the pass parameters are advanced to
 // (pos0 + M, one token, that id), so the next decode step can start without the host.
-__global__ void k_argmax2(const float* __restrict__ pv, const int* __restrict__ pi, int np, int32_t* __restrict__ prm,
+static __global__ void k_argmax2(const float* __restrict__ pv, const int* __restrict__ pi, int np, int32_t* __restrict__ prm,
                           int32_t* __restrict__ toklog, int ctx, int32_t* __restrict__ out) {
   float v = -INFINITY;
   int idx = 0x7fffffff;
@@ -982,7 +982,7 @@ __global__ void k_argmax2(const float* __restrict__ pv, const int* __restrict__ 
 // stage 2 of a batched decode step: block m merges row m's partials; the token of sequence seq_m (at position pos_m)
 // goes to out[m], is logged at tokens[seq_m][pos_m + 1] and becomes token m of the next step at pos_m + 1 (so
 // steps can be chained on the device, as k_argmax2 does for one sequence).
-__global__ void k_argmax2_batch(const float* __restrict__ pv, const int* __restrict__ pi, int np,
+static __global__ void k_argmax2_batch(const float* __restrict__ pv, const int* __restrict__ pi, int np,
                                 int32_t* __restrict__ prm, int32_t* __restrict__ toklog, int ctx,
                                 int32_t* __restrict__ out) {
   const int m = blockIdx.x;

@@ -83,10 +83,11 @@ int h2c_set_tensor(h2c_engine* e, int kind, int layer, int ggml_type, const void
 
 /* Run ids[0..n) of sequence `seq` at positions pos..pos+n-1 (prefill when n > 1, one decode step when n == 1)
  * and return the next token in *next: greedy argmax (ties to the lowest id) when temperature <= 0, else a
- * sample of softmax(logits / temperature) with mulberry32 seeded by (seed + pos) (cpu-worker.js:154-180).
+ * sample of softmax(logits / temperature) with mulberry32 seeded by (seed + pos) (cpu-worker.js:154-180), drawn on
+ * the device (the logits never leave it). temperature is a double, as the reference's JavaScript number is.
  * Prompts run in chunks of max_chunk tokens; logits exist for the last token only (kernels.c:404-414).
  * Replaces run() (kernels.c:454-465) plus the host loop of cpu-worker.js:169-182. */
-int h2c_forward(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t pos, float temperature,
+int h2c_forward(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t pos, double temperature,
                 uint32_t seed, int32_t* next);
 
 /* One decode step of n sessions at once (the multi-session serving form, forwardBatch of the CUDA backend; no
@@ -96,7 +97,7 @@ int h2c_forward(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t p
  * arithmetic is the single-token arithmetic, so the results equal n separate h2c_forward calls bit for bit.
  * 1 <= n <= min(max_chunk, 256). h2c_read_logits(seqs[m]) returns token m's logits afterwards. */
 int h2c_forward_batch(h2c_engine* e, int32_t n, const int32_t* seqs, const int32_t* ids, const int32_t* pos,
-                      float temperature, uint32_t seed, int32_t* next);
+                      double temperature, uint32_t seed, int32_t* next);
 
 /* Greedy decode of `steps` tokens of each of n sessions entirely on the device: batched steps as h2c_forward_batch,
  * each step's tokens fed to the next without a host round trip. out_tokens (nullable) receives [n][steps] ids;
@@ -163,7 +164,8 @@ int h2c_profile(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t p
 /* Free everything the engine owns (cpu.js:67 destroy). Safe on NULL. */
 int h2c_destroy(h2c_engine* e);
 
-/* Message of the last error on this engine (or of the last failed h2c_create when e is NULL). */
+/* Message of the last error on this engine; with e NULL, of the last failed call on this thread that has no engine
+ * (h2c_create, h2c_q4_matvec, h2c_q4_matvec_noalloc). */
 const char* h2c_last_error(const h2c_engine* e);
 
 /* Bytes of device memory the engine holds (cpu.js:53 memoryBytes / webgpu.js uploadedBytes). */

@@ -275,15 +275,167 @@ def test_errors():
     assert L.h2c_destroy(h) == 0
 
 
-def test_temperature_sampling_matches_oracle_sampler():
+def _oracle_kind():
+    """The reference's own kernels (oracle/_ref, multithreaded) when built, else the restatement."""
+    return "ref_mt" if O.available("ref_mt") else "oracle"
+
+
+@pytest.mark.parametrize("model", ["small", "qwen2-0.5b"])
+def test_temperature_sampling_on_device_matches_oracle_sampler(model):
+    """The device sampler (sample.cu) draws the token the CPU sampler of cpu-worker.js:153-167 (restated in the
+    oracle, on the host, in double precision) draws from the same logits, seed and position, over many seeds and
+    temperatures; single-token forward and batched steps alike."""
+    path = synth.ensure(model)
+    V = synth.CONFIGS[model]["vocab"]
+    be = backend.open_model(path, ctx=48, prefill_chunk=8, max_seqs=4)
+    samp = O.lib("oracle").h2o_sample
+    p = synth.prompt_ids(V, 6, seed=8)
+    checked = 0
+    for temp in (0.3, 0.7, 1.5):
+        for seed in range(0, 40, 3):
+            nxt = be.forward(p, 0, temperature=temp, seed=seed, want_logits=True)
+            lg = be.read_logits()
+            assert nxt == samp(lg.ctypes.data, lg.size, temp, seed & 0xFFFFFFFF), (temp, seed)
+            checked += 1
+    # batched: four sessions at different positions, one draw each seeded by seed + its position
+    pos = []
+    for s in range(4):
+        ps = synth.prompt_ids(V, 3 + s, seed=50 + s)
+        be.forward(ps, 0, seq=s)
+        pos.append(len(ps))
+    for seed in (1, 7, 123456789):
+        ids = [int(t) for t in synth.prompt_ids(V, 4, seed=seed)]
+        out = be.forward_batch([0, 1, 2, 3], ids, pos, temperature=0.8, seed=seed, want_logits=True)
+        for s in range(4):
+            lg = be.read_logits(s)
+            assert out[s] == samp(lg.ctypes.data, lg.size, 0.8, (seed + pos[s]) & 0xFFFFFFFF), (seed, s)
+            checked += 1
+    assert checked == 3 * 14 + 12
+    be.destroy()
+
+
+@pytest.mark.parametrize("model,n_prompt", [("small", 37), ("gqa7", 29), ("qwen2-0.5b", 40)])
+def test_teacher_forced_chunks_of_32(model, n_prompt):
+    """Prompt passes of 17..32 tokens: the largest token groups of the multi-token matmul (and, on the 0.5B
+    model, its 32-token instance on the gate/up and lm_head-sized matrices), bit-exact with the oracle."""
+    teacher_forced(model, n_prompt=n_prompt, steps=3, chunk=32, ctx=64)
+
+
+@pytest.mark.parametrize("N,K,M", [(4864, 896, 17), (4864, 896, 32), (9728, 896, 32), (896, 4864, 32),
+                                   (1152, 896, 24)])
+def test_q4_matvec_token_groups(N, K, M):
+    """The stand-alone Q4_0 matmul for 17-32 tokens (every token-group size of the multi-token kernel; matrices tall
+    enough for the 32-token groups), three ops, bit-exact with the oracle's quantize_row + matmul_q4."""
+    rng = np.random.default_rng(N * 7 + K + M)
+    blocks = G.q4_0_quantize(rng.standard_normal(N * K, dtype=np.float32) * np.float32(0.02))
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    bias = rng.standard_normal(N, dtype=np.float32)
+    L = _lib.load()
+    packed = np.zeros(L.h2c_q4_matrix_bytes(N, K), np.uint8)
+    assert L.h2c_q4_pack(blocks.ctypes.data, N, K, packed.ctypes.data) == 0
+    dev = torch.device("cuda")
+    w = torch.from_numpy(packed).to(dev)
+    xt = torch.from_numpy(x).to(dev)
+    scratch = torch.zeros(L.h2c_q4_matvec_scratch_bytes(M, K), dtype=torch.uint8, device=dev)
+    y0 = rng.standard_normal((M, N), dtype=np.float32)
+    for op in (0, 1, 2):
+        y = torch.from_numpy(y0).to(dev)
+        b = torch.from_numpy(bias).to(dev)
+        assert L.h2c_q4_matvec(w.data_ptr(), N, K, xt.data_ptr(), M, y.data_ptr(), op,
+                               b.data_ptr() if op == 1 else None, scratch.data_ptr(), None) == 0
+        torch.cuda.synchronize()
+        ref = O.matvec_q4(blocks, N, K, x, op=op, bias=bias if op == 1 else None, y=y0, nth=8)
+        got = y.cpu().numpy()
+        assert np.array_equal(bits(got), bits(ref)), f"op {op}: {rel_err(got, ref):.3g}"
+
+
+def test_multi_session_c4_shape():
+    """The multi-session configuration itself: 32 sessions per engine (max_seqs 32, 32-token prompt chunks),
+    128-token prompts, then batched decode steps. Every session's batched logits and token equal its own
+    single-session forward bit for bit, and two sessions equal the reference kernels step by step."""
+    path = synth.ensure("qwen2-0.5b")
+    S, P, steps, ctx = 32, 128, 3, 160
+    bat = backend.open_model(path, ctx=ctx, prefill_chunk=32, max_seqs=S)
+    sep = backend.open_model(path, ctx=ctx, prefill_chunk=32, max_seqs=S)
+    prompts = [synth.prompt_ids(151936, P, seed=1 + s) for s in range(S)]
+    tok = []
+    for s in range(S):
+        a = bat.forward(prompts[s], 0, seq=s)
+        assert sep.forward(prompts[s], 0, seq=s) == a
+        tok.append(a)
+    refs = {}
+    import os as _os
+    for s in (0, 17):
+        refs[s] = O.open_model(_oracle_kind(), path, ctx=ctx, mt=16, threads=_os.cpu_count() or 8)
+        assert refs[s].forward(prompts[s], 0)["next"] == tok[s]
+    pos = [P] * S
+    for k in range(steps):
+        out = bat.forward_batch(list(range(S)), tok, pos, want_logits=True)
+        for s in range(S):
+            ns = sep.forward([tok[s]], pos[s], seq=s, want_logits=True)
+            assert np.array_equal(bits(bat.read_logits(s)), bits(sep.read_logits(s))), f"step {k} seq {s}"
+            assert out[s] == ns
+            if s in refs:
+                r = refs[s].forward([tok[s]], pos[s], want_logits=True)
+                assert np.array_equal(bits(bat.read_logits(s)), bits(r["logits"])), f"step {k} seq {s} vs reference"
+                assert out[s] == r["next"]
+        tok, pos = out, [x + 1 for x in pos]
+    bat.destroy()
+    sep.destroy()
+
+
+def test_long_context_c3_prompt_4096():
+    """The long-context configuration at its real size: a 4096-token prompt (256 chunks of 16), then device-side
+    greedy decode; tokens and the last step's logits equal the reference kernels' (bit for bit)."""
+    import os as _os
+    path = synth.ensure("qwen2-0.5b")
+    n_prompt, steps, ctx = 4096, 4, 4609
+    be = backend.open_model(path, ctx=ctx, prefill_chunk=16)
+    prompt = synth.prompt_ids(151936, n_prompt, seed=3)
+    first = be.forward(prompt, 0)
+    dev, _ = be.generate(first, n_prompt, steps)
+    last = be.forward([int(dev[-1])], n_prompt + steps, want_logits=True)
+    ref = O.open_model(_oracle_kind(), path, ctx=ctx, mt=16, threads=_os.cpu_count() or 8)
+    r = ref.forward(prompt, 0)
+    assert r["next"] == first
+    want, nxt = [], r["next"]
+    for i in range(steps):
+        nxt = ref.forward([nxt], n_prompt + i)["next"]
+        want.append(nxt)
+    assert list(dev) == want
+    r = ref.forward([nxt], n_prompt + steps, want_logits=True)
+    assert last == r["next"]
+    assert np.array_equal(bits(be.read_logits()), bits(r["logits"]))
+    be.destroy()
+
+
+def test_llm_feed_reuses_the_common_prefix():
+    """LLM.feed (llm.js:45-54): a continuation runs only the new tokens, a repeated prompt re-runs its last token,
+    a diverging prompt keeps the common prefix; each result equals a fresh engine's run of the whole sequence."""
+    from e2e_browser_voice_agent_b200.llm import LLM
     path = synth.ensure("small")
-    be = backend.open_model(path, ctx=32, prefill_chunk=8)
-    p = synth.prompt_ids(2048, 6, seed=8)
-    for seed in range(5):
-        nxt = be.forward(p, 0, temperature=0.7, seed=seed, want_logits=True)
+    llm = LLM.load(path, ctx=96, prefill_chunk=8, keep_logits=True)
+    V = llm.cfg["vocab"]
+    a = [int(t) for t in synth.prompt_ids(V, 13, seed=61)]
+    b = [int(t) for t in synth.prompt_ids(V, 7, seed=62)]
+    c = [int(t) for t in synth.prompt_ids(V, 9, seed=63)]
+
+    def fresh(ids):
+        be = backend.open_model(path, ctx=96, prefill_chunk=8)
+        nxt = be.forward(ids, 0, want_logits=True)
         lg = be.read_logits()
-        exp = O.lib("oracle").h2o_sample(lg.ctypes.data, lg.size, 0.7, (seed + 0) & 0xFFFFFFFF)
-        assert nxt == exp
+        be.destroy()
+        return nxt, lg
+
+    cases = [(a, 0, 13), (a + b, 13, 7), (a + b, 19, 1), (a[:5] + c, 5, 9), (a[:5] + c + b, 14, 7)]
+    for ids, reused, prefilled in cases:
+        r = llm.feed(ids)
+        assert (r["reused"], r["prefilled"]) == (reused, prefilled), ids
+        nxt, lg = fresh(ids)
+        assert r["next"] == nxt
+        assert np.array_equal(bits(llm.be.read_logits()), bits(lg))
+    assert llm.seen == a[:5] + c + b
+    llm.be.destroy()
 
 
 def test_profile_names():
@@ -378,7 +530,7 @@ def test_forward_batch_errors():
     def call(seqs, ids, pos):
         s, t, p = (np.ascontiguousarray(np.asarray(v, dtype=np.int32)) for v in (seqs, ids, pos))
         out = np.zeros(max(len(seqs), 1), dtype=np.int32)
-        return L.h2c_forward_batch(h, len(seqs), s.ctypes.data, t.ctypes.data, p.ctypes.data, C.c_float(0.0),
+        return L.h2c_forward_batch(h, len(seqs), s.ctypes.data, t.ctypes.data, p.ctypes.data, C.c_double(0.0),
                                    C.c_uint32(1), out.ctypes.data)
 
     assert call([0, 0], [1, 2], [0, 0]) == _lib.ERR_INVALID           # a sequence twice

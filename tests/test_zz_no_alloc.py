@@ -61,3 +61,37 @@ def test_noalloc_rejects_inputs_beyond_its_buffer():
     rc = L.h2c_q4_matvec_noalloc(w.data_ptr(), 32, K, x.data_ptr(), M, y.data_ptr(), 0, None, None)
     assert rc == _lib.ERR_INVALID
     assert b"static buffer" in L.h2c_last_error(None)
+
+
+def test_noalloc_on_a_second_device():
+    """The library sets its kernels' shared-memory limits and looks the scratch address up per device: a call on
+    device 1 after calls on device 0 (no engine ever created on device 1) gives h2c_q4_matvec's result there."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two visible GPUs")
+    L = _lib.load()
+    N, K, M = 4864, 896, 3
+    rng = np.random.default_rng(9)
+    with torch.cuda.device(1):
+        w = packed_matrix(L, N, K, seed=5).to("cuda:1")
+        x = torch.from_numpy(rng.standard_normal((M, K), dtype=np.float32)).to("cuda:1")
+        scratch = torch.zeros(L.h2c_q4_matvec_scratch_bytes(M, K), dtype=torch.uint8, device="cuda:1")
+        y_ref = torch.zeros((M, N), dtype=torch.float32, device="cuda:1")
+        y_new = torch.zeros((M, N), dtype=torch.float32, device="cuda:1")
+        assert L.h2c_q4_matvec_noalloc(w.data_ptr(), N, K, x.data_ptr(), M, y_new.data_ptr(), 0, None, None) == 0, \
+            L.h2c_last_error(None)
+        assert L.h2c_q4_matvec(w.data_ptr(), N, K, x.data_ptr(), M, y_ref.data_ptr(), 0, None, scratch.data_ptr(),
+                               None) == 0
+        torch.cuda.synchronize()
+        assert np.array_equal(bits(y_new.cpu().numpy()), bits(y_ref.cpu().numpy()))
+
+
+def test_noalloc_reports_a_misaligned_input():
+    L = _lib.load()
+    N, K, M = 32, 96, 1
+    w = torch.zeros(L.h2c_q4_matrix_bytes(N, K), dtype=torch.uint8, device="cuda")
+    x = torch.zeros(K + 4, dtype=torch.float32, device="cuda")
+    y = torch.zeros((M, N), dtype=torch.float32, device="cuda")
+    rc = L.h2c_q4_matvec_noalloc(w.data_ptr(), N, K, x.data_ptr() + 4, M, y.data_ptr(), 0, None, None)
+    assert rc == _lib.ERR_INVALID
+    msg = L.h2c_last_error(None)
+    assert msg.startswith(b"h2c_q4_matvec_noalloc:") and b"16-byte aligned" in msg
