@@ -227,6 +227,21 @@ def cpu_baseline_sample():
                       f"{dt} decode threads of {cores} host cores (cpu.js:23 default)"}
 
 
+class nvtx_range:
+    """An NVTX range around a timed region (for profiler launch filters such as ncu --nvtx-include "c4_timed/")."""
+
+    def __init__(self, name):
+        self.name = name
+
+    def __enter__(self):
+        import torch
+        torch.cuda.nvtx.range_push(self.name)
+
+    def __exit__(self, *a):
+        import torch
+        torch.cuda.nvtx.range_pop()
+
+
 class Ctx:
     """Per-process benchmark context: rank, world, barrier and max-over-ranks."""
 
@@ -264,7 +279,8 @@ def measure_c4(cx: Ctx, steps: int, warm: int):
     clocks = Clocks(cx.local)
     cx.barrier()
     clocks.start()
-    _, ms = be.generate_batch(seqs, first, pos, steps)
+    with nvtx_range("c4_timed"):
+        _, ms = be.generate_batch(seqs, first, pos, steps)
     cx.barrier()
     ck = clocks.stop()
     ms = cx.max(ms)
@@ -326,7 +342,8 @@ def measure_prefill_and_c3(cx: Ctx, decode_steps: int):
         for _ in range(reps):
             cx.barrier()
             t0 = time.perf_counter()
-            first = be.forward(prompt, 0)
+            with nvtx_range(f"prefill_{n}"):
+                first = be.forward(prompt, 0)
             torch.cuda.synchronize()
             ts.append(time.perf_counter() - t0)
         t = cx.max(min(ts))
@@ -341,7 +358,8 @@ def measure_prefill_and_c3(cx: Ctx, decode_steps: int):
     clocks = Clocks(cx.local)
     cx.barrier()
     clocks.start()
-    _, ms = be.generate(first, C3_PROMPT, decode_steps)
+    with nvtx_range("c3_timed"):
+        _, ms = be.generate(first, C3_PROMPT, decode_steps)
     cx.barrier()
     ck = clocks.stop()
     ms = cx.max(ms)
@@ -471,7 +489,8 @@ def main():
     clocks = Clocks(local)
     cx.barrier()
     clocks.start()
-    ms, calls = device_rounds(steps)
+    with nvtx_range("c1_timed"):
+        ms, calls = device_rounds(steps)
     cx.barrier()
     ck = clocks.stop()
     ms = cx.max(ms)

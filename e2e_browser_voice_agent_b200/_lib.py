@@ -18,6 +18,7 @@ KIND_QKV, KIND_O, KIND_GATE_UP, KIND_DOWN, KIND_ATTN_NORM, KIND_FFN_NORM, KIND_Q
     KIND_OUTPUT_NORM = range(10)
 NPROF = 11
 DECODE_AUTO, DECODE_GRAPH, DECODE_PERSISTENT = 0, 1, 2
+MATMUL_AUTO, MATMUL_MMA_SYNC, MATMUL_TCGEN05 = 0, 1, 2
 PROFILE_NAMES = ["embed", "norm+quantize", "matvec qkv", "rope+kv", "attention", "quantize", "matvec o",
                  "matvec gate+up", "swiglu+quantize", "matvec down", "matvec output"]  # cpu-worker.js:32
 
@@ -26,7 +27,7 @@ EXPORTS = ["h2c_create", "h2c_set_tensor", "h2c_forward", "h2c_forward_batch", "
            "h2c_decode_path", "h2c_trace_decode", "h2c_decode_ctas", "h2c_set_decode_fault", "h2c_read_logits",
            "h2c_profile", "h2c_destroy", "h2c_selftest_math",
            "h2c_last_error", "h2c_device_bytes", "h2c_q4_matrix_bytes", "h2c_q4_pack", "h2c_q4_matvec_scratch_bytes",
-           "h2c_q4_matvec", "h2c_q4_matvec_noalloc"]
+           "h2c_q4_matvec", "h2c_q4_matvec_noalloc", "h2c_set_matmul_kernel", "h2c_matmul_kernel"]
 
 
 class Config(C.Structure):
@@ -81,10 +82,13 @@ def load(path: str = LIB_PATH) -> C.CDLL:
     L.h2c_q4_matvec_scratch_bytes.restype = u64
     L.h2c_q4_matvec.argtypes = [p, i32, i32, p, i32, p, i32, p, p, p]
     L.h2c_q4_matvec_noalloc.argtypes = [p, i32, i32, p, i32, p, i32, p, p]
+    L.h2c_set_matmul_kernel.argtypes = [C.c_int]
+    L.h2c_matmul_kernel.argtypes = []
     for name in ("h2c_create", "h2c_set_tensor", "h2c_forward", "h2c_forward_batch", "h2c_generate_batch", "h2c_batch_kernels", "h2c_generate", "h2c_decode_kernels", "h2c_set_decode_mode",
                  "h2c_decode_path", "h2c_trace_decode", "h2c_decode_ctas", "h2c_set_decode_fault", "h2c_read_logits",
                  "h2c_profile", "h2c_selftest_math",
-                 "h2c_destroy", "h2c_q4_pack", "h2c_q4_matvec", "h2c_q4_matvec_noalloc"):
+                 "h2c_destroy", "h2c_q4_pack", "h2c_q4_matvec", "h2c_q4_matvec_noalloc", "h2c_set_matmul_kernel",
+                 "h2c_matmul_kernel"):
         getattr(L, name).restype = C.c_int
     _lib = L
     return L

@@ -16,12 +16,28 @@
 #include "decode_mk.cuh"
 #include "kernels.cuh"
 #include "sample.cuh"
+#include "tc5.cuh"
 
 using namespace h2;
 
 namespace {
 
 thread_local std::string g_create_error;
+
+// The multi-token matmul kernel (h2c_set_matmul_kernel): H2C_MATMUL_AUTO / H2C_MATMUL_TCGEN05 take the tcgen05 form
+// (tc5.cu) for Q4_0 matrices, H2C_MATMUL_MMA_SYNC the warp-level int8 mma.sync form (k_matmul_tc).
+std::atomic<int> g_mm_kind{H2C_MATMUL_AUTO};
+bool use_tc5() { return g_mm_kind.load(std::memory_order_relaxed) != H2C_MATMUL_MMA_SYNC; }
+
+// What the tcgen05 matmul needs besides the activations: the transposed block scales, the rows of the activation
+// buffer, and the device word its bounded waits report into.
+struct MmCtx {
+  const float* xdT;
+  int ldT;
+  int xq_rows;
+  int* err;
+  bool* used;  // set when a launch took the tcgen05 form
+};
 
 struct Q4Mat {
   uint8_t* qs = nullptr;
@@ -57,6 +73,11 @@ struct h2c_engine {
   int8_t* xq = nullptr;
   float* xd = nullptr;
   int4* xs = nullptr;
+  float* xdT = nullptr;         // block scales transposed, [max(D, F) / 32][ldT] (tcgen05 matmul)
+  int ldT = 0;
+  int* tc5_err = nullptr;       // device: the tcgen05 matmul's failure record
+  int32_t* tc5_err_h = nullptr; // pinned copy
+  bool tc5_used = false;        // a pass of the current call took the tcgen05 matmul (its record is copied back)
   float* am_v = nullptr;
   int* am_i = nullptr;
   int am_np = 0;
@@ -85,6 +106,7 @@ struct h2c_engine {
   int32_t* next_bh = nullptr;  // pinned [P_CAP]
   std::vector<cudaGraphExec_t> bexec;
   std::vector<int> bkernels;   // kernel nodes of each batch graph
+  std::vector<char> btc5;      // the batch graph of that size contains tcgen05 matmuls
   std::string err;
   int64_t dev_bytes = 0;
   std::vector<void*> dallocs;
@@ -318,8 +340,13 @@ bool matmul_tc(int op, const uint8_t* qs, const __half* d, int N, int K, const i
 
 template <int WT>
 void matvec_w(int op, const uint8_t* qs, const __half* d, int N, int K, const int8_t* xq, const float* xd,
-              const int4* xs, int M, float* y, int ldy, const float* bias, cudaStream_t st) {
+              const int4* xs, int M, float* y, int ldy, const float* bias, cudaStream_t st, const MmCtx* mc = nullptr) {
   const int nb = K / 32;
+  if (WT == WQ4 && M > 1 && mc && use_tc5()) {  // several tokens on the tcgen05 tensor cores (tc5.cu)
+    launch_tc5(op, qs, d, N, K, xq, mc->xq_rows, mc->xdT, mc->ldT, M, y, ldy, bias, mc->err, st);
+    if (mc->used) *mc->used = true;
+    return;
+  }
   if (M == 1) {
     if (nb <= 64) launch_mv_t<WT, 32, 1>(op, qs, d, N, K, xq, xd, xs, 1, y, ldy, bias, st);
     else launch_mv_t<WT, 16, 1>(op, qs, d, N, K, xq, xd, xs, 1, y, ldy, bias, st);
@@ -336,8 +363,8 @@ void matvec_w(int op, const uint8_t* qs, const __half* d, int N, int K, const in
 }
 
 void matvec(int op, const Q4Mat& W, const int8_t* xq, const float* xd, const int4* xs, int M, float* y, int ldy,
-            const float* bias, cudaStream_t st) {
-  matvec_w<WQ4>(op, W.qs, W.d, W.N, W.K, xq, xd, xs, M, y, ldy, bias, st);
+            const float* bias, cudaStream_t st, const MmCtx* mc = nullptr) {
+  matvec_w<WQ4>(op, W.qs, W.d, W.N, W.K, xq, xd, xs, M, y, ldy, bias, st, mc);
 }
 
 // Opt every kernel that takes more than 48 KB of dynamic shared memory into the larger carve-out.
@@ -399,6 +426,7 @@ cudaError_t set_kernel_attrs() {
   if (c == cudaSuccess)
     c = cudaFuncSetAttribute(k_attention_gqa<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATTG_SMEM);
   if (c == cudaSuccess) c = cudaFuncSetAttribute(k_attention<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, att);
+  if (c == cudaSuccess) c = tc5_set_attrs();
   return c;
 }
 
@@ -445,14 +473,17 @@ void enqueue_pass(h2c_engine* e, int M, bool logits, Prof* pf, bool batch = fals
   const h2c_config& c = e->cfg;
   const int D = c.dim, F = c.ffn, H = c.heads, KVH = c.kv_heads, HD = e->HD, QKV = e->QKV, NL = c.layers;
   cudaStream_t st = e->st;
+  const MmCtx mcv{e->xdT, e->ldT, c.max_chunk, e->tc5_err, &e->tc5_used};
+  const MmCtx* mc = M > 1 ? &mcv : nullptr;
+  float* xdT = M > 1 ? e->xdT : nullptr;
   mark(pf, -1, st);
   k_embed<<<M, 128, 0, st>>>(e->prm, e->embd.qs, e->embd.d, D, e->x);
   mark(pf, 0, st);
   for (int l = 0; l < NL; l++) {
     const LayerW& W = e->L[l];
-    k_norm_quant<<<M, 256, D * 4, st>>>(e->x, 0, W.attn_norm, D, c.eps, e->xq, e->xd, e->xs);
+    k_norm_quant<<<M, 256, D * 4, st>>>(e->x, 0, W.attn_norm, D, c.eps, e->xq, e->xd, e->xs, xdT, e->ldT);
     mark(pf, 1, st);
-    matvec(OP_BIAS, W.qkv, e->xq, e->xd, e->xs, M, e->qkv, QKV, W.bqkv, st);
+    matvec(OP_BIAS, W.qkv, e->xq, e->xd, e->xs, M, e->qkv, QKV, W.bqkv, st, mc);
     mark(pf, 2, st);
     k_rope_kv<<<M, 256, 0, st>>>(e->prm, e->qkv, QKV, e->rope, e->kc, e->vc, H, KVH, HD, c.ctx, NL, l);
     mark(pf, 3, st);
@@ -471,30 +502,31 @@ void enqueue_pass(h2c_engine* e, int M, bool logits, Prof* pf, bool batch = fals
     mark(pf, 4, st);
     {
       const int warps = M * (D / 32);
-      k_quant<<<(warps + 7) / 8, 256, 0, st>>>(e->att, D, M, e->xq, e->xd, e->xs);
+      k_quant<<<(warps + 7) / 8, 256, 0, st>>>(e->att, D, M, e->xq, e->xd, e->xs, xdT, e->ldT);
     }
     mark(pf, 5, st);
-    matvec(OP_ADD, W.o, e->xq, e->xd, e->xs, M, e->x, D, nullptr, st);
+    matvec(OP_ADD, W.o, e->xq, e->xd, e->xs, M, e->x, D, nullptr, st, mc);
     mark(pf, 6, st);
-    k_norm_quant<<<M, 256, D * 4, st>>>(e->x, 0, W.ffn_norm, D, c.eps, e->xq, e->xd, e->xs);
+    k_norm_quant<<<M, 256, D * 4, st>>>(e->x, 0, W.ffn_norm, D, c.eps, e->xq, e->xd, e->xs, xdT, e->ldT);
     mark(pf, 1, st);
-    matvec(OP_STORE, W.gu, e->xq, e->xd, e->xs, M, e->gu, 2 * F, nullptr, st);
+    matvec(OP_STORE, W.gu, e->xq, e->xd, e->xs, M, e->gu, 2 * F, nullptr, st, mc);
     mark(pf, 7, st);
     {
       const int warps = M * (F / 32);
-      k_swiglu_quant<<<(warps + 7) / 8, 256, 0, st>>>(e->gu, F, M, e->xq, e->xd, e->xs);
+      k_swiglu_quant<<<(warps + 7) / 8, 256, 0, st>>>(e->gu, F, M, e->xq, e->xd, e->xs, xdT, e->ldT);
     }
     mark(pf, 8, st);
-    matvec(OP_ADD, W.down, e->xq, e->xd, e->xs, M, e->x, D, nullptr, st);
+    matvec(OP_ADD, W.down, e->xq, e->xd, e->xs, M, e->x, D, nullptr, st, mc);
     mark(pf, 9, st);
   }
   if (batch) {  // every token of a batched decode step is the last of its sequence: logits and a token for each
-    k_norm_quant<<<M, 256, D * 4, st>>>(e->x, 0, e->out_norm, D, c.eps, e->xq, e->xd, e->xs);
+    k_norm_quant<<<M, 256, D * 4, st>>>(e->x, 0, e->out_norm, D, c.eps, e->xq, e->xd, e->xs, xdT, e->ldT);
     if (e->out_type == 8) {
       matvec_w<WQ8>(OP_STORE, (const uint8_t*)e->out8.qs, e->out8.d, c.vocab, D, e->xq, e->xd, e->xs, M, e->logits_b,
                     c.vocab, nullptr, st);
     } else {
-      matvec(OP_STORE, e->out_type == 2 ? e->out4 : e->embd, e->xq, e->xd, e->xs, M, e->logits_b, c.vocab, nullptr, st);
+      matvec(OP_STORE, e->out_type == 2 ? e->out4 : e->embd, e->xq, e->xd, e->xs, M, e->logits_b, c.vocab, nullptr, st,
+             mc);
     }
     k_argmax1<<<dim3(e->am_np, M), 256, 0, st>>>(e->logits_b, c.vocab, e->am_vb, e->am_ib);
     k_argmax2_batch<<<M, 32, 0, st>>>(e->am_vb, e->am_ib, e->am_np, e->prm, e->toklog, e->cfg.ctx, e->next_b);
@@ -868,6 +900,23 @@ int mk_wait_done(h2c_engine* e, int32_t* next) {
   return H2C_OK;
 }
 
+// The tcgen05 matmul records a bounded wait that expired in e->tc5_err: copy it back after the passes that used it
+// (enqueued right behind them) and turn it into a status once the stream has reached the copy.
+int tc5_enqueue_check(h2c_engine* e) {
+  if (e->tc5_used)
+    CUDA_TRY(e, cudaMemcpyAsync(e->tc5_err_h, e->tc5_err, 4 * sizeof(int32_t), cudaMemcpyDeviceToHost, e->st));
+  return H2C_OK;
+}
+int tc5_status(h2c_engine* e) {
+  if (!e->tc5_used) return H2C_OK;
+  e->tc5_used = false;
+  if (e->tc5_err_h[0] == 0) return H2C_OK;
+  const int cta = e->tc5_err_h[1], role = e->tc5_err_h[2];
+  memset(e->tc5_err_h, 0, 4 * sizeof(int32_t));
+  CUDA_TRY(e, cudaMemsetAsync(e->tc5_err, 0, 4 * sizeof(int32_t), e->st));
+  return e->fail(H2C_ERR_TIMEOUT, "tcgen05 matmul: bounded wait expired (CTA %d, role %d)", cta, role);
+}
+
 int run_forward(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t pos, Prof* pf) {
   const h2c_config& c = e->cfg;
   if (!ids || n < 1) return e->fail(H2C_ERR_INVALID, "forward needs at least one token");
@@ -912,6 +961,7 @@ int run_forward(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t p
     } else {
       enqueue_pass(e, mlen, last, pf);
       CUDA_TRY(e, cudaGetLastError());
+      if ((r = tc5_enqueue_check(e))) return r;
     }
   }
   return H2C_OK;
@@ -981,8 +1031,10 @@ int h2c_create(int device, const h2c_config* cfg, h2c_engine** out) {
       (r = dalloc_t(e, &e->prm, (size_t)P_WORDS)) || (r = dalloc_t(e, &e->next_d, 1)) ||
       (r = dalloc_t(e, &e->toklog, (size_t)c.max_seqs * (c.ctx + 1))) ||
       (r = dalloc_t(e, &e->rope, (size_t)c.ctx * HD)) || (r = dalloc(e, &e->samp, sample_scratch_bytes(P_CAP))) ||
-      (r = dalloc_t(e, &e->seeds_d, (size_t)P_CAP)))
+      (r = dalloc_t(e, &e->seeds_d, (size_t)P_CAP)) ||
+      (r = dalloc_t(e, &e->xdT, (size_t)(KQ / 32) * ((MT + 3) / 4 * 4))) || (r = dalloc_t(e, &e->tc5_err, 4)))
     return bail(r);
+  e->ldT = (MT + 3) / 4 * 4;
   // RoPE table in double precision, cpu-worker.js:131-135
   {
     std::vector<float> t((size_t)c.ctx * HD);
@@ -1004,6 +1056,8 @@ int h2c_create(int device, const h2c_config* cfg, h2c_engine** out) {
   ce = cudaMallocHost(&e->prm_h, sizeof(int32_t) * (size_t)(P_IDS + MT) * e->prm_slots);
   if (ce == cudaSuccess) ce = cudaMallocHost(&e->next_h, sizeof(int32_t) * P_CAP);
   if (ce == cudaSuccess) ce = cudaMallocHost(&e->seeds_h, sizeof(uint32_t) * P_CAP);
+  if (ce == cudaSuccess) ce = cudaMallocHost(&e->tc5_err_h, sizeof(int32_t) * 4);
+  if (ce == cudaSuccess) memset(e->tc5_err_h, 0, sizeof(int32_t) * 4);
   if (ce != cudaSuccess) {
     e->err = std::string("pinned allocation: ") + cudaGetErrorString(ce);
     return bail(H2C_ERR_NO_MEMORY);
@@ -1098,6 +1152,7 @@ int h2c_forward(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t p
     CUDA_TRY(e, cudaStreamSynchronize(e->st));
     *next = *e->next_h;
   }
+  if ((r = tc5_status(e))) return r;
   e->last_logits_valid.assign(e->cfg.max_seqs, 0);
   e->last_logits_valid[seq] = 1;
   return H2C_OK;
@@ -1131,6 +1186,7 @@ int batch_launch(h2c_engine* e, int32_t n, const int32_t* seqs, const int32_t* i
     memset(e->prm_bh, 0, sizeof(int32_t) * P_WORDS);
     e->bexec.assign(cap + 1, nullptr);
     e->bkernels.assign(cap + 1, 0);
+    e->btc5.assign(cap + 1, 0);
   }
   int32_t* h = e->prm_bh;
   h[P_POS0] = 0; h[P_M] = n; h[P_SEQ] = 0; h[P_MODE] = 1;
@@ -1143,7 +1199,11 @@ int batch_launch(h2c_engine* e, int32_t n, const int32_t* seqs, const int32_t* i
   if (!e->bexec[n]) {  // one graph per batch size, captured on first use
     cudaGraph_t g = nullptr;
     CUDA_TRY(e, cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal));
+    const bool used_before = e->tc5_used;
+    e->tc5_used = false;
     enqueue_pass(e, n, false, nullptr, true);
+    e->btc5[n] = e->tc5_used;
+    e->tc5_used = used_before;
     cudaError_t ce = cudaStreamEndCapture(e->st, &g);
     if (ce != cudaSuccess) return e->fail(H2C_ERR_CUDA, "graph capture: %s", cudaGetErrorString(ce));
     ce = cudaGraphInstantiate(&e->bexec[n], g, 0);
@@ -1161,6 +1221,10 @@ int batch_launch(h2c_engine* e, int32_t n, const int32_t* seqs, const int32_t* i
   }
   if (before) CUDA_TRY(e, cudaEventRecord(before, e->st));
   for (int i = 0; i < steps; i++) CUDA_TRY(e, cudaGraphLaunch(e->bexec[n], e->st));
+  if (e->btc5[n]) {
+    e->tc5_used = true;
+    if ((r = tc5_enqueue_check(e))) return r;
+  }
   return H2C_OK;
 }
 
@@ -1182,6 +1246,7 @@ int h2c_forward_batch(h2c_engine* e, int32_t n, const int32_t* seqs, const int32
     CUDA_TRY(e, cudaStreamSynchronize(e->st));
     memcpy(next, e->next_bh, sizeof(int32_t) * n);
   }
+  if ((r = tc5_status(e))) return r;
   e->last_logits_valid.assign(c.max_seqs, 0);
   for (int m = 0; m < n; m++) e->last_logits_valid[seqs[m]] = 2 + m;  // row m of the batch logits
   return H2C_OK;
@@ -1200,6 +1265,7 @@ int h2c_generate_batch(h2c_engine* e, int32_t n, const int32_t* seqs, const int3
       CUDA_TRY(e, cudaMemcpyAsync(out_tokens + (size_t)m * steps, e->toklog + (size_t)seqs[m] * (c.ctx + 1) + pos[m] + 1,
                                   sizeof(int32_t) * steps, cudaMemcpyDeviceToHost, e->st));
   CUDA_TRY(e, cudaStreamSynchronize(e->st));
+  if ((r = tc5_status(e))) return r;
   if (device_ms) CUDA_TRY(e, cudaEventElapsedTime(device_ms, e->ev0, e->ev1));
   e->last_logits_valid.assign(c.max_seqs, 0);
   for (int m = 0; m < n; m++) e->last_logits_valid[seqs[m]] = 2 + m;
@@ -1360,6 +1426,7 @@ int h2c_profile(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t p
     cudaError_t c = cudaStreamSynchronize(e->st);
     if (c != cudaSuccess) r = e->fail(H2C_ERR_CUDA, "profile: %s", cudaGetErrorString(c));
   }
+  if (!r) r = tc5_status(e);
   for (int i = 0; i < H2C_NPROF; i++) ms[i] = 0;
   if (!r) {
     // events are reused in a ring when more than 64 marks are recorded: fold only the final window
@@ -1393,6 +1460,7 @@ int h2c_destroy(h2c_engine* e) {
   if (e->mk_done_h) cudaFreeHost(e->mk_done_h);
   if (e->next_h) cudaFreeHost(e->next_h);
   if (e->seeds_h) cudaFreeHost(e->seeds_h);
+  if (e->tc5_err_h) cudaFreeHost(e->tc5_err_h);
   if (e->ev0) cudaEventDestroy(e->ev0);
   if (e->ev1) cudaEventDestroy(e->ev1);
   if (e->st) cudaStreamDestroy(e->st);
@@ -1425,6 +1493,45 @@ uint64_t h2c_q4_matvec_scratch_bytes(int32_t m, int32_t k) {
   return align_up((uint64_t)m * k, 256) + align_up(nb * 4, 256) + align_up(nb * 16, 256);
 }
 
+}  // extern "C"
+
+namespace {
+// The failure record of tcgen05 matmuls launched by h2c_q4_matvec (no engine to hold one): a small __device__
+// array, its address looked up once per device.
+__device__ int g_tc5_err_words[4];
+int* g_tc5_err_ptr[ATTR_MAX_DEVICES];
+std::mutex g_tc5_err_mutex;
+int* tc5_standalone_err(std::string* why) {
+  int dev = -1;
+  cudaError_t c = cudaGetDevice(&dev);
+  if (c != cudaSuccess || dev < 0 || dev >= ATTR_MAX_DEVICES) {
+    *why = "cudaGetDevice failed";
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_tc5_err_mutex);
+  if (!g_tc5_err_ptr[dev]) {
+    void* p = nullptr;
+    c = cudaGetSymbolAddress(&p, g_tc5_err_words);
+    if (c != cudaSuccess || !p) {
+      *why = std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(c);
+      return nullptr;
+    }
+    g_tc5_err_ptr[dev] = static_cast<int*>(p);
+  }
+  return g_tc5_err_ptr[dev];
+}
+}  // namespace
+
+extern "C" {
+
+int h2c_set_matmul_kernel(int kind) {
+  if (kind < H2C_MATMUL_AUTO || kind > H2C_MATMUL_TCGEN05) return H2C_ERR_INVALID;
+  g_mm_kind.store(kind);
+  return H2C_OK;
+}
+
+int h2c_matmul_kernel(void) { return use_tc5() ? H2C_MATMUL_TCGEN05 : H2C_MATMUL_MMA_SYNC; }
+
 int h2c_q4_matvec(const void* w, int32_t n_rows, int32_t k, const float* x, int32_t m, float* y, int32_t op,
                   const float* bias, void* scratch, void* stream) {
   if (!w || !x || !y || !scratch || n_rows <= 0 || k <= 0 || k % 32 || m < 1 || op < 0 || op > 2 || (op == 1 && !bias)) {
@@ -1453,8 +1560,21 @@ int h2c_q4_matvec(const void* w, int32_t n_rows, int32_t k, const float* x, int3
   float* xd = (float*)(s + align_up((size_t)m * k, 256));
   int4* xs = (int4*)(s + align_up((size_t)m * k, 256) + align_up(mb * 4, 256));
   const int warps = (int)mb;
-  k_quant<<<(warps + 7) / 8, 256, 0, st>>>(x, k, m, xq, xd, xs);
-  matvec(op, W, xq, xd, xs, m, y, n_rows, bias, st);
+  if (m > 1 && use_tc5()) {  // the tcgen05 form reads the scales transposed, kept where the lane sums would go
+    int* err = tc5_standalone_err(&why);
+    if (!err) {
+      g_create_error = "h2c_q4_matvec: " + why;
+      return H2C_ERR_CUDA;
+    }
+    const int ldT = (m + 3) / 4 * 4;
+    float* xdT = reinterpret_cast<float*>(xs);
+    k_quant<<<(warps + 7) / 8, 256, 0, st>>>(x, k, m, xq, xd, nullptr, xdT, ldT);
+    const MmCtx mc{xdT, ldT, m, err, nullptr};
+    matvec(op, W, xq, xd, nullptr, m, y, n_rows, bias, st, &mc);
+  } else {
+    k_quant<<<(warps + 7) / 8, 256, 0, st>>>(x, k, m, xq, xd, xs);
+    matvec(op, W, xq, xd, xs, m, y, n_rows, bias, st);
+  }
   cudaError_t c = cudaGetLastError();
   if (c != cudaSuccess) {
     g_create_error = std::string("h2c_q4_matvec: launch failed: ") + cudaGetErrorString(c);

@@ -175,7 +175,9 @@ __device__ __forceinline__ float magic_to_float(int acc) { return __fsub_rn(__in
 // the integer max of the |x| bit patterns (order-preserving for non-negative floats); the four lane sums are two
 // packed add-reductions of the biased values q + 128 (eight of them per lane sum fit 16 bits), lanes 0 and 1 in one
 // word, 2 and 3 in the other.
-__device__ __forceinline__ void quant_block_redux(float v, int lane, int8_t* q, float* d, int4* s) {
+// dT (optional): a second copy of the scale (the transposed scale array the tensor-core matmul reads); s may be null
+// when no consumer needs the lane sums.
+__device__ __forceinline__ void quant_block_redux(float v, int lane, int8_t* q, float* d, int4* s, float* dT = nullptr) {
   const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v))));
   float dd, id;
   block_scales(amax, dd, id);
@@ -187,8 +189,10 @@ __device__ __forceinline__ void quant_block_redux(float v, int lane, int8_t* q, 
   const unsigned s23 = __reduce_add_sync(0xffffffffu, dl < 2 ? 0u : bq);
   if (lane == 0) {
     *d = dd;
-    *s = make_int4(MK_MAGIC - 8 * ((int)(s01 & 0xffffu) - 1024), MK_MAGIC - 8 * ((int)(s01 >> 16) - 1024),
-                   MK_MAGIC - 8 * ((int)(s23 & 0xffffu) - 1024), MK_MAGIC - 8 * ((int)(s23 >> 16) - 1024));
+    if (dT) *dT = dd;
+    if (s)
+      *s = make_int4(MK_MAGIC - 8 * ((int)(s01 & 0xffffu) - 1024), MK_MAGIC - 8 * ((int)(s01 >> 16) - 1024),
+                     MK_MAGIC - 8 * ((int)(s23 & 0xffffu) - 1024), MK_MAGIC - 8 * ((int)(s23 >> 16) - 1024));
   }
 }
 
@@ -221,9 +225,10 @@ static __global__ void k_embed(const int32_t* __restrict__ prm, const uint8_t* _
 // RMSNorm (kernels.c:80-86) of row (row0 + blockIdx.x) of x, then int8 quantization into slot blockIdx.x (the
 // scale with the exact fast division / square root / reciprocal, the blocks with quant_block_redux).
 // The sum of squares runs as the reference's four lane chains (threads 0..3), in element order.
-// dynamic smem: D floats
+// dynamic smem: D floats. xdT (optional): the scales again, transposed ([block][ldT], token slot blockIdx.x).
 static __global__ void k_norm_quant(const float* __restrict__ x, int row0, const float* __restrict__ w, int D, float eps,
-                             int8_t* __restrict__ xq, float* __restrict__ xd, int4* __restrict__ xs) {
+                             int8_t* __restrict__ xq, float* __restrict__ xd, int4* __restrict__ xs,
+                             float* __restrict__ xdT = nullptr, int ldT = 0) {
   extern __shared__ float xsm[];
   __shared__ float part[4];
   __shared__ float rs;
@@ -249,25 +254,28 @@ static __global__ void k_norm_quant(const float* __restrict__ x, int row0, const
   for (int b = warp; b < nb; b += nw) {
     const int i = b * 32 + lane;
     const float v = __fmul_rn(__fmul_rn(xsm[i], r), w[i]);
-    quant_block_redux(v, lane, xq + (size_t)slot * D + b * 32, xd + (size_t)slot * nb + b, xs + (size_t)slot * nb + b);
+    quant_block_redux(v, lane, xq + (size_t)slot * D + b * 32, xd + (size_t)slot * nb + b, xs + (size_t)slot * nb + b,
+                      xdT ? xdT + (size_t)b * ldT + slot : nullptr);
   }
 }
 
 // int8 quantization of M rows of length K (the attention output before the O projection, kernels.c:379):
-// one warp per 32-value block.
+// one warp per 32-value block. xs may be null (no lane sums); xdT (optional): the scales transposed ([block][ldT]).
 static __global__ void k_quant(const float* __restrict__ x, int K, int M, int8_t* __restrict__ xq, float* __restrict__ xd,
-                        int4* __restrict__ xs) {
+                        int4* __restrict__ xs, float* __restrict__ xdT = nullptr, int ldT = 0) {
   const int nb = K / 32;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (gw >= M * nb) return;
   const int m = gw / nb, b = gw % nb;
   const float v = x[(size_t)m * K + b * 32 + lane];
-  quant_block_redux(v, lane, xq + (size_t)m * K + b * 32, xd + (size_t)m * nb + b, xs + (size_t)m * nb + b);
+  quant_block_redux(v, lane, xq + (size_t)m * K + b * 32, xd + (size_t)m * nb + b, xs ? xs + (size_t)m * nb + b : nullptr,
+                    xdT ? xdT + (size_t)b * ldT + m : nullptr);
 }
 
 // act = silu(gate) * up, then int8 quantization (kernels.c:393-397); one warp per 32-value block of act.
 static __global__ void k_swiglu_quant(const float* __restrict__ gu, int F, int M, int8_t* __restrict__ xq,
-                               float* __restrict__ xd, int4* __restrict__ xs) {
+                               float* __restrict__ xd, int4* __restrict__ xs, float* __restrict__ xdT = nullptr,
+                               int ldT = 0) {
   const int nb = F / 32;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (gw >= M * nb) return;
@@ -275,7 +283,8 @@ static __global__ void k_swiglu_quant(const float* __restrict__ gu, int F, int M
   const float* g = gu + (size_t)m * 2 * F;
   const float gt = g[b * 32 + lane], up = g[F + b * 32 + lane];
   const float v = __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, fast_exp_ref(-gt))), up);
-  quant_block_redux(v, lane, xq + (size_t)m * F + b * 32, xd + (size_t)m * nb + b, xs + (size_t)m * nb + b);
+  quant_block_redux(v, lane, xq + (size_t)m * F + b * 32, xd + (size_t)m * nb + b, xs + (size_t)m * nb + b,
+                    xdT ? xdT + (size_t)b * ldT + m : nullptr);
 }
 
 enum { OP_STORE = 0, OP_BIAS = 1, OP_ADD = 2 };

@@ -314,6 +314,32 @@ def test_temperature_sampling_on_device_matches_oracle_sampler(model):
     be.destroy()
 
 
+@pytest.mark.parametrize("model,chunk", [("small", 64), ("gqa7", 128), ("qwen2-0.5b", 256)])
+def test_prompt_chunks_tcgen05_equal_mma_sync_and_oracle(model, chunk):
+    """Long prompt chunks (64-256 tokens, the tcgen05 kernel's 64- and 128-token CTAs): the engine gives the same
+    logits bit for bit with either multi-token kernel, and the oracle's."""
+    L = _lib.load()
+    path = synth.ensure(model)
+    V = synth.CONFIGS[model]["vocab"]
+    prompt = synth.prompt_ids(V, chunk + 11, seed=chunk)
+    got = {}
+    try:
+        for kind in (_lib.MATMUL_TCGEN05, _lib.MATMUL_MMA_SYNC):
+            assert L.h2c_set_matmul_kernel(kind) == 0
+            be = backend.open_model(path, ctx=chunk + 16, prefill_chunk=chunk)
+            got[kind] = (be.forward(prompt, 0, want_logits=True), be.read_logits())
+            be.destroy()
+    finally:
+        L.h2c_set_matmul_kernel(_lib.MATMUL_AUTO)
+    (n_a, l_a), (n_b, l_b) = got[_lib.MATMUL_TCGEN05], got[_lib.MATMUL_MMA_SYNC]
+    assert n_a == n_b and np.array_equal(bits(l_a), bits(l_b))
+    import os as _os
+    ref = O.open_model(_oracle_kind() if model == "qwen2-0.5b" else "oracle", path, ctx=chunk + 16, mt=16,
+                       threads=_os.cpu_count() or 8)
+    r = ref.forward(prompt, 0, want_logits=True)
+    assert n_a == r["next"] and np.array_equal(bits(l_a), bits(r["logits"]))
+
+
 @pytest.mark.parametrize("model,n_prompt", [("small", 37), ("gqa7", 29), ("qwen2-0.5b", 40)])
 def test_teacher_forced_chunks_of_32(model, n_prompt):
     """Prompt passes of 17..32 tokens: the largest token groups of the multi-token matmul (and, on the 0.5B
@@ -321,11 +347,23 @@ def test_teacher_forced_chunks_of_32(model, n_prompt):
     teacher_forced(model, n_prompt=n_prompt, steps=3, chunk=32, ctx=64)
 
 
+@pytest.mark.parametrize("kernel", ["tcgen05", "mma_sync"])
 @pytest.mark.parametrize("N,K,M", [(4864, 896, 17), (4864, 896, 32), (9728, 896, 32), (896, 4864, 32),
-                                   (1152, 896, 24)])
-def test_q4_matvec_token_groups(N, K, M):
-    """The stand-alone Q4_0 matmul for 17-32 tokens (every token-group size of the multi-token kernel; matrices tall
-    enough for the 32-token groups), three ops, bit-exact with the oracle's quantize_row + matmul_q4."""
+                                   (1152, 896, 24), (896, 896, 48), (1152, 896, 64), (896, 4864, 100),
+                                   (4864, 896, 128), (896, 896, 256), (70, 96, 40)])
+def test_q4_matvec_token_groups(N, K, M, kernel):
+    """The stand-alone Q4_0 matmul for 17-256 tokens in both multi-token kernels (tcgen05.mma with TMEM
+    accumulators: 16/32/64/128-token CTAs; mma.sync: 8/16/32-token groups), three ops, bit-exact with the oracle's
+    quantize_row + matmul_q4."""
+    L = _lib.load()
+    assert L.h2c_set_matmul_kernel(_lib.MATMUL_TCGEN05 if kernel == "tcgen05" else _lib.MATMUL_MMA_SYNC) == 0
+    try:
+        _token_groups(N, K, M)
+    finally:
+        L.h2c_set_matmul_kernel(_lib.MATMUL_AUTO)
+
+
+def _token_groups(N, K, M):
     rng = np.random.default_rng(N * 7 + K + M)
     blocks = G.q4_0_quantize(rng.standard_normal(N * K, dtype=np.float32) * np.float32(0.02))
     x = rng.standard_normal((M, K), dtype=np.float32)
