@@ -22,7 +22,8 @@ every rank (so a multi-GPU run records each at every N):
 Multi-GPU (torchrun, one rank per GPU): independent sessions per rank, weights replicated, no collective on the
 data path ("weak" scaling); timing barriers and the max-over-ranks reduction use NCCL.
 
---workload c4 prints the multi-session record alone as the line.
+--workload c4 prints the multi-session record alone as the line; --workload prefill the prompt passes and the
+long-context decode alone.
 --impl reference: the reference's own CPU kernels (kernels.c, compiled natively through oracle/shim into
 oracle/_ref, driven like cpu-worker.js) on this host's cores, same workload and config, rank 0 only (one CPU
 process whatever N is; the other ranks exit without work).
@@ -439,7 +440,7 @@ def main():
     ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="C1 only, without the nested records")
-    ap.add_argument("--workload", default="c1", choices=["c1", "c4"])
+    ap.add_argument("--workload", default="c1", choices=["c1", "c4", "prefill"])
     args = ap.parse_args()
     world, rank, local = dist_setup(args.gpus)
     if args.impl == "reference":
@@ -454,6 +455,14 @@ def main():
         sessions.init("nccl")
     cx = Ctx(world, rank, local)
     warm = max(3, args.warmup)
+    if args.workload == "prefill":  # the prompt passes and the long-context decode alone (one JSON object)
+        pre, lc = measure_prefill_and_c3(cx, C3_DECODE)
+        if rank == 0:
+            print(json.dumps({"prefill": pre, "long_context": lc}), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     if args.workload == "c4":
         rec = measure_c4(cx, args.steps if args.steps is not None else C4_DECODE, warm)
         if rank == 0:

@@ -19,8 +19,9 @@
 //
 // CTA = 4 warps + 4 warps per epilogue warpgroup, one token group of NT = EW x NW tokens, a list of 32-row tiles:
 //   warp 0 (lane 0)   producer: per chunk of 4 blocks, one TMA load of the token group's activation bytes (NT rows x
-//                     128 B, 128-byte swizzle), one TMA load of their transposed block scales (4 x NT floats) and one
-//                     bulk copy of the tile's 4 x 512 raw weight bytes, all completing on the chunk's mbarrier;
+//                     128 B, 128-byte swizzle), one TMA load of their transposed block scales (4 x NT floats) and two
+//                     bulk copies of the tile's 4 x 512 raw weight bytes and 4 x 32 fp16 scales, all completing on the
+//                     chunk's mbarrier;
 //   warp 1 (lane 0)   MMA issuer: one tcgen05.mma per block into a rotating TMEM slot, tcgen05.commit to release the
 //                     A tile, signal the epilogue and (per chunk) release the stage; warp 1 also owns the TMEM
 //                     allocation;
@@ -43,24 +44,29 @@ namespace h2 {
 namespace {
 
 constexpr int CB = 4;         // Q4_0 blocks per chunk (128 activation bytes per token: one 128-byte swizzle row)
-constexpr int NS = 4;         // chunk stages
-constexpr int NA = 8;         // A-tile slots
+constexpr int NA = 16;        // A-tile slots (4 chunks)
 constexpr int ATILE = 4096;   // one A tile: 128 rows x 32 bytes, no swizzle (core matrices 8 rows x 16 B)
 constexpr uint32_t FMAGIC = 0x4B400000u;
 constexpr unsigned long long TIMEOUT_NS = 1000000000ull;
 
+// Every hand-off between the roles is per chunk of 4 blocks (one mbarrier wait per role per chunk: a wait costs
+// about 0.1 us even when the phase has completed, which per block was the pipeline's whole budget), and the rings are
+// deep enough to cover one chunk's trip through the pipe (HBM load, conversion, MMA, epilogue: 4-5 us).
 template <int NT>
 struct Cfg {
   static constexpr int B_BYTES = NT * 128;
-  static constexpr int RAW_BYTES = CB * 512;
+  static constexpr int RAW_BYTES = CB * 512 + CB * 64;  // values, then the fp16 scales of the 32 rows
   static constexpr int DX_BYTES = CB * NT * 4;
   static constexpr int STG = (B_BYTES + RAW_BYTES + DX_BYTES + 1023) / 1024 * 1024;
-  static constexpr int NTS = NT <= 32 ? 8 : 4;  // TMEM slots (one block each)
-  static constexpr int COLS = NT * NTS;         // 128, 256, 256, 512: powers of two >= 32
+  static constexpr int NS = 8;                   // chunk stages
+  static constexpr int NAC = NA / CB;            // A chunk slots
+  static constexpr int NTC = NT <= 32 ? 4 : 2;   // TMEM chunk slots (CB blocks x NT columns each)
+  static constexpr int COLS = NTC * CB * NT;     // 256, 512, 512: powers of two >= 32
   static constexpr int OFF_A = NS * STG;
   static constexpr int OFF_BAR = OFF_A + NA * ATILE;
-  static constexpr int NBAR = 2 * NS + 2 * NA + 2 * NTS + 1;
+  static constexpr int NBAR = 2 * NS + 2 * NAC + 2 * NTC + 1;
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;  // + alignment slack of the dynamic base
+  static_assert(COLS <= 512 && SMEM <= 227 * 1024, "TMEM or shared memory budget");
 };
 
 __device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -73,12 +79,14 @@ __device__ __forceinline__ void bar_expect(uint64_t* b, unsigned bytes) {
 __device__ __forceinline__ void bar_arrive(uint64_t* b) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
 }
+// (with a suspend-time hint: a waiting thread sleeps in hardware until the phase completes, or at most ~20 us,
+// instead of polling; polling warps crowd the shared-memory pipe that the working warps need)
 __device__ __forceinline__ bool bar_try(uint64_t* b, unsigned parity) {
   uint32_t ok;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(ok)
-      : "r"(su32(b)), "r"(parity)
+      : "r"(su32(b)), "r"(parity), "r"(20000u)
       : "memory");
   return ok != 0;
 }
@@ -105,7 +113,7 @@ __device__ __forceinline__ bool wait_phase(uint64_t* b, unsigned parity, const A
   const unsigned long long t0 = now_ns();
   for (unsigned it = 0;; it++) {
     if (bar_try(b, parity)) return true;
-    if ((it & 31) == 31) {
+    if ((it & 3) == 3) {
       if (*a.flag) return false;
       if (now_ns() - t0 > TIMEOUT_NS) {
         raise_abort(a, role);
@@ -113,6 +121,15 @@ __device__ __forceinline__ bool wait_phase(uint64_t* b, unsigned parity, const A
       }
     }
   }
+}
+// the same for a whole warp: lane 0 polls (32 lanes polling one mbarrier serialize on it) and the warp follows;
+// false on every lane if it failed
+__device__ __forceinline__ bool wait_phase_warp(uint64_t* b, unsigned parity, const Abort& a, int role) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = wait_phase(b, parity, a, role);
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();
+  return ok != 0;
 }
 // the same, ignoring the abort flag (teardown: copies or MMAs that were issued must complete)
 __device__ __forceinline__ void drain_phase(uint64_t* b, unsigned parity) {
@@ -158,27 +175,13 @@ __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence:
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// 32 lanes x NW columns of 32-bit words (lane = thread's TMEM lane)
-template <int NW>
-__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&v)[NW]);
-template <>
-__device__ __forceinline__ void tmem_ld<16>(uint32_t taddr, uint32_t (&v)[16]) {
+// 32 lanes x 16 columns of 32-bit words (lane = the thread's TMEM lane) into v[0..16)
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* v) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
       "[%16];"
       : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
         "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-      : "r"(taddr));
-}
-template <>
-__device__ __forceinline__ void tmem_ld<32>(uint32_t taddr, uint32_t (&v)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
-        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
-        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
-        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
       : "r"(taddr));
 }
 // every one of the NW columns of the warp's 32 lanes set to w
@@ -223,7 +226,7 @@ enum { OPS = 0, OPB = 1, OPA = 2 };
 enum { ROLE_PRODUCER = 1, ROLE_MMA = 2, ROLE_CONVERT = 3, ROLE_EPILOGUE = 4 };
 
 template <int EW, int NW, int OP>
-__global__ void __launch_bounds__(128 + 128 * EW, EW * NW <= 32 ? 2 : 1)
+__global__ void __launch_bounds__(128 + 128 * EW, EW * NW <= 16 ? 2 : 1)
     k_matmul_tc5(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmD,
                  const uint8_t* __restrict__ qs, const __half* __restrict__ dsc, int N, int nb, int M,
                  float* __restrict__ y, int ldy, const float* __restrict__ bias, int* __restrict__ err,
@@ -232,27 +235,27 @@ __global__ void __launch_bounds__(128 + 128 * EW, EW * NW <= 32 ? 2 : 1)
   using C = Cfg<NT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = smem_raw + ((1024u - (su32(smem_raw) & 1023u)) & 1023u);
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + C::OFF_BAR);
-  uint64_t* empty = full + NS;
-  uint64_t* afull = empty + NS;
-  uint64_t* aempty = afull + NA;
-  uint64_t* tfull = aempty + NA;
-  uint64_t* tempty = tfull + C::NTS;
-  uint64_t* done = tempty + C::NTS;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + C::OFF_BAR);  // stage loaded (TMA / bulk copies)
+  uint64_t* empty = full + C::NS;                                  // stage consumed by every role
+  uint64_t* afull = empty + C::NS;                                 // A chunk written (converters)
+  uint64_t* aempty = afull + C::NAC;                               // A chunk read (MMA commit)
+  uint64_t* tfull = aempty + C::NAC;                               // TMEM chunk computed (MMA commit)
+  uint64_t* tempty = tfull + C::NTC;                               // TMEM chunk read and re-armed (epilogue)
+  uint64_t* done = tempty + C::NTC;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   int* abort_s = reinterpret_cast<int*>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < NS; s++) {
+    for (int s = 0; s < C::NS; s++) {
       bar_init(full + s, 1);
       bar_init(empty + s, 2 + 1 + 4 * EW);
     }
-    for (int a = 0; a < NA; a++) {
+    for (int a = 0; a < C::NAC; a++) {
       bar_init(afull + a, 2);
       bar_init(aempty + a, 1);
     }
-    for (int t = 0; t < C::NTS; t++) {
+    for (int t = 0; t < C::NTC; t++) {
       bar_init(tfull + t, 1);
       bar_init(tempty + t, 4 * EW);
     }
@@ -288,39 +291,38 @@ __global__ void __launch_bounds__(128 + 128 * EW, EW * NW <= 32 ? 2 : 1)
       uint32_t ci = 0;
       for (int tile = first_tile; tile < ntiles; tile += ctas_per_tg) {
         for (int c = 0; c < nchunk; c++, ci++) {
-          const int s = ci % NS;
-          if (!wait_phase(empty + s, ((ci / NS) & 1) ^ 1, ab, ROLE_PRODUCER)) goto producer_done;
+          const int s = ci % C::NS;
+          if (!wait_phase(empty + s, ((ci / C::NS) & 1) ^ 1, ab, ROLE_PRODUCER)) goto producer_done;
           const int b0 = c * CB, nbk = min(CB, nb - b0);
           uint8_t* stg = sm + s * C::STG;
-          bar_expect(full + s, C::B_BYTES + nbk * 512 + C::DX_BYTES);
+          bar_expect(full + s, C::B_BYTES + nbk * (512 + 64) + C::DX_BYTES);
           tma2d(stg, &tmB, 32 * b0, m0, full + s);
           bulk1d(stg + C::B_BYTES, qs + ((size_t)tile * nb + b0) * 512, nbk * 512, full + s);
+          bulk1d(stg + C::B_BYTES + CB * 512, dsc + ((size_t)tile * nb + b0) * 32, nbk * 64, full + s);
           tma2d(stg + C::B_BYTES + C::RAW_BYTES, &tmD, m0, b0, full + s);
         }
       }
     producer_done:
-      for (uint32_t k = ci > NS ? ci - NS : 0; k < ci; k++) drain_phase(full + k % NS, (k / NS) & 1);
+      for (uint32_t k = ci > C::NS ? ci - C::NS : 0; k < ci; k++) drain_phase(full + k % C::NS, (k / C::NS) & 1);
     }
   } else if (warp == 1) {
     if (lane == 0) {  // ---------------- MMA issuer
       const uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(NT >> 3) << 17) | (8u << 24);
-      uint32_t ci = 0, bi = 0;
+      uint32_t ci = 0;
       for (int tile = first_tile; tile < ntiles; tile += ctas_per_tg) {
         for (int c = 0; c < nchunk; c++, ci++) {
-          const int s = ci % NS;
-          if (!wait_phase(full + s, (ci / NS) & 1, ab, ROLE_MMA)) goto mma_done;
+          const int s = ci % C::NS, ac = ci % C::NAC, tc = ci % C::NTC;
+          if (!wait_phase(full + s, (ci / C::NS) & 1, ab, ROLE_MMA)) goto mma_done;
+          if (!wait_phase(afull + ac, (ci / C::NAC) & 1, ab, ROLE_MMA)) goto mma_done;
+          if (!wait_phase(tempty + tc, (ci / C::NTC) & 1, ab, ROLE_MMA)) goto mma_done;
+          tc_fence_after();
           const int nbk = min(CB, nb - c * CB);
-          const uint32_t bbase = su32(sm + s * C::STG);
-          for (int j = 0; j < nbk; j++, bi++) {
-            const int a = bi % NA, ts = bi % C::NTS;
-            if (!wait_phase(afull + a, (bi / NA) & 1, ab, ROLE_MMA)) goto mma_done;
-            if (!wait_phase(tempty + ts, (bi / C::NTS) & 1, ab, ROLE_MMA)) goto mma_done;
-            tc_fence_after();
-            mma_i8(tmem + ts * NT, desc_plain(su32(sm + C::OFF_A + a * ATILE), 128, 256),
-                   desc_sw128(bbase + 32 * j, 1024), idesc, 1);
-            mma_commit(aempty + a);
-            mma_commit(tfull + ts);
-          }
+          const uint32_t bbase = su32(sm + s * C::STG), abase = su32(sm + C::OFF_A + ac * CB * ATILE);
+          for (int j = 0; j < nbk; j++)
+            mma_i8(tmem + (tc * CB + j) * NT, desc_plain(abase + j * ATILE, 128, 256), desc_sw128(bbase + 32 * j, 1024),
+                   idesc, 1);
+          mma_commit(aempty + ac);
+          mma_commit(tfull + tc);
           mma_commit(empty + s);
         }
       }
@@ -328,35 +330,42 @@ __global__ void __launch_bounds__(128 + 128 * EW, EW * NW <= 32 ? 2 : 1)
       mma_commit(done);
       drain_phase(done, 0);
     }
-  } else if (warp < 4) {  // ---------------- converters (warps 2, 3)
+  } else if (warp < 4) {  // ---------------- converters (warps 2, 3): 2 A rows of every block per thread
     const int t64 = threadIdx.x - 64;
-    uint32_t ci = 0, bi = 0;
+    uint32_t ci = 0;
     for (int tile = first_tile; tile < ntiles; tile += ctas_per_tg) {
       for (int c = 0; c < nchunk; c++, ci++) {
-        const int s = ci % NS;
-        if (__any_sync(0xffffffffu, !wait_phase(full + s, (ci / NS) & 1, ab, ROLE_CONVERT))) goto convert_done;
+        const int s = ci % C::NS, ac = ci % C::NAC;
+        if (!wait_phase_warp(full + s, (ci / C::NS) & 1, ab, ROLE_CONVERT)) goto convert_done;
+        if (!wait_phase_warp(aempty + ac, ((ci / C::NAC) & 1) ^ 1, ab, ROLE_CONVERT)) goto convert_done;
         const int nbk = min(CB, nb - c * CB);
-        const uint8_t* raw = sm + s * C::STG + C::B_BYTES;
-        for (int j = 0; j < nbk; j++, bi++) {
-          const int a = bi % NA;
-          if (__any_sync(0xffffffffu, !wait_phase(aempty + a, ((bi / NA) & 1) ^ 1, ab, ROLE_CONVERT))) goto convert_done;
-          uint8_t* A = sm + C::OFF_A + a * ATILE;
+        const uint32_t* raw = reinterpret_cast<const uint32_t*>(sm + s * C::STG + C::B_BYTES);
+        uint32_t w[CB][2];
 #pragma unroll
-          for (int h = 0; h < 2; h++) {
-            const int i = t64 + 64 * h, r = i >> 2, l = i & 3;
-            const uint32_t w = *reinterpret_cast<const uint32_t*>(raw + j * 512 + r * 16 + 4 * l);
-            const uint32_t lo = ((w & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;         // q - 8 as signed bytes
-            const uint32_t hi = (((w >> 4) & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
-            const int o = (i >> 3) * 256 + (i & 7) * 16 + 4 * l;
-            *reinterpret_cast<uint32_t*>(A + o) = lo;
-            *reinterpret_cast<uint32_t*>(A + o + 128) = hi;
+        for (int j = 0; j < CB; j++)  // every load of the chunk first
+#pragma unroll
+          for (int h = 0; h < 2; h++) w[j][h] = j < nbk ? raw[j * 128 + t64 + 64 * h] : 0u;  // row r word l = 4r + l
+        uint8_t* A = sm + C::OFF_A + ac * CB * ATILE;
+#pragma unroll
+        for (int j = 0; j < CB; j++) {
+          if (j < nbk) {
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+              const int i = t64 + 64 * h, l = i & 3;
+              const uint32_t lo = ((w[j][h] & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;  // q - 8 as signed bytes
+              const uint32_t hi = (((w[j][h] >> 4) & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
+              const int o = j * ATILE + (i >> 3) * 256 + (i & 7) * 16 + 4 * l;
+              *reinterpret_cast<uint32_t*>(A + o) = lo;
+              *reinterpret_cast<uint32_t*>(A + o + 128) = hi;
+            }
           }
-          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          __syncwarp();
-          if (lane == 0) bar_arrive(afull + a);
         }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
-        if (lane == 0) bar_arrive(empty + s);
+        if (lane == 0) {
+          bar_arrive(afull + ac);
+          bar_arrive(empty + s);
+        }
       }
     }
   convert_done:;
@@ -364,62 +373,71 @@ __global__ void __launch_bounds__(128 + 128 * EW, EW * NW <= 32 ? 2 : 1)
     const int ew = (warp - 4) >> 2, q = warp & 3;
     const int i = 32 * q + lane, r = i >> 2, l = i & 3;
     const uint32_t tl = tmem + ((uint32_t)(32 * q) << 16) + ew * NW;
-    for (int ts = 0; ts < C::NTS; ts++) tmem_fill<NW>(tl + ts * NT, FMAGIC);
+    for (int k = 0; k < C::NTC * CB; k++) tmem_fill<NW>(tl + k * NT, FMAGIC);
     tc_wait_st();
     tc_fence_before();
     __syncwarp();
     if (lane == 0)
-      for (int ts = 0; ts < C::NTS; ts++) bar_arrive(tempty + ts);
+      for (int t = 0; t < C::NTC; t++) bar_arrive(tempty + t);
     const unsigned long long magic2 = pk(-12582912.0f, -12582912.0f);
-    uint32_t ci = 0, bi = 0;
+    uint32_t ci = 0;
     for (int tile = first_tile; tile < ntiles; tile += ctas_per_tg) {
       float acc[NW];
 #pragma unroll
       for (int t = 0; t < NW; t++) acc[t] = 0.f;
-      const __half* dg = dsc + (size_t)tile * nb * 32 + r;
-      float dw_next = __half2float(dg[0]);
       for (int c = 0; c < nchunk; c++, ci++) {
-        const int s = ci % NS;
-        if (__any_sync(0xffffffffu, !wait_phase(full + s, (ci / NS) & 1, ab, ROLE_EPILOGUE))) goto epi_done;
+        const int s = ci % C::NS, tc = ci % C::NTC;
+        if (!wait_phase_warp(full + s, (ci / C::NS) & 1, ab, ROLE_EPILOGUE)) goto epi_done;
+        if (!wait_phase_warp(tfull + tc, (ci / C::NTC) & 1, ab, ROLE_EPILOGUE)) goto epi_done;
+        tc_fence_after();
         const int nbk = min(CB, nb - c * CB);
         const float* dxs = reinterpret_cast<const float*>(sm + s * C::STG + C::B_BYTES + C::RAW_BYTES);
-        for (int j = 0; j < nbk; j++, bi++) {
-          const int ts = bi % C::NTS;
-          if (__any_sync(0xffffffffu, !wait_phase(tfull + ts, (bi / C::NTS) & 1, ab, ROLE_EPILOGUE))) goto epi_done;
-          tc_fence_after();
-          const int b = c * CB + j;
-          const float dw = dw_next;
-          if (b + 1 < nb) dw_next = __half2float(dg[(size_t)(b + 1) * 32]);
-          const unsigned long long dw2 = pk(dw, dw);
-          const float* dxr = dxs + j * NT + ew * NW;
+        const __half* dws = reinterpret_cast<const __half*>(sm + s * C::STG + C::B_BYTES + CB * 512) + r;
 #pragma unroll
-          for (int hh = 0; hh < NW / 16; hh++) {  // 16 columns at a time (fewer live registers)
-            uint32_t u[16];
-            tmem_ld<16>(tl + ts * NT + 16 * hh, u);
+        for (int jj = 0; jj < CB; jj += 2) {  // two blocks' columns in flight
+          if (jj < nbk) {
+            uint32_t u[2][NW];
+#pragma unroll
+            for (int e = 0; e < 2; e++)
+              if (jj + e < nbk)
+#pragma unroll
+                for (int hh = 0; hh < NW / 16; hh++)
+                  tmem_ld16(tl + (tc * CB + jj + e) * NT + 16 * hh, &u[e][16 * hh]);
             tc_wait_ld();
 #pragma unroll
-            for (int k = 0; k < 4; k++) {
-              const int t = 16 * hh + 4 * k;
-              const float4 d4 = *reinterpret_cast<const float4*>(dxr + t);
-              const unsigned long long s01 = pk_mul(dw2, pk(d4.x, d4.y)), s23 = pk_mul(dw2, pk(d4.z, d4.w));
-              const unsigned long long p01 = pk_add(pk(__uint_as_float(u[4 * k]), __uint_as_float(u[4 * k + 1])), magic2);
-              const unsigned long long p23 =
-                  pk_add(pk(__uint_as_float(u[4 * k + 2]), __uint_as_float(u[4 * k + 3])), magic2);
-              const unsigned long long q01 = pk_mul(p01, s01), q23 = pk_mul(p23, s23);
-              acc[t] = __fadd_rn(acc[t], lo_f(q01));
-              acc[t + 1] = __fadd_rn(acc[t + 1], hi_f(q01));
-              acc[t + 2] = __fadd_rn(acc[t + 2], lo_f(q23));
-              acc[t + 3] = __fadd_rn(acc[t + 3], hi_f(q23));
+            for (int e = 0; e < 2; e++) {
+              if (jj + e < nbk) {
+                const int j = jj + e;
+                const float dw = __half2float(dws[j * 32]);
+                const unsigned long long dw2 = pk(dw, dw);
+                const float* dxr = dxs + j * NT + ew * NW;
+#pragma unroll
+                for (int k = 0; k < NW / 4; k++) {
+                  const float4 d4 = *reinterpret_cast<const float4*>(dxr + 4 * k);
+                  const unsigned long long s01 = pk_mul(dw2, pk(d4.x, d4.y)), s23 = pk_mul(dw2, pk(d4.z, d4.w));
+                  const unsigned long long p01 =
+                      pk_add(pk(__uint_as_float(u[e][4 * k]), __uint_as_float(u[e][4 * k + 1])), magic2);
+                  const unsigned long long p23 =
+                      pk_add(pk(__uint_as_float(u[e][4 * k + 2]), __uint_as_float(u[e][4 * k + 3])), magic2);
+                  const unsigned long long q01 = pk_mul(p01, s01), q23 = pk_mul(p23, s23);
+                  acc[4 * k] = __fadd_rn(acc[4 * k], lo_f(q01));
+                  acc[4 * k + 1] = __fadd_rn(acc[4 * k + 1], hi_f(q01));
+                  acc[4 * k + 2] = __fadd_rn(acc[4 * k + 2], lo_f(q23));
+                  acc[4 * k + 3] = __fadd_rn(acc[4 * k + 3], hi_f(q23));
+                }
+              }
             }
           }
-          tmem_fill<NW>(tl + ts * NT, FMAGIC);  // re-arm the slot for its next block
-          tc_wait_st();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) bar_arrive(tempty + ts);
         }
+#pragma unroll
+        for (int j = 0; j < CB; j++) tmem_fill<NW>(tl + (tc * CB + j) * NT, FMAGIC);  // re-arm the chunk's columns
+        tc_wait_st();
+        tc_fence_before();
         __syncwarp();
-        if (lane == 0) bar_arrive(empty + s);
+        if (lane == 0) {
+          bar_arrive(tempty + tc);
+          bar_arrive(empty + s);
+        }
       }
       {  // the tile is complete: ((l0 + l1) + l2) + l3 across the row's four lane threads, then put()
         const int n = tile * 32 + r;
@@ -511,7 +529,7 @@ cudaError_t launch_inst(int op, const CUtensorMap& mb, const CUtensorMap& md, co
                         int N, int nb, int M, float* y, int ldy, const float* bias, int* err, cudaStream_t st) {
   constexpr int NT = EW * NW;
   const int ntg = (M + NT - 1) / NT, ntiles = (N + 31) / 32;
-  const int per_sm = NT <= 64 ? 2 : 1;
+  const int per_sm = NT <= 16 ? 2 : 1;
   const int ctas = std::max(1, std::min(ntiles, 148 * per_sm / ntg));
   const dim3 grid(ntg * ctas), block(128 + 128 * EW);
   const size_t smem = Cfg<NT>::SMEM;
@@ -532,13 +550,20 @@ cudaError_t attrs_inst() {
 
 }  // namespace
 
-int tc5_tokens_per_cta(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128; }
+int tc5_tokens_per_cta(int M, int N) {  // (16, 32 or 64)
+  // the widest token group (fewest passes over the weights) that still gives every SM a CTA; the narrowest otherwise
+  const int ntiles = (N + 31) / 32;
+  for (int nt = 64; nt >= 16; nt /= 2) {
+    if (nt > 16 && (M + nt / 2 - 1) / (nt / 2) == 1) continue;  // a narrower group already holds every token
+    if ((long long)ntiles * ((M + nt - 1) / nt) >= 148) return nt;
+  }
+  return 16;
+}
 
 cudaError_t tc5_set_attrs() {
   cudaError_t c = attrs_inst<1, 16>();
   if (c == cudaSuccess) c = attrs_inst<1, 32>();
   if (c == cudaSuccess) c = attrs_inst<2, 32>();
-  if (c == cudaSuccess) c = attrs_inst<4, 32>();
   return c;
 }
 
@@ -547,7 +572,7 @@ cudaError_t launch_tc5(int op, const uint8_t* qs, const __half* dsc, int N, int 
                        cudaStream_t st) {
   if (N < 1 || K < 32 || K % 32 || M < 1 || xq_rows < M || ldT < M || ldT % 4 || !err) return cudaErrorInvalidValue;
   if (((uintptr_t)xq | (uintptr_t)xdT | (uintptr_t)qs) & 15) return cudaErrorInvalidValue;
-  const int NT = tc5_tokens_per_cta(M), nb = K / 32;
+  const int NT = tc5_tokens_per_cta(M, N), nb = K / 32;
   CUtensorMap mb, md;
   if (!make_map(&mb, 0, xq, (uint64_t)K, (uint64_t)xq_rows, (uint64_t)K, 128, (uint32_t)NT) ||
       !make_map(&md, 1, xdT, (uint64_t)ldT, (uint64_t)nb, (uint64_t)ldT * 4, (uint32_t)NT, CB))
@@ -555,8 +580,7 @@ cudaError_t launch_tc5(int op, const uint8_t* qs, const __half* dsc, int N, int 
   switch (NT) {
     case 16: return launch_inst<1, 16>(op, mb, md, qs, dsc, N, nb, M, y, ldy, bias, err, st);
     case 32: return launch_inst<1, 32>(op, mb, md, qs, dsc, N, nb, M, y, ldy, bias, err, st);
-    case 64: return launch_inst<2, 32>(op, mb, md, qs, dsc, N, nb, M, y, ldy, bias, err, st);
-    default: return launch_inst<4, 32>(op, mb, md, qs, dsc, N, nb, M, y, ldy, bias, err, st);
+    default: return launch_inst<2, 32>(op, mb, md, qs, dsc, N, nb, M, y, ldy, bias, err, st);
   }
 }
 

@@ -8,8 +8,8 @@
 
 namespace h2 {
 
-// Tokens per CTA the kernel instance for M tokens takes (16, 32, 64 or 128).
-int tc5_tokens_per_cta(int M);
+// Tokens per CTA the kernel takes for M tokens and N weight rows (16, 32, 64 or 128).
+int tc5_tokens_per_cta(int M, int N);
 
 // y[m][n] (op)= W[n] . x[m] for m < M, n < N (op: 0 store, 1 add bias[n], 2 accumulate: put(), kernels.c:190-194).
 //   qs, dsc : the Q4_0 matrix in the grouped device layout (rows in groups of 32, [group][block][32 rows][16 B] with

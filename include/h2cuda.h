@@ -125,15 +125,16 @@ int h2c_set_decode_mode(h2c_engine* e, int mode);
 int h2c_decode_path(h2c_engine* e);
 
 /* The kernel of passes of several tokens (prompt chunks, batched decode steps), process-wide (no reference
- * counterpart: the reference has one CPU matmul). AUTO (default) and TCGEN05 take the Blackwell tensor-core form
- * (tcgen05.mma into TMEM) for Q4_0 matrices; MMA_SYNC the warp-level int8 mma.sync form. Both are bit-identical to
- * the reference. Takes effect for passes enqueued afterwards (a batch step's CUDA graph keeps the kernel it was
- * captured with). */
+ * counterpart: the reference has one CPU matmul). TCGEN05 takes the Blackwell tensor-core form (tcgen05.mma into
+ * TMEM) for Q4_0 matrices, MMA_SYNC the warp-level int8 mma.sync form; AUTO (default) the tcgen05 form for passes of
+ * 64 or more tokens and the mma.sync form for fewer (the faster of the two at each size on B200). All are
+ * bit-identical to the reference. Takes effect for passes enqueued afterwards (a batch step's CUDA graph keeps the
+ * kernel it was captured with). */
 #define H2C_MATMUL_AUTO 0
 #define H2C_MATMUL_MMA_SYNC 1
 #define H2C_MATMUL_TCGEN05 2
 int h2c_set_matmul_kernel(int kind);
-/* The form passes of several tokens take now: H2C_MATMUL_TCGEN05 or H2C_MATMUL_MMA_SYNC. */
+/* The current setting (H2C_MATMUL_AUTO, _MMA_SYNC or _TCGEN05). */
 int h2c_matmul_kernel(void);
 
 /* Profiling aid for the persistent decode kernel: runs h2c_generate's device-side greedy decode once with
