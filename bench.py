@@ -19,6 +19,7 @@ every rank (so a multi-GPU run records each at every N):
   microbench     the Q4_0 matvec shapes (one token), with weight copies rotated so that bytes come from HBM, and
                  the two small shapes also L2-resident;
   long_context   a 4096-token prompt, then device-chained greedy decode at positions 4096..
+  c5_7b          the 7B architecture on one GPU: 512-token prompt, then 256 device-chained greedy decode steps
 Multi-GPU (torchrun, one rank per GPU): independent sessions per rank, weights replicated, no collective on the
 data path ("weak" scaling); timing barriers and the max-over-ranks reduction use NCCL.
 
@@ -72,6 +73,13 @@ C4_METRIC = "decode tok/s multi-session (32 concurrent per GPU) Qwen2-0.5B Q4_0"
 C3_PROMPT = 4096
 C3_DECODE = 64
 C2_SHAPES = [(896, 896), (128, 896), (4864, 896), (896, 4864), (151936, 896)]
+# the 7B configuration: 512-token prompt, 256 greedy decode tokens; bytes per decode token (Q4_0 layers, norms and
+# biases, untied Q4_0 lm_head) and KV bytes per cached position (28 layers x 4 kv heads x 128 dims x f32 x K,V)
+C5_PROMPT = 512
+C5_DECODE = 256
+C5_WEIGHT_BYTES = 3_670_474_752 + 1_333_248 + 306_561_024
+C5_KV_BYTES_PER_POS = 28 * 4 * 128 * 4 * 2
+C5_LAYER_PARAMS = 6_525_288_448  # 28 layers x 233,046,016 weights
 
 
 def step_bytes(pos: int) -> int:
@@ -432,6 +440,59 @@ def measure_c2(cx: Ctx):
             "peak": hbm, "peak_source": src, "shapes": out}
 
 
+def measure_c5(cx: Ctx):
+    """The 7B configuration on one GPU: seeded weights generated on the device (synth.device_tensors), a 512-token
+    prompt (two 256-token passes on the tcgen05 matmul), then 256 device-chained greedy decode steps (per-op CUDA graph
+    path; the 7B rows are too long for the persistent kernel's tiles)."""
+    import torch
+    from e2e_browser_voice_agent_b200 import backend, synth
+    t0 = time.perf_counter()
+    cfg, src = synth.device_tensors("qwen2-7b", seed=0, device=cx.local)
+    be = backend.CudaBackend(src, None, cfg, ctx=C5_PROMPT + C5_DECODE + 2, prefill_chunk=256, device=cx.local)
+    load_s = time.perf_counter() - t0
+    prompt = synth.prompt_ids(cfg["vocab"], C5_PROMPT, seed=5)
+    be.forward(prompt[:64], 0)  # warm-up
+    ts = []
+    for _ in range(2):
+        cx.barrier()
+        t1 = time.perf_counter()
+        with nvtx_range("c5_prefill"):
+            first = be.forward(prompt, 0)
+        torch.cuda.synchronize()
+        ts.append(time.perf_counter() - t1)
+    pre = cx.max(min(ts))
+    be.generate(first, C5_PROMPT, 3)
+    clocks = Clocks(cx.local)
+    cx.barrier()
+    clocks.start()
+    with nvtx_range("c5_timed"):
+        _, ms = be.generate(first, C5_PROMPT, C5_DECODE)
+    cx.barrier()
+    ck = clocks.stop()
+    ms = cx.max(ms)
+    hbm, bf16, src_kind = peaks()
+    tot = sum(C5_WEIGHT_BYTES + C5_KV_BYTES_PER_POS * (p + 2) for p in range(C5_PROMPT, C5_PROMPT + C5_DECODE))
+    achieved = tot / (ms / 1e3) / 1e9
+    ops = 2 * C5_LAYER_PARAMS * C5_PROMPT
+    path, mem = be.decode_path, be.memory_bytes
+    be.destroy()
+    return {"metric": "decode tok/s @bs1 Qwen2-7B-architecture Q4_0 (1 GPU)",
+            "value": round(cx.world * C5_DECODE / (ms / 1e3), 2), "unit": UNIT, "steps": C5_DECODE,
+            "ms_per_step": round(ms / C5_DECODE, 5), "positions": [C5_PROMPT, C5_PROMPT + C5_DECODE - 1],
+            "config": {"workload": "c5: 28 layers, hidden 3584, 28/4 heads of 128, FFN 18944, vocab 152064, untied "
+                                   "Q4_0 lm_head; 512-token prompt then 256 greedy steps", "parallelism": "none (TP 1)",
+                       "weights": "seeded N(0,0.02) generated on the device, Q4_0", "device_bytes": mem,
+                       "load_s": round(load_s, 1)},
+            "roofline": {"bound": "hbm", "kernel": f"decode step ({path})", "achieved": round(achieved, 1),
+                         "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4), "peak_source": src_kind,
+                         "bytes_per_step": round(tot / C5_DECODE)},
+            "prefill": {"tokens": C5_PROMPT, "ms": round(pre * 1e3, 2), "tok_per_s": round(C5_PROMPT / pre, 1),
+                        "roofline": {"bound": "tensor", "achieved": round(ops / pre / 1e12, 2), "peak": 2 * bf16,
+                                     "unit": "int8 TOP/s", "frac": round(ops / pre / 1e12 / (2 * bf16), 5),
+                                     "peak_source": f"2 x {src_kind} bf16 (dense int8 rate)", "ops": ops}},
+            "clocks": ck}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -440,7 +501,7 @@ def main():
     ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="C1 only, without the nested records")
-    ap.add_argument("--workload", default="c1", choices=["c1", "c4", "prefill"])
+    ap.add_argument("--workload", default="c1", choices=["c1", "c4", "prefill", "c5"])
     args = ap.parse_args()
     world, rank, local = dist_setup(args.gpus)
     if args.impl == "reference":
@@ -455,6 +516,14 @@ def main():
         sessions.init("nccl")
     cx = Ctx(world, rank, local)
     warm = max(3, args.warmup)
+    if args.workload == "c5":  # the 7B record alone
+        rec = measure_c5(cx)
+        if rank == 0:
+            print(json.dumps(rec), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     if args.workload == "prefill":  # the prompt passes and the long-context decode alone (one JSON object)
         pre, lc = measure_prefill_and_c3(cx, C3_DECODE)
         if rank == 0:
@@ -548,6 +617,7 @@ def main():
         extra["multi_session"] = measure_c4(cx, steps, warm)
         extra["prefill"], extra["long_context"] = measure_prefill_and_c3(cx, C3_DECODE)
         extra["microbench"] = measure_c2(cx)
+        extra["c5_7b"] = measure_c5(cx)
         extra["extra_wall_s"] = round(time.perf_counter() - t_extra, 1)
 
     cpu = None

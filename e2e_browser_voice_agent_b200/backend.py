@@ -31,6 +31,9 @@ from . import gguf as G
 
 
 class CudaBackend:
+    """parsed, data: the GGUF file (parse_gguf result and its bytes), or parsed = a callable name -> (ggml type, raw
+    tensor bytes) or None, with data unused (models generated without a file, e.g. synth.device_tensors)."""
+
     name = "cuda"
 
     def __init__(self, parsed, data, cfg: Dict, ctx: int = 2048, prefill_chunk: int = 16, max_seqs: int = 1,
@@ -51,16 +54,24 @@ class CudaBackend:
         self._h = h
         self._next = C.c_int32()
         self._last_logits: Dict[int, Optional[np.ndarray]] = {}
-        T = parsed["tensors"]
+        # tensor source: name -> (ggml type, raw bytes), from the GGUF file (parsed, data) or a callable
+        if callable(parsed):
+            source = parsed
+        else:
+            T = parsed["tensors"]
+
+            def source(name: str):
+                t = T.get(name)
+                return None if t is None else (t["type"], G.tensor_view(data, t))
 
         def raw(name: str, want: int) -> np.ndarray:
-            t = T.get(name)
+            t = source(name)
             if t is None:
                 raise ValueError(f"{name}: missing")
-            if t["type"] != want:
+            if t[0] != want:
                 kind = {G.TYPE["Q4_0"]: "Q4_0", G.TYPE["F32"]: "F32"}.get(want, str(want))
                 raise ValueError(f"{name}: expected {kind}")  # cpu-worker.js:105, 112
-            return G.tensor_view(data, t)
+            return t[1]
 
         def put(kind: int, layer: int, ggml_type: int, blob: np.ndarray) -> None:
             blob = np.ascontiguousarray(blob)
@@ -79,11 +90,11 @@ class CudaBackend:
             if on_progress:
                 on_progress(l + 1, NL)
         put(_lib.KIND_EMBED, 0, q4, raw("token_embd.weight", q4))
-        out = T.get("output.weight")
+        out = source("output.weight")
         if out is not None:
-            if out["type"] not in (G.TYPE["Q8_0"], G.TYPE["Q4_0"]):
+            if out[0] not in (G.TYPE["Q8_0"], G.TYPE["Q4_0"]):
                 raise ValueError("output.weight: expected Q8_0")  # cpu-worker.js:126
-            put(_lib.KIND_OUTPUT, 0, out["type"], G.tensor_view(data, out))
+            put(_lib.KIND_OUTPUT, 0, out[0], out[1])
         put(_lib.KIND_OUTPUT_NORM, 0, f32, raw("output_norm.weight", f32))
         if decode_mode != "auto":
             self.set_decode_mode(decode_mode)

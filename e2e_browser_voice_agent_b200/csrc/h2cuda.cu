@@ -328,19 +328,21 @@ void launch_mmtc(int op, const uint8_t* qs, const __half* d, int N, int K, const
   else k_matmul_tc<WT, TG, OP_ADD><<<grid, 256, smem, st>>>(qs, d, N, K, xq, xd, xs, M, rows, y, ldy, bias);
 }
 
+// (st null: only report whether a token group of the mma.sync form fits the row length)
 template <int WT>
 bool matmul_tc(int op, const uint8_t* qs, const __half* d, int N, int K, const int8_t* xq, const float* xd,
-               const int4* xs, int M, float* y, int ldy, const float* bias, cudaStream_t st) {
+               const int4* xs, int M, float* y, int ldy, const float* bias, cudaStream_t st, bool dry = false) {
   const int nb = K / 32, groups = (N + 31) / 32;
   auto enough = [&](int tg) { return (size_t)((M + tg - 1) / tg) * groups >= 148; };
-  if (M > 16 && enough(32) && mmtc_smem<WT, 32>(nb) <= MMTC_SMEM_FAST)
-    launch_mmtc<WT, 32>(op, qs, d, N, K, xq, xd, xs, M, y, ldy, bias, st);
-  else if (M > 8 && enough(16) && mmtc_smem<WT, 16>(nb) <= MMTC_SMEM_FAST)
-    launch_mmtc<WT, 16>(op, qs, d, N, K, xq, xd, xs, M, y, ldy, bias, st);
-  else if (mmtc_smem<WT, 8>(nb) <= MM_SMEM)
-    launch_mmtc<WT, 8>(op, qs, d, N, K, xq, xd, xs, M, y, ldy, bias, st);
-  else
+  if (M > 16 && enough(32) && mmtc_smem<WT, 32>(nb) <= MMTC_SMEM_FAST) {
+    if (!dry) launch_mmtc<WT, 32>(op, qs, d, N, K, xq, xd, xs, M, y, ldy, bias, st);
+  } else if (M > 8 && enough(16) && mmtc_smem<WT, 16>(nb) <= MMTC_SMEM_FAST) {
+    if (!dry) launch_mmtc<WT, 16>(op, qs, d, N, K, xq, xd, xs, M, y, ldy, bias, st);
+  } else if (mmtc_smem<WT, 8>(nb) <= MM_SMEM) {
+    if (!dry) launch_mmtc<WT, 8>(op, qs, d, N, K, xq, xd, xs, M, y, ldy, bias, st);
+  } else {
     return false;
+  }
   return true;
 }
 
@@ -348,7 +350,11 @@ template <int WT>
 void matvec_w(int op, const uint8_t* qs, const __half* d, int N, int K, const int8_t* xq, const float* xd,
               const int4* xs, int M, float* y, int ldy, const float* bias, cudaStream_t st, const MmCtx* mc = nullptr) {
   const int nb = K / 32;
-  if (WT == WQ4 && M > 1 && mc && use_tc5(M)) {  // several tokens on the tcgen05 tensor cores (tc5.cu)
+  // several tokens on the tcgen05 tensor cores (tc5.cu): from TC5_MIN_TOKENS, or whenever the mma.sync form's resident
+  // activations do not fit (long rows, e.g. the 7B down projection: it streams them)
+  if (WT == WQ4 && M > 1 && mc &&
+      (use_tc5(M) || (g_mm_kind.load(std::memory_order_relaxed) == H2C_MATMUL_AUTO &&
+                      !matmul_tc<WT>(op, qs, d, N, K, xq, xd, xs, M, y, ldy, bias, st, true)))) {
     launch_tc5(op, qs, d, N, K, xq, mc->xq_rows, mc->xdT, mc->ldT, M, y, ldy, bias, mc->err, st);
     if (mc->used) *mc->used = true;
     return;

@@ -40,6 +40,10 @@ CONFIGS: Dict[str, Dict] = {
                  lm_head="tied"),
     "hd128": dict(layers=2, dim=512, heads=4, kv_heads=2, ffn=1024, vocab=2048, rope_theta=1e6, eps=1e-6,
                   lm_head="q4"),
+    # the 7B layer shapes (hidden 3584, 28 / 4 heads of 128, FFN 18944, untied lm_head) with 2 layers and a smaller
+    # vocabulary, for parity tests against the oracle at the 7B matrix sizes
+    "qwen2-7b-2l": dict(layers=2, dim=3584, heads=28, kv_heads=4, ffn=18944, vocab=8192, rope_theta=1e6, eps=1e-6,
+                        lm_head="q4"),
 }
 
 
@@ -134,3 +138,59 @@ def file_sha256(path: str) -> str:
         for chunk in iter(lambda: f.read(1 << 22), b""):
             h.update(chunk)
     return h.hexdigest()
+
+
+def device_tensors(name: str, seed: int = 0, device: int = 0):
+    """A seeded synthetic model of CONFIGS[name] generated on the GPU without a file (the full 7B configuration's
+    3.98 GB of Q4_0 would take minutes to write with numpy): returns (cfg, source) with source(tensor name) ->
+    (ggml type, raw GGUF bytes as a host array) or None, for backend.CudaBackend(source, None, cfg). Linear and
+    embedding weights ~ N(0, 0.02) (torch's generator, seeded per tensor) quantized to Q4_0 with the ggml reference
+    algorithm (the one of gguf.q4_0_quantize, on the GPU); norm weights 1.0; q/k/v biases ~ N(0, 0.02)."""
+    import torch
+
+    c = CONFIGS[name]
+    D, F, H, KVH, L, V = c["dim"], c["ffn"], c["heads"], c["kv_heads"], c["layers"], c["vocab"]
+    HD = D // H
+    dev = torch.device("cuda", device)
+    shapes = {"token_embd.weight": (V, D), "output.weight": (V, D)}
+    for l in range(L):
+        p = f"blk.{l}."
+        shapes.update({p + "attn_q.weight": (D, D), p + "attn_k.weight": (KVH * HD, D),
+                       p + "attn_v.weight": (KVH * HD, D), p + "attn_output.weight": (D, D),
+                       p + "ffn_gate.weight": (F, D), p + "ffn_up.weight": (F, D), p + "ffn_down.weight": (D, F),
+                       p + "attn_q.bias": (D,), p + "attn_k.bias": (KVH * HD,), p + "attn_v.bias": (KVH * HD,)})
+    names = sorted(shapes)
+
+    def normal(n, key):
+        g = torch.Generator(device=dev)
+        g.manual_seed((seed * 1000003 + names.index(key) * 7919 + 17) & 0x7FFFFFFFFFFFFFFF)
+        return torch.randn(n, generator=g, device=dev, dtype=torch.float32) * 0.02
+
+    def q4_0(x):
+        x = x.reshape(-1, 32)
+        idx = torch.argmax(x.abs(), dim=1)                  # first of equal magnitudes
+        m = x.gather(1, idx[:, None])[:, 0]
+        d = m / -8.0
+        inv = torch.where(d != 0, 1.0 / d, torch.zeros_like(d))
+        q = torch.clamp((x * inv[:, None] + 8.5).to(torch.int32), max=15).to(torch.uint8)  # trunc toward zero
+        out = torch.empty(x.shape[0], 18, dtype=torch.uint8, device=dev)
+        out[:, 0:2] = d.to(torch.float16).view(torch.uint8).reshape(-1, 2)
+        out[:, 2:] = q[:, :16] | (q[:, 16:] << 4)
+        return out.reshape(-1).cpu().numpy()
+
+    def source(tname: str):
+        if tname.endswith("norm.weight"):
+            return G.TYPE["F32"], np.ones(D, dtype=np.float32).view(np.uint8)
+        if tname == "output.weight" and c.get("lm_head", "tied") == "tied":
+            return None
+        if tname not in shapes:
+            return None
+        sh = shapes[tname]
+        n = int(np.prod(sh))
+        if len(sh) == 1:
+            return G.TYPE["F32"], normal(n, tname).cpu().numpy().view(np.uint8)
+        return G.TYPE["Q4_0"], q4_0(normal(n, tname))
+
+    cfg = {"arch": "qwen2", "dim": D, "layers": L, "ffn": F, "heads": H, "kv_heads": KVH, "vocab": V,
+           "eps": c["eps"], "rope_theta": c["rope_theta"]}
+    return cfg, source

@@ -340,6 +340,14 @@ def test_prompt_chunks_tcgen05_equal_mma_sync_and_oracle(model, chunk):
     assert n_a == r["next"] and np.array_equal(bits(l_a), bits(r["logits"]))
 
 
+@pytest.mark.parametrize("chunk,n_prompt", [(16, 21), (128, 70)])
+def test_qwen2_7b_layer_shapes_bit_exact(chunk, n_prompt):
+    """The 7B configuration's matrices (hidden 3584, 28 query / 4 kv heads of 128, FFN 18944, untied Q4_0 lm_head) in
+    a 2-layer model: prompt chunks of 16 (mma.sync; the 18944-long down rows on tcgen05) and 128 tokens (tcgen05),
+    then teacher-forced decode steps (per-op graph path), bit-identical to the oracle."""
+    teacher_forced("qwen2-7b-2l", n_prompt=n_prompt, steps=3, chunk=chunk, ctx=96)
+
+
 @pytest.mark.parametrize("model,n_prompt", [("small", 37), ("gqa7", 29), ("qwen2-0.5b", 40)])
 def test_teacher_forced_chunks_of_32(model, n_prompt):
     """Prompt passes of 17..32 tokens: the largest token groups of the multi-token matmul (and, on the 0.5B
