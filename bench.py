@@ -61,6 +61,9 @@ LAYER_MACS = LAYER_WEIGHT_BYTES // 18 * 32
 # DRAM bytes (read + write) of one decode step of k_decode_persistent, from the ncu capture of a 4-step launch at
 # positions 32..35: 1,123,380,992 B / 4
 NCU_TRAFFIC_PER_STEP = 280_845_248
+# DRAM bytes (read + write) of one batched 32-session step, ncu launch list of two steps of the timed region
+# (bench.py --workload c4 --steps 2): 933,209,344 B / 2
+NCU_TRAFFIC_C4_STEP = 466604672
 
 C1_CONFIG = {"workload": "qwen2-0.5b Q4_0 tied lm_head, batch 1, 32-token prompt then greedy decode rounds of 64 "
                          "(positions 32..95)",
@@ -325,7 +328,8 @@ def measure_c4(cx: Ctx, steps: int, warm: int):
                    "l2": "no flush: 278 MB of weights per step > 126 MB L2"},
         "roofline": {"bound": "hbm", "kernel": f"batched decode step ({kernels} kernels in one CUDA graph)",
                      "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
-                     "peak_source": src, "bytes_per_step": round(bytes_step), "traffic": None},
+                     "peak_source": src, "bytes_per_step": round(bytes_step), "traffic": NCU_TRAFFIC_C4_STEP,
+                     "traffic_note": "DRAM read+write bytes per batched step, ncu launch list of the step's kernels"},
         "e2e": {"value": round(e2e, 2), "unit": UNIT, "h2d_bytes_per_step": 4 * 4 + 3 * 4 * 256,
                 "d2h_bytes_per_step": 4 * S},
         "prompt_prefill_ms": round(prefill_s * 1e3, 2),

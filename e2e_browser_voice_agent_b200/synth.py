@@ -51,8 +51,9 @@ def _normal(rng: np.random.Generator, n: int, std: float = 0.02) -> np.ndarray:
     return (rng.standard_normal(n, dtype=np.float32) * np.float32(std)).astype(np.float32)
 
 
-def build(path: str, cfg: Dict, seed: int = 0) -> None:
-    """Write the seeded model described by cfg to path (GGUF v3)."""
+def build(path: str, cfg: Dict, seed: int = 0, tokenizer=None) -> None:
+    """Write the seeded model described by cfg to path (GGUF v3). tokenizer (optional): (tokens, merges, token
+    types) written as the GGUF tokenizer arrays (len(tokens) must be cfg["vocab"]); else synthetic token strings."""
     D, F, H, KVH, L, V = cfg["dim"], cfg["ffn"], cfg["heads"], cfg["kv_heads"], cfg["layers"], cfg["vocab"]
     HD = D // H
     rng = np.random.default_rng(seed)
@@ -105,9 +106,16 @@ def build(path: str, cfg: Dict, seed: int = 0) -> None:
         ("qwen2.rope.freq_base", 6, float(cfg["rope_theta"])),
         ("qwen2.attention.layer_norm_rms_epsilon", 6, float(cfg["eps"])),
         ("tokenizer.ggml.model", 8, "gpt2"),
-        ("tokenizer.ggml.tokens", 9, (8, [f"<t{i}>" for i in range(V)])),
-        ("tokenizer.ggml.eos_token_id", 4, V - 1),
     ]
+    if tokenizer is None:
+        kv += [("tokenizer.ggml.tokens", 9, (8, [f"<t{i}>" for i in range(V)])), ("tokenizer.ggml.eos_token_id", 4, V - 1)]
+    else:
+        toks, merges, types = tokenizer
+        if len(toks) != V:
+            raise ValueError(f"tokenizer has {len(toks)} tokens, the model's vocabulary {V}")
+        eos = toks.index("<|endoftext|>") if "<|endoftext|>" in toks else V - 1
+        kv += [("tokenizer.ggml.tokens", 9, (8, list(toks))), ("tokenizer.ggml.merges", 9, (8, list(merges))),
+               ("tokenizer.ggml.token_type", 9, (5, [int(t) for t in types])), ("tokenizer.ggml.eos_token_id", 4, eos)]
     G.write_gguf(path, kv, t)
 
 
