@@ -414,8 +414,9 @@ bool attg_ok(int G, int HD, int ctx) {
   return (HD == 64 ? attg_smem_bytes<64>(G, ctx) : attg_smem_bytes<128>(G, ctx)) <= ATTG_SMEM;
 }
 
-// The largest context h2c_create accepts: k_attention keeps one float score per position in shared memory.
-constexpr int MAX_CTX = 50000;
+// The largest context h2c_create accepts: k_attention keeps one float score per position in shared memory, next to
+// its V staging ring (16 KB at head_dim 64, 32 KB at 128), within the 227 KB a CTA can have.
+constexpr int MAX_CTX = 49152;
 
 // The attributes are per device and only ever raised to fixed maxima (a launch's own size decides its occupancy),
 // so engines with different contexts on one device never lower each other's limits.
@@ -431,13 +432,14 @@ cudaError_t set_kernel_attrs() {
   if (c == cudaSuccess) c = mm_attr_mt<WQ8, 8>();
   if (c == cudaSuccess) c = mm_attr_mt<WQ8, 16>();
   if (c == cudaSuccess) c = mm_attr_mt<WQ8, 32>();
-  const int att = MAX_CTX * 4;
-  if (c == cudaSuccess) c = cudaFuncSetAttribute(k_attention<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, att);
+  if (c == cudaSuccess)
+    c = cudaFuncSetAttribute(k_attention<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)at_smem_bytes<64>(MAX_CTX));
   if (c == cudaSuccess)
     c = cudaFuncSetAttribute(k_attention_gqa<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATTG_SMEM);
   if (c == cudaSuccess)
     c = cudaFuncSetAttribute(k_attention_gqa<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATTG_SMEM);
-  if (c == cudaSuccess) c = cudaFuncSetAttribute(k_attention<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, att);
+  if (c == cudaSuccess)
+    c = cudaFuncSetAttribute(k_attention<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)at_smem_bytes<128>(MAX_CTX));
   if (c == cudaSuccess) c = tc5_set_attrs();
   return c;
 }
@@ -507,9 +509,9 @@ void enqueue_pass(h2c_engine* e, int M, bool logits, Prof* pf, bool batch = fals
         k_attention_gqa<128><<<dim3(KVH, M), 256, attg_smem_bytes<128>(H / KVH, c.ctx), st>>>(
             e->prm, e->qkv, QKV, e->kc, e->vc, H, KVH, c.ctx, NL, l, e->att, D);
     } else if (HD == 64) {
-      k_attention<64><<<dim3(H, M), 128, (size_t)c.ctx * 4, st>>>(e->prm, e->qkv, QKV, e->kc, e->vc, H, KVH, c.ctx, NL, l, e->att, D);
+      k_attention<64><<<dim3(H, M), 128, at_smem_bytes<64>(c.ctx), st>>>(e->prm, e->qkv, QKV, e->kc, e->vc, H, KVH, c.ctx, NL, l, e->att, D);
     } else {
-      k_attention<128><<<dim3(H, M), 128, (size_t)c.ctx * 4, st>>>(e->prm, e->qkv, QKV, e->kc, e->vc, H, KVH, c.ctx, NL, l, e->att, D);
+      k_attention<128><<<dim3(H, M), 128, at_smem_bytes<128>(c.ctx), st>>>(e->prm, e->qkv, QKV, e->kc, e->vc, H, KVH, c.ctx, NL, l, e->att, D);
     }
     mark(pf, 4, st);
     {
@@ -1028,7 +1030,7 @@ int h2c_create(int device, const h2c_config* cfg, h2c_engine** out) {
   const size_t kv = (size_t)c.max_seqs * c.layers * c.kv_heads * c.ctx * HD;
   e->am_np = 296;
   if (c.ctx > MAX_CTX) {
-    e->err = "ctx above 50000 positions (attention keeps one score per position in shared memory)";
+    e->err = "ctx above 49152 positions (attention keeps one score per position in shared memory)";
     return bail(H2C_ERR_INVALID);
   }
   if (!kernel_attrs_on_current_device(&e->err)) return bail(H2C_ERR_CUDA);

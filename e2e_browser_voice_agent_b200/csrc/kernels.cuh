@@ -746,14 +746,24 @@ static __global__ void k_rope_kv(const int32_t* __restrict__ prm, float* __restr
 
 // Attention for one (head, token), kernels.c:355-377: scores q.k_t in four lanes of HD/4 products each,
 // * 1/sqrt(HD); max; e_t = fast_exp(s_t - max); sum in position order; p_t = e_t / sum; o = sum_t p_t v_t in
-// position order. Scores and exponentials run one position per thread; the two ordered sums run as chains.
-// grid (H, M), 128 threads, dynamic smem T_max floats.
+// position order. Scores and exponentials run one position per thread (16 of a K row's 16-byte loads in flight per
+// thread); the two ordered sums run as chains. The V rows of the p.v chains stream through shared memory in chunks of
+// AT_VC positions, AT_NST chunks in flight (cp.async; the first ones are requested before the scores), so a chain
+// step reads shared memory instead of waiting on a global load.
+// grid (H, M), 128 threads, dynamic smem at_smem_bytes<HD>(T_max).
+constexpr int AT_VC = 16;
+constexpr int AT_NST = 4;
+template <int HD>
+__host__ __device__ constexpr size_t at_smem_bytes(int ctx) {
+  return ((size_t)((ctx + 3) & ~3) + (size_t)AT_NST * AT_VC * HD) * 4;
+}
 template <int HD>
 __global__ void __launch_bounds__(128) k_attention(const int32_t* __restrict__ prm, const float* __restrict__ qkv, int QKV,
                                                    const float* __restrict__ kc, const float* __restrict__ vc, int H,
                                                    int KVH, int ctx, int layers, int layer, float* __restrict__ att,
                                                    int D) {
-  extern __shared__ float sc[];
+  extern __shared__ __align__(16) float sc[];
+  float* vst = sc + ((ctx + 3) & ~3);  // [AT_NST][AT_VC][HD]
   __shared__ float q_s[HD];
   __shared__ float red[4];
   __shared__ float sum_s;
@@ -762,15 +772,26 @@ __global__ void __launch_bounds__(128) k_attention(const int32_t* __restrict__ p
   const int kh = h / (H / KVH);
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
   for (int i = tid; i < HD; i += blockDim.x) q_s[i] = qkv[(size_t)m * QKV + (size_t)h * HD + i];
-  __syncthreads();
   const size_t cbase = (((size_t)seq * layers + layer) * KVH + kh) * (size_t)ctx * HD;
   const float* kb = kc + cbase;
   const float* vb = vc + cbase;
+  const int nvc = (T + AT_VC - 1) / AT_VC;
+  auto stage_v = [&](int c) {  // V rows of chunk c into buffer c % AT_NST (an empty group past the last chunk)
+    if (c < nvc) {
+      const int t0 = c * AT_VC, tc = min(AT_VC, T - t0);
+      float* dst = vst + (c % AT_NST) * AT_VC * HD;
+      for (int i = tid; i < tc * (HD / 4); i += blockDim.x) cp_async16(dst + 4 * i, vb + (size_t)t0 * HD + 4 * i);
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int c = 0; c < AT_NST - 1; c++) stage_v(c);
+  __syncthreads();
   float mx = -1e30f;
   for (int t = tid; t < T; t += blockDim.x) {
     const float4* kr = reinterpret_cast<const float4*>(kb + (size_t)t * HD);
     float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-#pragma unroll 8
+#pragma unroll 16
     for (int i = 0; i < HD / 4; i++) {
       const float4 k4 = __ldg(kr + i);
       s0 = __fadd_rn(s0, __fmul_rn(q_s[4 * i], k4.x));
@@ -797,13 +818,34 @@ __global__ void __launch_bounds__(128) k_attention(const int32_t* __restrict__ p
   __syncthreads();
   const float sum = sum_s;
   for (int t = tid; t < T; t += blockDim.x) sc[t] = __fdiv_rn(sc[t], sum);
-  __syncthreads();
-  for (int d = tid; d < HD; d += blockDim.x) {
-    float o = 0.f;
-    const float* vp = vb + d;
-#pragma unroll 8
-    for (int t = 0; t < T; t++) o = __fadd_rn(o, __fmul_rn(sc[t], __ldg(vp + (size_t)t * HD)));
-    att[(size_t)m * D + (size_t)h * HD + d] = o;
+  // o[d] = sum_t p_t v_t[d] in position order (kernels.c:372-375), chain d per thread, V from shared memory
+  constexpr int ND = (HD + 127) / 128;
+  float o[ND];
+#pragma unroll
+  for (int k = 0; k < ND; k++) o[k] = 0.f;
+  for (int cc = 0; cc < nvc; cc++) {
+    const int t0 = cc * AT_VC, tc = min(AT_VC, T - t0);
+    cp_async_wait_group<AT_NST - 2>();  // chunk cc has landed (the later ones may still be in flight)
+    __syncthreads();                    // (also orders the p writes above before their first use)
+    const float* vbuf = vst + (cc % AT_NST) * AT_VC * HD;
+#pragma unroll
+    for (int k = 0; k < ND; k++) {
+      const int d = tid + 128 * k;
+      if (d < HD) {
+        float acc = o[k];
+#pragma unroll 4
+        for (int t = 0; t < tc; t++) acc = __fadd_rn(acc, __fmul_rn(sc[t0 + t], vbuf[t * HD + d]));
+        o[k] = acc;
+      }
+    }
+    __syncthreads();  // buffer cc % AT_NST is free again
+    stage_v(cc + AT_NST - 1);
+  }
+  cp_async_wait_all();
+#pragma unroll
+  for (int k = 0; k < ND; k++) {
+    const int d = tid + 128 * k;
+    if (d < HD) att[(size_t)m * D + (size_t)h * HD + d] = o[k];
   }
 }
 
