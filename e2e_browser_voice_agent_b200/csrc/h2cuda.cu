@@ -360,8 +360,10 @@ void matvec_w(int op, const uint8_t* qs, const __half* d, int N, int K, const in
     return;
   }
   if (M == 1) {
+    // rows per CTA: the product buffer (rows x blocks x 16 B) small enough for several CTAs per SM
     if (nb <= 64) launch_mv_t<WT, 32, 1>(op, qs, d, N, K, xq, xd, xs, 1, y, ldy, bias, st);
-    else launch_mv_t<WT, 16, 1>(op, qs, d, N, K, xq, xd, xs, 1, y, ldy, bias, st);
+    else if (nb <= 256) launch_mv_t<WT, 16, 1>(op, qs, d, N, K, xq, xd, xs, 1, y, ldy, bias, st);
+    else launch_mv_t<WT, 8, 1>(op, qs, d, N, K, xq, xd, xs, 1, y, ldy, bias, st);
     return;
   }
   if (matmul_tc<WT>(op, qs, d, N, K, xq, xd, xs, M, y, ldy, bias, st)) return;
@@ -424,6 +426,8 @@ cudaError_t set_kernel_attrs() {
   const int big = 200 * 1024;
   cudaError_t c = mv_attr<WQ4, 32, 1>(big);
   if (c == cudaSuccess) c = mv_attr<WQ4, 16, 1>(big);
+  if (c == cudaSuccess) c = mv_attr<WQ4, 8, 1>(big);
+  if (c == cudaSuccess) c = mv_attr<WQ8, 8, 1>(big);
   if (c == cudaSuccess) c = mv_attr<WQ8, 32, 1>(big);
   if (c == cudaSuccess) c = mv_attr<WQ8, 16, 1>(big);
   if (c == cudaSuccess) c = mm_attr_mt<WQ4, 8>();

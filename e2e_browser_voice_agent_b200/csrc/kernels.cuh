@@ -335,6 +335,7 @@ __global__ void __launch_bounds__(256) k_matvec(const uint8_t* __restrict__ qs, 
   const int g = n0 >> 5, r0 = n0 & 31;
   const uint8_t* wg = qs + (size_t)g * nb * 32 * BB;
   const __half* dg = dsc + (size_t)g * nb * 32;
+#pragma unroll 8  // (8 items' weight loads in flight per thread: one token's matvec is bound by memory parallelism)
   for (int it = threadIdx.x; it < nb * ROWS; it += blockDim.x) {
     const int b = it / ROWS, r = it % ROWS;
     const size_t e = (size_t)b * 32 + r0 + r;
