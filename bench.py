@@ -19,7 +19,9 @@ every rank (so a multi-GPU run records each at every N):
   microbench     the Q4_0 matvec shapes (one token), with weight copies rotated so that bytes come from HBM, and
                  the two small shapes also L2-resident;
   long_context   a 4096-token prompt, then device-chained greedy decode at positions 4096..
-  c5_7b          the 7B architecture on one GPU: 512-token prompt, then 256 device-chained greedy decode steps
+  c5_7b          the 7B architecture: 512-token prompt, then 256 device-chained greedy decode steps; on N GPUs
+                 tensor-parallel groups (tp.plan: TP 2 on 2 GPUs, TP 4 on 4, two TP-4 groups on 8) with NCCL
+                 all-gathers inside the decode step's CUDA graph
 Multi-GPU (torchrun, one rank per GPU): independent sessions per rank, weights replicated, no collective on the
 data path ("weak" scaling); timing barriers and the max-over-ranks reduction use NCCL.
 
@@ -445,16 +447,22 @@ def measure_c2(cx: Ctx):
 
 
 def measure_c5(cx: Ctx):
-    """The 7B configuration on one GPU: seeded weights generated on the device (synth.device_tensors), a 512-token
-    prompt (two 256-token passes on the tcgen05 matmul), then 256 device-chained greedy decode steps (per-op CUDA graph
-    path; the 7B rows are too long for the persistent kernel's tiles)."""
+    """The 7B configuration: seeded weights generated on the device (synth.device_tensors), a 512-token prompt (two
+    256-token passes on the tcgen05 matmul), then 256 device-chained greedy decode steps (per-op CUDA graph path; the
+    7B rows are too long for the persistent kernel's tiles). On N GPUs: tensor-parallel groups of G = tp.plan(N)
+    ranks (NCCL all-gathers inside the step's CUDA graph), N / G groups decoding independent sequences."""
     import torch
-    from e2e_browser_voice_agent_b200 import backend, synth
+    from e2e_browser_voice_agent_b200 import _lib, backend, synth, tp
     t0 = time.perf_counter()
     cfg, src = synth.device_tensors("qwen2-7b", seed=0, device=cx.local)
-    be = backend.CudaBackend(src, None, cfg, ctx=C5_PROMPT + C5_DECODE + 2, prefill_chunk=256, device=cx.local)
+    G, reps = tp.plan(cfg, cx.world)
+    tpa = None
+    if G > 1:
+        tpa = (G, cx.rank % G, tp.exchange_ids(cx.world, cx.rank, G, _lib.tp_unique_id))
+    be = backend.CudaBackend(src, None, cfg, ctx=C5_PROMPT + C5_DECODE + 2, prefill_chunk=256, device=cx.local,
+                             tp=tpa, tp_timeout_ms=120000)
     load_s = time.perf_counter() - t0
-    prompt = synth.prompt_ids(cfg["vocab"], C5_PROMPT, seed=5)
+    prompt = synth.prompt_ids(cfg["vocab"], C5_PROMPT, seed=5 + cx.rank // G)
     be.forward(prompt[:64], 0)  # warm-up
     ts = []
     for _ in range(2):
@@ -475,19 +483,23 @@ def measure_c5(cx: Ctx):
     ck = clocks.stop()
     ms = cx.max(ms)
     hbm, bf16, src_kind = peaks()
-    tot = sum(C5_WEIGHT_BYTES + C5_KV_BYTES_PER_POS * (p + 2) for p in range(C5_PROMPT, C5_PROMPT + C5_DECODE))
+    # bytes one rank reads per step: its 1/G of the weights and of the KV cache
+    tot = sum(C5_WEIGHT_BYTES + C5_KV_BYTES_PER_POS * (p + 2) for p in range(C5_PROMPT, C5_PROMPT + C5_DECODE)) / G
     achieved = tot / (ms / 1e3) / 1e9
-    ops = 2 * C5_LAYER_PARAMS * C5_PROMPT
+    ops = 2 * C5_LAYER_PARAMS * C5_PROMPT / G  # one rank's share of the prompt pass's multiply-adds
     path, mem = be.decode_path, be.memory_bytes
     be.destroy()
-    return {"metric": "decode tok/s @bs1 Qwen2-7B-architecture Q4_0 (1 GPU)",
-            "value": round(cx.world * C5_DECODE / (ms / 1e3), 2), "unit": UNIT, "steps": C5_DECODE,
+    par = "none (TP 1)" if G == 1 and reps == 1 else f"tensor parallel {G} (NCCL all-gathers) x {reps} replica(s)"
+    return {"metric": "decode tok/s @bs1 Qwen2-7B-architecture Q4_0 (1 GPU)" if cx.world == 1 else
+            f"decode tok/s @bs1 Qwen2-7B-architecture Q4_0 ({cx.world} GPUs: TP {G} x {reps})",
+            "value": round(reps * C5_DECODE / (ms / 1e3), 2), "unit": UNIT, "steps": C5_DECODE, "n_gpus": cx.world,
+            "tp": G, "replicas": reps,
             "ms_per_step": round(ms / C5_DECODE, 5), "positions": [C5_PROMPT, C5_PROMPT + C5_DECODE - 1],
             "config": {"workload": "c5: 28 layers, hidden 3584, 28/4 heads of 128, FFN 18944, vocab 152064, untied "
-                                   "Q4_0 lm_head; 512-token prompt then 256 greedy steps", "parallelism": "none (TP 1)",
+                                   "Q4_0 lm_head; 512-token prompt then 256 greedy steps", "parallelism": par,
                        "weights": "seeded N(0,0.02) generated on the device, Q4_0", "device_bytes": mem,
                        "load_s": round(load_s, 1)},
-            "roofline": {"bound": "hbm", "kernel": f"decode step ({path})", "achieved": round(achieved, 1),
+            "roofline": {"bound": "hbm", "kernel": f"decode step ({path}), per rank", "achieved": round(achieved, 1),
                          "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4), "peak_source": src_kind,
                          "bytes_per_step": round(tot / C5_DECODE)},
             "prefill": {"tokens": C5_PROMPT, "ms": round(pre * 1e3, 2), "tok_per_s": round(C5_PROMPT / pre, 1),

@@ -12,7 +12,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libh2cuda.so")
 
 OK = 0
-ERR_INVALID, ERR_CONTEXT_FULL, ERR_BAD_TYPE, ERR_CUDA, ERR_NOT_READY, ERR_NO_MEMORY, ERR_TIMEOUT = range(-1, -8, -1)
+ERR_INVALID, ERR_CONTEXT_FULL, ERR_BAD_TYPE, ERR_CUDA, ERR_NOT_READY, ERR_NO_MEMORY, ERR_TIMEOUT, ERR_UNSUPPORTED = \
+    range(-1, -9, -1)
+TP_ID_BYTES = 128
 GGML_F32, GGML_Q4_0, GGML_Q8_0 = 0, 2, 8
 KIND_QKV, KIND_O, KIND_GATE_UP, KIND_DOWN, KIND_ATTN_NORM, KIND_FFN_NORM, KIND_QKV_BIAS, KIND_EMBED, KIND_OUTPUT, \
     KIND_OUTPUT_NORM = range(10)
@@ -27,7 +29,8 @@ EXPORTS = ["h2c_create", "h2c_set_tensor", "h2c_forward", "h2c_forward_batch", "
            "h2c_decode_path", "h2c_trace_decode", "h2c_decode_ctas", "h2c_set_decode_fault", "h2c_read_logits",
            "h2c_profile", "h2c_destroy", "h2c_selftest_math",
            "h2c_last_error", "h2c_device_bytes", "h2c_q4_matrix_bytes", "h2c_q4_pack", "h2c_q4_matvec_scratch_bytes",
-           "h2c_q4_matvec", "h2c_q4_matvec_noalloc", "h2c_set_matmul_kernel", "h2c_matmul_kernel"]
+           "h2c_q4_matvec", "h2c_q4_matvec_noalloc", "h2c_set_matmul_kernel", "h2c_matmul_kernel",
+           "h2c_tp_unique_id", "h2c_create_tp", "h2c_tp_rank", "h2c_tp_world"]
 
 
 class Config(C.Structure):
@@ -84,11 +87,17 @@ def load(path: str = LIB_PATH) -> C.CDLL:
     L.h2c_q4_matvec_noalloc.argtypes = [p, i32, i32, p, i32, p, i32, p, p]
     L.h2c_set_matmul_kernel.argtypes = [C.c_int]
     L.h2c_matmul_kernel.argtypes = []
+    L.h2c_tp_unique_id.argtypes = [p]
+    L.h2c_create_tp.argtypes = [C.c_int, C.POINTER(Config), i32, i32, p, i32, C.POINTER(p)]
+    L.h2c_tp_rank.argtypes = [p]
+    L.h2c_tp_rank.restype = i32
+    L.h2c_tp_world.argtypes = [p]
+    L.h2c_tp_world.restype = i32
     for name in ("h2c_create", "h2c_set_tensor", "h2c_forward", "h2c_forward_batch", "h2c_generate_batch", "h2c_batch_kernels", "h2c_generate", "h2c_decode_kernels", "h2c_set_decode_mode",
                  "h2c_decode_path", "h2c_trace_decode", "h2c_decode_ctas", "h2c_set_decode_fault", "h2c_read_logits",
                  "h2c_profile", "h2c_selftest_math",
                  "h2c_destroy", "h2c_q4_pack", "h2c_q4_matvec", "h2c_q4_matvec_noalloc", "h2c_set_matmul_kernel",
-                 "h2c_matmul_kernel"):
+                 "h2c_matmul_kernel", "h2c_tp_unique_id", "h2c_create_tp"):
         getattr(L, name).restype = C.c_int
     _lib = L
     return L
@@ -98,3 +107,11 @@ def check(rc: int, handle=None) -> None:
     if rc != OK:
         msg = load().h2c_last_error(handle)
         raise H2CError(rc, (msg or b"").decode(errors="replace") or f"h2cuda error {rc}")
+
+
+def tp_unique_id() -> bytes:
+    """A new tensor-parallel group id (rank 0 creates it; every rank passes it to CudaBackend(tp=...))."""
+    L = load()
+    buf = (C.c_uint8 * TP_ID_BYTES)()
+    check(L.h2c_tp_unique_id(C.cast(buf, C.c_void_p)), None)
+    return bytes(buf)

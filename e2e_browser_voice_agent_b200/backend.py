@@ -13,6 +13,9 @@ create_cuda returns an object with the same members (snake_case) whose work runs
   profile(ids, pos) -> {op name: ms} (cpu-worker.js:31-37 names)
   destroy()
 Added for the multi-session configuration: every call takes an optional `seq` (an independent KV cache).
+Added for the 7B configuration: tp=(world, rank, group id) makes this object one rank of a tensor-parallel group
+(h2c_create_tp): every rank loads the same full tensors (the library keeps its rows) and makes the same calls; each
+returns the same tokens and logits as one GPU would.
 
 Weight upload follows the CPU host's init (cpu-worker.js:57-128): per layer the [q;k;v] and [gate;up] Q4_0
 matrices are concatenated row-wise, norms and [bq;bk;bv] biases are F32, token_embd is Q4_0 and output.weight is
@@ -22,7 +25,7 @@ from __future__ import annotations
 
 import ctypes as C
 import time
-from typing import Dict, List, Optional, Sequence
+from typing import Dict, List, Optional, Sequence, Tuple
 
 import numpy as np
 
@@ -37,7 +40,8 @@ class CudaBackend:
     name = "cuda"
 
     def __init__(self, parsed, data, cfg: Dict, ctx: int = 2048, prefill_chunk: int = 16, max_seqs: int = 1,
-                 device: int = 0, keep_logits: bool = False, on_progress=None, decode_mode: str = "auto"):
+                 device: int = 0, keep_logits: bool = False, on_progress=None, decode_mode: str = "auto",
+                 tp: Optional[Tuple[int, int, bytes]] = None, tp_timeout_ms: int = 0):
         L = _lib.load()
         self._L = L
         D, NL, F, H, KVH, V = cfg["dim"], cfg["layers"], cfg["ffn"], cfg["heads"], cfg["kv_heads"], cfg["vocab"]
@@ -50,7 +54,17 @@ class CudaBackend:
                         max_chunk=self.prefill_chunk, max_seqs=self.max_seqs, eps=float(cfg["eps"]),
                         rope_theta=float(cfg["rope_theta"]))
         h = C.c_void_p()
-        _lib.check(L.h2c_create(int(device), C.byref(c), C.byref(h)), None)
+        if tp is None:
+            _lib.check(L.h2c_create(int(device), C.byref(c), C.byref(h)), None)
+        else:  # one rank of a tensor-parallel group: (world, rank, group id from _lib.tp_unique_id on rank 0)
+            world, rank, gid = tp
+            if len(gid) != _lib.TP_ID_BYTES:
+                raise ValueError(f"tensor-parallel id must be {_lib.TP_ID_BYTES} bytes")
+            idbuf = (C.c_uint8 * _lib.TP_ID_BYTES).from_buffer_copy(gid)
+            _lib.check(L.h2c_create_tp(int(device), C.byref(c), int(world), int(rank), C.cast(idbuf, C.c_void_p),
+                                       int(tp_timeout_ms), C.byref(h)), None)
+        self.tp_world = int(L.h2c_tp_world(h))
+        self.tp_rank = int(L.h2c_tp_rank(h))
         self._h = h
         self._next = C.c_int32()
         self._last_logits: Dict[int, Optional[np.ndarray]] = {}

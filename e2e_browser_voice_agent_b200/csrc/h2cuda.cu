@@ -1,6 +1,8 @@
 // h2cuda: C-ABI implementation (include/h2cuda.h). The engine owns device weights, KV cache, scratch and the
 // CUDA graph of one decode step; callers pass host pointers only.
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
 #include <cmath>
 #include <cstdarg>
@@ -9,7 +11,10 @@
 #include <algorithm>
 #include <atomic>
 #include <mutex>
+#include <chrono>
 #include <string>
+#include <thread>
+#include <type_traits>
 #include <vector>
 
 #include "../../include/h2cuda.h"
@@ -33,6 +38,52 @@ std::atomic<int> g_mm_kind{H2C_MATMUL_AUTO};
 bool use_tc5(int M) {
   const int k = g_mm_kind.load(std::memory_order_relaxed);
   return k == H2C_MATMUL_TCGEN05 || (k == H2C_MATMUL_AUTO && M >= TC5_MIN_TOKENS);
+}
+
+// NCCL for tensor-parallel engines (h2c_create_tp), resolved at run time from the libnccl.so.2 the process has (a
+// PyTorch host has already loaded its own) or the system's, so single-GPU users need none. Communicators are created
+// non-blocking: every call that answers ncclInProgress is polled to completion against a deadline, and a peer that
+// never joins or stops answering ends in ncclCommAbort and an error instead of a wait without end.
+struct NcclApi {
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*init_rank_config)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*group_start)() = nullptr;
+  ncclResult_t (*group_end)() = nullptr;
+  ncclResult_t (*async_error)(ncclComm_t, ncclResult_t*) = nullptr;
+  ncclResult_t (*finalize)(ncclComm_t) = nullptr;
+  ncclResult_t (*destroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*abort)(ncclComm_t) = nullptr;
+  const char* (*error_string)(ncclResult_t) = nullptr;
+  std::string why;  // empty when every entry point resolved
+};
+const NcclApi& nccl() {
+  static NcclApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) {
+      const char* d = dlerror();
+      api.why = std::string("libnccl.so.2 not found: ") + (d ? d : "");
+      return;
+    }
+    auto sym = [&](auto& fn, const char* name) {
+      fn = reinterpret_cast<std::remove_reference_t<decltype(fn)>>(dlsym(h, name));
+      if (!fn && api.why.empty()) api.why = std::string("libnccl.so.2 lacks ") + name;
+    };
+    sym(api.get_unique_id, "ncclGetUniqueId");
+    sym(api.init_rank_config, "ncclCommInitRankConfig");
+    sym(api.all_gather, "ncclAllGather");
+    sym(api.group_start, "ncclGroupStart");
+    sym(api.group_end, "ncclGroupEnd");
+    sym(api.async_error, "ncclCommGetAsyncError");
+    sym(api.finalize, "ncclCommFinalize");
+    sym(api.destroy, "ncclCommDestroy");
+    sym(api.abort, "ncclCommAbort");
+    sym(api.error_string, "ncclGetErrorString");
+  });
+  return api;
 }
 
 // What the tcgen05 matmul needs besides the activations: the transposed block scales, the rows of the activation
@@ -147,6 +198,20 @@ struct h2c_engine {
   int32_t* mk_done_d = nullptr;  // its device alias
   int32_t mk_launch_seq = 0;
   bool mk_pending = false;    // the last pass of the current forward ran on the persistent kernel
+  // tensor parallelism (h2c_create_tp). Every matrix is split by output rows, so each row is computed whole, in the
+  // reference's order, by one rank: this rank holds its heads' q/k/v rows (Hl query and KVHl kv heads) and their
+  // KV cache, Dl = D / G rows of O and of down, Fl = F / G rows of gate and of up, and Vl rows of the lm_head
+  // (rank r from row r * Vp). NCCL all-gathers give every rank the full vectors between the matrices; the
+  // normalisations and quantizations of full vectors run on every rank. Without TP: G = 1 and the full sizes.
+  int tp_rank = 0, tp_world = 1;
+  ncclComm_t comm = nullptr;
+  bool comm_dead = false;        // aborted after a failure: passes are refused
+  int64_t tp_timeout_ms = 0;     // deadline of NCCL set-up, of enqueueing and of a pass's completion
+  std::string tp_fail;           // first NCCL failure inside an enqueue (reported after it)
+  int Hl = 0, KVHl = 0, Dl = 0, Fl = 0, Vp = 0, Vl = 0;
+  uint8_t* tp_send = nullptr;    // passes of several tokens: this rank's columns, packed, before a gather
+  uint8_t* tp_recv = nullptr;    // ... and the gathered [G][M][columns], before they are unpacked into [M][full row]
+  size_t tp_stage = 0;           // bytes of tp_send (tp_recv has G times as many)
 
   int fail(int code, const char* fmt, ...) {
     char buf[512];
@@ -485,15 +550,122 @@ inline void mark(Prof* p, int op, cudaStream_t st) {
   }
 }
 
+// ---------------------------------------------------------------- tensor parallelism: the all-gathers
+
+// Gathered columns [G][M][w] (32-bit words) -> rows of ld words with rank g's columns at g * w.
+static __global__ void k_tp_unpack(const uint32_t* __restrict__ src, int G, int M, int w, uint32_t* __restrict__ dst,
+                                   int ld) {
+  const size_t total = (size_t)G * M * w;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int j = (int)(i % w);
+    const size_t gm = i / w;
+    const int m = (int)(gm % M), g = (int)(gm / M);
+    dst[(size_t)m * ld + (size_t)g * w + j] = src[i];
+  }
+}
+
+int64_t steady_ms() {
+  return std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now().time_since_epoch())
+      .count();
+}
+
+// Settle a call on the non-blocking communicator: poll its state while it answers ncclInProgress, up to the engine's
+// deadline. Records the first failure in e->tp_fail; returns whether the call succeeded.
+bool nccl_settle(h2c_engine* e, ncclResult_t res, const char* what) {
+  const NcclApi& nc = nccl();
+  bool late = false;
+  if (res == ncclInProgress) {
+    const int64_t t0 = steady_ms();
+    while (res == ncclInProgress) {
+      if (nc.async_error(e->comm, &res) != ncclSuccess) break;
+      if (res == ncclInProgress && steady_ms() - t0 > e->tp_timeout_ms) {
+        late = true;
+        break;
+      }
+      if (res == ncclInProgress) std::this_thread::yield();
+    }
+  }
+  if (res == ncclSuccess) return true;
+  if (e->tp_fail.empty())
+    e->tp_fail = std::string(what) + (late ? ": no answer within the deadline" : std::string(": ") + nc.error_string(res));
+  return false;
+}
+
+// One column range of a buffer that every rank fills in part: rows of ld bytes, this rank's cols bytes of each row at
+// tp_rank * cols. rows == 1: a contiguous range, gathered in place.
+struct TpPart {
+  uint8_t* full;
+  size_t cols, ld;
+  int rows;
+};
+
+size_t tp_stage_bytes(const TpPart* p, int n) {
+  size_t o = 0;
+  for (int i = 0; i < n; i++)
+    if (p[i].rows > 1) o += align_up(p[i].cols * p[i].rows, 256);
+  return o;
+}
+
+// All-gather the parts in one NCCL group so that every rank's buffers hold every rank's columns. Rows of several
+// tokens are packed first (their columns are not contiguous) and unpacked after.
+void tp_gather(h2c_engine* e, cudaStream_t st, const TpPart* p, int n) {
+  if (e->tp_world == 1 || !e->tp_fail.empty()) return;
+  const NcclApi& nc = nccl();
+  const int G = e->tp_world, r = e->tp_rank;
+  size_t off[4], o = 0;
+  for (int i = 0; i < n; i++) {
+    off[i] = o;
+    if (p[i].rows > 1) {
+      cudaMemcpy2DAsync(e->tp_send + o, p[i].cols, p[i].full + (size_t)r * p[i].cols, p[i].ld, p[i].cols, p[i].rows,
+                        cudaMemcpyDeviceToDevice, st);
+      o += align_up(p[i].cols * p[i].rows, 256);
+    }
+  }
+  if (o > e->tp_stage) {
+    e->tp_fail = "gather staging too small";
+    return;
+  }
+  if (!nccl_settle(e, nc.group_start(), "ncclGroupStart")) return;
+  for (int i = 0; i < n; i++) {
+    const ncclResult_t res =
+        p[i].rows > 1 ? nc.all_gather(e->tp_send + off[i], e->tp_recv + off[i] * G, p[i].cols * p[i].rows, ncclUint8,
+                                      e->comm, st)
+                      : nc.all_gather(p[i].full + (size_t)r * p[i].cols, p[i].full, p[i].cols, ncclUint8, e->comm, st);
+    if (!nccl_settle(e, res, "ncclAllGather")) {
+      nc.group_end();
+      return;
+    }
+  }
+  if (!nccl_settle(e, nc.group_end(), "ncclGroupEnd")) return;
+  for (int i = 0; i < n; i++) {
+    if (p[i].rows == 1) continue;
+    const size_t words = (size_t)G * p[i].rows * (p[i].cols / 4);
+    const int grid = (int)std::min<size_t>((words + 255) / 256, 148 * 8);
+    k_tp_unpack<<<grid, 256, 0, st>>>(reinterpret_cast<const uint32_t*>(e->tp_recv + off[i] * G), G, p[i].rows,
+                                      (int)(p[i].cols / 4), reinterpret_cast<uint32_t*>(p[i].full), (int)(p[i].ld / 4));
+  }
+}
+
 // Enqueue one pass of M tokens (positions and ids are read from e->prm on the device). logits: compute the
-// last token's logits and the greedy next token into e->next_d.
+// last token's logits and the greedy next token into e->next_d. Under tensor parallelism every matrix product
+// computes this rank's rows and an all-gather completes the vector (QKV and attention stay per head: only the
+// attention output is gathered).
 void enqueue_pass(h2c_engine* e, int M, bool logits, Prof* pf, bool batch = false) {
   const h2c_config& c = e->cfg;
-  const int D = c.dim, F = c.ffn, H = c.heads, KVH = c.kv_heads, HD = e->HD, QKV = e->QKV, NL = c.layers;
+  const int D = c.dim, F = c.ffn, H = e->Hl, KVH = e->KVHl, HD = e->HD, QKV = e->QKV, NL = c.layers;
+  const int rk = e->tp_rank, Dl = e->Dl, Fl = e->Fl, nbf = F / 32, nbl = Fl / 32;
   cudaStream_t st = e->st;
   const MmCtx mcv{e->xdT, e->ldT, c.max_chunk, e->tc5_err, &e->tc5_used};
   const MmCtx* mc = M > 1 ? &mcv : nullptr;
   float* xdT = M > 1 ? e->xdT : nullptr;
+  float* att_r = e->att + (size_t)rk * H * HD;  // this rank's heads' columns of the attention output
+  float* x_r = e->x + (size_t)rk * Dl;          // this rank's rows of O and down
+  const TpPart g_att{reinterpret_cast<uint8_t*>(e->att), (size_t)H * HD * 4, (size_t)D * 4, M};
+  const TpPart g_x{reinterpret_cast<uint8_t*>(e->x), (size_t)Dl * 4, (size_t)D * 4, M};
+  const TpPart g_act[4] = {{reinterpret_cast<uint8_t*>(e->xq), (size_t)Fl, (size_t)F, M},
+                           {reinterpret_cast<uint8_t*>(e->xd), (size_t)nbl * 4, (size_t)nbf * 4, M},
+                           {reinterpret_cast<uint8_t*>(e->xs), (size_t)nbl * 16, (size_t)nbf * 16, M},
+                           {reinterpret_cast<uint8_t*>(e->xdT), (size_t)nbl * e->ldT * 4, 0, 1}};
   mark(pf, -1, st);
   k_embed<<<M, 128, 0, st>>>(e->prm, e->embd.qs, e->embd.d, D, e->x);
   mark(pf, 0, st);
@@ -508,33 +680,39 @@ void enqueue_pass(h2c_engine* e, int M, bool logits, Prof* pf, bool batch = fals
     if (M > 1 && attg_ok(H / KVH, HD, c.ctx)) {  // several tokens: one CTA per (kv head, token)
       if (HD == 64)
         k_attention_gqa<64><<<dim3(KVH, M), 256, attg_smem_bytes<64>(H / KVH, c.ctx), st>>>(
-            e->prm, e->qkv, QKV, e->kc, e->vc, H, KVH, c.ctx, NL, l, e->att, D);
+            e->prm, e->qkv, QKV, e->kc, e->vc, H, KVH, c.ctx, NL, l, att_r, D);
       else
         k_attention_gqa<128><<<dim3(KVH, M), 256, attg_smem_bytes<128>(H / KVH, c.ctx), st>>>(
-            e->prm, e->qkv, QKV, e->kc, e->vc, H, KVH, c.ctx, NL, l, e->att, D);
+            e->prm, e->qkv, QKV, e->kc, e->vc, H, KVH, c.ctx, NL, l, att_r, D);
     } else if (HD == 64) {
-      k_attention<64><<<dim3(H, M), 128, at_smem_bytes<64>(c.ctx), st>>>(e->prm, e->qkv, QKV, e->kc, e->vc, H, KVH, c.ctx, NL, l, e->att, D);
+      k_attention<64><<<dim3(H, M), 128, at_smem_bytes<64>(c.ctx), st>>>(e->prm, e->qkv, QKV, e->kc, e->vc, H, KVH, c.ctx, NL, l, att_r, D);
     } else {
-      k_attention<128><<<dim3(H, M), 128, at_smem_bytes<128>(c.ctx), st>>>(e->prm, e->qkv, QKV, e->kc, e->vc, H, KVH, c.ctx, NL, l, e->att, D);
+      k_attention<128><<<dim3(H, M), 128, at_smem_bytes<128>(c.ctx), st>>>(e->prm, e->qkv, QKV, e->kc, e->vc, H, KVH, c.ctx, NL, l, att_r, D);
     }
+    tp_gather(e, st, &g_att, 1);
     mark(pf, 4, st);
     {
       const int warps = M * (D / 32);
       k_quant<<<(warps + 7) / 8, 256, 0, st>>>(e->att, D, M, e->xq, e->xd, e->xs, xdT, e->ldT);
     }
     mark(pf, 5, st);
-    matvec(OP_ADD, W.o, e->xq, e->xd, e->xs, M, e->x, D, nullptr, st, mc);
+    matvec(OP_ADD, W.o, e->xq, e->xd, e->xs, M, x_r, D, nullptr, st, mc);
+    tp_gather(e, st, &g_x, 1);
     mark(pf, 6, st);
     k_norm_quant<<<M, 256, D * 4, st>>>(e->x, 0, W.ffn_norm, D, c.eps, e->xq, e->xd, e->xs, xdT, e->ldT);
     mark(pf, 1, st);
-    matvec(OP_STORE, W.gu, e->xq, e->xd, e->xs, M, e->gu, 2 * F, nullptr, st, mc);
+    matvec(OP_STORE, W.gu, e->xq, e->xd, e->xs, M, e->gu, 2 * Fl, nullptr, st, mc);
     mark(pf, 7, st);
     {
-      const int warps = M * (F / 32);
-      k_swiglu_quant<<<(warps + 7) / 8, 256, 0, st>>>(e->gu, F, M, e->xq, e->xd, e->xs, xdT, e->ldT);
+      const int warps = M * nbl;
+      k_swiglu_quant<<<(warps + 7) / 8, 256, 0, st>>>(e->gu, Fl, M, e->xq + (size_t)rk * Fl, e->xd + (size_t)rk * nbl,
+                                                      e->xs + (size_t)rk * nbl,
+                                                      xdT ? xdT + (size_t)rk * nbl * e->ldT : nullptr, e->ldT, F);
     }
+    tp_gather(e, st, g_act, M > 1 ? 4 : 3);
     mark(pf, 8, st);
-    matvec(OP_ADD, W.down, e->xq, e->xd, e->xs, M, e->x, D, nullptr, st, mc);
+    matvec(OP_ADD, W.down, e->xq, e->xd, e->xs, M, x_r, D, nullptr, st, mc);
+    tp_gather(e, st, &g_x, 1);
     mark(pf, 9, st);
   }
   if (batch) {  // every token of a batched decode step is the last of its sequence: logits and a token for each
@@ -551,16 +729,71 @@ void enqueue_pass(h2c_engine* e, int M, bool logits, Prof* pf, bool batch = fals
     mark(pf, 10, st);
   } else if (logits) {
     k_norm_quant<<<1, 256, D * 4, st>>>(e->x, M - 1, e->out_norm, D, c.eps, e->xq, e->xd, e->xs);
+    // this rank's lm_head rows [rk * Vp, rk * Vp + Vl) straight into their place in the logits, then gathered
+    float* lg = e->logits + (size_t)rk * e->Vp;
     if (e->out_type == 8) {
-      matvec_w<WQ8>(OP_STORE, (const uint8_t*)e->out8.qs, e->out8.d, c.vocab, D, e->xq, e->xd, e->xs, 1, e->logits,
-                    c.vocab, nullptr, st);
-    } else {
-      matvec(OP_STORE, e->out_type == 2 ? e->out4 : e->embd, e->xq, e->xd, e->xs, 1, e->logits, c.vocab, nullptr, st);
+      matvec_w<WQ8>(OP_STORE, (const uint8_t*)e->out8.qs, e->out8.d, e->Vl, D, e->xq, e->xd, e->xs, 1, lg, e->Vl,
+                    nullptr, st);
+    } else if (e->out_type == 2) {
+      matvec(OP_STORE, e->out4, e->xq, e->xd, e->xs, 1, lg, e->Vl, nullptr, st);
+    } else {  // tied: this rank's rows of the embedding (groups of 32 rows from row rk * Vp)
+      const size_t g0 = (size_t)rk * e->Vp / 32, nb = (size_t)D / 32;
+      matvec_w<WQ4>(OP_STORE, e->embd.qs + g0 * nb * 32 * 16, e->embd.d + g0 * nb * 32, e->Vl, D, e->xq, e->xd, e->xs,
+                    1, lg, e->Vl, nullptr, st);
     }
+    const TpPart g_lg{reinterpret_cast<uint8_t*>(e->logits), (size_t)e->Vp * 4, 0, 1};
+    tp_gather(e, st, &g_lg, 1);
     k_argmax1<<<e->am_np, 256, 0, st>>>(e->logits, c.vocab, e->am_v, e->am_i);
     k_argmax2<<<1, 32, 0, st>>>(e->am_v, e->am_i, e->am_np, e->prm, e->toklog, e->cfg.ctx, e->next_d);
     mark(pf, 10, st);
   }
+}
+
+// Wait for the stream. Under tensor parallelism the wait has the engine's deadline: a peer that stops answering
+// leaves this rank's collective waiting, so on expiry the communicator is aborted (its kernels return) and the
+// engine refuses further passes.
+int sync_stream(h2c_engine* e) {
+  if (e->tp_world == 1) {
+    CUDA_TRY(e, cudaStreamSynchronize(e->st));
+    return H2C_OK;
+  }
+  const int64_t t0 = steady_ms();
+  for (;;) {
+    const cudaError_t q = cudaStreamQuery(e->st);
+    if (q == cudaSuccess) return H2C_OK;
+    if (q != cudaErrorNotReady) return e->fail(H2C_ERR_CUDA, "stream: %s", cudaGetErrorString(q));
+    ncclResult_t a = ncclSuccess;
+    if (nccl().async_error(e->comm, &a) == ncclSuccess && a != ncclSuccess && a != ncclInProgress) {
+      nccl().abort(e->comm);
+      e->comm = nullptr;
+      e->comm_dead = true;
+      cudaStreamSynchronize(e->st);
+      return e->fail(H2C_ERR_CUDA, "NCCL: %s (communicator aborted)", nccl().error_string(a));
+    }
+    if (steady_ms() - t0 > e->tp_timeout_ms) {
+      nccl().abort(e->comm);  // the collectives in flight see the abort and return
+      e->comm = nullptr;
+      e->comm_dead = true;
+      cudaStreamSynchronize(e->st);
+      return e->fail(H2C_ERR_TIMEOUT, "tensor-parallel pass not finished within %lld ms: a peer stopped answering "
+                     "(communicator aborted)", (long long)e->tp_timeout_ms);
+    }
+    std::this_thread::yield();
+  }
+}
+
+// After enqueueing passes: an NCCL failure while enqueueing aborts the communicator.
+int tp_enqueue_status(h2c_engine* e) {
+  if (e->tp_fail.empty()) return H2C_OK;
+  const std::string why = e->tp_fail;
+  e->tp_fail.clear();
+  if (e->comm) {
+    nccl().abort(e->comm);
+    e->comm = nullptr;
+  }
+  e->comm_dead = true;
+  cudaStreamSynchronize(e->st);
+  return e->fail(H2C_ERR_CUDA, "%s (communicator aborted)", why.c_str());
 }
 
 int check_ready(h2c_engine* e) {
@@ -573,9 +806,16 @@ int check_ready(h2c_engine* e) {
 
 int build_graph(h2c_engine* e) {
   if (e->gexec) return H2C_OK;
-  CUDA_TRY(e, cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal));
+  // (relaxed under tensor parallelism: NCCL may set up a connection on the first use of a collective's algorithm)
+  CUDA_TRY(e, cudaStreamBeginCapture(e->st, e->tp_world > 1 ? cudaStreamCaptureModeRelaxed
+                                                              : cudaStreamCaptureModeThreadLocal));
   enqueue_pass(e, 1, true, nullptr);
   cudaError_t c = cudaStreamEndCapture(e->st, &e->graph);
+  if (!e->tp_fail.empty()) {
+    if (e->graph) cudaGraphDestroy(e->graph);
+    e->graph = nullptr;
+    return tp_enqueue_status(e);
+  }
   if (c != cudaSuccess) return e->fail(H2C_ERR_CUDA, "graph capture: %s", cudaGetErrorString(c));
   CUDA_TRY(e, cudaGraphInstantiate(&e->gexec, e->graph, 0));
   size_t nn = 0;
@@ -638,6 +878,7 @@ int mk_unsupported(h2c_engine* e, const char* why) {
 int mk_build(h2c_engine* e) {
   if (e->mk_built) return H2C_OK;
   e->mk_built = true;
+  if (e->tp_world > 1) return mk_unsupported(e, "tensor parallelism (steps run on the CUDA graph path)");
   const h2c_config& c = e->cfg;
   const int D = c.dim, F = c.ffn, H = c.heads, KVH = c.kv_heads, HD = e->HD, QKV = e->QKV, NL = c.layers,
             V = c.vocab;
@@ -945,6 +1186,7 @@ int run_forward(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t p
     if (ids[i] < 0 || ids[i] >= c.vocab) return e->fail(H2C_ERR_INVALID, "token id %d out of range", ids[i]);
   int r = check_ready(e);
   if (r) return r;
+  if (e->comm_dead) return e->fail(H2C_ERR_INVALID, "tensor-parallel communicator aborted after a failure");
   const int MT = c.max_chunk;
   const int nchunks = (n + MT - 1) / MT;
   if (nchunks > e->prm_slots) return e->fail(H2C_ERR_INVALID, "too many chunks");
@@ -978,6 +1220,7 @@ int run_forward(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t p
       CUDA_TRY(e, cudaGraphLaunch(e->gexec, e->st));
     } else {
       enqueue_pass(e, mlen, last, pf);
+      if ((r = tp_enqueue_status(e))) return r;
       CUDA_TRY(e, cudaGetLastError());
       if ((r = tc5_enqueue_check(e))) return r;
     }
@@ -989,7 +1232,12 @@ int run_forward(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t p
 
 extern "C" {
 
-int h2c_create(int device, const h2c_config* cfg, h2c_engine** out) {
+}  // extern "C"
+
+namespace {
+
+// Create an engine for one rank of a tensor-parallel group of G (G = 1: the whole model on this device).
+int create_engine(int device, const h2c_config* cfg, int G, int rk, h2c_engine** out) {
   if (!out || !cfg) {
     g_create_error = "null argument";
     return H2C_ERR_INVALID;
@@ -1007,11 +1255,28 @@ int h2c_create(int device, const h2c_config* cfg, h2c_engine** out) {
     g_create_error = "head_dim must be 64 or 128";
     return H2C_ERR_INVALID;
   }
+  if (G > 1 && (c.kv_heads % G || c.dim % (32 * G) || c.ffn % (32 * G))) {
+    g_create_error = "tensor parallelism needs kv_heads, dim / 32 and ffn / 32 divisible by the group size";
+    return H2C_ERR_INVALID;
+  }
+  const int Vp = G == 1 ? c.vocab : (c.vocab + 32 * G - 1) / (32 * G) * 32;
+  if (G > 1 && c.vocab <= (G - 1) * Vp) {
+    g_create_error = "vocabulary too small for the group size";
+    return H2C_ERR_INVALID;
+  }
   h2c_engine* e = new h2c_engine();
   e->cfg = c;
   e->dev = device;
   e->HD = HD;
-  e->QKV = c.dim + 2 * c.kv_heads * HD;
+  e->tp_world = G;
+  e->tp_rank = rk;
+  e->Hl = c.heads / G;
+  e->KVHl = c.kv_heads / G;
+  e->Dl = c.dim / G;
+  e->Fl = c.ffn / G;
+  e->Vp = Vp;
+  e->Vl = std::min(Vp, c.vocab - rk * Vp);
+  e->QKV = (e->Hl + 2 * e->KVHl) * HD;
   e->L.resize(c.layers);
   e->layer_set.assign(c.layers, 0);
   e->last_logits_valid.assign(c.max_seqs, 0);
@@ -1031,7 +1296,7 @@ int h2c_create(int device, const h2c_config* cfg, h2c_engine** out) {
     return bail(H2C_ERR_CUDA);
   }
   const int MT = c.max_chunk, D = c.dim, F = c.ffn;
-  const size_t kv = (size_t)c.max_seqs * c.layers * c.kv_heads * c.ctx * HD;
+  const size_t kv = (size_t)c.max_seqs * c.layers * e->KVHl * c.ctx * HD;
   e->am_np = 296;
   if (c.ctx > MAX_CTX) {
     e->err = "ctx above 49152 positions (attention keeps one score per position in shared memory)";
@@ -1042,7 +1307,7 @@ int h2c_create(int device, const h2c_config* cfg, h2c_engine** out) {
   const int KQ = F > D ? F : D;
   if ((r = dalloc_t(e, &e->kc, kv)) || (r = dalloc_t(e, &e->vc, kv)) || (r = dalloc_t(e, &e->x, (size_t)MT * D)) ||
       (r = dalloc_t(e, &e->qkv, (size_t)MT * e->QKV)) || (r = dalloc_t(e, &e->att, (size_t)MT * D)) ||
-      (r = dalloc_t(e, &e->gu, (size_t)MT * 2 * F)) || (r = dalloc_t(e, &e->logits, (size_t)c.vocab)) ||
+      (r = dalloc_t(e, &e->gu, (size_t)MT * 2 * e->Fl)) || (r = dalloc_t(e, &e->logits, (size_t)G * Vp)) ||
       (r = dalloc_t(e, &e->xq, (size_t)MT * KQ)) || (r = dalloc_t(e, &e->xd, (size_t)MT * KQ / 32)) ||
       (r = dalloc_t(e, &e->xs, (size_t)MT * KQ / 32)) ||
       (r = dalloc_t(e, &e->am_v, (size_t)e->am_np)) || (r = dalloc_t(e, &e->am_i, (size_t)e->am_np)) ||
@@ -1053,6 +1318,13 @@ int h2c_create(int device, const h2c_config* cfg, h2c_engine** out) {
       (r = dalloc_t(e, &e->xdT, (size_t)(KQ / 32) * ((MT + 3) / 4 * 4))) || (r = dalloc_t(e, &e->tc5_err, 4)))
     return bail(r);
   e->ldT = (MT + 3) / 4 * 4;
+  if (G > 1 && MT > 1) {  // staging of the gathers of passes of several tokens (the largest of them)
+    const size_t nbl = (size_t)e->Fl / 32;
+    const TpPart act[3] = {{nullptr, (size_t)e->Fl, 0, MT}, {nullptr, nbl * 4, 0, MT}, {nullptr, nbl * 16, 0, MT}};
+    const TpPart xp{nullptr, (size_t)e->Dl * 4, 0, MT};
+    e->tp_stage = std::max(tp_stage_bytes(act, 3), tp_stage_bytes(&xp, 1));
+    if ((r = dalloc_t(e, &e->tp_send, e->tp_stage)) || (r = dalloc_t(e, &e->tp_recv, e->tp_stage * G))) return bail(r);
+  }
   // RoPE table in double precision, cpu-worker.js:131-135
   {
     std::vector<float> t((size_t)c.ctx * HD);
@@ -1090,15 +1362,123 @@ int h2c_create(int device, const h2c_config* cfg, h2c_engine** out) {
   return H2C_OK;
 }
 
+}  // namespace
+
+extern "C" {
+
+int h2c_create(int device, const h2c_config* cfg, h2c_engine** out) { return create_engine(device, cfg, 1, 0, out); }
+
+int h2c_tp_unique_id(uint8_t* id) {
+  if (!id) return H2C_ERR_INVALID;
+  const NcclApi& nc = nccl();
+  if (!nc.why.empty()) {
+    g_create_error = nc.why;
+    return H2C_ERR_UNSUPPORTED;
+  }
+  ncclUniqueId u;
+  const ncclResult_t res = nc.get_unique_id(&u);
+  if (res != ncclSuccess) {
+    g_create_error = std::string("ncclGetUniqueId: ") + nc.error_string(res);
+    return H2C_ERR_CUDA;
+  }
+  static_assert(sizeof(u.internal) == H2C_TP_ID_BYTES, "NCCL unique id size");
+  memcpy(id, u.internal, H2C_TP_ID_BYTES);
+  return H2C_OK;
+}
+
+int h2c_create_tp(int device, const h2c_config* cfg, int32_t world, int32_t rank, const uint8_t* id,
+                  int32_t timeout_ms, h2c_engine** out) {
+  if (out) *out = nullptr;
+  if (!id || world < 1 || world > 8 || rank < 0 || rank >= world) {
+    g_create_error = "tensor parallelism: world in [1, 8], rank in [0, world) and an id are required";
+    return H2C_ERR_INVALID;
+  }
+  const NcclApi& nc = nccl();
+  if (world > 1 && !nc.why.empty()) {
+    g_create_error = nc.why;
+    return H2C_ERR_UNSUPPORTED;
+  }
+  h2c_engine* e = nullptr;
+  int r = create_engine(device, cfg, world, rank, &e);
+  if (r) return r;
+  e->tp_timeout_ms = timeout_ms > 0 ? timeout_ms : 120000;
+  if (world == 1) {
+    *out = e;
+    return H2C_OK;
+  }
+  ncclUniqueId u;
+  memcpy(u.internal, id, H2C_TP_ID_BYTES);
+  ncclConfig_t conf = NCCL_CONFIG_INITIALIZER;
+  conf.blocking = 0;  // every call returns at once; nccl_settle polls it against the deadline
+  ncclResult_t res = nc.init_rank_config(&e->comm, world, u, rank, &conf);
+  if (res != ncclSuccess && res != ncclInProgress) {
+    e->comm = nullptr;
+    g_create_error = std::string("ncclCommInitRankConfig: ") + nc.error_string(res);
+    h2c_destroy(e);
+    return H2C_ERR_CUDA;
+  }
+  if (!nccl_settle(e, res, "ncclCommInitRankConfig")) {  // a peer that never joined: abort, then report
+    nc.abort(e->comm);
+    e->comm = nullptr;
+    const bool late = e->tp_fail.find("deadline") != std::string::npos;
+    g_create_error = e->tp_fail + " (communicator aborted)";
+    h2c_destroy(e);
+    return late ? H2C_ERR_TIMEOUT : H2C_ERR_CUDA;
+  }
+  // first collectives outside any graph capture (connections are set up on first use): a small and a large gather
+  for (size_t bytes : {(size_t)e->Dl * 4, (size_t)e->Vp * 4}) {
+    const TpPart warm{reinterpret_cast<uint8_t*>(e->logits), bytes, 0, 1};
+    tp_gather(e, e->st, &warm, 1);
+    if ((r = tp_enqueue_status(e)) || (r = sync_stream(e))) {
+      g_create_error = e->err;
+      h2c_destroy(e);
+      return r;
+    }
+  }
+  *out = e;
+  return H2C_OK;
+}
+
+int32_t h2c_tp_rank(const h2c_engine* e) { return e ? e->tp_rank : -1; }
+int32_t h2c_tp_world(const h2c_engine* e) { return e ? e->tp_world : 0; }
+
 int h2c_set_tensor(h2c_engine* e, int kind, int layer, int ggml_type, const void* data, uint64_t nbytes) {
   if (!e || !data) return H2C_ERR_INVALID;
   const h2c_config& c = e->cfg;
   CUDA_TRY(e, cudaSetDevice(e->dev));
   if (kind < 0 || kind > 9) return e->fail(H2C_ERR_INVALID, "unknown tensor kind %d", kind);
   if (kind <= 6 && (layer < 0 || layer >= c.layers)) return e->fail(H2C_ERR_INVALID, "layer %d out of range", layer);
-  const int D = c.dim, F = c.ffn;
+  const int D = c.dim, F = c.ffn, HD = e->HD, rk = e->tp_rank;
+  const int Hl = e->Hl, KVHl = e->KVHl, Dl = e->Dl, Fl = e->Fl;
   int r = H2C_OK;
   auto need = [&](int t) { return ggml_type == t; };
+  // Under tensor parallelism the caller passes the full tensor (full_rows rows of row_bytes): keep this rank's rows,
+  // the ranges {first row, rows}, in that order.
+  std::vector<uint8_t> part;
+  auto keep = [&](int full_rows, size_t row_bytes, std::initializer_list<std::pair<int, int>> ranges) {
+    if (e->tp_world == 1) return true;
+    if (nbytes != (uint64_t)full_rows * row_bytes) {
+      e->fail(H2C_ERR_INVALID, "kind %d: %llu bytes, expected the full tensor of %lld", kind, (unsigned long long)nbytes,
+              (long long)full_rows * (long long)row_bytes);
+      return false;
+    }
+    size_t n = 0;
+    for (auto& g : ranges) n += (size_t)g.second * row_bytes;
+    part.resize(n);
+    size_t o = 0;
+    for (auto& g : ranges) {
+      memcpy(part.data() + o, (const uint8_t*)data + (size_t)g.first * row_bytes, (size_t)g.second * row_bytes);
+      o += (size_t)g.second * row_bytes;
+    }
+    data = part.data();
+    nbytes = n;
+    return true;
+  };
+  const int qkv_full = D + 2 * c.kv_heads * HD;
+  // q rows of this rank's heads, then the k and v rows of its kv heads
+  const std::initializer_list<std::pair<int, int>> qkv_rows = {
+      {rk * Hl * HD, Hl * HD}, {D + rk * KVHl * HD, KVHl * HD}, {D + (c.kv_heads + rk * KVHl) * HD, KVHl * HD}};
+  const size_t q4_row_d = (size_t)(D / 32) * 18;
   switch (kind) {
     case H2C_KIND_QKV:
     case H2C_KIND_O:
@@ -1106,10 +1486,16 @@ int h2c_set_tensor(h2c_engine* e, int kind, int layer, int ggml_type, const void
     case H2C_KIND_DOWN: {
       if (!need(H2C_GGML_Q4_0)) return e->fail(H2C_ERR_BAD_TYPE, "layer %d kind %d: expected Q4_0", layer, kind);
       LayerW& W = e->L[layer];
+      bool ok = true;
+      if (kind == 0) ok = keep(qkv_full, q4_row_d, qkv_rows);
+      if (kind == 1) ok = keep(D, q4_row_d, {{rk * Dl, Dl}});
+      if (kind == 2) ok = keep(2 * F, q4_row_d, {{rk * Fl, Fl}, {F + rk * Fl, Fl}});
+      if (kind == 3) ok = keep(D, (size_t)(F / 32) * 18, {{rk * Dl, Dl}});
+      if (!ok) return H2C_ERR_INVALID;
       if (kind == 0) r = upload_q4(e, &W.qkv, e->QKV, D, data, nbytes);
-      if (kind == 1) r = upload_q4(e, &W.o, D, D, data, nbytes);
-      if (kind == 2) r = upload_q4(e, &W.gu, 2 * F, D, data, nbytes);
-      if (kind == 3) r = upload_q4(e, &W.down, D, F, data, nbytes);
+      if (kind == 1) r = upload_q4(e, &W.o, Dl, D, data, nbytes);
+      if (kind == 2) r = upload_q4(e, &W.gu, 2 * Fl, D, data, nbytes);
+      if (kind == 3) r = upload_q4(e, &W.down, Dl, F, data, nbytes);
       break;
     }
     case H2C_KIND_ATTN_NORM:
@@ -1119,20 +1505,25 @@ int h2c_set_tensor(h2c_engine* e, int kind, int layer, int ggml_type, const void
       LayerW& W = e->L[layer];
       if (kind == 4) r = upload_f32(e, &W.attn_norm, D, data, nbytes);
       if (kind == 5) r = upload_f32(e, &W.ffn_norm, D, data, nbytes);
-      if (kind == 6) r = upload_f32(e, &W.bqkv, e->QKV, data, nbytes);
+      if (kind == 6) {
+        if (!keep(qkv_full, 4, qkv_rows)) return H2C_ERR_INVALID;
+        r = upload_f32(e, &W.bqkv, e->QKV, data, nbytes);
+      }
       break;
     }
-    case H2C_KIND_EMBED:
+    case H2C_KIND_EMBED:  // every rank keeps the whole table (token lookups; the tied lm_head uses its rows)
       if (!need(H2C_GGML_Q4_0)) return e->fail(H2C_ERR_BAD_TYPE, "token_embd: expected Q4_0");
       r = upload_q4(e, &e->embd, c.vocab, D, data, nbytes);
       if (!r) e->embd_set = true;
       return r;
     case H2C_KIND_OUTPUT:
       if (need(H2C_GGML_Q8_0)) {
-        r = upload_q8(e, &e->out8, c.vocab, D, data, nbytes);
+        if (!keep(c.vocab, (size_t)(D / 32) * 34, {{rk * e->Vp, e->Vl}})) return H2C_ERR_INVALID;
+        r = upload_q8(e, &e->out8, e->Vl, D, data, nbytes);
         if (!r) e->out_type = 8;
       } else if (need(H2C_GGML_Q4_0)) {
-        r = upload_q4(e, &e->out4, c.vocab, D, data, nbytes);
+        if (!keep(c.vocab, q4_row_d, {{rk * e->Vp, e->Vl}})) return H2C_ERR_INVALID;
+        r = upload_q4(e, &e->out4, e->Vl, D, data, nbytes);
         if (!r) e->out_type = 2;
       } else {
         return e->fail(H2C_ERR_BAD_TYPE, "output.weight: expected Q8_0 or Q4_0");
@@ -1160,14 +1551,14 @@ int h2c_forward(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t p
     CUDA_TRY(e, cudaMemcpyAsync(e->next_h, e->next_d, 4, cudaMemcpyDeviceToHost, e->st));
     if (e->mk_pending)
       CUDA_TRY(e, cudaMemcpyAsync(e->mk_io_h, e->mk_io, 8 * sizeof(int32_t), cudaMemcpyDeviceToHost, e->st));
-    CUDA_TRY(e, cudaStreamSynchronize(e->st));
+    if ((r = sync_stream(e))) return r;
     if (e->mk_pending && (r = mk_status(e))) return r;
     *next = *e->next_h;
   } else if (e->mk_pending) {
     if ((r = mk_wait_done(e, next))) return r;
   } else {
     CUDA_TRY(e, cudaMemcpyAsync(e->next_h, e->next_d, 4, cudaMemcpyDeviceToHost, e->st));
-    CUDA_TRY(e, cudaStreamSynchronize(e->st));
+    if ((r = sync_stream(e))) return r;
     *next = *e->next_h;
   }
   if ((r = tc5_status(e))) return r;
@@ -1181,6 +1572,7 @@ int h2c_forward(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t p
 int batch_launch(h2c_engine* e, int32_t n, const int32_t* seqs, const int32_t* ids, const int32_t* pos, int steps,
                  cudaEvent_t before = nullptr) {
   const h2c_config& c = e->cfg;
+  if (e->tp_world > 1) return e->fail(H2C_ERR_INVALID, "batched steps are not available with tensor parallelism");
   const int cap = c.max_chunk < P_CAP ? c.max_chunk : P_CAP;
   if (n < 1 || n > cap) return e->fail(H2C_ERR_INVALID, "batch of %d sequences (1 .. %d per step)", n, cap);
   std::vector<char> seen(c.max_seqs, 0);
@@ -1300,6 +1692,7 @@ int h2c_generate(h2c_engine* e, int seq, int32_t first_id, int32_t pos, int32_t 
   CUDA_TRY(e, cudaSetDevice(e->dev));
   int r = check_ready(e);
   if (r) return r;
+  if (e->comm_dead) return e->fail(H2C_ERR_INVALID, "tensor-parallel communicator aborted after a failure");
   if (e->decode_mode != H2C_DECODE_GRAPH && (r = mk_build(e))) return r;
   if (!use_persistent(e) && !e->gexec && (r = build_graph(e))) return r;
   int32_t* h = e->prm_h;
@@ -1321,7 +1714,7 @@ int h2c_generate(h2c_engine* e, int seq, int32_t first_id, int32_t pos, int32_t 
   if (out_tokens)
     CUDA_TRY(e, cudaMemcpyAsync(out_tokens, e->toklog + (size_t)seq * (c.ctx + 1) + pos + 1, sizeof(int32_t) * steps,
                                 cudaMemcpyDeviceToHost, e->st));
-  CUDA_TRY(e, cudaStreamSynchronize(e->st));
+  if ((r = sync_stream(e))) return r;
   if (mk && (r = mk_status(e))) return r;
   if (device_ms) CUDA_TRY(e, cudaEventElapsedTime(device_ms, e->ev0, e->ev1));
   e->last_logits_valid.assign(c.max_seqs, 0);
@@ -1429,8 +1822,7 @@ int h2c_read_logits(h2c_engine* e, int seq, float* out, int64_t n) {
   const int v = e->last_logits_valid[seq];
   const float* src = v >= 2 ? e->logits_b + (size_t)(v - 2) * e->cfg.vocab : e->logits;
   CUDA_TRY(e, cudaMemcpyAsync(out, src, (size_t)e->cfg.vocab * 4, cudaMemcpyDeviceToHost, e->st));
-  CUDA_TRY(e, cudaStreamSynchronize(e->st));
-  return H2C_OK;
+  return sync_stream(e);
 }
 
 int h2c_profile(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t pos, double* ms) {
@@ -1440,10 +1832,7 @@ int h2c_profile(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t p
   for (int i = 0; i < 64; i++) CUDA_TRY(e, cudaEventCreate(&pf.ev[i]));
   pf.on = true;
   int r = run_forward(e, seq, ids, n, pos, &pf);
-  if (!r) {
-    cudaError_t c = cudaStreamSynchronize(e->st);
-    if (c != cudaSuccess) r = e->fail(H2C_ERR_CUDA, "profile: %s", cudaGetErrorString(c));
-  }
+  if (!r) r = sync_stream(e);
   if (!r) r = tc5_status(e);
   for (int i = 0; i < H2C_NPROF; i++) ms[i] = 0;
   if (!r) {
@@ -1472,6 +1861,18 @@ int h2c_destroy(h2c_engine* e) {
   if (e->prm_bh) cudaFreeHost(e->prm_bh);
   if (e->next_bh) cudaFreeHost(e->next_bh);
   if (e->graph) cudaGraphDestroy(e->graph);
+  if (e->comm) {  // after the graphs that hold its collectives; a finalize that does not settle ends in an abort
+    const NcclApi& nc = nccl();
+    ncclResult_t res = nc.finalize(e->comm);
+    const int64_t t0 = steady_ms();
+    while (res == ncclInProgress && steady_ms() - t0 < std::max<int64_t>(e->tp_timeout_ms, 1000)) {
+      std::this_thread::yield();
+      if (nc.async_error(e->comm, &res) != ncclSuccess) break;
+    }
+    if (res == ncclSuccess) nc.destroy(e->comm);
+    else nc.abort(e->comm);
+    e->comm = nullptr;
+  }
   for (void* p : e->dallocs) cudaFree(p);
   if (e->prm_h) cudaFreeHost(e->prm_h);
   if (e->mk_io_h) cudaFreeHost(e->mk_io_h);

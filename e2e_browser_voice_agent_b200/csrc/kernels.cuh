@@ -273,17 +273,20 @@ static __global__ void k_quant(const float* __restrict__ x, int K, int M, int8_t
 }
 
 // act = silu(gate) * up, then int8 quantization (kernels.c:393-397); one warp per 32-value block of act.
+// gu: [M][2F] (gate, then up); outputs with a row pitch of ldo values (ldo >= F: a tensor-parallel rank writes its
+// F columns into rows of the full width).
 static __global__ void k_swiglu_quant(const float* __restrict__ gu, int F, int M, int8_t* __restrict__ xq,
                                float* __restrict__ xd, int4* __restrict__ xs, float* __restrict__ xdT = nullptr,
-                               int ldT = 0) {
+                               int ldT = 0, int ldo = 0) {
   const int nb = F / 32;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (gw >= M * nb) return;
-  const int m = gw / nb, b = gw % nb;
+  if (ldo == 0) ldo = F;
+  const int m = gw / nb, b = gw % nb, nbo = ldo / 32;
   const float* g = gu + (size_t)m * 2 * F;
   const float gt = g[b * 32 + lane], up = g[F + b * 32 + lane];
   const float v = __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, fast_exp_ref(-gt))), up);
-  quant_block_redux(v, lane, xq + (size_t)m * F + b * 32, xd + (size_t)m * nb + b, xs + (size_t)m * nb + b,
+  quant_block_redux(v, lane, xq + (size_t)m * ldo + b * 32, xd + (size_t)m * nbo + b, xs + (size_t)m * nbo + b,
                     xdT ? xdT + (size_t)b * ldT + m : nullptr);
 }
 

@@ -35,7 +35,9 @@ extern "C" {
 #define H2C_ERR_CUDA (-4)         /* a CUDA runtime call failed */
 #define H2C_ERR_NOT_READY (-5)    /* forward before every tensor was set */
 #define H2C_ERR_NO_MEMORY (-6)    /* device or pinned allocation failed */
-#define H2C_ERR_TIMEOUT (-7)      /* a bounded device-side wait expired (persistent decode kernel) */
+#define H2C_ERR_TIMEOUT (-7)      /* a bounded device-side wait expired (persistent decode kernel, tcgen05 matmul) or a
+                                     tensor-parallel peer did not answer within the engine's deadline */
+#define H2C_ERR_UNSUPPORTED (-8)  /* tensor parallelism without an NCCL library (libnccl.so.2) in the process */
 
 /* GGML tensor types accepted by h2c_set_tensor (gguf.js:6) */
 #define H2C_GGML_F32 0
@@ -75,6 +77,33 @@ typedef struct h2c_engine h2c_engine;
 /* Create an engine on CUDA device `device`: allocates the KV cache and scratch (replaces set_config +
  * set_buffers, kernels.c:418-437 and the layout of cpu-worker.js:52-88). */
 int h2c_create(int device, const h2c_config* cfg, h2c_engine** out);
+
+/* Tensor parallelism over G GPUs of one node, one process (or thread) per GPU: the 7B configuration split so that
+ * each rank reads 1/G of the weights per token (no reference counterpart: the reference runs one CPU process).
+ * Every matrix is split by output rows, so each output value is computed whole, in the reference's order, by one
+ * rank, and the results stay bit-identical to one GPU's: rank r owns query heads [r*H/G, (r+1)*H/G) with their
+ * kv heads (and that part of the KV cache), rows [r*D/G, (r+1)*D/G) of O and of down, rows [r*F/G, (r+1)*F/G) of
+ * gate and of up, and rows [r*Vp, r*Vp + Vp) of the lm_head (Vp = vocab / G rounded up to 32 rows). NCCL
+ * all-gathers of the attention output, of the residual after O and after down, of the quantized FFN activation and
+ * of the logits give every rank the full vectors in between; every rank computes the same token. Requires
+ * kv_heads, dim / 32 and ffn / 32 divisible by G (Qwen2-7B: G = 1, 2 or 4; 4 kv heads cannot be split 8 ways).
+ *
+ * h2c_tp_unique_id: rank 0 creates the group's id (H2C_TP_ID_BYTES bytes) and the host hands it to every rank.
+ * h2c_create_tp: every rank calls it at about the same time with the same cfg and id; the engine then takes the
+ * FULL tensors in h2c_set_tensor and keeps this rank's rows. Every rank must then make the same calls with the same
+ * arguments (h2c_forward, h2c_generate, h2c_profile). timeout_ms (<= 0: 120 s) bounds the group's set-up and each
+ * call's wait: a peer that never joins or stops answering ends in H2C_ERR_TIMEOUT with the communicator aborted
+ * (the engine then only accepts h2c_destroy). Not available with tensor parallelism: h2c_forward_batch,
+ * h2c_generate_batch, the persistent decode kernel (steps run on the CUDA graph path), h2c_trace_decode. NCCL is
+ * loaded at run time (libnccl.so.2 of the process, else the system's): H2C_ERR_UNSUPPORTED without one. G = 1
+ * behaves as h2c_create. */
+#define H2C_TP_ID_BYTES 128
+int h2c_tp_unique_id(uint8_t* id);
+int h2c_create_tp(int device, const h2c_config* cfg, int32_t world, int32_t rank, const uint8_t* id,
+                  int32_t timeout_ms, h2c_engine** out);
+/* This engine's rank and group size (0 and 1 without tensor parallelism). */
+int32_t h2c_tp_rank(const h2c_engine* e);
+int32_t h2c_tp_world(const h2c_engine* e);
 
 /* Upload one tensor from host memory holding raw GGUF bytes of `ggml_type` (blocks for Q4_0 / Q8_0, floats for
  * F32). Replaces set_tensor (kernels.c:423-431) and the repack of cpu-worker.js:97-128: the library splits
