@@ -131,6 +131,7 @@ struct h2c_engine {
   float* xd = nullptr;
   int4* xs = nullptr;
   float* xdT = nullptr;         // block scales transposed, [max(D, F) / 32][ldT] (tcgen05 matmul)
+  float* att_s = nullptr;       // single-token attention scores [heads][ctx]
   int ldT = 0;
   int* tc5_err = nullptr;       // device: the tcgen05 matmul's failure record
   int32_t* tc5_err_h = nullptr; // pinned copy
@@ -340,6 +341,37 @@ void launch_mv_t(int op, const uint8_t* qs, const __half* d, int N, int K, const
   else k_matvec<WT, ROWS, MB, OP_ADD><<<blocks, 256, smem, st>>>(qs, d, N, K, xq, xd, xs, M, y, ldy, bias);
 }
 
+// One token: k_mv with 32-row CTAs when the matrix has enough rows for two CTAs per SM and rows of at most 256
+// blocks, else 8-row CTAs (more CTAs for short matrices, shorter chunks of long rows). Returns false when the
+// token's staged values do not fit in shared memory (k_matvec then takes the call).
+constexpr size_t MV_SMEM = 227 * 1024;
+template <int WT, int R>
+void launch_mv_r(int op, const uint8_t* qs, const __half* d, int N, int K, const int8_t* xq, const float* xd,
+                 const int4* xs, float* y, const float* bias, cudaStream_t st) {
+  const int blocks = (int)(padded_rows(N) / R);
+  const size_t smem = mv_smem_bytes<WT, R>(K);
+  if (op == OP_STORE) k_mv<WT, R, OP_STORE><<<blocks, 256, smem, st>>>(qs, d, N, K, xq, xd, xs, y, bias);
+  else if (op == OP_BIAS) k_mv<WT, R, OP_BIAS><<<blocks, 256, smem, st>>>(qs, d, N, K, xq, xd, xs, y, bias);
+  else k_mv<WT, R, OP_ADD><<<blocks, 256, smem, st>>>(qs, d, N, K, xq, xd, xs, y, bias);
+}
+template <int WT>
+bool launch_mv(int op, const uint8_t* qs, const __half* d, int N, int K, const int8_t* xq, const float* xd,
+               const int4* xs, float* y, const float* bias, cudaStream_t st) {
+  const bool wide = padded_rows(N) / 32 >= 296 && K / 32 <= 256;
+  if ((wide ? mv_smem_bytes<WT, 32>(K) : mv_smem_bytes<WT, 8>(K)) > MV_SMEM) return false;
+  if (wide) launch_mv_r<WT, 32>(op, qs, d, N, K, xq, xd, xs, y, bias, st);
+  else launch_mv_r<WT, 8>(op, qs, d, N, K, xq, xd, xs, y, bias, st);
+  return true;
+}
+template <int WT, int R>
+cudaError_t mv2_attr() {
+  const int smem = (int)MV_SMEM;
+  cudaError_t c = cudaFuncSetAttribute(k_mv<WT, R, OP_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (c == cudaSuccess) c = cudaFuncSetAttribute(k_mv<WT, R, OP_BIAS>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (c == cudaSuccess) c = cudaFuncSetAttribute(k_mv<WT, R, OP_ADD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  return c;
+}
+
 // Several tokens (prompt chunks, batched decode steps): k_matmul with token groups of 32, 16 or 8 (the largest whose
 // activations fit next to the weight ring in a third of an SM's shared memory, so three CTAs share an SM) and row
 // ranges that give about four CTAs per SM.
@@ -425,6 +457,7 @@ void matvec_w(int op, const uint8_t* qs, const __half* d, int N, int K, const in
     return;
   }
   if (M == 1) {
+    if (launch_mv<WT>(op, qs, d, N, K, xq, xd, xs, y, bias, st)) return;
     // rows per CTA: the product buffer (rows x blocks x 16 B) small enough for several CTAs per SM
     if (nb <= 64) launch_mv_t<WT, 32, 1>(op, qs, d, N, K, xq, xd, xs, 1, y, ldy, bias, st);
     else if (nb <= 256) launch_mv_t<WT, 16, 1>(op, qs, d, N, K, xq, xd, xs, 1, y, ldy, bias, st);
@@ -484,6 +517,8 @@ bool attg_ok(int G, int HD, int ctx) {
 // The largest context h2c_create accepts: k_attention keeps one float score per position in shared memory, next to
 // its V staging ring (16 KB at head_dim 64, 32 KB at 128), within the 227 KB a CTA can have.
 constexpr int MAX_CTX = 49152;
+// The largest hidden size: k_norm_quant keeps a row, its weights and its squares in shared memory.
+constexpr int MAX_DIM = 8192;
 
 // The attributes are per device and only ever raised to fixed maxima (a launch's own size decides its occupancy),
 // so engines with different contexts on one device never lower each other's limits.
@@ -509,6 +544,16 @@ cudaError_t set_kernel_attrs() {
     c = cudaFuncSetAttribute(k_attention_gqa<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATTG_SMEM);
   if (c == cudaSuccess)
     c = cudaFuncSetAttribute(k_attention<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)at_smem_bytes<128>(MAX_CTX));
+  if (c == cudaSuccess)
+    c = cudaFuncSetAttribute(k_att_pv<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ap_smem_bytes(MAX_CTX));
+  if (c == cudaSuccess)
+    c = cudaFuncSetAttribute(k_att_pv<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ap_smem_bytes(MAX_CTX));
+  if (c == cudaSuccess)
+    c = cudaFuncSetAttribute(k_norm_quant, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)nq_smem_bytes(MAX_DIM));
+  if (c == cudaSuccess) c = mv2_attr<WQ4, 32>();
+  if (c == cudaSuccess) c = mv2_attr<WQ4, 8>();
+  if (c == cudaSuccess) c = mv2_attr<WQ8, 32>();
+  if (c == cudaSuccess) c = mv2_attr<WQ8, 8>();
   if (c == cudaSuccess) c = tc5_set_attrs();
   return c;
 }
@@ -671,13 +716,26 @@ void enqueue_pass(h2c_engine* e, int M, bool logits, Prof* pf, bool batch = fals
   mark(pf, 0, st);
   for (int l = 0; l < NL; l++) {
     const LayerW& W = e->L[l];
-    k_norm_quant<<<M, 256, D * 4, st>>>(e->x, 0, W.attn_norm, D, c.eps, e->xq, e->xd, e->xs, xdT, e->ldT);
+    k_norm_quant<<<M, NQ_THREADS, nq_smem_bytes(D), st>>>(e->x, 0, W.attn_norm, D, c.eps, e->xq, e->xd, e->xs, xdT,
+                                                         e->ldT);
     mark(pf, 1, st);
     matvec(OP_BIAS, W.qkv, e->xq, e->xd, e->xs, M, e->qkv, QKV, W.bqkv, st, mc);
     mark(pf, 2, st);
-    k_rope_kv<<<M, 256, 0, st>>>(e->prm, e->qkv, QKV, e->rope, e->kc, e->vc, H, KVH, HD, c.ctx, NL, l);
+    k_rope_kv<<<dim3(((H + KVH) * (HD / 2) + 127) / 128, M), 128, 0, st>>>(e->prm, e->qkv, QKV, e->rope, e->kc, e->vc,
+                                                                            H, KVH, HD, c.ctx, NL, l);
     mark(pf, 3, st);
-    if (M > 1 && attg_ok(H / KVH, HD, c.ctx)) {  // several tokens: one CTA per (kv head, token)
+    if (M == 1) {  // one token: scores over many CTAs per head, then the softmax and p.v chains per slice of dims
+      const int ns = std::min(16, (c.ctx + AS_T - 1) / AS_T);
+      if (HD == 64) {
+        k_att_scores<64><<<dim3(H, ns), AS_T, 0, st>>>(e->prm, e->qkv, e->kc, H, KVH, c.ctx, NL, l, e->att_s);
+        k_att_pv<64><<<dim3(H, 64 / AP_DS), 128, ap_smem_bytes(c.ctx), st>>>(e->prm, e->att_s, e->vc, H, KVH, c.ctx, NL,
+                                                                          l, att_r);
+      } else {
+        k_att_scores<128><<<dim3(H, ns), AS_T, 0, st>>>(e->prm, e->qkv, e->kc, H, KVH, c.ctx, NL, l, e->att_s);
+        k_att_pv<128><<<dim3(H, 128 / AP_DS), 128, ap_smem_bytes(c.ctx), st>>>(e->prm, e->att_s, e->vc, H, KVH, c.ctx,
+                                                                            NL, l, att_r);
+      }
+    } else if (attg_ok(H / KVH, HD, c.ctx)) {  // several tokens: one CTA per (kv head, token)
       if (HD == 64)
         k_attention_gqa<64><<<dim3(KVH, M), 256, attg_smem_bytes<64>(H / KVH, c.ctx), st>>>(
             e->prm, e->qkv, QKV, e->kc, e->vc, H, KVH, c.ctx, NL, l, att_r, D);
@@ -699,7 +757,8 @@ void enqueue_pass(h2c_engine* e, int M, bool logits, Prof* pf, bool batch = fals
     matvec(OP_ADD, W.o, e->xq, e->xd, e->xs, M, x_r, D, nullptr, st, mc);
     tp_gather(e, st, &g_x, 1);
     mark(pf, 6, st);
-    k_norm_quant<<<M, 256, D * 4, st>>>(e->x, 0, W.ffn_norm, D, c.eps, e->xq, e->xd, e->xs, xdT, e->ldT);
+    k_norm_quant<<<M, NQ_THREADS, nq_smem_bytes(D), st>>>(e->x, 0, W.ffn_norm, D, c.eps, e->xq, e->xd, e->xs, xdT,
+                                                         e->ldT);
     mark(pf, 1, st);
     matvec(OP_STORE, W.gu, e->xq, e->xd, e->xs, M, e->gu, 2 * Fl, nullptr, st, mc);
     mark(pf, 7, st);
@@ -716,7 +775,8 @@ void enqueue_pass(h2c_engine* e, int M, bool logits, Prof* pf, bool batch = fals
     mark(pf, 9, st);
   }
   if (batch) {  // every token of a batched decode step is the last of its sequence: logits and a token for each
-    k_norm_quant<<<M, 256, D * 4, st>>>(e->x, 0, e->out_norm, D, c.eps, e->xq, e->xd, e->xs, xdT, e->ldT);
+    k_norm_quant<<<M, NQ_THREADS, nq_smem_bytes(D), st>>>(e->x, 0, e->out_norm, D, c.eps, e->xq, e->xd, e->xs, xdT,
+                                                         e->ldT);
     if (e->out_type == 8) {
       matvec_w<WQ8>(OP_STORE, (const uint8_t*)e->out8.qs, e->out8.d, c.vocab, D, e->xq, e->xd, e->xs, M, e->logits_b,
                     c.vocab, nullptr, st);
@@ -728,7 +788,7 @@ void enqueue_pass(h2c_engine* e, int M, bool logits, Prof* pf, bool batch = fals
     k_argmax2_batch<<<M, 32, 0, st>>>(e->am_vb, e->am_ib, e->am_np, e->prm, e->toklog, e->cfg.ctx, e->next_b);
     mark(pf, 10, st);
   } else if (logits) {
-    k_norm_quant<<<1, 256, D * 4, st>>>(e->x, M - 1, e->out_norm, D, c.eps, e->xq, e->xd, e->xs);
+    k_norm_quant<<<1, NQ_THREADS, nq_smem_bytes(D), st>>>(e->x, M - 1, e->out_norm, D, c.eps, e->xq, e->xd, e->xs);
     // this rank's lm_head rows [rk * Vp, rk * Vp + Vl) straight into their place in the logits, then gathered
     float* lg = e->logits + (size_t)rk * e->Vp;
     if (e->out_type == 8) {
@@ -1245,8 +1305,8 @@ int create_engine(int device, const h2c_config* cfg, int G, int rk, h2c_engine**
   *out = nullptr;
   const h2c_config& c = *cfg;
   if (c.dim <= 0 || c.dim % 32 || c.ffn <= 0 || c.ffn % 32 || c.heads <= 0 || c.kv_heads <= 0 || c.heads % c.kv_heads ||
-      c.dim % c.heads || c.layers <= 0 || c.vocab <= 0 || c.ctx < 2 || c.max_chunk < 1 || c.max_chunk > 256 ||
-      c.max_seqs < 1) {
+      c.dim % c.heads || c.dim > MAX_DIM || c.layers <= 0 || c.vocab <= 0 || c.ctx < 2 || c.max_chunk < 1 ||
+      c.max_chunk > 256 || c.max_seqs < 1) {
     g_create_error = "invalid configuration";
     return H2C_ERR_INVALID;
   }
@@ -1315,7 +1375,8 @@ int create_engine(int device, const h2c_config* cfg, int G, int rk, h2c_engine**
       (r = dalloc_t(e, &e->toklog, (size_t)c.max_seqs * (c.ctx + 1))) ||
       (r = dalloc_t(e, &e->rope, (size_t)c.ctx * HD)) || (r = dalloc(e, &e->samp, sample_scratch_bytes(P_CAP))) ||
       (r = dalloc_t(e, &e->seeds_d, (size_t)P_CAP)) ||
-      (r = dalloc_t(e, &e->xdT, (size_t)(KQ / 32) * ((MT + 3) / 4 * 4))) || (r = dalloc_t(e, &e->tc5_err, 4)))
+      (r = dalloc_t(e, &e->xdT, (size_t)(KQ / 32) * ((MT + 3) / 4 * 4))) || (r = dalloc_t(e, &e->tc5_err, 4)) ||
+      (r = dalloc_t(e, &e->att_s, (size_t)e->Hl * c.ctx)))
     return bail(r);
   e->ldT = (MT + 3) / 4 * 4;
   if (G > 1 && MT > 1) {  // staging of the gathers of passes of several tokens (the largest of them)

@@ -222,38 +222,58 @@ static __global__ void k_embed(const int32_t* __restrict__ prm, const uint8_t* _
   }
 }
 
-// RMSNorm (kernels.c:80-86) of row (row0 + blockIdx.x) of x, then int8 quantization into slot blockIdx.x (the
-// scale with the exact fast division / square root / reciprocal, the blocks with quant_block_redux).
-// The sum of squares runs as the reference's four lane chains (threads 0..3), in element order.
-// dynamic smem: D floats. xdT (optional): the scales again, transposed ([block][ldT], token slot blockIdx.x).
-static __global__ void k_norm_quant(const float* __restrict__ x, int row0, const float* __restrict__ w, int D, float eps,
-                             int8_t* __restrict__ xq, float* __restrict__ xd, int4* __restrict__ xs,
-                             float* __restrict__ xdT = nullptr, int ldT = 0) {
-  extern __shared__ float xsm[];
-  __shared__ float part[4];
+// RMSNorm then int8 quantization of rows row0 + blockIdx.x (kernels.c:80-86, 90-114), one CTA of NQ_THREADS per row.
+// All threads load x and w with 16-byte loads into shared memory and store the squares lane-major (element 4k + l at
+// sqT[l][k], lane rows padded by 4 floats against bank conflicts); threads 0..3 then run the reference's four lane
+// chains of the sum of squares (lane l: x[l]^2 + x[l+4]^2 + ... in index order) from 16-byte shared loads, the
+// scale is formed from ((l0 + l1) + l2) + l3, and every warp quantizes 32-value blocks of (x * scale) * w.
+// D a multiple of 32; dynamic smem nq_smem_bytes(D).
+constexpr int NQ_THREADS = 512;
+__host__ __device__ constexpr size_t nq_smem_bytes(int D) { return ((size_t)2 * D + 4 * ((size_t)D / 4 + 4)) * 4; }
+static __global__ void __launch_bounds__(NQ_THREADS) k_norm_quant(const float* __restrict__ x, int row0,
+                                                                  const float* __restrict__ w, int D, float eps,
+                                                                  int8_t* __restrict__ xq, float* __restrict__ xd,
+                                                                  int4* __restrict__ xs,
+                                                                  float* __restrict__ xdT = nullptr, int ldT = 0) {
+  extern __shared__ __align__(16) float nsm[];
+  float* xsm = nsm;
+  float* wsm = nsm + D;
+  float* sqT = nsm + 2 * D;
+  const int L4 = D / 4 + 4;
   __shared__ float rs;
   const int slot = blockIdx.x;
-  const float* xr = x + (size_t)(row0 + slot) * D;
-  for (int i = threadIdx.x; i < D; i += blockDim.x) xsm[i] = xr[i];
-  __syncthreads();
-  if (threadIdx.x < 4) {
-    float s = 0.f;
-    const int l = threadIdx.x;
-#pragma unroll 8
-    for (int i = l; i < D; i += 4) s = __fadd_rn(s, __fmul_rn(xsm[i], xsm[i]));
-    part[l] = s;
+  const float4* xr = reinterpret_cast<const float4*>(x + (size_t)(row0 + slot) * D);
+  const float4* wr = reinterpret_cast<const float4*>(w);
+  for (int k = threadIdx.x; k < D / 4; k += blockDim.x) {
+    const float4 a = xr[k], b = __ldg(wr + k);
+    reinterpret_cast<float4*>(xsm)[k] = a;
+    reinterpret_cast<float4*>(wsm)[k] = b;
+    sqT[k] = __fmul_rn(a.x, a.x);
+    sqT[L4 + k] = __fmul_rn(a.y, a.y);
+    sqT[2 * L4 + k] = __fmul_rn(a.z, a.z);
+    sqT[3 * L4 + k] = __fmul_rn(a.w, a.w);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    const float ss = __fadd_rn(__fadd_rn(__fadd_rn(part[0], part[1]), part[2]), part[3]);
-    rs = norm_scale(ss, D, eps);
+  if (threadIdx.x < 32) {
+    float s = 0.f;
+    if (threadIdx.x < 4) {
+      const float4* p = reinterpret_cast<const float4*>(sqT + threadIdx.x * L4);
+#pragma unroll 8
+      for (int j = 0; j < D / 16; j++) {
+        const float4 a = p[j];
+        s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, a.x), a.y), a.z), a.w);
+      }
+    }
+    const float s1 = __shfl_sync(0xffffffffu, s, 1), s2 = __shfl_sync(0xffffffffu, s, 2),
+                s3 = __shfl_sync(0xffffffffu, s, 3);
+    if (threadIdx.x == 0) rs = norm_scale(__fadd_rn(__fadd_rn(__fadd_rn(s, s1), s2), s3), D, eps);
   }
   __syncthreads();
   const float r = rs;
   const int nb = D / 32, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   for (int b = warp; b < nb; b += nw) {
     const int i = b * 32 + lane;
-    const float v = __fmul_rn(__fmul_rn(xsm[i], r), w[i]);
+    const float v = __fmul_rn(__fmul_rn(xsm[i], r), wsm[i]);
     quant_block_redux(v, lane, xq + (size_t)slot * D + b * 32, xd + (size_t)slot * nb + b, xs + (size_t)slot * nb + b,
                       xdT ? xdT + (size_t)b * ldT + slot : nullptr);
   }
@@ -387,6 +407,111 @@ __global__ void __launch_bounds__(256) k_matvec(const uint8_t* __restrict__ qs, 
       else if (OP == OP_BIAS) *o = __fadd_rn(v, bias[n]);
       else *o = v;
     }
+  }
+}
+
+// One token's matvec y[n] (op)= W[n] . x (matmul_q4 / dot_q8_q8 with M = 1, kernels.c:121-273), the decode step's
+// hot loop. CTA = R rows of one 32-row group (256 threads), streaming its rows' blocks in chunks of CB = 256 / R
+// blocks (thread (j, r) of a chunk takes block j, row r):
+//   - the token's int8 values, scales and lane sums are staged in shared memory once;
+//   - the weight bytes and fp16 scales of chunk c land in stage c % MV_P of a cp.async ring, MV_P - 1 chunks ahead;
+//   - after the chunk's barrier every thread forms its item's four exact lane products f32(p_l) * (dw * dx) into
+//     the product buffer of the chunk (two, alternating), while threads 0..4R-1 (row r = t / 4, lane l = t % 4)
+//     add the previous chunk's products to their running lane sum in block order;
+//   - at the end ((l0 + l1) + l2) + l3 and the epilogue (put(), kernels.c:190-194).
+// Every product and every sum is the reference's; only the order of independent work differs.
+// dynamic smem: mv_smem_bytes<WT, R>(K).
+constexpr int MV_P = 6;
+template <int WT, int R>
+__host__ __device__ constexpr size_t mv_stage_bytes() { return (size_t)(256 / R) * R * (WT == WQ4 ? 16 : 32); }
+template <int WT, int R>
+__host__ __device__ constexpr size_t mv_smem_bytes(int K) {
+  return (size_t)MV_P * (mv_stage_bytes<WT, R>() + 512) + 2 * 256 * 16 + (size_t)K +
+         (((size_t)K / 32 * 4 + 15) & ~(size_t)15) + (WT == WQ4 ? (size_t)K / 32 * 16 : 0);
+}
+template <int WT, int R, int OP>
+__global__ void __launch_bounds__(256) k_mv(const uint8_t* __restrict__ qs, const __half* __restrict__ dsc, int N,
+                                            int K, const int8_t* __restrict__ xq, const float* __restrict__ xd,
+                                            const int4* __restrict__ xs, float* __restrict__ y,
+                                            const float* __restrict__ bias) {
+  constexpr int BB = WT == WQ4 ? 16 : 32;
+  constexpr int CB = 256 / R;
+  constexpr int WS = (int)mv_stage_bytes<WT, R>();
+  extern __shared__ __align__(16) uint8_t mvs[];
+  uint8_t* wst = mvs;                                                     // [MV_P][CB][R][BB]
+  __half* sst = reinterpret_cast<__half*>(mvs + MV_P * WS);               // [MV_P][CB][R]
+  float4* prod = reinterpret_cast<float4*>(mvs + MV_P * (WS + 512));      // [2][CB][R]
+  int8_t* xqs = reinterpret_cast<int8_t*>(prod + 2 * 256);
+  const int nb = K / 32, nch = (nb + CB - 1) / CB;
+  float* xds = reinterpret_cast<float*>(xqs + K);
+  int4* xss = reinterpret_cast<int4*>(xds + ((nb + 3) & ~3));
+  const int tid = threadIdx.x, n0 = blockIdx.x * R, g = n0 >> 5, r0 = n0 & 31;
+  const uint8_t* wg = qs + (size_t)g * nb * 32 * BB;
+  const __half* dg = dsc + (size_t)g * nb * 32;
+  for (int i = tid; i < K / 16; i += 256) cp_async16(xqs + 16 * i, xq + 16 * i);
+  for (int i = tid; i < nb; i += 256) {
+    cp_async4(xds + i, xd + i);
+    if (WT == WQ4) cp_async16(xss + i, xs + i);
+  }
+  const int j = tid / R, r = tid % R;
+  auto stage = [&](int c) {  // chunk c into stage c % MV_P (an empty group past the last chunk)
+    const int b = c * CB + j;
+    if (c < nch && b < nb) {
+      const size_t e = (size_t)b * 32 + r0 + r;
+      uint8_t* dst = wst + (c % MV_P) * WS + (j * R + r) * BB;
+      cp_async16(dst, wg + e * BB);
+      if (BB == 32) cp_async16(dst + 16, wg + e * BB + 16);
+      if ((r & 1) == 0) cp_async4(sst + (c % MV_P) * 256 + j * R + r, dg + e);
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int c = 0; c < MV_P - 1; c++) stage(c);  // (the first group also carries the token's values)
+  const int cr = tid >> 2, cl = tid & 3;
+  float acc = 0.f;
+  for (int c = 0; c <= nch; c++) {
+    if (c < nch) cp_async_wait_group<MV_P - 2>();  // chunk c has landed
+    __syncthreads();
+    stage(c + MV_P - 1);  // into the stage chunk c - 1 used (every thread is past it)
+    if (c >= 1 && tid < R * 4) {  // the previous chunk's products, in block order
+      const int cb = min(CB, nb - (c - 1) * CB);
+      const float* pp = reinterpret_cast<const float*>(prod + ((c - 1) & 1) * 256) + cr * 4 + cl;
+#pragma unroll 8
+      for (int jj = 0; jj < cb; jj++) acc = __fadd_rn(acc, pp[jj * R * 4]);
+    }
+    const int b = c * CB + j;
+    if (c < nch && b < nb) {
+      const int s = c % MV_P;
+      const uint4 w0 = *reinterpret_cast<const uint4*>(wst + s * WS + (j * R + r) * BB);
+      const float dw = __half2float(sst[s * 256 + j * R + r]);
+      const int4* xp = reinterpret_cast<const int4*>(xqs + b * 32);
+      const int4 x0 = xp[0], x1 = xp[1];
+      const float sc = __fmul_rn(dw, xds[b]);
+      float p0, p1, p2, p3;
+      if (WT == WQ4) {
+        const int4 sm = xss[b];
+        p0 = q4_lane(w0.x, x0.x, x1.x, sm.x);
+        p1 = q4_lane(w0.y, x0.y, x1.y, sm.y);
+        p2 = q4_lane(w0.z, x0.z, x1.z, sm.z);
+        p3 = q4_lane(w0.w, x0.w, x1.w, sm.w);
+      } else {
+        const uint4 w1 = *reinterpret_cast<const uint4*>(wst + s * WS + (j * R + r) * BB + 16);
+        p0 = magic_to_float(__dp4a((int)w0.x, x0.x, __dp4a((int)w1.x, x1.x, MK_MAGIC)));
+        p1 = magic_to_float(__dp4a((int)w0.y, x0.y, __dp4a((int)w1.y, x1.y, MK_MAGIC)));
+        p2 = magic_to_float(__dp4a((int)w0.z, x0.z, __dp4a((int)w1.z, x1.z, MK_MAGIC)));
+        p3 = magic_to_float(__dp4a((int)w0.w, x0.w, __dp4a((int)w1.w, x1.w, MK_MAGIC)));
+      }
+      prod[(c & 1) * 256 + j * R + r] = make_float4(__fmul_rn(p0, sc), __fmul_rn(p1, sc), __fmul_rn(p2, sc),
+                                                    __fmul_rn(p3, sc));
+    }
+  }
+  cp_async_wait_all();
+  const float v = hsum4_quad(acc);  // (every warp takes part; threads past 4R hold 0)
+  const int n = n0 + cr;
+  if (tid < R * 4 && cl == 0 && n < N) {
+    if (OP == OP_ADD) y[n] = __fadd_rn(y[n], v);
+    else if (OP == OP_BIAS) y[n] = __fadd_rn(v, bias[n]);
+    else y[n] = v;
   }
 }
 
@@ -719,16 +844,17 @@ __global__ void __launch_bounds__(256) k_matmul_tc(const uint8_t* __restrict__ q
 }
 
 // RoPE on the Q and K heads of each token (pairs (i, i + HD/2), table cos/sin), then K and V appended to the
-// cache of (seq, layer) (kernels.c:337-352). One CTA per token.
+// cache of (seq, layer) (kernels.c:337-352). grid (x, tokens): the (head, pair) tasks of a token spread over
+// gridDim.x CTAs, one task per thread when the grid covers them.
 static __global__ void k_rope_kv(const int32_t* __restrict__ prm, float* __restrict__ qkv, int QKV, const float* __restrict__ rope,
                           float* __restrict__ kc, float* __restrict__ vc, int H, int KVH, int HD, int ctx, int layers,
                           int layer) {
-  const int m = blockIdx.x;
+  const int m = blockIdx.y;
   const int pos = tok_pos(prm, m), seq = tok_seq(prm, m);
   const int D = H * HD, half = HD / 2;
   float* row = qkv + (size_t)m * QKV;
   const float* cs = rope + (size_t)pos * HD;
-  for (int task = threadIdx.x; task < (H + KVH) * half; task += blockDim.x) {
+  for (int task = blockIdx.x * blockDim.x + threadIdx.x; task < (H + KVH) * half; task += gridDim.x * blockDim.x) {
     const int h = task / half, i = task % half;
     float* v = row + (size_t)h * HD;
     const float c = cs[2 * i], s = cs[2 * i + 1], x0 = v[i], x1 = v[i + half];
@@ -851,6 +977,125 @@ __global__ void __launch_bounds__(128) k_attention(const int32_t* __restrict__ p
     const int d = tid + 128 * k;
     if (d < HD) att[(size_t)m * D + (size_t)h * HD + d] = o[k];
   }
+}
+
+// The single-token attention of the decode step, kernels.c:355-377, split so that many CTAs share the work of one
+// head and its K and V rows stream through many SMs; the ordered sums stay single chains, so every value is the
+// reference's.
+//   k_att_scores: grid (H, NS): CTA (h, j) computes s_t = (q . k_t in four lane chains of HD/4 products,
+//     ((l0 + l1) + l2) + l3) * (1 / sqrt(HD)) for positions t in chunks j, j + NS, ... of 128 (one position per
+//     thread, 16 of the K row's 16-byte loads in flight), into S[h][t].
+//   k_att_pv: grid (H, HD / AP_DS): CTA (h, j) takes the max over S[h][0..T), e_t = fast_exp(s_t - max), the sum of
+//     e_t in position order (one chain, from 16-byte shared loads), p_t = e_t / sum, and the AP_DS ordered chains
+//     o[d] = sum_t p_t v_t[d] of its slice of dims (one per thread), whose V columns stream through a shared-memory
+//     ring (cp.async, requested at the start so they arrive during the softmax). Each slice's CTA repeats the softmax
+//     of the head (it is short) instead of waiting on another CTA.
+constexpr int AS_T = 128;  // positions per score chunk (one per thread)
+template <int HD>
+__global__ void __launch_bounds__(AS_T) k_att_scores(const int32_t* __restrict__ prm, const float* __restrict__ qkv,
+                                                     const float* __restrict__ kc, int H, int KVH, int ctx,
+                                                     int layers, int layer, float* __restrict__ S) {
+  __shared__ float q_s[HD];
+  const int h = blockIdx.x, tid = threadIdx.x;
+  const int T = tok_pos(prm, 0) + 1, seq = tok_seq(prm, 0);
+  const int kh = h / (H / KVH);
+  if ((int)blockIdx.y * AS_T >= T) return;
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
+  for (int i = tid; i < HD; i += AS_T) q_s[i] = qkv[(size_t)h * HD + i];
+  __syncthreads();
+  const float* kb = kc + (((size_t)seq * layers + layer) * KVH + kh) * (size_t)ctx * HD;
+  for (int c = blockIdx.y; c * AS_T < T; c += gridDim.y) {
+    const int t = c * AS_T + tid;
+    if (t >= T) break;
+    const float4* kr = reinterpret_cast<const float4*>(kb + (size_t)t * HD);
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll 16
+    for (int i = 0; i < HD / 4; i++) {
+      const float4 k4 = __ldg(kr + i);
+      s0 = __fadd_rn(s0, __fmul_rn(q_s[4 * i], k4.x));
+      s1 = __fadd_rn(s1, __fmul_rn(q_s[4 * i + 1], k4.y));
+      s2 = __fadd_rn(s2, __fmul_rn(q_s[4 * i + 2], k4.z));
+      s3 = __fadd_rn(s3, __fmul_rn(q_s[4 * i + 3], k4.w));
+    }
+    S[(size_t)h * ctx + t] = __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(s0, s1), s2), s3), scale);
+  }
+}
+
+constexpr int AP_DS = 16;   // dims per p.v CTA
+constexpr int AP_VC = 128;  // positions per V stage
+constexpr int AP_NST = 4;   // V stages in flight
+__host__ __device__ constexpr size_t ap_smem_bytes(int ctx) {
+  return ((size_t)((ctx + 3) & ~3) + (size_t)AP_NST * AP_VC * AP_DS) * 4;
+}
+template <int HD>
+__global__ void __launch_bounds__(128) k_att_pv(const int32_t* __restrict__ prm, const float* __restrict__ S,
+                                                const float* __restrict__ vc, int H, int KVH, int ctx, int layers,
+                                                int layer, float* __restrict__ att) {
+  extern __shared__ __align__(16) float sc[];
+  float* vst = sc + ((ctx + 3) & ~3);  // [AP_NST][AP_VC][AP_DS]
+  __shared__ float red[4];
+  __shared__ float sum_s;
+  const int h = blockIdx.x, d0 = blockIdx.y * AP_DS, tid = threadIdx.x;
+  const int T = tok_pos(prm, 0) + 1, seq = tok_seq(prm, 0);
+  const int kh = h / (H / KVH);
+  const float* vb = vc + (((size_t)seq * layers + layer) * KVH + kh) * (size_t)ctx * HD + d0;
+  const int nvc = (T + AP_VC - 1) / AP_VC;
+  auto stage_v = [&](int c) {  // V columns d0..d0+AP_DS of chunk c into stage c % AP_NST (an empty group past the end)
+    if (c < nvc) {
+      const int t0 = c * AP_VC, tc = min(AP_VC, T - t0);
+      float* dst = vst + (c % AP_NST) * AP_VC * AP_DS;
+      for (int i = tid; i < tc * (AP_DS / 4); i += blockDim.x) {
+        const int t = i / (AP_DS / 4), q = i % (AP_DS / 4);
+        cp_async16(dst + t * AP_DS + 4 * q, vb + (size_t)(t0 + t) * HD + 4 * q);
+      }
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int c = 0; c < AP_NST - 1; c++) stage_v(c);
+  const float* Sh = S + (size_t)h * ctx;
+  float mx = -1e30f;
+  for (int t = tid; t < T; t += blockDim.x) {
+    const float v = Sh[t];
+    sc[t] = v;
+    mx = fmaxf(mx, v);
+  }
+  mx = warp_max(mx);
+  if ((tid & 31) == 0) red[tid >> 5] = mx;
+  __syncthreads();
+  mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  for (int t = tid; t < T; t += blockDim.x) sc[t] = fast_exp_ref(__fsub_rn(sc[t], mx));
+  __syncthreads();
+  if (tid == 0) {  // sum in position order
+    float s = 0.f;
+    const float4* p4 = reinterpret_cast<const float4*>(sc);
+#pragma unroll 8
+    for (int j = 0; j < T / 4; j++) {
+      const float4 a = p4[j];
+      s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, a.x), a.y), a.z), a.w);
+    }
+    for (int t = T & ~3; t < T; t++) s = __fadd_rn(s, sc[t]);
+    sum_s = s;
+  }
+  __syncthreads();
+  const float sum = sum_s;
+  for (int t = tid; t < T; t += blockDim.x) sc[t] = __fdiv_rn(sc[t], sum);
+  float acc = 0.f;
+  for (int cc = 0; cc < nvc; cc++) {
+    const int t0 = cc * AP_VC, tc = min(AP_VC, T - t0);
+    cp_async_wait_group<AP_NST - 2>();  // chunk cc has landed
+    __syncthreads();                    // (also orders the p writes before their first use)
+    if (tid < AP_DS) {
+      const float* vbuf = vst + (cc % AP_NST) * AP_VC * AP_DS + tid;
+      const float* pp = sc + t0;
+#pragma unroll 8
+      for (int t = 0; t < tc; t++) acc = __fadd_rn(acc, __fmul_rn(pp[t], vbuf[t * AP_DS]));
+    }
+    __syncthreads();  // stage cc % AP_NST is free again
+    stage_v(cc + AP_NST - 1);
+  }
+  cp_async_wait_all();
+  if (tid < AP_DS) att[(size_t)h * HD + d0 + tid] = acc;
 }
 
 // The same attention for the G = H / KVH query heads that share kv head kh, one CTA per (kv head, token): each K row
