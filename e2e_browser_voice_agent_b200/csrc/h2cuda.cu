@@ -349,7 +349,7 @@ template <int WT, int R>
 void launch_mv_r(int op, const uint8_t* qs, const __half* d, int N, int K, const int8_t* xq, const float* xd,
                  const int4* xs, float* y, const float* bias, cudaStream_t st) {
   const int blocks = (int)(padded_rows(N) / R);
-  const size_t smem = mv_smem_bytes<WT, R>(K);
+  const size_t smem = mv_smem_bytes<WT, R>();
   if (op == OP_STORE) k_mv<WT, R, OP_STORE><<<blocks, 256, smem, st>>>(qs, d, N, K, xq, xd, xs, y, bias);
   else if (op == OP_BIAS) k_mv<WT, R, OP_BIAS><<<blocks, 256, smem, st>>>(qs, d, N, K, xq, xd, xs, y, bias);
   else k_mv<WT, R, OP_ADD><<<blocks, 256, smem, st>>>(qs, d, N, K, xq, xd, xs, y, bias);
@@ -358,11 +358,40 @@ template <int WT>
 bool launch_mv(int op, const uint8_t* qs, const __half* d, int N, int K, const int8_t* xq, const float* xd,
                const int4* xs, float* y, const float* bias, cudaStream_t st) {
   const bool wide = padded_rows(N) / 32 >= 296 && K / 32 <= 256;
-  if ((wide ? mv_smem_bytes<WT, 32>(K) : mv_smem_bytes<WT, 8>(K)) > MV_SMEM) return false;
   if (wide) launch_mv_r<WT, 32>(op, qs, d, N, K, xq, xd, xs, y, bias, st);
   else launch_mv_r<WT, 8>(op, qs, d, N, K, xq, xd, xs, y, bias, st);
   return true;
 }
+// One token on the tensor cores (k_mvt) for matrices of at least 296 groups of 32 rows (gate/up, the output matrix):
+// CTAs of 2 warps x 32 rows with 5-chunk rings of 8 blocks (four CTAs per SM, 18 KB of weights in flight per warp).
+// Returns false for the other matrices (k_mv takes them: their few rows need the blocks of a row spread over many
+// threads) and when the staging does not fit.
+template <int WT, int W, int RG, int NSTG, int CK>
+void launch_mvt_w(int op, const uint8_t* qs, const __half* d, int N, int K, const int8_t* xq, const float* xd,
+                  const int4* xs, float* y, const float* bias, cudaStream_t st) {
+  const int blocks = (int)((padded_rows(N) / (8 * RG) + W - 1) / W);
+  const size_t smem = mt_smem_bytes<WT, W, RG, NSTG, CK>(K);
+  if (op == OP_STORE) k_mvt<WT, W, RG, NSTG, CK, OP_STORE><<<blocks, W * 32, smem, st>>>(qs, d, N, K, xq, xd, xs, y, bias);
+  else if (op == OP_BIAS) k_mvt<WT, W, RG, NSTG, CK, OP_BIAS><<<blocks, W * 32, smem, st>>>(qs, d, N, K, xq, xd, xs, y, bias);
+  else k_mvt<WT, W, RG, NSTG, CK, OP_ADD><<<blocks, W * 32, smem, st>>>(qs, d, N, K, xq, xd, xs, y, bias);
+}
+template <int WT>
+bool launch_mvt(int op, const uint8_t* qs, const __half* d, int N, int K, const int8_t* xq, const float* xd,
+                const int4* xs, float* y, const float* bias, cudaStream_t st) {
+  const bool wide = padded_rows(N) / 32 >= 296;
+  if (!wide || mt_smem_bytes<WT, 2, 4, 5, 8>(K) > MV_SMEM) return false;
+  launch_mvt_w<WT, 2, 4, 5, 8>(op, qs, d, N, K, xq, xd, xs, y, bias, st);
+  return true;
+}
+template <int WT, int W, int RG, int NSTG, int CK>
+cudaError_t mvt_attr() {
+  const int smem = (int)MV_SMEM;
+  cudaError_t c = cudaFuncSetAttribute(k_mvt<WT, W, RG, NSTG, CK, OP_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (c == cudaSuccess) c = cudaFuncSetAttribute(k_mvt<WT, W, RG, NSTG, CK, OP_BIAS>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (c == cudaSuccess) c = cudaFuncSetAttribute(k_mvt<WT, W, RG, NSTG, CK, OP_ADD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  return c;
+}
+
 template <int WT, int R>
 cudaError_t mv2_attr() {
   const int smem = (int)MV_SMEM;
@@ -457,6 +486,7 @@ void matvec_w(int op, const uint8_t* qs, const __half* d, int N, int K, const in
     return;
   }
   if (M == 1) {
+    if (launch_mvt<WT>(op, qs, d, N, K, xq, xd, xs, y, bias, st)) return;
     if (launch_mv<WT>(op, qs, d, N, K, xq, xd, xs, y, bias, st)) return;
     // rows per CTA: the product buffer (rows x blocks x 16 B) small enough for several CTAs per SM
     if (nb <= 64) launch_mv_t<WT, 32, 1>(op, qs, d, N, K, xq, xd, xs, 1, y, ldy, bias, st);
@@ -550,6 +580,8 @@ cudaError_t set_kernel_attrs() {
     c = cudaFuncSetAttribute(k_att_pv<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ap_smem_bytes(MAX_CTX));
   if (c == cudaSuccess)
     c = cudaFuncSetAttribute(k_norm_quant, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)nq_smem_bytes(MAX_DIM));
+  if (c == cudaSuccess) c = mvt_attr<WQ4, 2, 4, 5, 8>();
+  if (c == cudaSuccess) c = mvt_attr<WQ8, 2, 4, 5, 8>();
   if (c == cudaSuccess) c = mv2_attr<WQ4, 32>();
   if (c == cudaSuccess) c = mv2_attr<WQ4, 8>();
   if (c == cudaSuccess) c = mv2_attr<WQ8, 32>();

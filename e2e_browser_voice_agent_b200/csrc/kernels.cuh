@@ -413,22 +413,22 @@ __global__ void __launch_bounds__(256) k_matvec(const uint8_t* __restrict__ qs, 
 // One token's matvec y[n] (op)= W[n] . x (matmul_q4 / dot_q8_q8 with M = 1, kernels.c:121-273), the decode step's
 // hot loop. CTA = R rows of one 32-row group (256 threads), streaming its rows' blocks in chunks of CB = 256 / R
 // blocks (thread (j, r) of a chunk takes block j, row r):
-//   - the token's int8 values, scales and lane sums are staged in shared memory once;
-//   - the weight bytes and fp16 scales of chunk c land in stage c % MV_P of a cp.async ring, MV_P - 1 chunks ahead;
+//   - the weight bytes and fp16 scales of chunk c, and the token's int8 values, scales and lane sums of its blocks,
+//     land in stage c % MV_P of a cp.async ring, MV_P - 1 chunks ahead;
 //   - after the chunk's barrier every thread forms its item's four exact lane products f32(p_l) * (dw * dx) into
 //     the product buffer of the chunk (two, alternating), while threads 0..4R-1 (row r = t / 4, lane l = t % 4)
 //     add the previous chunk's products to their running lane sum in block order;
 //   - at the end ((l0 + l1) + l2) + l3 and the epilogue (put(), kernels.c:190-194).
 // Every product and every sum is the reference's; only the order of independent work differs.
-// dynamic smem: mv_smem_bytes<WT, R>(K).
+// dynamic smem: mv_smem_bytes<WT, R>().
 constexpr int MV_P = 6;
 template <int WT, int R>
-__host__ __device__ constexpr size_t mv_stage_bytes() { return (size_t)(256 / R) * R * (WT == WQ4 ? 16 : 32); }
-template <int WT, int R>
-__host__ __device__ constexpr size_t mv_smem_bytes(int K) {
-  return (size_t)MV_P * (mv_stage_bytes<WT, R>() + 512) + 2 * 256 * 16 + (size_t)K +
-         (((size_t)K / 32 * 4 + 15) & ~(size_t)15) + (WT == WQ4 ? (size_t)K / 32 * 16 : 0);
+__host__ __device__ constexpr size_t mv_stage_bytes() {
+  // weights, fp16 scales, then the token's values (32 B), lane sums (16 B) and scale (4 B) per block
+  return (size_t)256 * (WT == WQ4 ? 16 : 32) + 512 + (size_t)(256 / R) * 52;
 }
+template <int WT, int R>
+__host__ __device__ constexpr size_t mv_smem_bytes() { return (size_t)MV_P * mv_stage_bytes<WT, R>() + 2 * 256 * 16; }
 template <int WT, int R, int OP>
 __global__ void __launch_bounds__(256) k_mv(const uint8_t* __restrict__ qs, const __half* __restrict__ dsc, int N,
                                             int K, const int8_t* __restrict__ xq, const float* __restrict__ xd,
@@ -436,37 +436,41 @@ __global__ void __launch_bounds__(256) k_mv(const uint8_t* __restrict__ qs, cons
                                             const float* __restrict__ bias) {
   constexpr int BB = WT == WQ4 ? 16 : 32;
   constexpr int CB = 256 / R;
-  constexpr int WS = (int)mv_stage_bytes<WT, R>();
+  constexpr int WS = 256 * BB;            // weight bytes per stage
+  constexpr int ST = (int)mv_stage_bytes<WT, R>();
   extern __shared__ __align__(16) uint8_t mvs[];
-  uint8_t* wst = mvs;                                                     // [MV_P][CB][R][BB]
-  __half* sst = reinterpret_cast<__half*>(mvs + MV_P * WS);               // [MV_P][CB][R]
-  float4* prod = reinterpret_cast<float4*>(mvs + MV_P * (WS + 512));      // [2][CB][R]
-  int8_t* xqs = reinterpret_cast<int8_t*>(prod + 2 * 256);
+  float4* prod = reinterpret_cast<float4*>(mvs + MV_P * ST);  // [2][CB][R]
   const int nb = K / 32, nch = (nb + CB - 1) / CB;
-  float* xds = reinterpret_cast<float*>(xqs + K);
-  int4* xss = reinterpret_cast<int4*>(xds + ((nb + 3) & ~3));
   const int tid = threadIdx.x, n0 = blockIdx.x * R, g = n0 >> 5, r0 = n0 & 31;
   const uint8_t* wg = qs + (size_t)g * nb * 32 * BB;
   const __half* dg = dsc + (size_t)g * nb * 32;
-  for (int i = tid; i < K / 16; i += 256) cp_async16(xqs + 16 * i, xq + 16 * i);
-  for (int i = tid; i < nb; i += 256) {
-    cp_async4(xds + i, xd + i);
-    if (WT == WQ4) cp_async16(xss + i, xs + i);
-  }
   const int j = tid / R, r = tid % R;
+  // stage s: [WS] weights [j][r], [512] scales [j][r], [CB * 32] token values, [CB * 16] lane sums, [CB * 4] scales
   auto stage = [&](int c) {  // chunk c into stage c % MV_P (an empty group past the last chunk)
-    const int b = c * CB + j;
-    if (c < nch && b < nb) {
-      const size_t e = (size_t)b * 32 + r0 + r;
-      uint8_t* dst = wst + (c % MV_P) * WS + (j * R + r) * BB;
-      cp_async16(dst, wg + e * BB);
-      if (BB == 32) cp_async16(dst + 16, wg + e * BB + 16);
-      if ((r & 1) == 0) cp_async4(sst + (c % MV_P) * 256 + j * R + r, dg + e);
+    if (c < nch) {
+      uint8_t* st = mvs + (c % MV_P) * ST;
+      const int b = c * CB + j;
+      if (b < nb) {
+        const size_t e = (size_t)b * 32 + r0 + r;
+        uint8_t* dst = st + (j * R + r) * BB;
+        cp_async16(dst, wg + e * BB);
+        if (BB == 32) cp_async16(dst + 16, wg + e * BB + 16);
+        if ((r & 1) == 0) cp_async4(st + WS + (j * R + r) * 2, dg + e);
+      }
+      const int b0 = c * CB;
+      if (tid < 2 * CB) {  // the token's values of the chunk's blocks, 16 bytes per thread
+        if (b0 + tid / 2 < nb) cp_async16(st + WS + 512 + tid * 16, xq + (size_t)b0 * 32 + tid * 16);
+      } else if (tid < 3 * CB) {
+        if (WT == WQ4 && b0 + tid - 2 * CB < nb)
+          cp_async16(st + WS + 512 + CB * 32 + (tid - 2 * CB) * 16, xs + b0 + tid - 2 * CB);
+      } else if (tid < 4 * CB) {
+        if (b0 + tid - 3 * CB < nb) cp_async4(st + WS + 512 + CB * 48 + (tid - 3 * CB) * 4, xd + b0 + tid - 3 * CB);
+      }
     }
     cp_async_commit();
   };
 #pragma unroll
-  for (int c = 0; c < MV_P - 1; c++) stage(c);  // (the first group also carries the token's values)
+  for (int c = 0; c < MV_P - 1; c++) stage(c);
   const int cr = tid >> 2, cl = tid & 3;
   float acc = 0.f;
   for (int c = 0; c <= nch; c++) {
@@ -481,21 +485,21 @@ __global__ void __launch_bounds__(256) k_mv(const uint8_t* __restrict__ qs, cons
     }
     const int b = c * CB + j;
     if (c < nch && b < nb) {
-      const int s = c % MV_P;
-      const uint4 w0 = *reinterpret_cast<const uint4*>(wst + s * WS + (j * R + r) * BB);
-      const float dw = __half2float(sst[s * 256 + j * R + r]);
-      const int4* xp = reinterpret_cast<const int4*>(xqs + b * 32);
+      const uint8_t* st = mvs + (c % MV_P) * ST;
+      const uint4 w0 = *reinterpret_cast<const uint4*>(st + (j * R + r) * BB);
+      const float dw = __half2float(*reinterpret_cast<const __half*>(st + WS + (j * R + r) * 2));
+      const int4* xp = reinterpret_cast<const int4*>(st + WS + 512 + j * 32);
       const int4 x0 = xp[0], x1 = xp[1];
-      const float sc = __fmul_rn(dw, xds[b]);
+      const float sc = __fmul_rn(dw, *reinterpret_cast<const float*>(st + WS + 512 + CB * 48 + j * 4));
       float p0, p1, p2, p3;
       if (WT == WQ4) {
-        const int4 sm = xss[b];
+        const int4 sm = *reinterpret_cast<const int4*>(st + WS + 512 + CB * 32 + j * 16);
         p0 = q4_lane(w0.x, x0.x, x1.x, sm.x);
         p1 = q4_lane(w0.y, x0.y, x1.y, sm.y);
         p2 = q4_lane(w0.z, x0.z, x1.z, sm.z);
         p3 = q4_lane(w0.w, x0.w, x1.w, sm.w);
       } else {
-        const uint4 w1 = *reinterpret_cast<const uint4*>(wst + s * WS + (j * R + r) * BB + 16);
+        const uint4 w1 = *reinterpret_cast<const uint4*>(st + (j * R + r) * BB + 16);
         p0 = magic_to_float(__dp4a((int)w0.x, x0.x, __dp4a((int)w1.x, x1.x, MK_MAGIC)));
         p1 = magic_to_float(__dp4a((int)w0.y, x0.y, __dp4a((int)w1.y, x1.y, MK_MAGIC)));
         p2 = magic_to_float(__dp4a((int)w0.z, x0.z, __dp4a((int)w1.z, x1.z, MK_MAGIC)));
@@ -678,6 +682,160 @@ __device__ __forceinline__ unsigned long long f2_mul(unsigned long long a, unsig
 }
 __device__ __forceinline__ float f2_lo(unsigned long long v) { return __uint_as_float((uint32_t)v); }
 __device__ __forceinline__ float f2_hi(unsigned long long v) { return __uint_as_float((uint32_t)(v >> 32)); }
+
+// One token's matvec on the tensor cores (mma.sync m16n8k32), y[n] (op)= W[n] . x, the decode step's hot loop
+// (matmul_q4 / dot_q8_q8 with M = 1, kernels.c:121-273). Each warp owns 8 RG weight rows and walks their blocks in
+// order; per block and per group of 8 rows one MMA:
+//   - B = the 8 rows' block (k = the permuted byte order: 4t .. 4t+3 and 16+4t .. 16+4t+3 are lane t's bytes of the
+//     two halves; u8 low and high nibbles for Q4_0, s8 for Q8_0), one 32-bit shared load per thread;
+//   - A = the token's int8 block masked per reference lane: row m keeps only lane m's bytes (rows 4..15 zero), so
+//     D[m][n] = lane m's exact integer dot of row n; the accumulator input is MK_MAGIC - 8 x (lane sum) for Q4_0 (the
+//     -8 nibble offset folded in) or MK_MAGIC for Q8_0, so D holds the bit pattern of 12582912 + dot. A, the
+//     accumulator input and the token's block scale are loaded once per block for the RG groups;
+//   - thread t (t < 16) holds lane t / 4 of rows 2 (t % 4) and 2 (t % 4) + 1 of each group and keeps their running
+//     sums in registers: acc += f32(dot) * (dw * dx) in block order; at the end ((l0 + l1) + l2) + l3 across four
+//     threads and the epilogue (put(), kernels.c:190-194).
+// The rows' weight bytes and scales stream through a per-warp cp.async ring of NSTG chunks of CK blocks; the token's
+// values are staged in shared memory once per CTA. CTA: W warps; dynamic smem mt_smem_bytes<WT, W, RG, NSTG, CK>(K).
+template <int WT>
+__host__ __device__ constexpr int mt_bb() { return WT == WQ4 ? 16 : 32; }
+template <int WT, int RG, int NSTG, int CK>
+__host__ __device__ constexpr size_t mt_warp_bytes() { return (size_t)NSTG * CK * 8 * RG * (mt_bb<WT>() + 2); }
+template <int WT, int W, int RG, int NSTG, int CK>
+__host__ __device__ constexpr size_t mt_smem_bytes(int K) {
+  return (size_t)W * mt_warp_bytes<WT, RG, NSTG, CK>() + (size_t)K + (((size_t)K / 32 * 4 + 15) & ~(size_t)15) +
+         (WT == WQ4 ? (size_t)K / 32 * 16 : 0);
+}
+template <int WT, int W, int RG, int NSTG, int CK, int OP>
+__global__ void __launch_bounds__(W * 32) k_mvt(const uint8_t* __restrict__ qs, const __half* __restrict__ dsc, int N,
+                                                int K, const int8_t* __restrict__ xq, const float* __restrict__ xd,
+                                                const int4* __restrict__ xs, float* __restrict__ y,
+                                                const float* __restrict__ bias) {
+  constexpr int BB = mt_bb<WT>();
+  constexpr int RB = 8 * RG * BB;     // weight bytes of the warp's rows per block
+  constexpr int SW = CK * RB;         // weight bytes per stage
+  constexpr int SS = CK * 16 * RG;    // scale bytes per stage (8 RG fp16 per block)
+  static_assert(SW % 512 == 0 && SS % 16 == 0, "stage sizes");
+  extern __shared__ __align__(16) uint8_t mts[];
+  const int nb = K / 32, nch = (nb + CK - 1) / CK;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t* ring = mts + warp * mt_warp_bytes<WT, RG, NSTG, CK>();  // [NSTG][SW], then [NSTG][SS] scales
+  uint8_t* sring = ring + NSTG * SW;
+  int8_t* xqs = reinterpret_cast<int8_t*>(mts + W * mt_warp_bytes<WT, RG, NSTG, CK>());
+  float* xds = reinterpret_cast<float*>(xqs + K);
+  int* xss = reinterpret_cast<int*>(xds + ((nb + 3) & ~3));
+  for (int i = threadIdx.x; i < K / 16; i += W * 32) cp_async16(xqs + 16 * i, xq + 16 * i);
+  for (int i = threadIdx.x; i < nb; i += W * 32) {
+    cp_async4(xds + i, xd + i);
+    if (WT == WQ4) cp_async16(xss + 4 * i, xs + i);
+  }
+  const int n0 = (blockIdx.x * W + warp) * 8 * RG;
+  const bool live = n0 < ((N + 31) & ~31);
+  const int g32 = n0 >> 5, r0 = n0 & 31;
+  const uint8_t* wg = qs + ((size_t)g32 * nb * 32 + r0) * BB;  // block b of the warp's rows: wg + b * 32 * BB
+  const __half* dg = dsc + (size_t)g32 * nb * 32 + r0;          // their scales: dg + b * 32
+  auto stage = [&](int c) {  // chunk c into stage c % NSTG (an empty group past the last chunk)
+    if (live && c < nch) {
+      const int b0 = c * CK;
+      uint8_t* dst = ring + (c % NSTG) * SW;
+#pragma unroll
+      for (int i = 0; i < SW / 16 / 32; i++) {
+        const int pc = lane + 32 * i, bl = pc / (RB / 16);
+        if (b0 + bl < nb) cp_async16(dst + pc * 16, wg + (size_t)(b0 + bl) * 32 * BB + (pc % (RB / 16)) * 16);
+      }
+#pragma unroll
+      for (int i = 0; i < (SS / 16 + 31) / 32; i++) {
+        const int pc = lane + 32 * i, bl = pc / RG;
+        if (pc < SS / 16 && b0 + bl < nb)
+          cp_async16(sring + (c % NSTG) * SS + pc * 16, dg + (size_t)(b0 + bl) * 32 + (pc % RG) * 8);
+      }
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int c = 0; c < NSTG - 1; c++) stage(c);  // (the first group also carries the token's values)
+  cp_async_wait_group<NSTG - 2>();
+  __syncthreads();  // the token's values, staged by all threads, are visible to every warp
+  if (!live) return;
+  // masks instead of branches: A keeps lane m's bytes only in row m (lanes 0, 5, 10, 15), C only in rows 0..3
+  const int tq = lane & 3, lm = (lane >> 2) & 3;
+  const int amask = (lane < 16 && (lane >> 2) == tq) ? -1 : 0;
+  const int cmask = lane < 16 ? -1 : 0;
+  const unsigned long long magic2 = f2(-12582912.0f, -12582912.0f);
+  float acc[RG][2];  // (meaningful in lanes 0..15)
+#pragma unroll
+  for (int g = 0; g < RG; g++) acc[g][0] = acc[g][1] = 0.f;
+  auto block = [&](const uint8_t* ws, const uint8_t* ss, int bl, int b) {
+    const int* xb = reinterpret_cast<const int*>(xqs + b * 32);
+    const int a0 = xb[tq] & amask, a2 = xb[4 + tq] & amask;
+    const int c0 = (WT == WQ4 ? xss[4 * b + lm] : MK_MAGIC) & cmask;
+    const float dx = xds[b];
+    const unsigned long long dx2 = f2(dx, dx);
+#pragma unroll
+    for (int g = 0; g < RG; g++) {
+      uint32_t b0r, b1r;
+      if (WT == WQ4) {
+        const uint32_t w = *reinterpret_cast<const uint32_t*>(ws + bl * RB + g * 128 + 4 * lane);
+        b0r = w & 0x0f0f0f0fu;
+        b1r = (w >> 4) & 0x0f0f0f0fu;
+      } else {
+        const uint8_t* wr = ws + bl * RB + g * 256 + (lane >> 2) * 32 + tq * 4;
+        b0r = *reinterpret_cast<const uint32_t*>(wr);
+        b1r = *reinterpret_cast<const uint32_t*>(wr + 16);
+      }
+      int d0, d1, d2, d3;
+      if (WT == WQ4)
+        asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+            "{%10, %11, %12, %13};"
+            : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3)
+            : "r"(a0), "r"(0), "r"(a2), "r"(0), "r"(b0r), "r"(b1r), "r"(c0), "r"(c0), "r"(0), "r"(0));
+      else
+        asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+            "{%10, %11, %12, %13};"
+            : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3)
+            : "r"(a0), "r"(0), "r"(a2), "r"(0), "r"(b0r), "r"(b1r), "r"(c0), "r"(c0), "r"(0), "r"(0));
+      const float2 dw = __half22float2(*reinterpret_cast<const __half2*>(ss + (bl * RG + g) * 16 + 4 * tq));
+      const unsigned long long p = f2_add(f2(__int_as_float(d0), __int_as_float(d1)), magic2);
+      const unsigned long long q = f2_mul(p, f2_mul(f2(dw.x, dw.y), dx2));
+      // (scalar adds for the running sums: a packed multiply feeding a packed add could become one fused op)
+      acc[g][0] = __fadd_rn(acc[g][0], f2_lo(q));
+      acc[g][1] = __fadd_rn(acc[g][1], f2_hi(q));
+    }
+  };
+  for (int c = 0; c < nch; c++) {
+    if (c > 0) cp_async_wait_group<NSTG - 2>();  // chunk c has landed
+    __syncwarp();
+    stage(c + NSTG - 1);  // into the stage of chunk c - 1 (every lane is past it)
+    const int s = c % NSTG, b0 = c * CK;
+    const uint8_t* ws = ring + s * SW;
+    const uint8_t* ss = sring + s * SS;
+    if (b0 + CK <= nb) {
+#pragma unroll
+      for (int bl = 0; bl < CK; bl++) block(ws, ss, bl, b0 + bl);
+    } else {
+      for (int bl = 0; bl < nb - b0; bl++) block(ws, ss, bl, b0 + bl);
+    }
+  }
+  cp_async_wait_all();
+  // lanes m = 0..3 of rows 2j, 2j+1 of a group sit at threads j, 4 + j, 8 + j, 12 + j
+#pragma unroll
+  for (int g = 0; g < RG; g++) {
+#pragma unroll
+    for (int k = 0; k < 2; k++) {
+      const float a = acc[g][k];
+      const float u1 = __shfl_down_sync(0xffffffffu, a, 4), u2 = __shfl_down_sync(0xffffffffu, a, 8),
+                  u3 = __shfl_down_sync(0xffffffffu, a, 12);
+      const int n = n0 + g * 8 + 2 * lane + k;
+      if (lane < 4 && n < N) {
+        const float v = __fadd_rn(__fadd_rn(__fadd_rn(a, u1), u2), u3);
+        if (OP == OP_ADD) y[n] = __fadd_rn(y[n], v);
+        else if (OP == OP_BIAS) y[n] = __fadd_rn(v, bias[n]);
+        else y[n] = v;
+      }
+    }
+  }
+}
+
 
 template <int WT, int TG, int OP>
 __global__ void __launch_bounds__(256) k_matmul_tc(const uint8_t* __restrict__ qs, const __half* __restrict__ dsc,

@@ -18,13 +18,19 @@ const h2c = require("./build/Release/h2cuda.node");
 const KIND = { qkv: 0, o: 1, gu: 2, down: 3, attn_norm: 4, ffn_norm: 5, bqkv: 6, embd: 7, out: 8, out_norm: 9 };
 const GGML = { F32: 0, Q4_0: 2, Q8_0: 8 };
 
+export const tpUniqueId = () => h2c.tpUniqueId();
+
 export async function createCUDA(gguf, bytes, cfg, opts = {}) {
   const ctx = opts.ctx || 2048;
   const maxSeqs = opts.maxSeqs || 1;
-  const eng = h2c.create(opts.device ?? 0, {
+  const ccfg = {
     dim: cfg.dim, layers: cfg.layers, ffn: cfg.ffn, heads: cfg.heads, kv_heads: cfg.kvHeads, vocab: cfg.vocab,
     ctx, max_chunk: opts.prefillChunk || 16, max_seqs: maxSeqs, eps: cfg.eps, rope_theta: cfg.ropeTheta,
-  });
+  };
+  // opts.tp = {world, rank, id} (id: the Buffer h2c.tpUniqueId() made on rank 0): one rank of a tensor-parallel
+  // group, one process per GPU; every rank loads the same file and makes the same calls
+  const eng = opts.tp ? h2c.createTp(opts.device ?? 0, ccfg, opts.tp.world, opts.tp.rank, opts.tp.id, opts.tp.timeoutMs ?? 0)
+                      : h2c.create(opts.device ?? 0, ccfg);
   const T = gguf.tensors;  // parseGGUF offsets (gguf.js:15-70)
   const need = (name, type) => {
     const t = T[name];

@@ -33,10 +33,7 @@ std::vector<int32_t> ints(const Napi::Value& v) {
 
 int32_t field(const Napi::Object& o, const char* k) { return o.Get(k).As<Napi::Number>().Int32Value(); }
 
-// h2c.create(device, {dim, layers, ffn, heads, kv_heads, vocab, ctx, max_chunk, max_seqs, eps, rope_theta})
-Napi::Value Create(const Napi::CallbackInfo& info) {
-  Napi::Env env = info.Env();
-  const Napi::Object o = info[1].As<Napi::Object>();
+h2c_config config_of(const Napi::Object& o) {
   h2c_config c{};
   c.dim = field(o, "dim");
   c.layers = field(o, "layers");
@@ -49,6 +46,36 @@ Napi::Value Create(const Napi::CallbackInfo& info) {
   c.max_seqs = field(o, "max_seqs");
   c.eps = o.Get("eps").As<Napi::Number>().FloatValue();
   c.rope_theta = o.Get("rope_theta").As<Napi::Number>().DoubleValue();
+  return c;
+}
+
+// h2c.tpUniqueId() -> Buffer(H2C_TP_ID_BYTES): a tensor-parallel group's id, created by rank 0 and handed to the
+// other ranks' processes by the host (e.g. over the page's or the server's own channel)
+Napi::Value TpUniqueId(const Napi::CallbackInfo& info) {
+  Napi::Env env = info.Env();
+  auto buf = Napi::Buffer<uint8_t>::New(env, H2C_TP_ID_BYTES);
+  check(env, nullptr, h2c_tp_unique_id(buf.Data()));
+  return buf;
+}
+
+// h2c.createTp(device, cfg, world, rank, Buffer id, timeoutMs): one rank of a tensor-parallel group (every rank then
+// loads the same full tensors and makes the same calls)
+Napi::Value CreateTp(const Napi::CallbackInfo& info) {
+  Napi::Env env = info.Env();
+  const h2c_config c = config_of(info[1].As<Napi::Object>());
+  auto id = info[4].As<Napi::Buffer<uint8_t>>();
+  if (id.Length() != H2C_TP_ID_BYTES) throw Napi::Error::New(env, "tensor-parallel id has the wrong length");
+  h2c_engine* e = nullptr;
+  check(env, nullptr, h2c_create_tp(info[0].As<Napi::Number>().Int32Value(), &c, info[2].As<Napi::Number>().Int32Value(),
+                                    info[3].As<Napi::Number>().Int32Value(), id.Data(),
+                                    info[5].As<Napi::Number>().Int32Value(), &e));
+  return Napi::External<h2c_engine>::New(env, e);
+}
+
+// h2c.create(device, {dim, layers, ffn, heads, kv_heads, vocab, ctx, max_chunk, max_seqs, eps, rope_theta})
+Napi::Value Create(const Napi::CallbackInfo& info) {
+  Napi::Env env = info.Env();
+  const h2c_config c = config_of(info[1].As<Napi::Object>());
   h2c_engine* e = nullptr;
   check(env, nullptr, h2c_create(info[0].As<Napi::Number>().Int32Value(), &c, &e));
   return Napi::External<h2c_engine>::New(env, e);
@@ -193,6 +220,8 @@ Napi::Value Destroy(const Napi::CallbackInfo& info) {
 
 Napi::Object Init(Napi::Env env, Napi::Object exports) {
   exports.Set("create", Napi::Function::New(env, Create));
+  exports.Set("tpUniqueId", Napi::Function::New(env, TpUniqueId));
+  exports.Set("createTp", Napi::Function::New(env, CreateTp));
   exports.Set("setTensor", Napi::Function::New(env, SetTensor));
   exports.Set("setTensorConcat", Napi::Function::New(env, SetTensorConcat));
   exports.Set("forward", Napi::Function::New(env, Forward));

@@ -40,6 +40,11 @@ CONFIGS: Dict[str, Dict] = {
                  lm_head="tied"),
     "hd128": dict(layers=2, dim=512, heads=4, kv_heads=2, ffn=1024, vocab=2048, rope_theta=1e6, eps=1e-6,
                   lm_head="q4"),
+    # lm_heads of 16384 rows (the wide one-token matvec instances, as the real vocabularies take them)
+    "q8-wide": dict(layers=2, dim=256, heads=4, kv_heads=2, ffn=640, vocab=16384, rope_theta=1e6, eps=1e-6,
+                    lm_head="q8"),
+    "q4-wide": dict(layers=2, dim=512, heads=4, kv_heads=2, ffn=1024, vocab=16384, rope_theta=1e6, eps=1e-6,
+                    lm_head="q4"),
     # the 7B layer shapes (hidden 3584, 28 / 4 heads of 128, FFN 18944, untied lm_head) with 2 layers and a smaller
     # vocabulary, for parity tests against the oracle at the 7B matrix sizes
     "qwen2-7b-2l": dict(layers=2, dim=3584, heads=28, kv_heads=4, ffn=18944, vocab=8192, rope_theta=1e6, eps=1e-6,

@@ -77,7 +77,8 @@ def teacher_forced(model, n_prompt, steps, chunk, ctx=96, seed=0, mode="auto"):
 
 
 @pytest.mark.parametrize("mode", ["graph", "persistent"])
-@pytest.mark.parametrize("model,chunk", [("tiny", 4), ("small", 16), ("gqa7", 3), ("small-q8", 8), ("hd128", 5)])
+@pytest.mark.parametrize("model,chunk", [("tiny", 4), ("small", 16), ("gqa7", 3), ("small-q8", 8), ("hd128", 5),
+                                         ("q8-wide", 8), ("q4-wide", 6)])
 def test_teacher_forced_logits(model, chunk, mode):
     teacher_forced(model, n_prompt=11, steps=8, chunk=chunk, mode=mode)
 
