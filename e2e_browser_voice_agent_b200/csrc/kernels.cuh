@@ -446,17 +446,20 @@ __global__ void __launch_bounds__(256) k_mv(const uint8_t* __restrict__ qs, cons
   const __half* dg = dsc + (size_t)g * nb * 32;
   const int j = tid / R, r = tid % R;
   // stage s: [WS] weights [j][r], [512] scales [j][r], [CB * 32] token values, [CB * 16] lane sums, [CB * 4] scales
-  auto stage = [&](int c) {  // chunk c into stage c % MV_P (an empty group past the last chunk)
-    if (c < nch) {
+  auto stage_w = [&](int c) {  // chunk c's weights and their scales into stage c % MV_P
+    uint8_t* st = mvs + (c % MV_P) * ST;
+    const int b = c * CB + j;
+    if (b < nb) {
+      const size_t e = (size_t)b * 32 + r0 + r;
+      uint8_t* dst = st + (j * R + r) * BB;
+      cp_async16(dst, wg + e * BB);
+      if (BB == 32) cp_async16(dst + 16, wg + e * BB + 16);
+      if ((r & 1) == 0) cp_async4(st + WS + (j * R + r) * 2, dg + e);
+    }
+  };
+  auto stage_x = [&](int c) {  // the token's values of chunk c's blocks into stage c % MV_P
+    {
       uint8_t* st = mvs + (c % MV_P) * ST;
-      const int b = c * CB + j;
-      if (b < nb) {
-        const size_t e = (size_t)b * 32 + r0 + r;
-        uint8_t* dst = st + (j * R + r) * BB;
-        cp_async16(dst, wg + e * BB);
-        if (BB == 32) cp_async16(dst + 16, wg + e * BB + 16);
-        if ((r & 1) == 0) cp_async4(st + WS + (j * R + r) * 2, dg + e);
-      }
       const int b0 = c * CB;
       if (tid < 2 * CB) {  // the token's values of the chunk's blocks, 16 bytes per thread
         if (b0 + tid / 2 < nb) cp_async16(st + WS + 512 + tid * 16, xq + (size_t)b0 * 32 + tid * 16);
@@ -467,14 +470,29 @@ __global__ void __launch_bounds__(256) k_mv(const uint8_t* __restrict__ qs, cons
         if (b0 + tid - 3 * CB < nb) cp_async4(st + WS + 512 + CB * 48 + (tid - 3 * CB) * 4, xd + b0 + tid - 3 * CB);
       }
     }
+  };
+  auto stage = [&](int c) {  // chunk c into stage c % MV_P (an empty group past the last chunk)
+    if (c < nch) {
+      stage_w(c);
+      stage_x(c);
+    }
     cp_async_commit();
   };
+  // the first chunks' weights first, then the token's values of those chunks (one more group)
 #pragma unroll
-  for (int c = 0; c < MV_P - 1; c++) stage(c);
+  for (int c = 0; c < MV_P - 1; c++) {
+    if (c < nch) stage_w(c);
+    cp_async_commit();
+  }
+#pragma unroll
+  for (int c = 0; c < MV_P - 1; c++)
+    if (c < nch) stage_x(c);
+  cp_async_commit();
   const int cr = tid >> 2, cl = tid & 3;
   float acc = 0.f;
   for (int c = 0; c <= nch; c++) {
-    if (c < nch) cp_async_wait_group<MV_P - 2>();  // chunk c has landed
+    if (c == 0) cp_async_wait_all();                // the first chunk and the token's first values
+    else if (c < nch) cp_async_wait_group<MV_P - 2>();  // chunk c has landed
     __syncthreads();
     stage(c + MV_P - 1);  // into the stage chunk c - 1 used (every thread is past it)
     if (c >= 1 && tid < R * 4) {  // the previous chunk's products, in block order
@@ -724,11 +742,6 @@ __global__ void __launch_bounds__(W * 32) k_mvt(const uint8_t* __restrict__ qs, 
   int8_t* xqs = reinterpret_cast<int8_t*>(mts + W * mt_warp_bytes<WT, RG, NSTG, CK>());
   float* xds = reinterpret_cast<float*>(xqs + K);
   int* xss = reinterpret_cast<int*>(xds + ((nb + 3) & ~3));
-  for (int i = threadIdx.x; i < K / 16; i += W * 32) cp_async16(xqs + 16 * i, xq + 16 * i);
-  for (int i = threadIdx.x; i < nb; i += W * 32) {
-    cp_async4(xds + i, xd + i);
-    if (WT == WQ4) cp_async16(xss + 4 * i, xs + i);
-  }
   const int n0 = (blockIdx.x * W + warp) * 8 * RG;
   const bool live = n0 < ((N + 31) & ~31);
   const int g32 = n0 >> 5, r0 = n0 & 31;
@@ -752,9 +765,16 @@ __global__ void __launch_bounds__(W * 32) k_mvt(const uint8_t* __restrict__ qs, 
     }
     cp_async_commit();
   };
+  // the first chunks' weights first, then the token's values (one more group)
 #pragma unroll
-  for (int c = 0; c < NSTG - 1; c++) stage(c);  // (the first group also carries the token's values)
-  cp_async_wait_group<NSTG - 2>();
+  for (int c = 0; c < NSTG - 1; c++) stage(c);
+  for (int i = threadIdx.x; i < K / 16; i += W * 32) cp_async16(xqs + 16 * i, xq + 16 * i);
+  for (int i = threadIdx.x; i < nb; i += W * 32) {
+    cp_async4(xds + i, xd + i);
+    if (WT == WQ4) cp_async16(xss + 4 * i, xs + i);
+  }
+  cp_async_commit();
+  cp_async_wait_all();
   __syncthreads();  // the token's values, staged by all threads, are visible to every warp
   if (!live) return;
   // masks instead of branches: A keeps lane m's bytes only in row m (lanes 0, 5, 10, 15), C only in rows 0..3
