@@ -210,6 +210,18 @@ struct h2c_engine {
   int64_t tp_timeout_ms = 0;     // deadline of NCCL set-up, of enqueueing and of a pass's completion
   std::string tp_fail;           // first NCCL failure inside an enqueue (reported after it)
   int Hl = 0, KVHl = 0, Dl = 0, Fl = 0, Vp = 0, Vl = 0;
+  // one-token passes exchange over peer memory instead: each rank's buffers that receive other ranks' slices are
+  // mapped into every rank (CUDA IPC), a copy kernel writes this rank's slice into each peer's buffer and counts
+  // its arrival there, and waits (bounded) until every peer's slice has arrived here (k_xch)
+  bool xch = false;
+  void* xtab_d = nullptr;                 // XchTab on the device: every rank's buffer bases
+  std::vector<void*> ipc_open;            // peer mappings (closed on destroy)
+  unsigned long long* xcnt = nullptr;     // [0] pass epoch, [1 + slot] arrivals, [4 L + 2] logits epoch
+  int32_t* xerr_h = nullptr;              // mapped pinned: {1, slot, 0, 0} when a wait expired
+  int32_t* xerr_d = nullptr;
+  int8_t* actq = nullptr;                 // the FFN activation received for the down matrix (one token)
+  float* actd = nullptr;
+  int4* acts = nullptr;
   uint8_t* tp_send = nullptr;    // passes of several tokens: this rank's columns, packed, before a gather
   uint8_t* tp_recv = nullptr;    // ... and the gathered [G][M][columns], before they are unpacked into [M][full row]
   size_t tp_stage = 0;           // bytes of tp_send (tp_recv has G times as many)
@@ -723,6 +735,175 @@ void tp_gather(h2c_engine* e, cudaStream_t st, const TpPart* p, int n) {
   }
 }
 
+// ---------------------------------------------------------------- tensor parallelism: the peer-memory exchange
+
+// Buffers of each rank that receive the other ranks' slices in a one-token pass (mapped into every rank).
+enum { XB_X, XB_ATT, XB_ACTQ, XB_ACTD, XB_ACTS, XB_LOGITS, XB_CNT, XB_N };
+constexpr int XCH_MAX_RANKS = 8;
+struct XchTab {
+  uint8_t* base[XB_N][XCH_MAX_RANKS];
+};
+struct XchPart {
+  int buf, bytes;
+  long long off;
+};
+struct XchArgs {
+  const XchTab* tab;
+  XchPart part[3];
+  int nparts, rank, world, slot, epoch_idx;
+  int* err;
+  unsigned long long timeout_ns;
+};
+constexpr unsigned long long XCH_TIMEOUT_NS = 2000000000ull;
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned long long now_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// A new epoch for the exchanges of one one-token pass, or of its logits (every rank runs the same passes, so epochs
+// agree; the logits slot has its own epoch since not every pass computes logits).
+static __global__ void k_xch_step(unsigned long long* epoch) { *epoch += 1; }
+
+// All-gather of this rank's slices over peer memory: every CTA copies its share of the slices into each peer's
+// buffers (the same offsets), then, after a system-scope fence, adds one arrival to each peer's counter of the slot;
+// CTA 0 waits until every peer's CTAs have arrived here for this epoch (acquire), with a time limit: on expiry it
+// records {1, slot} in err and returns (the host reports the failure; no trap).
+static __global__ void __launch_bounds__(256) k_xch(XchArgs a) {
+  const XchTab* t = a.tab;
+  unsigned long long* cnt = reinterpret_cast<unsigned long long*>(t->base[XB_CNT][a.rank]);
+  const unsigned long long epoch = reinterpret_cast<volatile unsigned long long*>(cnt)[a.epoch_idx];
+  for (int p = 0; p < a.world; p++) {
+    if (p == a.rank) continue;
+    for (int q = 0; q < a.nparts; q++) {
+      const XchPart& x = a.part[q];
+      const uint8_t* src = t->base[x.buf][a.rank] + x.off;
+      uint8_t* dst = t->base[x.buf][p] + x.off;
+      if (((x.off | x.bytes) & 15) == 0) {
+        for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < x.bytes / 16; i += gridDim.x * blockDim.x)
+          reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
+      } else {
+        for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < x.bytes / 4; i += gridDim.x * blockDim.x)
+          reinterpret_cast<uint32_t*>(dst)[i] = reinterpret_cast<const uint32_t*>(src)[i];
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    for (int p = 0; p < a.world; p++)
+      if (p != a.rank) atomicAdd_system(reinterpret_cast<unsigned long long*>(t->base[XB_CNT][p]) + 1 + a.slot, 1ull);
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    const unsigned long long want = epoch * (unsigned long long)(a.world - 1) * gridDim.x;
+    const unsigned long long t0 = now_ns();
+    while (ld_acquire_sys(cnt + 1 + a.slot) < want) {
+      if (now_ns() - t0 > a.timeout_ns) {
+        *reinterpret_cast<volatile int*>(a.err + 1) = a.slot;
+        *reinterpret_cast<volatile int*>(a.err) = 1;
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+}
+
+// Enqueue the peer-memory exchange of up to three contiguous slices (this rank's range of one token's vector).
+void tp_xch(h2c_engine* e, cudaStream_t st, std::initializer_list<XchPart> parts, int slot, int epoch_idx = 0) {
+  XchArgs a{};
+  a.tab = reinterpret_cast<const XchTab*>(e->xtab_d);
+  a.nparts = 0;
+  long long total = 0;
+  for (const XchPart& p : parts) {
+    a.part[a.nparts++] = p;
+    total += p.bytes;
+  }
+  a.rank = e->tp_rank;
+  a.world = e->tp_world;
+  a.slot = slot;
+  a.epoch_idx = epoch_idx;
+  a.err = e->xerr_d;
+  a.timeout_ns = XCH_TIMEOUT_NS;
+  const int grid = (int)std::min<long long>(32, std::max<long long>(1, (total + 16383) / 16384));
+  k_xch<<<grid, 256, 0, st>>>(a);
+}
+
+int sync_stream(h2c_engine* e);
+
+// Set up the peer exchange after the communicator: map every rank's receive buffers (IPC handles all-gathered
+// through NCCL) and build the device table. Returns false (the engine keeps NCCL for every pass) when a step fails.
+bool tp_setup_xch(h2c_engine* e, std::string* why) {
+  const int G = e->tp_world, rk = e->tp_rank;
+  const h2c_config& c = e->cfg;
+  if (G > XCH_MAX_RANKS) {
+    *why = "too many ranks";
+    return false;
+  }
+  const int slots = 4 * c.layers + 1;
+  int r = 0;
+  if ((r = dalloc_t(e, &e->xcnt, (size_t)slots + 2)) || (r = dalloc_t(e, &e->actq, (size_t)c.ffn)) ||
+      (r = dalloc_t(e, &e->actd, (size_t)c.ffn / 32 + 4)) || (r = dalloc_t(e, &e->acts, (size_t)c.ffn / 32)) ||
+      (r = dalloc(e, &e->xtab_d, sizeof(XchTab)))) {
+    *why = e->err;
+    return false;
+  }
+  if (cudaHostAlloc(&e->xerr_h, 4 * sizeof(int32_t), cudaHostAllocMapped) != cudaSuccess ||
+      cudaHostGetDevicePointer(reinterpret_cast<void**>(&e->xerr_d), e->xerr_h, 0) != cudaSuccess) {
+    *why = "mapped pinned allocation";
+    return false;
+  }
+  memset(e->xerr_h, 0, 4 * sizeof(int32_t));
+  void* mine[XB_N] = {e->x, e->att, e->actq, e->actd, e->acts, e->logits, e->xcnt};
+  std::vector<cudaIpcMemHandle_t> h((size_t)G * XB_N);
+  for (int b = 0; b < XB_N; b++)
+    if (cudaIpcGetMemHandle(&h[(size_t)rk * XB_N + b], mine[b]) != cudaSuccess) {
+      *why = "cudaIpcGetMemHandle";
+      return false;
+    }
+  // every rank's handles to every rank
+  uint8_t* hd = nullptr;
+  const size_t hb = sizeof(cudaIpcMemHandle_t) * XB_N;
+  if (dalloc(e, reinterpret_cast<void**>(&hd), hb * G) ||
+      cudaMemcpy(hd + hb * rk, &h[(size_t)rk * XB_N], hb, cudaMemcpyHostToDevice) != cudaSuccess) {
+    *why = "handle buffer";
+    return false;
+  }
+  const TpPart hp{hd, hb, 0, 1};
+  tp_gather(e, e->st, &hp, 1);
+  if (!e->tp_fail.empty() || sync_stream(e) != H2C_OK ||
+      cudaMemcpy(h.data(), hd, hb * G, cudaMemcpyDeviceToHost) != cudaSuccess) {
+    *why = "handle exchange: " + (e->tp_fail.empty() ? e->err : e->tp_fail);
+    return false;
+  }
+  XchTab tab{};
+  for (int b = 0; b < XB_N; b++) tab.base[b][rk] = static_cast<uint8_t*>(mine[b]);
+  for (int p = 0; p < G; p++) {
+    if (p == rk) continue;
+    for (int b = 0; b < XB_N; b++) {
+      void* ptr = nullptr;
+      const cudaError_t ce = cudaIpcOpenMemHandle(&ptr, h[(size_t)p * XB_N + b], cudaIpcMemLazyEnablePeerAccess);
+      if (ce != cudaSuccess) {
+        *why = std::string("cudaIpcOpenMemHandle: ") + cudaGetErrorString(ce);
+        return false;
+      }
+      e->ipc_open.push_back(ptr);
+      tab.base[b][p] = static_cast<uint8_t*>(ptr);
+    }
+  }
+  if (cudaMemcpy(e->xtab_d, &tab, sizeof(tab), cudaMemcpyHostToDevice) != cudaSuccess) {
+    *why = "exchange table upload";
+    return false;
+  }
+  e->xch = true;
+  return true;
+}
+
 // Enqueue one pass of M tokens (positions and ids are read from e->prm on the device). logits: compute the
 // last token's logits and the greedy next token into e->next_d. Under tensor parallelism every matrix product
 // computes this rank's rows and an all-gather completes the vector (QKV and attention stay per head: only the
@@ -743,6 +924,10 @@ void enqueue_pass(h2c_engine* e, int M, bool logits, Prof* pf, bool batch = fals
                            {reinterpret_cast<uint8_t*>(e->xd), (size_t)nbl * 4, (size_t)nbf * 4, M},
                            {reinterpret_cast<uint8_t*>(e->xs), (size_t)nbl * 16, (size_t)nbf * 16, M},
                            {reinterpret_cast<uint8_t*>(e->xdT), (size_t)nbl * e->ldT * 4, 0, 1}};
+  // one token under tensor parallelism: the exchanges go through peer memory (k_xch), slots 4 l + {0 attention, 1 x
+  // after O, 2 FFN activation, 3 x after down} and 4 L (logits), under a new epoch
+  const bool px = e->xch && M == 1 && !pf && !batch;
+  if (px) k_xch_step<<<1, 1, 0, st>>>(e->xcnt);
   mark(pf, -1, st);
   k_embed<<<M, 128, 0, st>>>(e->prm, e->embd.qs, e->embd.d, D, e->x);
   mark(pf, 0, st);
@@ -779,7 +964,8 @@ void enqueue_pass(h2c_engine* e, int M, bool logits, Prof* pf, bool batch = fals
     } else {
       k_attention<128><<<dim3(H, M), 128, at_smem_bytes<128>(c.ctx), st>>>(e->prm, e->qkv, QKV, e->kc, e->vc, H, KVH, c.ctx, NL, l, att_r, D);
     }
-    tp_gather(e, st, &g_att, 1);
+    if (px) tp_xch(e, st, {{XB_ATT, H * HD * 4, (long long)rk * H * HD * 4}}, 4 * l);
+    else tp_gather(e, st, &g_att, 1);
     mark(pf, 4, st);
     {
       const int warps = M * (D / 32);
@@ -787,7 +973,8 @@ void enqueue_pass(h2c_engine* e, int M, bool logits, Prof* pf, bool batch = fals
     }
     mark(pf, 5, st);
     matvec(OP_ADD, W.o, e->xq, e->xd, e->xs, M, x_r, D, nullptr, st, mc);
-    tp_gather(e, st, &g_x, 1);
+    if (px) tp_xch(e, st, {{XB_X, Dl * 4, (long long)rk * Dl * 4}}, 4 * l + 1);
+    else tp_gather(e, st, &g_x, 1);
     mark(pf, 6, st);
     k_norm_quant<<<M, NQ_THREADS, nq_smem_bytes(D), st>>>(e->x, 0, W.ffn_norm, D, c.eps, e->xq, e->xd, e->xs, xdT,
                                                          e->ldT);
@@ -796,14 +983,23 @@ void enqueue_pass(h2c_engine* e, int M, bool logits, Prof* pf, bool batch = fals
     mark(pf, 7, st);
     {
       const int warps = M * nbl;
-      k_swiglu_quant<<<(warps + 7) / 8, 256, 0, st>>>(e->gu, Fl, M, e->xq + (size_t)rk * Fl, e->xd + (size_t)rk * nbl,
-                                                      e->xs + (size_t)rk * nbl,
+      int8_t* aq = px ? e->actq : e->xq;  // (the received activation must not share the buffer other stages use)
+      float* ad = px ? e->actd : e->xd;
+      int4* as = px ? e->acts : e->xs;
+      k_swiglu_quant<<<(warps + 7) / 8, 256, 0, st>>>(e->gu, Fl, M, aq + (size_t)rk * Fl, ad + (size_t)rk * nbl,
+                                                      as + (size_t)rk * nbl,
                                                       xdT ? xdT + (size_t)rk * nbl * e->ldT : nullptr, e->ldT, F);
     }
-    tp_gather(e, st, g_act, M > 1 ? 4 : 3);
+    if (px)
+      tp_xch(e, st, {{XB_ACTQ, Fl, (long long)rk * Fl}, {XB_ACTD, nbl * 4, (long long)rk * nbl * 4},
+                     {XB_ACTS, nbl * 16, (long long)rk * nbl * 16}}, 4 * l + 2);
+    else
+      tp_gather(e, st, g_act, M > 1 ? 4 : 3);
     mark(pf, 8, st);
-    matvec(OP_ADD, W.down, e->xq, e->xd, e->xs, M, x_r, D, nullptr, st, mc);
-    tp_gather(e, st, &g_x, 1);
+    if (px) matvec(OP_ADD, W.down, e->actq, e->actd, e->acts, M, x_r, D, nullptr, st, mc);
+    else matvec(OP_ADD, W.down, e->xq, e->xd, e->xs, M, x_r, D, nullptr, st, mc);
+    if (px) tp_xch(e, st, {{XB_X, Dl * 4, (long long)rk * Dl * 4}}, 4 * l + 3);
+    else tp_gather(e, st, &g_x, 1);
     mark(pf, 9, st);
   }
   if (batch) {  // every token of a batched decode step is the last of its sequence: logits and a token for each
@@ -834,7 +1030,11 @@ void enqueue_pass(h2c_engine* e, int M, bool logits, Prof* pf, bool batch = fals
                     1, lg, e->Vl, nullptr, st);
     }
     const TpPart g_lg{reinterpret_cast<uint8_t*>(e->logits), (size_t)e->Vp * 4, 0, 1};
-    tp_gather(e, st, &g_lg, 1);
+    if (px) {
+      k_xch_step<<<1, 1, 0, st>>>(e->xcnt + 4 * NL + 2);
+      tp_xch(e, st, {{XB_LOGITS, e->Vp * 4, (long long)rk * e->Vp * 4}}, 4 * NL, 4 * NL + 2);
+    }
+    else tp_gather(e, st, &g_lg, 1);
     k_argmax1<<<e->am_np, 256, 0, st>>>(e->logits, c.vocab, e->am_v, e->am_i);
     k_argmax2<<<1, 32, 0, st>>>(e->am_v, e->am_i, e->am_np, e->prm, e->toklog, e->cfg.ctx, e->next_d);
     mark(pf, 10, st);
@@ -852,7 +1052,15 @@ int sync_stream(h2c_engine* e) {
   const int64_t t0 = steady_ms();
   for (;;) {
     const cudaError_t q = cudaStreamQuery(e->st);
-    if (q == cudaSuccess) return H2C_OK;
+    if (q == cudaSuccess) {
+      if (e->xch && e->xerr_h[0]) {  // a peer-exchange wait expired: a peer stopped answering
+        const int slot = e->xerr_h[1];
+        e->comm_dead = true;
+        return e->fail(H2C_ERR_TIMEOUT, "peer exchange %d: a peer's slice did not arrive within %llu ms (engine "
+                       "closed for passes)", slot, (unsigned long long)(XCH_TIMEOUT_NS / 1000000));
+      }
+      return H2C_OK;
+    }
     if (q != cudaErrorNotReady) return e->fail(H2C_ERR_CUDA, "stream: %s", cudaGetErrorString(q));
     ncclResult_t a = ncclSuccess;
     if (nccl().async_error(e->comm, &a) == ncclSuccess && a != ncclSuccess && a != ncclInProgress) {
@@ -1528,6 +1736,12 @@ int h2c_create_tp(int device, const h2c_config* cfg, int32_t world, int32_t rank
       return r;
     }
   }
+  std::string why;
+  if (!tp_setup_xch(e, &why)) {
+    g_create_error = "tensor parallelism: peer exchange set-up failed: " + why;
+    h2c_destroy(e);
+    return H2C_ERR_CUDA;
+  }
   *out = e;
   return H2C_OK;
 }
@@ -1954,6 +2168,8 @@ int h2c_destroy(h2c_engine* e) {
   if (e->prm_bh) cudaFreeHost(e->prm_bh);
   if (e->next_bh) cudaFreeHost(e->next_bh);
   if (e->graph) cudaGraphDestroy(e->graph);
+  for (void* p : e->ipc_open) cudaIpcCloseMemHandle(p);
+  if (e->xerr_h) cudaFreeHost(e->xerr_h);
   if (e->comm) {  // after the graphs that hold its collectives; a finalize that does not settle ends in an abort
     const NcclApi& nc = nccl();
     ncclResult_t res = nc.finalize(e->comm);
