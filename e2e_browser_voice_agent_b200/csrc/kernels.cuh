@@ -228,7 +228,7 @@ static __global__ void k_embed(const int32_t* __restrict__ prm, const uint8_t* _
 // chains of the sum of squares (lane l: x[l]^2 + x[l+4]^2 + ... in index order) from 16-byte shared loads, the
 // scale is formed from ((l0 + l1) + l2) + l3, and every warp quantizes 32-value blocks of (x * scale) * w.
 // D a multiple of 32; dynamic smem nq_smem_bytes(D).
-constexpr int NQ_THREADS = 512;
+constexpr int NQ_THREADS = 1024;
 __host__ __device__ constexpr size_t nq_smem_bytes(int D) { return ((size_t)2 * D + 4 * ((size_t)D / 4 + 4)) * 4; }
 static __global__ void __launch_bounds__(NQ_THREADS) k_norm_quant(const float* __restrict__ x, int row0,
                                                                   const float* __restrict__ w, int D, float eps,
