@@ -1161,14 +1161,14 @@ __global__ void __launch_bounds__(128) k_attention(const int32_t* __restrict__ p
 // head and its K and V rows stream through many SMs; the ordered sums stay single chains, so every value is the
 // reference's.
 //   k_att_scores: grid (H, NS): CTA (h, j) computes s_t = (q . k_t in four lane chains of HD/4 products,
-//     ((l0 + l1) + l2) + l3) * (1 / sqrt(HD)) for positions t in chunks j, j + NS, ... of 128 (one position per
+//     ((l0 + l1) + l2) + l3) * (1 / sqrt(HD)) for positions t in chunks j, j + NS, ... of AS_T (one position per
 //     thread, 16 of the K row's 16-byte loads in flight), into S[h][t].
 //   k_att_pv: grid (H, HD / AP_DS): CTA (h, j) takes the max over S[h][0..T), e_t = fast_exp(s_t - max), the sum of
 //     e_t in position order (one chain, from 16-byte shared loads), p_t = e_t / sum, and the AP_DS ordered chains
 //     o[d] = sum_t p_t v_t[d] of its slice of dims (one per thread), whose V columns stream through a shared-memory
 //     ring (cp.async, requested at the start so they arrive during the softmax). Each slice's CTA repeats the softmax
 //     of the head (it is short) instead of waiting on another CTA.
-constexpr int AS_T = 128;  // positions per score chunk (one per thread)
+constexpr int AS_T = 64;   // positions per score chunk (one per thread)
 template <int HD>
 __global__ void __launch_bounds__(AS_T) k_att_scores(const int32_t* __restrict__ prm, const float* __restrict__ qkv,
                                                      const float* __restrict__ kc, int H, int KVH, int ctx,
@@ -1199,7 +1199,7 @@ __global__ void __launch_bounds__(AS_T) k_att_scores(const int32_t* __restrict__
   }
 }
 
-constexpr int AP_DS = 16;   // dims per p.v CTA
+constexpr int AP_DS = 8;    // dims per p.v CTA
 constexpr int AP_VC = 128;  // positions per V stage
 constexpr int AP_NST = 4;   // V stages in flight
 __host__ __device__ constexpr size_t ap_smem_bytes(int ctx) {
