@@ -354,8 +354,9 @@ void launch_mv_t(int op, const uint8_t* qs, const __half* d, int N, int K, const
 }
 
 // One token: k_mv with 32-row CTAs when the matrix has enough rows for two CTAs per SM and rows of at most 256
-// blocks, else 8-row CTAs (more CTAs for short matrices, shorter chunks of long rows). Returns false when the
-// token's staged values do not fit in shared memory (k_matvec then takes the call).
+// blocks, else 8-row CTAs (more CTAs for short matrices, shorter chunks of long rows). Returns false for matrices
+// of many short rows (fewer than 64 blocks, e.g. the 0.5B output matrix: 24.6 us on k_matvec against 35.7 us here,
+// where each CTA's few chunks leave its pipeline unfilled); k_matvec then takes the call.
 constexpr size_t MV_SMEM = 227 * 1024;
 template <int WT, int R>
 void launch_mv_r(int op, const uint8_t* qs, const __half* d, int N, int K, const int8_t* xq, const float* xd,
@@ -369,7 +370,9 @@ void launch_mv_r(int op, const uint8_t* qs, const __half* d, int N, int K, const
 template <int WT>
 bool launch_mv(int op, const uint8_t* qs, const __half* d, int N, int K, const int8_t* xq, const float* xd,
                const int4* xs, float* y, const float* bias, cudaStream_t st) {
-  const bool wide = padded_rows(N) / 32 >= 296 && K / 32 <= 256;
+  const bool many = padded_rows(N) / 32 >= 296;
+  if (many && K / 32 < 64) return false;
+  const bool wide = many && K / 32 <= 256;
   if (wide) launch_mv_r<WT, 32>(op, qs, d, N, K, xq, xd, xs, y, bias, st);
   else launch_mv_r<WT, 8>(op, qs, d, N, K, xq, xd, xs, y, bias, st);
   return true;
@@ -390,7 +393,8 @@ void launch_mvt_w(int op, const uint8_t* qs, const __half* d, int N, int K, cons
 template <int WT>
 bool launch_mvt(int op, const uint8_t* qs, const __half* d, int N, int K, const int8_t* xq, const float* xd,
                 const int4* xs, float* y, const float* bias, cudaStream_t st) {
-  const bool wide = padded_rows(N) / 32 >= 296;
+  // (rows of fewer than 64 blocks, e.g. the 0.5B output matrix, are faster on k_matvec: 24.6 against 32.6 us)
+  const bool wide = padded_rows(N) / 32 >= 296 && K / 32 >= 64;
   if (!wide || mt_smem_bytes<WT, 2, 4, 5, 8>(K) > MV_SMEM) return false;
   launch_mvt_w<WT, 2, 4, 5, 8>(op, qs, d, N, K, xq, xd, xs, y, bias, st);
   return true;

@@ -40,10 +40,10 @@ CONFIGS: Dict[str, Dict] = {
                  lm_head="tied"),
     "hd128": dict(layers=2, dim=512, heads=4, kv_heads=2, ffn=1024, vocab=2048, rope_theta=1e6, eps=1e-6,
                   lm_head="q4"),
-    # lm_heads of 16384 rows (the wide one-token matvec instances, as the real vocabularies take them)
-    "q8-wide": dict(layers=2, dim=256, heads=4, kv_heads=2, ffn=640, vocab=16384, rope_theta=1e6, eps=1e-6,
+    # lm_heads of 16384 rows of 64 blocks (the tensor-core one-token matvec, as the 7B output matrix takes it)
+    "q8-wide": dict(layers=1, dim=2048, heads=16, kv_heads=4, ffn=2048, vocab=16384, rope_theta=1e6, eps=1e-6,
                     lm_head="q8"),
-    "q4-wide": dict(layers=2, dim=512, heads=4, kv_heads=2, ffn=1024, vocab=16384, rope_theta=1e6, eps=1e-6,
+    "q4-wide": dict(layers=1, dim=2048, heads=16, kv_heads=4, ffn=2048, vocab=16384, rope_theta=1e6, eps=1e-6,
                     lm_head="q4"),
     # the 7B layer shapes (hidden 3584, 28 / 4 heads of 128, FFN 18944, untied lm_head) with 2 layers and a smaller
     # vocabulary, for parity tests against the oracle at the 7B matrix sizes
