@@ -131,7 +131,6 @@ struct h2c_engine {
   float* xd = nullptr;
   int4* xs = nullptr;
   float* xdT = nullptr;         // block scales transposed, [max(D, F) / 32][ldT] (tcgen05 matmul)
-  float* att_s = nullptr;       // single-token attention scores [heads][ctx]
   int ldT = 0;
   int* tc5_err = nullptr;       // device: the tcgen05 matmul's failure record
   int32_t* tc5_err_h = nullptr; // pinned copy
@@ -591,9 +590,9 @@ cudaError_t set_kernel_attrs() {
   if (c == cudaSuccess)
     c = cudaFuncSetAttribute(k_attention<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)at_smem_bytes<128>(MAX_CTX));
   if (c == cudaSuccess)
-    c = cudaFuncSetAttribute(k_att_pv<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ap_smem_bytes(MAX_CTX));
+    c = cudaFuncSetAttribute(k_att_cl<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ac_smem_bytes<64>(MAX_CTX));
   if (c == cudaSuccess)
-    c = cudaFuncSetAttribute(k_att_pv<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ap_smem_bytes(MAX_CTX));
+    c = cudaFuncSetAttribute(k_att_cl<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ac_smem_bytes<128>(MAX_CTX));
   if (c == cudaSuccess)
     c = cudaFuncSetAttribute(k_norm_quant, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)nq_smem_bytes(MAX_DIM));
   if (c == cudaSuccess) c = mvt_attr<WQ4, 2, 4, 5, 8>();
@@ -945,17 +944,13 @@ void enqueue_pass(h2c_engine* e, int M, bool logits, Prof* pf, bool batch = fals
     k_rope_kv<<<dim3(((H + KVH) * (HD / 2) + 127) / 128, M), 128, 0, st>>>(e->prm, e->qkv, QKV, e->rope, e->kc, e->vc,
                                                                             H, KVH, HD, c.ctx, NL, l);
     mark(pf, 3, st);
-    if (M == 1) {  // one token: scores over many CTAs per head, then the softmax and p.v chains per slice of dims
-      const int ns = std::min(16, (c.ctx + AS_T - 1) / AS_T);
-      if (HD == 64) {
-        k_att_scores<64><<<dim3(H, ns), AS_T, 0, st>>>(e->prm, e->qkv, e->kc, H, KVH, c.ctx, NL, l, e->att_s);
-        k_att_pv<64><<<dim3(H, 64 / AP_DS), 128, ap_smem_bytes(c.ctx), st>>>(e->prm, e->att_s, e->vc, H, KVH, c.ctx, NL,
-                                                                          l, att_r);
-      } else {
-        k_att_scores<128><<<dim3(H, ns), AS_T, 0, st>>>(e->prm, e->qkv, e->kc, H, KVH, c.ctx, NL, l, e->att_s);
-        k_att_pv<128><<<dim3(H, 128 / AP_DS), 128, ap_smem_bytes(c.ctx), st>>>(e->prm, e->att_s, e->vc, H, KVH, c.ctx,
-                                                                            NL, l, att_r);
-      }
+    if (M == 1) {  // one token: a cluster of CTAs per head (scores shared through distributed shared memory)
+      if (HD == 64)
+        k_att_cl<64><<<H * AC_CL, 128, ac_smem_bytes<64>(c.ctx), st>>>(e->prm, e->qkv, e->kc, e->vc, H, KVH, c.ctx, NL,
+                                                                      l, att_r);
+      else
+        k_att_cl<128><<<H * AC_CL, 128, ac_smem_bytes<128>(c.ctx), st>>>(e->prm, e->qkv, e->kc, e->vc, H, KVH, c.ctx,
+                                                                        NL, l, att_r);
     } else if (attg_ok(H / KVH, HD, c.ctx)) {  // several tokens: one CTA per (kv head, token)
       if (HD == 64)
         k_attention_gqa<64><<<dim3(KVH, M), 256, attg_smem_bytes<64>(H / KVH, c.ctx), st>>>(
@@ -1619,8 +1614,7 @@ int create_engine(int device, const h2c_config* cfg, int G, int rk, h2c_engine**
       (r = dalloc_t(e, &e->toklog, (size_t)c.max_seqs * (c.ctx + 1))) ||
       (r = dalloc_t(e, &e->rope, (size_t)c.ctx * HD)) || (r = dalloc(e, &e->samp, sample_scratch_bytes(P_CAP))) ||
       (r = dalloc_t(e, &e->seeds_d, (size_t)P_CAP)) ||
-      (r = dalloc_t(e, &e->xdT, (size_t)(KQ / 32) * ((MT + 3) / 4 * 4))) || (r = dalloc_t(e, &e->tc5_err, 4)) ||
-      (r = dalloc_t(e, &e->att_s, (size_t)e->Hl * c.ctx)))
+      (r = dalloc_t(e, &e->xdT, (size_t)(KQ / 32) * ((MT + 3) / 4 * 4))) || (r = dalloc_t(e, &e->tc5_err, 4)))
     return bail(r);
   e->ldT = (MT + 3) / 4 * 4;
   if (G > 1 && MT > 1) {  // staging of the gathers of passes of several tokens (the largest of them)

@@ -26,6 +26,7 @@
 //   activations: x [M][D] f32 residual stream; qkv [M][D + 2*KVH*HD]; att [M][D]; gu [M][2F].
 //   KV cache [seq][layer][kv_head][ctx][HD] f32 (the reference's dtype and order, kernels.c:347-348).
 #pragma once
+#include <cooperative_groups.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
 
@@ -1157,34 +1158,60 @@ __global__ void __launch_bounds__(128) k_attention(const int32_t* __restrict__ p
   }
 }
 
-// The single-token attention of the decode step, kernels.c:355-377, split so that many CTAs share the work of one
-// head and its K and V rows stream through many SMs; the ordered sums stay single chains, so every value is the
-// reference's.
-//   k_att_scores: grid (H, NS): CTA (h, j) computes s_t = (q . k_t in four lane chains of HD/4 products,
-//     ((l0 + l1) + l2) + l3) * (1 / sqrt(HD)) for positions t in chunks j, j + NS, ... of AS_T (one position per
-//     thread, 16 of the K row's 16-byte loads in flight), into S[h][t].
-//   k_att_pv: grid (H, HD / AP_DS): CTA (h, j) takes the max over S[h][0..T), e_t = fast_exp(s_t - max), the sum of
-//     e_t in position order (one chain, from 16-byte shared loads), p_t = e_t / sum, and the AP_DS ordered chains
-//     o[d] = sum_t p_t v_t[d] of its slice of dims (one per thread), whose V columns stream through a shared-memory
-//     ring (cp.async, requested at the start so they arrive during the softmax). Each slice's CTA repeats the softmax
-//     of the head (it is short) instead of waiting on another CTA.
-constexpr int AS_T = 64;   // positions per score chunk (one per thread)
+// Single-token attention, kernels.c:355-377: V rows stream through a shared-memory ring of AP_NST chunks of AP_VC
+// positions (cp.async).
+constexpr int AP_VC = 128;  // positions per V stage
+constexpr int AP_NST = 4;   // V stages in flight
+
+// The attention of the decode step for one token: a cluster of AC_CL CTAs per head. CTA r of head h computes the
+// scores of positions [r T / AC_CL, (r + 1) T / AC_CL) and stores each into every CTA of the cluster (distributed
+// shared memory), so after the cluster barrier every CTA holds all T scores; each then takes the max, the
+// exponentials, the ordered sum and p = e / sum itself, and runs the ordered p.v chains of its HD / AC_CL dims with V
+// columns from the cp.async ring requested at the start. The two ordered sums stay single chains (bit-exact); the
+// scores need no round trip through global memory.
+// grid (H x AC_CL), 128 threads, dynamic smem ac_smem_bytes<HD>(ctx).
+constexpr int AC_CL = 8;
 template <int HD>
-__global__ void __launch_bounds__(AS_T) k_att_scores(const int32_t* __restrict__ prm, const float* __restrict__ qkv,
-                                                     const float* __restrict__ kc, int H, int KVH, int ctx,
-                                                     int layers, int layer, float* __restrict__ S) {
+__host__ __device__ constexpr size_t ac_smem_bytes(int ctx) {
+  return ((size_t)((ctx + 3) & ~3) + (size_t)AP_NST * AP_VC * (HD / AC_CL)) * 4;
+}
+template <int HD>
+__global__ void __cluster_dims__(AC_CL, 1, 1) __launch_bounds__(128)
+    k_att_cl(const int32_t* __restrict__ prm, const float* __restrict__ qkv, const float* __restrict__ kc,
+             const float* __restrict__ vc, int H, int KVH, int ctx, int layers, int layer, float* __restrict__ att) {
+  namespace cg = cooperative_groups;
+  constexpr int DS = HD / AC_CL;
+  cg::cluster_group cl = cg::this_cluster();
+  extern __shared__ __align__(16) float sc[];
+  float* vst = sc + ((ctx + 3) & ~3);  // [AP_NST][AP_VC][DS]
   __shared__ float q_s[HD];
-  const int h = blockIdx.x, tid = threadIdx.x;
+  __shared__ float red[4];
+  __shared__ float sum_s;
+  const int h = blockIdx.x / AC_CL, rk = (int)cl.block_rank(), tid = threadIdx.x;
   const int T = tok_pos(prm, 0) + 1, seq = tok_seq(prm, 0);
   const int kh = h / (H / KVH);
-  if ((int)blockIdx.y * AS_T >= T) return;
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
-  for (int i = tid; i < HD; i += AS_T) q_s[i] = qkv[(size_t)h * HD + i];
-  __syncthreads();
-  const float* kb = kc + (((size_t)seq * layers + layer) * KVH + kh) * (size_t)ctx * HD;
-  for (int c = blockIdx.y; c * AS_T < T; c += gridDim.y) {
-    const int t = c * AS_T + tid;
-    if (t >= T) break;
+  const size_t cbase = (((size_t)seq * layers + layer) * KVH + kh) * (size_t)ctx * HD;
+  const float* kb = kc + cbase;
+  const float* vb = vc + cbase + rk * DS;
+  const int nvc = (T + AP_VC - 1) / AP_VC;
+  auto stage_v = [&](int c) {  // V columns of this CTA's dims for chunk c into stage c % AP_NST
+    if (c < nvc) {
+      const int t0 = c * AP_VC, tc = min(AP_VC, T - t0);
+      float* dst = vst + (c % AP_NST) * AP_VC * DS;
+      for (int i = tid; i < tc * (DS / 4); i += blockDim.x) {
+        const int t = i / (DS / 4), q = i % (DS / 4);
+        cp_async16(dst + t * DS + 4 * q, vb + (size_t)(t0 + t) * HD + 4 * q);
+      }
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int c = 0; c < AP_NST - 1; c++) stage_v(c);
+  for (int i = tid; i < HD; i += blockDim.x) q_s[i] = qkv[(size_t)h * HD + i];
+  cl.sync();  // every CTA of the cluster is running (its shared memory can be written) and q_s is in place
+  const int t0 = (int)((long long)rk * T / AC_CL), t1 = (int)((long long)(rk + 1) * T / AC_CL);
+  for (int t = t0 + tid; t < t1; t += blockDim.x) {
     const float4* kr = reinterpret_cast<const float4*>(kb + (size_t)t * HD);
     float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll 16
@@ -1195,49 +1222,13 @@ __global__ void __launch_bounds__(AS_T) k_att_scores(const int32_t* __restrict__
       s2 = __fadd_rn(s2, __fmul_rn(q_s[4 * i + 2], k4.z));
       s3 = __fadd_rn(s3, __fmul_rn(q_s[4 * i + 3], k4.w));
     }
-    S[(size_t)h * ctx + t] = __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(s0, s1), s2), s3), scale);
-  }
-}
-
-constexpr int AP_DS = 8;    // dims per p.v CTA
-constexpr int AP_VC = 128;  // positions per V stage
-constexpr int AP_NST = 4;   // V stages in flight
-__host__ __device__ constexpr size_t ap_smem_bytes(int ctx) {
-  return ((size_t)((ctx + 3) & ~3) + (size_t)AP_NST * AP_VC * AP_DS) * 4;
-}
-template <int HD>
-__global__ void __launch_bounds__(128) k_att_pv(const int32_t* __restrict__ prm, const float* __restrict__ S,
-                                                const float* __restrict__ vc, int H, int KVH, int ctx, int layers,
-                                                int layer, float* __restrict__ att) {
-  extern __shared__ __align__(16) float sc[];
-  float* vst = sc + ((ctx + 3) & ~3);  // [AP_NST][AP_VC][AP_DS]
-  __shared__ float red[4];
-  __shared__ float sum_s;
-  const int h = blockIdx.x, d0 = blockIdx.y * AP_DS, tid = threadIdx.x;
-  const int T = tok_pos(prm, 0) + 1, seq = tok_seq(prm, 0);
-  const int kh = h / (H / KVH);
-  const float* vb = vc + (((size_t)seq * layers + layer) * KVH + kh) * (size_t)ctx * HD + d0;
-  const int nvc = (T + AP_VC - 1) / AP_VC;
-  auto stage_v = [&](int c) {  // V columns d0..d0+AP_DS of chunk c into stage c % AP_NST (an empty group past the end)
-    if (c < nvc) {
-      const int t0 = c * AP_VC, tc = min(AP_VC, T - t0);
-      float* dst = vst + (c % AP_NST) * AP_VC * AP_DS;
-      for (int i = tid; i < tc * (AP_DS / 4); i += blockDim.x) {
-        const int t = i / (AP_DS / 4), q = i % (AP_DS / 4);
-        cp_async16(dst + t * AP_DS + 4 * q, vb + (size_t)(t0 + t) * HD + 4 * q);
-      }
-    }
-    cp_async_commit();
-  };
+    const float v = __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(s0, s1), s2), s3), scale);
 #pragma unroll
-  for (int c = 0; c < AP_NST - 1; c++) stage_v(c);
-  const float* Sh = S + (size_t)h * ctx;
-  float mx = -1e30f;
-  for (int t = tid; t < T; t += blockDim.x) {
-    const float v = Sh[t];
-    sc[t] = v;
-    mx = fmaxf(mx, v);
+    for (int r = 0; r < AC_CL; r++) cl.map_shared_rank(sc, r)[t] = v;
   }
+  cl.sync();  // all T scores in every CTA (no shared memory of another CTA is touched after this)
+  float mx = -1e30f;
+  for (int t = tid; t < T; t += blockDim.x) mx = fmaxf(mx, sc[t]);
   mx = warp_max(mx);
   if ((tid & 31) == 0) red[tid >> 5] = mx;
   __syncthreads();
@@ -1260,20 +1251,20 @@ __global__ void __launch_bounds__(128) k_att_pv(const int32_t* __restrict__ prm,
   for (int t = tid; t < T; t += blockDim.x) sc[t] = __fdiv_rn(sc[t], sum);
   float acc = 0.f;
   for (int cc = 0; cc < nvc; cc++) {
-    const int t0 = cc * AP_VC, tc = min(AP_VC, T - t0);
+    const int c0 = cc * AP_VC, tc = min(AP_VC, T - c0);
     cp_async_wait_group<AP_NST - 2>();  // chunk cc has landed
     __syncthreads();                    // (also orders the p writes before their first use)
-    if (tid < AP_DS) {
-      const float* vbuf = vst + (cc % AP_NST) * AP_VC * AP_DS + tid;
-      const float* pp = sc + t0;
+    if (tid < DS) {
+      const float* vbuf = vst + (cc % AP_NST) * AP_VC * DS + tid;
+      const float* pp = sc + c0;
 #pragma unroll 8
-      for (int t = 0; t < tc; t++) acc = __fadd_rn(acc, __fmul_rn(pp[t], vbuf[t * AP_DS]));
+      for (int t = 0; t < tc; t++) acc = __fadd_rn(acc, __fmul_rn(pp[t], vbuf[t * DS]));
     }
     __syncthreads();  // stage cc % AP_NST is free again
     stage_v(cc + AP_NST - 1);
   }
   cp_async_wait_all();
-  if (tid < AP_DS) att[(size_t)h * HD + d0 + tid] = acc;
+  if (tid < DS) att[(size_t)h * HD + rk * DS + tid] = acc;
 }
 
 // The same attention for the G = H / KVH query heads that share kv head kh, one CTA per (kv head, token): each K row
