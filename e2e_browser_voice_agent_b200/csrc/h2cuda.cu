@@ -590,9 +590,17 @@ cudaError_t set_kernel_attrs() {
   if (c == cudaSuccess)
     c = cudaFuncSetAttribute(k_attention<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)at_smem_bytes<128>(MAX_CTX));
   if (c == cudaSuccess)
-    c = cudaFuncSetAttribute(k_att_cl<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ac_smem_bytes<64>(MAX_CTX));
+    c = cudaFuncSetAttribute(k_att_cl<64, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)ac_smem_bytes<64>(MAX_CTX));
   if (c == cudaSuccess)
-    c = cudaFuncSetAttribute(k_att_cl<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ac_smem_bytes<128>(MAX_CTX));
+    c = cudaFuncSetAttribute(k_att_cl<64, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)ac_smem_bytes<64>(MAX_CTX));
+  if (c == cudaSuccess)
+    c = cudaFuncSetAttribute(k_att_cl<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)ac_smem_bytes<128>(MAX_CTX));
+  if (c == cudaSuccess)
+    c = cudaFuncSetAttribute(k_att_cl<128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)ac_smem_bytes<128>(MAX_CTX));
   if (c == cudaSuccess)
     c = cudaFuncSetAttribute(k_norm_quant, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)nq_smem_bytes(MAX_DIM));
   if (c == cudaSuccess) c = mvt_attr<WQ4, 2, 4, 5, 8>();
@@ -944,13 +952,24 @@ void enqueue_pass(h2c_engine* e, int M, bool logits, Prof* pf, bool batch = fals
     k_rope_kv<<<dim3(((H + KVH) * (HD / 2) + 127) / 128, M), 128, 0, st>>>(e->prm, e->qkv, QKV, e->rope, e->kc, e->vc,
                                                                             H, KVH, HD, c.ctx, NL, l);
     mark(pf, 3, st);
-    if (M == 1) {  // one token: a cluster of CTAs per head (scores shared through distributed shared memory)
-      if (HD == 64)
-        k_att_cl<64><<<H * AC_CL, 128, ac_smem_bytes<64>(c.ctx), st>>>(e->prm, e->qkv, e->kc, e->vc, H, KVH, c.ctx, NL,
-                                                                      l, att_r);
+    // one token: a cluster of CTAs per head (scores shared through distributed shared memory); on one GPU it also
+    // quantizes its output for the O matrix (k_quant below is then skipped)
+    const bool fq = M == 1 && e->tp_world == 1;
+    if (M == 1) {
+      if (HD == 64 && fq)
+        k_att_cl<64, true><<<H * AC_CL, 128, ac_smem_bytes<64>(c.ctx), st>>>(e->prm, e->qkv, e->kc, e->vc, H, KVH, c.ctx,
+                                                                            NL, l, att_r, e->xq, e->xd, e->xs);
+      else if (HD == 64)
+        k_att_cl<64, false><<<H * AC_CL, 128, ac_smem_bytes<64>(c.ctx), st>>>(e->prm, e->qkv, e->kc, e->vc, H, KVH,
+                                                                             c.ctx, NL, l, att_r, nullptr, nullptr,
+                                                                             nullptr);
+      else if (fq)
+        k_att_cl<128, true><<<H * AC_CL, 128, ac_smem_bytes<128>(c.ctx), st>>>(e->prm, e->qkv, e->kc, e->vc, H, KVH,
+                                                                              c.ctx, NL, l, att_r, e->xq, e->xd, e->xs);
       else
-        k_att_cl<128><<<H * AC_CL, 128, ac_smem_bytes<128>(c.ctx), st>>>(e->prm, e->qkv, e->kc, e->vc, H, KVH, c.ctx,
-                                                                        NL, l, att_r);
+        k_att_cl<128, false><<<H * AC_CL, 128, ac_smem_bytes<128>(c.ctx), st>>>(e->prm, e->qkv, e->kc, e->vc, H, KVH,
+                                                                               c.ctx, NL, l, att_r, nullptr, nullptr,
+                                                                               nullptr);
     } else if (attg_ok(H / KVH, HD, c.ctx)) {  // several tokens: one CTA per (kv head, token)
       if (HD == 64)
         k_attention_gqa<64><<<dim3(KVH, M), 256, attg_smem_bytes<64>(H / KVH, c.ctx), st>>>(
@@ -966,7 +985,7 @@ void enqueue_pass(h2c_engine* e, int M, bool logits, Prof* pf, bool batch = fals
     if (px) tp_xch(e, st, {{XB_ATT, H * HD * 4, (long long)rk * H * HD * 4}}, 4 * l);
     else tp_gather(e, st, &g_att, 1);
     mark(pf, 4, st);
-    {
+    if (!fq) {
       const int warps = M * (D / 32);
       k_quant<<<(warps + 7) / 8, 256, 0, st>>>(e->att, D, M, e->xq, e->xd, e->xs, xdT, e->ldT);
     }

@@ -1169,16 +1169,20 @@ constexpr int AP_NST = 4;   // V stages in flight
 // exponentials, the ordered sum and p = e / sum itself, and runs the ordered p.v chains of its HD / AC_CL dims with V
 // columns from the cp.async ring requested at the start. The two ordered sums stay single chains (bit-exact); the
 // scores need no round trip through global memory.
+// QNT: instead of writing the attention output, quantize it (the input of the O matrix, kernels.c:379): the CTAs of
+// each 32-value block send their values to the block's first CTA (distributed shared memory), which quantizes it
+// with one warp (quant_block_redux: the int8 values, the scale and the lane sums of block (h HD + r HD/8) / 32).
 // grid (H x AC_CL), 128 threads, dynamic smem ac_smem_bytes<HD>(ctx).
 constexpr int AC_CL = 8;
 template <int HD>
 __host__ __device__ constexpr size_t ac_smem_bytes(int ctx) {
   return ((size_t)((ctx + 3) & ~3) + (size_t)AP_NST * AP_VC * (HD / AC_CL)) * 4;
 }
-template <int HD>
+template <int HD, bool QNT>
 __global__ void __cluster_dims__(AC_CL, 1, 1) __launch_bounds__(128)
     k_att_cl(const int32_t* __restrict__ prm, const float* __restrict__ qkv, const float* __restrict__ kc,
-             const float* __restrict__ vc, int H, int KVH, int ctx, int layers, int layer, float* __restrict__ att) {
+             const float* __restrict__ vc, int H, int KVH, int ctx, int layers, int layer, float* __restrict__ att,
+             int8_t* __restrict__ xq, float* __restrict__ xd, int4* __restrict__ xs) {
   namespace cg = cooperative_groups;
   constexpr int DS = HD / AC_CL;
   cg::cluster_group cl = cg::this_cluster();
@@ -1264,7 +1268,19 @@ __global__ void __cluster_dims__(AC_CL, 1, 1) __launch_bounds__(128)
     stage_v(cc + AP_NST - 1);
   }
   cp_async_wait_all();
-  if (tid < DS) att[(size_t)h * HD + rk * DS + tid] = acc;
+  if (!QNT) {
+    if (tid < DS) att[(size_t)h * HD + rk * DS + tid] = acc;
+    return;
+  }
+  __shared__ float ob[32];
+  constexpr int PER = 32 / DS;  // CTAs per 32-value block
+  const int lead = rk - rk % PER;
+  if (tid < DS) cl.map_shared_rank(ob, lead)[(rk % PER) * DS + tid] = acc;
+  cl.sync();
+  if (rk % PER == 0 && tid < 32) {
+    const int b = (h * HD + rk * DS) / 32;
+    quant_block_redux(ob[tid], tid, xq + (size_t)b * 32, xd + b, xs + b, nullptr);
+  }
 }
 
 // The same attention for the G = H / KVH query heads that share kv head kh, one CTA per (kv head, token): each K row
