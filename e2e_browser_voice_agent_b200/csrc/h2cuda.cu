@@ -20,6 +20,7 @@
 #include "../../include/h2cuda.h"
 #include "decode_mk.cuh"
 #include "kernels.cuh"
+#include "prompt_att.cuh"
 #include "sample.cuh"
 #include "tc5.cuh"
 
@@ -34,6 +35,8 @@ thread_local std::string g_create_error;
 // for passes of TC5_MIN_TOKENS or more tokens and the mma.sync form below (measured on B200: at 32 tokens the
 // mma.sync form is 1.2-2x faster, from 64 tokens on the tcgen05 form is as fast or up to 1.8x faster).
 constexpr int TC5_MIN_TOKENS = 64;
+// Prompt passes of this many tokens or more (one sequence) take the tiled prompt attention (prompt_att.cuh).
+constexpr int PF_MIN_TOKENS = 32;
 std::atomic<int> g_mm_kind{H2C_MATMUL_AUTO};
 bool use_tc5(int M) {
   const int k = g_mm_kind.load(std::memory_order_relaxed);
@@ -132,6 +135,9 @@ struct h2c_engine {
   int4* xs = nullptr;
   float* xdT = nullptr;         // block scales transposed, [max(D, F) / 32][ldT] (tcgen05 matmul)
   int ldT = 0;
+  float* pf_s = nullptr;        // prompt attention: scores / exponentials of a pass (prompt_att.cuh), pf_bytes
+  float* pf_sum = nullptr;      // and the rows' sums, [heads x max_chunk]
+  size_t pf_bytes = 0;          // 0: prompt passes take the per-token attention
   int* tc5_err = nullptr;       // device: the tcgen05 matmul's failure record
   int32_t* tc5_err_h = nullptr; // pinned copy
   bool tc5_used = false;        // a pass of the current call took the tcgen05 matmul (its record is copied back)
@@ -609,6 +615,10 @@ cudaError_t set_kernel_attrs() {
   if (c == cudaSuccess) c = mv2_attr<WQ4, 8>();
   if (c == cudaSuccess) c = mv2_attr<WQ8, 32>();
   if (c == cudaSuccess) c = mv2_attr<WQ8, 8>();
+  if (c == cudaSuccess) c = cudaFuncSetAttribute(k_pf_scores<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, pf_scores_smem<64>());
+  if (c == cudaSuccess) c = cudaFuncSetAttribute(k_pf_scores<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, pf_scores_smem<128>());
+  if (c == cudaSuccess) c = cudaFuncSetAttribute(k_pf_pv<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, pf_pv_smem<64>());
+  if (c == cudaSuccess) c = cudaFuncSetAttribute(k_pf_pv<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, pf_pv_smem<128>());
   if (c == cudaSuccess) c = tc5_set_attrs();
   return c;
 }
@@ -915,11 +925,43 @@ bool tp_setup_xch(h2c_engine* e, std::string* why) {
   return true;
 }
 
+// Attention of a prompt pass of M tokens of sequence seq at positions pos0 .. pos0+M-1 (prompt_att.cuh): scores,
+// softmax and p.v over e->pf_s, in query blocks whose score rows fit the buffer. Output rows at att_r (stride D).
+void launch_prompt_attention(h2c_engine* e, int M, int pos0, int seq, int layer, float* att_r, cudaStream_t st) {
+  const h2c_config& c = e->cfg;
+  const int H = e->Hl, KVH = e->KVHl, HD = e->HD, G = H / KVH, QKV = e->QKV, NL = c.layers, D = c.dim;
+  for (int q0 = 0; q0 < M;) {
+    const int P0 = pos0 + q0, left = M - q0;
+    const size_t per = (size_t)H * 4 * (size_t)((P0 + left + 3) & ~3);
+    const int Mq = (int)std::min<size_t>((size_t)left, e->pf_bytes / per);  // >= 1: the buffer holds one full row
+    const int ldS = (P0 + Mq + 3) & ~3, R = G * Mq;
+    const float* q = e->qkv + (size_t)q0 * QKV;
+    float* o = att_r + (size_t)q0 * D;
+    const dim3 gs((P0 + Mq + PF_TB - 1) / PF_TB, (R + PF_RB - 1) / PF_RB, KVH);
+    const int soft_grid = (KVH * R + PF_SR - 1) / PF_SR;
+    if (HD == 64) {
+      k_pf_scores<64><<<gs, 256, pf_scores_smem<64>(), st>>>(q, QKV, e->kc, H, KVH, c.ctx, NL, layer, seq, P0, Mq,
+                                                              e->pf_s, ldS);
+      k_pf_soft<<<soft_grid, 256, 0, st>>>(e->pf_s, ldS, KVH * R, R, G, P0, e->pf_sum);
+      k_pf_pv<64><<<dim3((R + pf_pv_rows<64>() - 1) / pf_pv_rows<64>(), KVH), 128, pf_pv_smem<64>(), st>>>(
+          e->pf_s, ldS, e->pf_sum, e->vc, H, KVH, c.ctx, NL, layer, seq, P0, Mq, o, D);
+    } else {
+      k_pf_scores<128><<<gs, 256, pf_scores_smem<128>(), st>>>(q, QKV, e->kc, H, KVH, c.ctx, NL, layer, seq, P0, Mq,
+                                                               e->pf_s, ldS);
+      k_pf_soft<<<soft_grid, 256, 0, st>>>(e->pf_s, ldS, KVH * R, R, G, P0, e->pf_sum);
+      k_pf_pv<128><<<dim3((R + pf_pv_rows<128>() - 1) / pf_pv_rows<128>(), KVH), 128, pf_pv_smem<128>(), st>>>(
+          e->pf_s, ldS, e->pf_sum, e->vc, H, KVH, c.ctx, NL, layer, seq, P0, Mq, o, D);
+    }
+    q0 += Mq;
+  }
+}
+
 // Enqueue one pass of M tokens (positions and ids are read from e->prm on the device). logits: compute the
 // last token's logits and the greedy next token into e->next_d. Under tensor parallelism every matrix product
 // computes this rank's rows and an all-gather completes the vector (QKV and attention stay per head: only the
-// attention output is gathered).
-void enqueue_pass(h2c_engine* e, int M, bool logits, Prof* pf, bool batch = false) {
+// attention output is gathered). pos0 / seq: the pass's first position and its sequence when the host knows them
+// (prompt passes), else -1.
+void enqueue_pass(h2c_engine* e, int M, bool logits, Prof* pf, bool batch = false, int pos0 = -1, int seq = -1) {
   const h2c_config& c = e->cfg;
   const int D = c.dim, F = c.ffn, H = e->Hl, KVH = e->KVHl, HD = e->HD, QKV = e->QKV, NL = c.layers;
   const int rk = e->tp_rank, Dl = e->Dl, Fl = e->Fl, nbf = F / 32, nbl = Fl / 32;
@@ -970,6 +1012,8 @@ void enqueue_pass(h2c_engine* e, int M, bool logits, Prof* pf, bool batch = fals
         k_att_cl<128, false><<<H * AC_CL, 128, ac_smem_bytes<128>(c.ctx), st>>>(e->prm, e->qkv, e->kc, e->vc, H, KVH,
                                                                                c.ctx, NL, l, att_r, nullptr, nullptr,
                                                                                nullptr);
+    } else if (!batch && pos0 >= 0 && M >= PF_MIN_TOKENS && e->pf_bytes) {  // a prompt pass: tiled over tokens
+      launch_prompt_attention(e, M, pos0, seq, l, att_r, st);
     } else if (attg_ok(H / KVH, HD, c.ctx)) {  // several tokens: one CTA per (kv head, token)
       if (HD == 64)
         k_attention_gqa<64><<<dim3(KVH, M), 256, attg_smem_bytes<64>(H / KVH, c.ctx), st>>>(
@@ -1537,7 +1581,7 @@ int run_forward(h2c_engine* e, int seq, const int32_t* ids, int32_t n, int32_t p
       }
       CUDA_TRY(e, cudaGraphLaunch(e->gexec, e->st));
     } else {
-      enqueue_pass(e, mlen, last, pf);
+      enqueue_pass(e, mlen, last, pf, false, pos + c0, seq);
       if ((r = tp_enqueue_status(e))) return r;
       CUDA_TRY(e, cudaGetLastError());
       if ((r = tc5_enqueue_check(e))) return r;
@@ -1636,6 +1680,21 @@ int create_engine(int device, const h2c_config* cfg, int G, int rk, h2c_engine**
       (r = dalloc_t(e, &e->xdT, (size_t)(KQ / 32) * ((MT + 3) / 4 * 4))) || (r = dalloc_t(e, &e->tc5_err, 4)))
     return bail(r);
   e->ldT = (MT + 3) / 4 * 4;
+  // prompt attention (prompt_att.cuh) for passes of PF_MIN_TOKENS or more: scores of up to max_chunk tokens x all
+  // positions, within a cap (H2C_PROMPT_SCORES_MB, default 256 MB); longer passes run in several query blocks
+  if (MT >= PF_MIN_TOKENS && (HD == 64 || HD == 128)) {
+    size_t cap = (size_t)256 << 20;
+    if (const char* v = getenv("H2C_PROMPT_SCORES_MB")) {
+      const long mb = atol(v);
+      if (mb > 0) cap = (size_t)mb << 20;
+    }
+    const size_t row = (size_t)e->Hl * 4 * (size_t)((c.ctx + 3) & ~3);  // one token's score rows at full context
+    e->pf_bytes = std::min(row * MT, cap);
+    if (e->pf_bytes < row) e->pf_bytes = 0;
+    if (e->pf_bytes && ((r = dalloc(e, reinterpret_cast<void**>(&e->pf_s), e->pf_bytes)) ||
+                        (r = dalloc_t(e, &e->pf_sum, (size_t)e->Hl * MT))))
+      return bail(r);
+  }
   if (G > 1 && MT > 1) {  // staging of the gathers of passes of several tokens (the largest of them)
     const size_t nbl = (size_t)e->Fl / 32;
     const TpPart act[3] = {{nullptr, (size_t)e->Fl, 0, MT}, {nullptr, nbl * 4, 0, MT}, {nullptr, nbl * 16, 0, MT}};

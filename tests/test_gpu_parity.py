@@ -432,28 +432,59 @@ def test_multi_session_c4_shape():
 
 
 def test_long_context_c3_prompt_4096():
-    """The long-context configuration at its real size: a 4096-token prompt (256 chunks of 16), then device-side
-    greedy decode; tokens and the last step's logits equal the reference kernels' (bit for bit)."""
+    """The long-context configuration at its real size: a 4096-token prompt, then device-side greedy decode; tokens
+    and the last step's logits equal the reference kernels' (bit for bit), with the prompt in 256 chunks of 16 (the
+    per-token attention) and in 16 chunks of 256 (the bench's chunking: the tiled prompt attention)."""
     import os as _os
     path = synth.ensure("qwen2-0.5b")
     n_prompt, steps, ctx = 4096, 4, 4609
-    be = backend.open_model(path, ctx=ctx, prefill_chunk=16)
     prompt = synth.prompt_ids(151936, n_prompt, seed=3)
-    first = be.forward(prompt, 0)
-    dev, _ = be.generate(first, n_prompt, steps)
-    last = be.forward([int(dev[-1])], n_prompt + steps, want_logits=True)
     ref = O.open_model(_oracle_kind(), path, ctx=ctx, mt=16, threads=_os.cpu_count() or 8)
     r = ref.forward(prompt, 0)
-    assert r["next"] == first
+    first_ref = r["next"]
     want, nxt = [], r["next"]
     for i in range(steps):
         nxt = ref.forward([nxt], n_prompt + i)["next"]
         want.append(nxt)
-    assert list(dev) == want
     r = ref.forward([nxt], n_prompt + steps, want_logits=True)
-    assert last == r["next"]
-    assert np.array_equal(bits(be.read_logits()), bits(r["logits"]))
-    be.destroy()
+    for chunk in (16, 256):
+        be = backend.open_model(path, ctx=ctx, prefill_chunk=chunk)
+        first = be.forward(prompt, 0)
+        assert first == first_ref, chunk
+        dev, _ = be.generate(first, n_prompt, steps)
+        assert list(dev) == want, chunk
+        last = be.forward([int(dev[-1])], n_prompt + steps, want_logits=True)
+        assert last == r["next"], chunk
+        assert np.array_equal(bits(be.read_logits()), bits(r["logits"])), chunk
+        be.destroy()
+
+
+@pytest.mark.parametrize("model,chunk,n_prompt,scores_mb", [
+    ("small", 64, 150, None), ("gqa7", 128, 300, None), ("hd128", 32, 100, None), ("qwen2-7b-2l", 64, 150, None),
+    ("qwen2-0.5b", 256, 1100, None), ("qwen2-0.5b", 256, 600, "1"), ("hd128", 128, 260, "1")])
+def test_prompt_attention_tiles_equal_per_token_form(model, chunk, n_prompt, scores_mb, monkeypatch):
+    """Prompt passes of 32 or more tokens take the tiled attention (scores, softmax and p.v over a score buffer);
+    passes of 16 the per-token kernel. Both give the same logits bit for bit and the same decode afterwards, for
+    head_dim 64 and 128, 1 to 7 query heads per kv head, and score buffers too small for a whole pass (a 1 MB cap:
+    the pass runs in several query blocks)."""
+    path = synth.ensure(model)
+    p = np.random.default_rng(5).integers(0, synth.CONFIGS[model]["vocab"], size=n_prompt).astype(np.int32)
+
+    def run(ch, mb):
+        if mb:
+            monkeypatch.setenv("H2C_PROMPT_SCORES_MB", mb)
+        else:
+            monkeypatch.delenv("H2C_PROMPT_SCORES_MB", raising=False)
+        be = backend.open_model(path, ctx=n_prompt + 16, prefill_chunk=ch)
+        t0 = be.forward(p, 0, want_logits=True)
+        lg = be.read_logits()
+        ids, _ = be.generate(t0, n_prompt, 4)
+        be.destroy()
+        return t0, bits(lg), [int(i) for i in ids]
+
+    tiled, per_token = run(chunk, scores_mb), run(16, None)
+    assert tiled[0] == per_token[0] and tiled[2] == per_token[2]
+    assert np.array_equal(tiled[1], per_token[1])
 
 
 def test_llm_feed_reuses_the_common_prefix():
