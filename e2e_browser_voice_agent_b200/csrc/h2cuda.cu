@@ -137,6 +137,7 @@ struct h2c_engine {
   int ldT = 0;
   float* pf_s = nullptr;        // prompt attention: scores / exponentials of a pass (prompt_att.cuh), pf_bytes
   float* pf_sum = nullptr;      // and the rows' sums, [heads x max_chunk]
+  float* pf_pm = nullptr;       // and the rows' maxima per 64 positions, [heads x max_chunk][pf_pm_pitch(ctx)]
   size_t pf_bytes = 0;          // 0: prompt passes take the per-token attention
   int* tc5_err = nullptr;       // device: the tcgen05 matmul's failure record
   int32_t* tc5_err_h = nullptr; // pinned copy
@@ -938,17 +939,17 @@ void launch_prompt_attention(h2c_engine* e, int M, int pos0, int seq, int layer,
     const float* q = e->qkv + (size_t)q0 * QKV;
     float* o = att_r + (size_t)q0 * D;
     const dim3 gs((P0 + Mq + PF_TB - 1) / PF_TB, (R + PF_RB - 1) / PF_RB, KVH);
-    const int soft_grid = (KVH * R + PF_SR - 1) / PF_SR;
+    const int soft_grid = (KVH * R + PF_SR - 1) / PF_SR, ldP = pf_pm_pitch(c.ctx);
     if (HD == 64) {
       k_pf_scores<64><<<gs, 256, pf_scores_smem<64>(), st>>>(q, QKV, e->kc, H, KVH, c.ctx, NL, layer, seq, P0, Mq,
-                                                              e->pf_s, ldS);
-      k_pf_soft<<<soft_grid, 256, 0, st>>>(e->pf_s, ldS, KVH * R, R, G, P0, e->pf_sum);
+                                                              e->pf_s, ldS, e->pf_pm, ldP);
+      k_pf_soft<<<soft_grid, 256, 0, st>>>(e->pf_s, ldS, e->pf_pm, ldP, KVH * R, R, G, P0, e->pf_sum);
       k_pf_pv<64><<<dim3((R + pf_pv_rows<64>() - 1) / pf_pv_rows<64>(), KVH), 128, pf_pv_smem<64>(), st>>>(
           e->pf_s, ldS, e->pf_sum, e->vc, H, KVH, c.ctx, NL, layer, seq, P0, Mq, o, D);
     } else {
       k_pf_scores<128><<<gs, 256, pf_scores_smem<128>(), st>>>(q, QKV, e->kc, H, KVH, c.ctx, NL, layer, seq, P0, Mq,
-                                                               e->pf_s, ldS);
-      k_pf_soft<<<soft_grid, 256, 0, st>>>(e->pf_s, ldS, KVH * R, R, G, P0, e->pf_sum);
+                                                               e->pf_s, ldS, e->pf_pm, ldP);
+      k_pf_soft<<<soft_grid, 256, 0, st>>>(e->pf_s, ldS, e->pf_pm, ldP, KVH * R, R, G, P0, e->pf_sum);
       k_pf_pv<128><<<dim3((R + pf_pv_rows<128>() - 1) / pf_pv_rows<128>(), KVH), 128, pf_pv_smem<128>(), st>>>(
           e->pf_s, ldS, e->pf_sum, e->vc, H, KVH, c.ctx, NL, layer, seq, P0, Mq, o, D);
     }
@@ -1692,7 +1693,8 @@ int create_engine(int device, const h2c_config* cfg, int G, int rk, h2c_engine**
     e->pf_bytes = std::min(row * MT, cap);
     if (e->pf_bytes < row) e->pf_bytes = 0;
     if (e->pf_bytes && ((r = dalloc(e, reinterpret_cast<void**>(&e->pf_s), e->pf_bytes)) ||
-                        (r = dalloc_t(e, &e->pf_sum, (size_t)e->Hl * MT))))
+                        (r = dalloc_t(e, &e->pf_sum, (size_t)e->Hl * MT)) ||
+                        (r = dalloc_t(e, &e->pf_pm, (size_t)e->Hl * MT * pf_pm_pitch(c.ctx)))))
       return bail(r);
   }
   if (G > 1 && MT > 1) {  // staging of the gathers of passes of several tokens (the largest of them)

@@ -6,13 +6,16 @@
 // (token m, query head kh G + g, G = H / KVH); row r attends to T_r = pos0 + r / G + 1 positions.
 //
 //  k_pf_scores  S[kh][r][t] = ((((s0 + s1) + s2) + s3) * (1 / sqrt(HD)) for t < T_r, where lane l sums q[4i+l] k_t[4i+l]
-//               in order i = 0 .. HD/4-1 (products and sums rounded separately, no fused multiply-add);
-//               64 rows x 64 positions per CTA, 4 x 4 (row, position) pairs per thread, four lane sums each.
-//  k_pf_soft    max over t < T_r; e_t = fast_exp(s_t - max) written back over s_t; sum_t e_t in position order.
-//               32 rows per CTA: seven warps compute the exponentials of a 64-position chunk into shared memory while
-//               warp 0 runs the 32 rows' ordered sums over the previous chunk (lane j = row j).
+//               in order i = 0 .. HD/4-1 (products and sums rounded separately, no fused multiply-add; the products
+//               two at a time as packed f32x2 multiplies); 64 rows x 64 positions per CTA, 4 x 4 (row, position)
+//               pairs per thread, four lane sums each; also each row's maximum over the CTA's 64 positions (PM).
+//  k_pf_soft    max over t < T_r (from the partial maxima: max is order-free); e_t = fast_exp(s_t - max) written
+//               back over s_t; sum_t e_t in position order. 16 rows per CTA: seven warps compute the exponentials of
+//               a 64-position chunk into shared memory (the next chunk's scores already loading) while 16 lanes of
+//               warp 0 run the rows' ordered sums over the previous chunk (lane j = row j).
 //  k_pf_pv      o[r][d] = sum_t (e_t / sum) v_t[d] in position order; 2 rows x 4 dims per thread, V tiles of 64
-//               positions double-buffered through cp.async, the next tile's e values loaded while this one is used.
+//               positions double-buffered through cp.async, the next tile's e values loaded while this one is used;
+//               p staged twice per position so that packed multiplies take (p, p) x (v_d, v_d+1) straight from it.
 //
 // Exactness: every value is formed by the same operations in the same order as the reference's per-token loop;
 // only which thread computes it changes. Positions t >= T_r of a row are never added to its sums (the rows of one
@@ -24,7 +27,7 @@ namespace h2 {
 
 constexpr int PF_RB = 64;  // score rows per CTA
 constexpr int PF_TB = 64;  // score positions per CTA
-constexpr int PF_SR = 32;  // softmax rows per CTA
+constexpr int PF_SR = 16;  // softmax rows per CTA
 constexpr int PF_SC = 64;  // softmax positions per chunk
 constexpr int PF_VT = 64;  // p.v positions per V tile
 
@@ -33,14 +36,18 @@ __host__ __device__ constexpr int pf_scores_smem() { return (PF_RB + PF_TB) * (H
 template <int HD>
 __host__ __device__ constexpr int pf_pv_rows() { return 1024 / HD; }  // 128 threads x 2 rows x 4 dims
 template <int HD>
-__host__ __device__ constexpr int pf_pv_smem() { return (2 * PF_VT * HD + 2 * pf_pv_rows<HD>() * (PF_VT + 4)) * 4; }
+__host__ __device__ constexpr int pf_pv_smem() { return (2 * PF_VT * HD + 2 * pf_pv_rows<HD>() * (2 * PF_VT + 4)) * 4; }
+// partial maxima per row: one per PF_TB positions of the context
+__host__ __device__ constexpr int pf_pm_pitch(int ctx) { return (ctx + PF_TB - 1) / PF_TB; }
 
 // grid (ceil((pos0 + M) / PF_TB), ceil(G M / PF_RB), KVH), 256 threads, dynamic smem pf_scores_smem<HD>().
-// q: the pass's qkv rows (row stride QKV; query head h at h HD); S: [KVH][G M][ldS].
+// q: the pass's qkv rows (row stride QKV; query head h at h HD); S: [KVH][G M][ldS]; PM: [KVH][G M][ldP], entry b
+// the row's maximum over positions [64 b, 64 b + 64) below its length.
 template <int HD>
 __global__ void __launch_bounds__(256) k_pf_scores(const float* __restrict__ qkv, int QKV, const float* __restrict__ kc,
                                                    int H, int KVH, int ctx, int layers, int layer, int seq, int pos0,
-                                                   int M, float* __restrict__ S, int ldS) {
+                                                   int M, float* __restrict__ S, int ldS, float* __restrict__ PM,
+                                                   int ldP) {
   constexpr int LD = HD + 4;  // padded rows: the 16 positions a warp reads fall in distinct banks
   extern __shared__ __align__(16) float pfs[];
   float* qs = pfs;              // [PF_RB][LD]
@@ -82,11 +89,13 @@ __global__ void __launch_bounds__(256) k_pf_scores(const float* __restrict__ qkv
 #pragma unroll
     for (int a = 0; a < 4; a++)
 #pragma unroll
-      for (int b = 0; b < 4; b++) {
-        acc[a][b][0] = __fadd_rn(acc[a][b][0], __fmul_rn(q[a].x, k[b].x));
-        acc[a][b][1] = __fadd_rn(acc[a][b][1], __fmul_rn(q[a].y, k[b].y));
-        acc[a][b][2] = __fadd_rn(acc[a][b][2], __fmul_rn(q[a].z, k[b].z));
-        acc[a][b][3] = __fadd_rn(acc[a][b][3], __fmul_rn(q[a].w, k[b].w));
+      for (int b = 0; b < 4; b++) {  // products packed in pairs, sums as scalars (never fused with the products)
+        const unsigned long long p01 = f2_mul(f2(q[a].x, q[a].y), f2(k[b].x, k[b].y));
+        const unsigned long long p23 = f2_mul(f2(q[a].z, q[a].w), f2(k[b].z, k[b].w));
+        acc[a][b][0] = __fadd_rn(acc[a][b][0], f2_lo(p01));
+        acc[a][b][1] = __fadd_rn(acc[a][b][1], f2_hi(p01));
+        acc[a][b][2] = __fadd_rn(acc[a][b][2], f2_lo(p23));
+        acc[a][b][3] = __fadd_rn(acc[a][b][3], f2_hi(p23));
       }
   }
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
@@ -94,77 +103,89 @@ __global__ void __launch_bounds__(256) k_pf_scores(const float* __restrict__ qkv
 #pragma unroll
   for (int a = 0; a < 4; a++) {
     const int r = r0 + 4 * tr + a;
-    if (r >= R) continue;
-    const int T = pos0 + r / G + 1;
+    const int T = r < R ? pos0 + r / G + 1 : 0;
+    float mx = -1e30f;
 #pragma unroll
     for (int b = 0; b < 4; b++) {
       const int t = t0 + tc + 16 * b;
-      if (t < T)
-        Sk[(size_t)r * ldS + t] =
+      if (t < T) {
+        const float v =
             __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(acc[a][b][0], acc[a][b][1]), acc[a][b][2]), acc[a][b][3]), scale);
+        Sk[(size_t)r * ldS + t] = v;
+        mx = fmaxf(mx, v);
+      }
     }
+#pragma unroll
+    for (int o = 8; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));  // the 16 threads of row r
+    if (tc == 0 && r < R) PM[((size_t)kh * R + r) * ldP + blockIdx.x] = mx;
   }
 }
 
-// grid ceil(KVH G M / PF_SR), 256 threads. Flattened rows w = kh G M + r of S; sums[w] = the row's ordered sum.
-__global__ void __launch_bounds__(256) k_pf_soft(float* __restrict__ S, int ldS, int rows, int R, int G, int pos0,
-                                                 float* __restrict__ sums) {
-  constexpr int EPT = (PF_SR * PF_SC + 223) / 224;  // exponentials per thread of warps 1..7 per chunk
+// grid ceil(KVH G M / PF_SR), 256 threads. Flattened rows w = kh G M + r of S and PM; sums[w] = the row's ordered
+// sum.
+__global__ void __launch_bounds__(256) k_pf_soft(float* __restrict__ S, int ldS, const float* __restrict__ PM, int ldP,
+                                                 int rows, int R, int G, int pos0, float* __restrict__ sums) {
+  constexpr int NEL = PF_SR * PF_SC, EPT = (NEL + 223) / 224;  // exponentials per thread of warps 1..7 per chunk
   __shared__ __align__(16) float eb[2][PF_SR][PF_SC + 4];
   __shared__ float mxs[PF_SR];
   __shared__ int ts[PF_SR];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, row0 = blockIdx.x * PF_SR;
   if (tid < PF_SR) ts[tid] = row0 + tid < rows ? pos0 + ((row0 + tid) % R) / G + 1 : 0;
   __syncthreads();
-  for (int j = warp; j < PF_SR; j += 8) {  // max over the row's positions (order-free)
-    const int T = ts[j];
-    const float* s = S + (size_t)(row0 + j) * ldS;
+  for (int j = warp; j < PF_SR; j += 8) {  // the row's maximum from its partial maxima (order-free)
+    const int nb = (ts[j] + PF_TB - 1) / PF_TB;
     float mx = -1e30f;
-    for (int t = lane; t < T; t += 32) mx = fmaxf(mx, s[t]);
+    for (int b = lane; b < nb; b += 32) mx = fmaxf(mx, PM[(size_t)(row0 + j) * ldP + b]);
     mx = warp_max(mx);
     if (lane == 0) mxs[j] = mx;
   }
   int Tc = 0;
-#pragma unroll 8
+#pragma unroll
   for (int j = 0; j < PF_SR; j++) Tc = max(Tc, ts[j]);
   __syncthreads();
   const int nc = (Tc + PF_SC - 1) / PF_SC;
-  const int Tl = ts[lane];  // warp 0: lane j sums row j
+  const int Tl = lane < PF_SR ? ts[lane] : 0;  // warp 0: lane j sums row j
   float sum = 0.f;
+  float v[EPT];
+  auto load = [&](int c, float* dst) {  // chunk c's scores of this thread's elements
+#pragma unroll
+    for (int k = 0; k < EPT; k++) {
+      const int i = tid - 32 + 224 * k, j = i / PF_SC, t = c * PF_SC + i % PF_SC;
+      dst[k] = c < nc && i < NEL && t < ts[j] ? S[(size_t)(row0 + j) * ldS + t] : 0.f;
+    }
+  };
+  if (warp > 0) load(0, v);
   for (int c = 0; c <= nc; c++) {
     if (warp > 0 && c < nc) {
-      float v[EPT];
-#pragma unroll
-      for (int k = 0; k < EPT; k++) {
-        const int i = tid - 32 + 224 * k, j = i / PF_SC, t = c * PF_SC + i % PF_SC;
-        v[k] = i < PF_SR * PF_SC && t < ts[j] ? S[(size_t)(row0 + j) * ldS + t] : 0.f;
-      }
+      float nv[EPT];
+      load(c + 1, nv);  // in flight while chunk c is used
 #pragma unroll
       for (int k = 0; k < EPT; k++) {
         const int i = tid - 32 + 224 * k, j = i / PF_SC, tt = i % PF_SC, t = c * PF_SC + tt;
-        if (i < PF_SR * PF_SC && t < ts[j]) {
+        if (i < NEL && t < ts[j]) {
           const float e = fast_exp_ref(__fsub_rn(v[k], mxs[j]));
           S[(size_t)(row0 + j) * ldS + t] = e;
           eb[c & 1][j][tt] = e;
         }
+        v[k] = nv[k];
       }
     }
-    if (warp == 0 && c > 0) {  // the ordered sums over chunk c - 1 (kernels.c:368)
+    if (warp == 0 && c > 0 && lane < PF_SR) {  // the ordered sums over chunk c - 1 (kernels.c:368)
       const float* b = &eb[(c - 1) & 1][lane][0];
       const int tb = (c - 1) * PF_SC;
 #pragma unroll
       for (int q = 0; q < PF_SC / 4; q++) {
-        const float4 v = *reinterpret_cast<const float4*>(b + 4 * q);
+        const float4 x = *reinterpret_cast<const float4*>(b + 4 * q);
         const int t = tb + 4 * q;
-        if (t < Tl) sum = __fadd_rn(sum, v.x);
-        if (t + 1 < Tl) sum = __fadd_rn(sum, v.y);
-        if (t + 2 < Tl) sum = __fadd_rn(sum, v.z);
-        if (t + 3 < Tl) sum = __fadd_rn(sum, v.w);
+        if (t < Tl) sum = __fadd_rn(sum, x.x);
+        if (t + 1 < Tl) sum = __fadd_rn(sum, x.y);
+        if (t + 2 < Tl) sum = __fadd_rn(sum, x.z);
+        if (t + 3 < Tl) sum = __fadd_rn(sum, x.w);
       }
     }
     __syncthreads();  // chunk c's buffer is complete; chunk c - 1's buffer is free for chunk c + 1
   }
-  if (warp == 0 && row0 + lane < rows) sums[row0 + lane] = sum;
+  if (warp == 0 && lane < PF_SR && row0 + lane < rows) sums[row0 + lane] = sum;
 }
 
 // grid (ceil(G M / pf_pv_rows<HD>()), KVH), 128 threads, dynamic smem pf_pv_smem<HD>(). att: row stride D, query
@@ -173,10 +194,10 @@ template <int HD>
 __global__ void __launch_bounds__(128) k_pf_pv(const float* __restrict__ S, int ldS, const float* __restrict__ sums,
                                                const float* __restrict__ vc, int H, int KVH, int ctx, int layers,
                                                int layer, int seq, int pos0, int M, float* __restrict__ att, int D) {
-  constexpr int RB = pf_pv_rows<HD>(), DG = HD / 4, PL = PF_VT + 4, PF4 = RB * PF_VT / 4 / 128;
+  constexpr int RB = pf_pv_rows<HD>(), DG = HD / 4, PL = 2 * PF_VT + 4, PF4 = RB * PF_VT / 4 / 128;
   extern __shared__ __align__(16) float pvs[];
   float* vs = pvs;                   // [2][PF_VT][HD]
-  float* ps = pvs + 2 * PF_VT * HD;  // [2][RB][PL]
+  float* ps = pvs + 2 * PF_VT * HD;  // [2][RB][PL]: p of position t at 2 t and 2 t + 1
   const int kh = blockIdx.y, G = H / KVH, R = G * M, tid = threadIdx.x;
   const int r0 = blockIdx.x * RB;
   if (r0 >= R) return;
@@ -229,7 +250,9 @@ __global__ void __launch_bounds__(128) k_pf_pv(const float* __restrict__ S, int 
       p.y = t + 1 < pT[k] ? __fdiv_rn(sv[k].y, psum[k]) : 0.f;
       p.z = t + 2 < pT[k] ? __fdiv_rn(sv[k].z, psum[k]) : 0.f;
       p.w = t + 3 < pT[k] ? __fdiv_rn(sv[k].w, psum[k]) : 0.f;
-      *reinterpret_cast<float4*>(ps + (c & 1) * RB * PL + pr[k] * PL + 4 * pq[k]) = p;
+      float* d = ps + (c & 1) * RB * PL + pr[k] * PL + 8 * pq[k];
+      *reinterpret_cast<float4*>(d) = make_float4(p.x, p.x, p.y, p.y);
+      *reinterpret_cast<float4*>(d + 4) = make_float4(p.z, p.z, p.w, p.w);
     }
   };
   stage_v(0);
@@ -247,21 +270,23 @@ __global__ void __launch_bounds__(128) k_pf_pv(const float* __restrict__ S, int 
     const int t0 = c * PF_VT;
     if (t0 + PF_VT <= Tlo) {  // every row of the block attends to the whole tile
 #pragma unroll 2
-      for (int q = 0; q < PF_VT / 4; q++) {
-        const float4 xa = *reinterpret_cast<const float4*>(pa + 4 * q);
-        const float4 xb = *reinterpret_cast<const float4*>(pb + 4 * q);
-        const float pa4[4] = {xa.x, xa.y, xa.z, xa.w}, pb4[4] = {xb.x, xb.y, xb.z, xb.w};
+      for (int q = 0; q < PF_VT / 2; q++) {  // positions 2 q, 2 q + 1: (p, p) pairs straight from shared memory
+        const ulonglong2 xa = *reinterpret_cast<const ulonglong2*>(pa + 4 * q);
+        const ulonglong2 xb = *reinterpret_cast<const ulonglong2*>(pb + 4 * q);
 #pragma unroll
-        for (int u = 0; u < 4; u++) {
-          const float4 w = *reinterpret_cast<const float4*>(v + (4 * q + u) * HD);
-          a0[0] = __fadd_rn(a0[0], __fmul_rn(pa4[u], w.x));
-          a0[1] = __fadd_rn(a0[1], __fmul_rn(pa4[u], w.y));
-          a0[2] = __fadd_rn(a0[2], __fmul_rn(pa4[u], w.z));
-          a0[3] = __fadd_rn(a0[3], __fmul_rn(pa4[u], w.w));
-          a1[0] = __fadd_rn(a1[0], __fmul_rn(pb4[u], w.x));
-          a1[1] = __fadd_rn(a1[1], __fmul_rn(pb4[u], w.y));
-          a1[2] = __fadd_rn(a1[2], __fmul_rn(pb4[u], w.z));
-          a1[3] = __fadd_rn(a1[3], __fmul_rn(pb4[u], w.w));
+        for (int u = 0; u < 2; u++) {
+          const ulonglong2 w = *reinterpret_cast<const ulonglong2*>(v + (2 * q + u) * HD);
+          const unsigned long long pa2 = u ? xa.y : xa.x, pb2 = u ? xb.y : xb.x;
+          const unsigned long long qa01 = f2_mul(pa2, w.x), qa23 = f2_mul(pa2, w.y);
+          const unsigned long long qb01 = f2_mul(pb2, w.x), qb23 = f2_mul(pb2, w.y);
+          a0[0] = __fadd_rn(a0[0], f2_lo(qa01));
+          a0[1] = __fadd_rn(a0[1], f2_hi(qa01));
+          a0[2] = __fadd_rn(a0[2], f2_lo(qa23));
+          a0[3] = __fadd_rn(a0[3], f2_hi(qa23));
+          a1[0] = __fadd_rn(a1[0], f2_lo(qb01));
+          a1[1] = __fadd_rn(a1[1], f2_hi(qb01));
+          a1[2] = __fadd_rn(a1[2], f2_lo(qb23));
+          a1[3] = __fadd_rn(a1[3], f2_hi(qb23));
         }
       }
     } else {  // the rows' last positions: each row adds only t < its length
@@ -269,17 +294,18 @@ __global__ void __launch_bounds__(128) k_pf_pv(const float* __restrict__ S, int 
       for (int u = 0; u < tn; u++) {
         const int t = t0 + u;
         const float4 w = *reinterpret_cast<const float4*>(v + u * HD);
+        const float p0 = pa[2 * u], p1 = pb[2 * u];
         if (t < Ta) {
-          a0[0] = __fadd_rn(a0[0], __fmul_rn(pa[u], w.x));
-          a0[1] = __fadd_rn(a0[1], __fmul_rn(pa[u], w.y));
-          a0[2] = __fadd_rn(a0[2], __fmul_rn(pa[u], w.z));
-          a0[3] = __fadd_rn(a0[3], __fmul_rn(pa[u], w.w));
+          a0[0] = __fadd_rn(a0[0], __fmul_rn(p0, w.x));
+          a0[1] = __fadd_rn(a0[1], __fmul_rn(p0, w.y));
+          a0[2] = __fadd_rn(a0[2], __fmul_rn(p0, w.z));
+          a0[3] = __fadd_rn(a0[3], __fmul_rn(p0, w.w));
         }
         if (t < Tb) {
-          a1[0] = __fadd_rn(a1[0], __fmul_rn(pb[u], w.x));
-          a1[1] = __fadd_rn(a1[1], __fmul_rn(pb[u], w.y));
-          a1[2] = __fadd_rn(a1[2], __fmul_rn(pb[u], w.z));
-          a1[3] = __fadd_rn(a1[3], __fmul_rn(pb[u], w.w));
+          a1[0] = __fadd_rn(a1[0], __fmul_rn(p1, w.x));
+          a1[1] = __fadd_rn(a1[1], __fmul_rn(p1, w.y));
+          a1[2] = __fadd_rn(a1[2], __fmul_rn(p1, w.z));
+          a1[3] = __fadd_rn(a1[3], __fmul_rn(p1, w.w));
         }
       }
     }
