@@ -562,7 +562,7 @@ def test_fast_correctly_rounded_math_is_exact():
     assert list(out) == [0, 0, 0, 0], f"mismatches (x/127, x/896, 1/x, sqrt x): {list(out)}"
 
 
-@pytest.mark.parametrize("model", ["tiny", "gqa7", "small-q8", "qwen2-0.5b"])
+@pytest.mark.parametrize("model", ["tiny", "gqa7", "small-q8", "hd128", "qwen2-0.5b"])
 def test_forward_batch_matches_separate_sessions(model):
     """A batched decode step of several sessions (each at its own position, ragged membership across steps) gives
     every session the logits and token that its own single-token forward gives, bit for bit; on the small models
