@@ -75,7 +75,9 @@ typedef struct h2c_engine h2c_engine;
  * 8 swiglu+quantize, 9 matvec down, 10 matvec output */
 
 /* Create an engine on CUDA device `device`: allocates the KV cache and scratch (replaces set_config +
- * set_buffers, kernels.c:418-437 and the layout of cpu-worker.js:52-88). */
+ * set_buffers, kernels.c:418-437 and the layout of cpu-worker.js:52-88). With max_chunk >= 32 the scratch includes
+ * the score buffer of prompt passes: heads x max_chunk x ctx floats, at most 256 MB (the environment variable
+ * H2C_PROMPT_SCORES_MB, read here, sets another cap; longer passes then run in query blocks, same results). */
 int h2c_create(int device, const h2c_config* cfg, h2c_engine** out);
 
 /* Tensor parallelism over G GPUs of one node, one process (or thread) per GPU: the 7B configuration split so that
